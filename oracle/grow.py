@@ -1,0 +1,298 @@
+"""Oracle restatement of the level-wise tree grower (test infrastructure only).
+
+Restates ``grow_tree_levelwise`` (yabt/tree.py:362-625) on its torch-scatter
+branch (yabt/tree.py:442-452), which is the CPU execution of the exact math
+that the reference's CUDA histogram kernel (yabt/_cuda/hist.cu:27-133)
+replaces. Float arithmetic follows what torch does on the CPU for the same
+expressions, which the golden vectors pin:
+
+* histogram bins: float32 additions in row order (torch CPU ``scatter_add_``
+  is sequential; ``np.add.at`` performs the same sequence of float32 adds);
+* ``cumsum`` over bins: accumulated in float64, each prefix rounded to float32
+  (torch CPU accumulates float cumsum in double);
+* split gain, validity, boost and leaf values: float32 element-wise operations
+  in the reference's operand order, Python scalars rounded to float32;
+* argmax: first maximum in flat (feature * 256 + bin) order.
+
+Two places where the reference's order is implementation-defined are fixed
+here and documented as "parity unpinned" where they matter:
+* the ``topk`` leaf-budget cut (yabt/tree.py:527-530): kept splits are the
+  highest gains, ties broken by the lower active position;
+* ``Gtot/Htot/Ctot`` (yabt/tree.py:533-534) are float32 sums whose torch
+  reduction order is ISA specific; they are summed in float64 here and rounded.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+B = 256
+LEAF = -1
+f32 = np.float32
+
+
+@dataclass
+class TreeParams:
+    """yabt/tree.py:22-36 (axis-split fields)."""
+    max_leaves: int = 31
+    max_depth: int = 64
+    reg_lambda: float = 1.0
+    gamma: float = 0.0
+    min_child_weight: float = 1e-3
+    min_samples_leaf: int = 20
+    learning_rate: float = 0.1
+
+
+@dataclass
+class OTree:
+    """Flat tree arrays, the layout of ``Tree`` (yabt/tree.py:39-76)."""
+    feature: np.ndarray
+    threshold: np.ndarray
+    left: np.ndarray
+    right: np.ndarray
+    value: np.ndarray
+    depth: int
+    gate_scale: np.ndarray
+    leaf_net_feats: np.ndarray | None = None
+    leaf_net_linear: np.ndarray | None = None
+    leaf_net_lo: np.ndarray | None = None
+    leaf_net_hi: np.ndarray | None = None
+    # split bins (not part of Tree, kept for parity checks)
+    split_bin: np.ndarray | None = None
+    extras: dict = field(default_factory=dict)
+
+    def apply(self, X: np.ndarray) -> np.ndarray:
+        """Leaf index per row of raw X (yabt/tree.py:82-116)."""
+        n = X.shape[0]
+        node = np.zeros(n, dtype=np.int64)
+        is_leaf = self.feature == LEAF
+        for _ in range(self.depth):
+            f = np.maximum(self.feature[node], 0)
+            x = X[np.arange(n), f]
+            go_left = x <= self.threshold[node]
+            nxt = np.where(go_left, self.left[node], self.right[node])
+            node = np.where(is_leaf[node], node, nxt)
+        return node
+
+    def net_contribution(self, X: np.ndarray, node: np.ndarray) -> np.ndarray:
+        """yabt/tree.py:118-128 (linear leaves)."""
+        if self.leaf_net_feats is None:
+            return np.zeros(X.shape[0], dtype=np.float32)
+        Xs = X[:, self.leaf_net_feats]
+        Xs = np.minimum(np.maximum(Xs, self.leaf_net_lo[node]), self.leaf_net_hi[node])
+        return (self.leaf_net_linear[node] * Xs).sum(axis=1, dtype=np.float32)
+
+    def predict(self, X: np.ndarray) -> np.ndarray:
+        """yabt/tree.py:130-135."""
+        node = self.apply(X)
+        out = self.value[node]
+        if self.leaf_net_feats is not None:
+            out = out + self.net_contribution(X, node)
+        return out
+
+    def path_feature_pairs(self) -> list[tuple[int, int]]:
+        """(ancestor feature, descendant feature) pairs, yabt/tree.py:186-203."""
+        pairs: list[tuple[int, int]] = []
+        stack: list[tuple[int, tuple[int, ...]]] = [(0, ())]
+        while stack:
+            nid, anc = stack.pop()
+            f = int(self.feature[nid])
+            if f == LEAF:
+                continue
+            pairs.extend((a, f) for a in anc)
+            anc = anc + (f,)
+            stack.append((int(self.left[nid]), anc))
+            stack.append((int(self.right[nid]), anc))
+        return pairs
+
+
+def scatter_hist(binned: np.ndarray, slot: np.ndarray, g: np.ndarray, h: np.ndarray,
+                 w: np.ndarray | None, K: int) -> np.ndarray:
+    """(3, K, F, 256) float32 histogram, sequential float32 adds in row-major
+    element order (yabt/tree.py:442-452; yabt/_cuda/hist.cu:27-49 computes the
+    same sums with atomics)."""
+    n, F = binned.shape
+    flat = (slot.astype(np.int64)[:, None] * (F * B)
+            + np.arange(F, dtype=np.int64)[None, :] * B
+            + binned.astype(np.int64)).reshape(-1)
+    out = np.zeros((3, K * F * B), dtype=np.float32)
+    np.add.at(out[0], flat, np.repeat(g.astype(np.float32), F))
+    np.add.at(out[1], flat, np.repeat(h.astype(np.float32), F))
+    ww = np.ones(n, np.float32) if w is None else w.astype(np.float32)
+    np.add.at(out[2], flat, np.repeat(ww, F))
+    return out.reshape(3, K, F, B)
+
+
+def split_scan(hist: np.ndarray, lam: float, gamma: float, mcw: float, msl: int,
+               feature_mask: np.ndarray | None = None,
+               boost: np.ndarray | None = None):
+    """Per-node best split over (feature, bin), yabt/tree.py:504-525.
+
+    hist: (3, M, F, 256) float32. boost: (M, F) float32 selection multiplier
+    or None. Returns (best_idx (M,), best_gain (M,) float32, cum (3,M,F,256))."""
+    cum = np.cumsum(hist.astype(np.float64), axis=-1).astype(np.float32)
+    GL, HL, CL = cum[0], cum[1], cum[2]
+    G, H, C = GL[..., -1:], HL[..., -1:], CL[..., -1:]
+    GR, HR, CR = G - GL, H - HL, C - CL
+    lam32 = f32(lam)
+    t = GL * GL / (HL + lam32) + GR * GR / (HR + lam32) - G * G / (H + lam32)
+    gain = f32(0.5) * t - f32(gamma)
+    mcw32 = f32(mcw)
+    valid = (CL >= msl) & (CR >= msl) & (HL >= mcw32) & (HR >= mcw32)
+    valid[..., -1] = False
+    if feature_mask is not None:
+        valid &= feature_mask.reshape(1, -1, 1)
+    gain = np.where(valid, gain, f32(-np.inf)).astype(np.float32)
+    M = gain.shape[0]
+    flat = gain.reshape(M, -1)
+    if boost is None:
+        idx = flat.argmax(axis=1)
+    else:
+        sel = (gain * boost[:, :, None]).reshape(M, -1)
+        idx = sel.argmax(axis=1)
+    best_gain = flat[np.arange(M), idx]
+    return idx, best_gain, cum
+
+
+def budget_keep(best_gain: np.ndarray, remaining: int) -> np.ndarray:
+    """Leaf budget, yabt/tree.py:526-530: keep the ``remaining`` highest gains
+    among positive ones; ties go to the lower active position (the reference's
+    ``topk`` tie order is implementation defined)."""
+    do = best_gain > 0
+    if int(do.sum()) <= remaining:
+        return do
+    pos = np.arange(best_gain.shape[0])
+    cand = np.where(do, best_gain, -np.inf)
+    order = np.lexsort((pos, -cand.astype(np.float64)))
+    keep = np.zeros_like(do)
+    keep[order[:remaining]] = True
+    return keep
+
+
+def grow_levelwise(binned: np.ndarray, grad: np.ndarray, hess: np.ndarray,
+                   edges: list[np.ndarray], scales: np.ndarray, params: TreeParams,
+                   feature_mask: np.ndarray | None = None,
+                   interaction_matrix: np.ndarray | None = None,
+                   interaction_boost: float = 0.5):
+    """Restates yabt/tree.py:362-625. Returns (OTree, node_of_row, trace) where
+    trace records per level the histograms and chosen splits for parity tests."""
+    n, F = binned.shape
+    lam, gamma = params.reg_lambda, params.gamma
+    mcw, msl, lr = params.min_child_weight, params.min_samples_leaf, params.learning_rate
+    scales_c = np.maximum(scales.astype(np.float32), f32(1e-12))
+    imat = None if interaction_matrix is None else interaction_matrix.astype(np.float32)
+
+    feature, threshold, left, right, value, node_depth, gate, sbin = [], [], [], [], [], [], [], []
+
+    def add_leaf(v: float, d: int) -> int:
+        feature.append(LEAF); threshold.append(0.0); left.append(-1); right.append(-1)
+        value.append(v); node_depth.append(d); gate.append(1.0); sbin.append(-1)
+        return len(feature) - 1
+
+    # yabt/tree.py:473 (Python float arithmetic on the float32 sums)
+    gsum = float(np.sum(grad.astype(np.float64)).astype(np.float32))
+    hsum = float(np.sum(hess.astype(np.float64)).astype(np.float32))
+    add_leaf(-lr * gsum / (hsum + lam), 0)
+    node_of_row = np.zeros(n, dtype=np.int64)
+    active = [0]
+    hist = scatter_hist(binned, np.zeros(n, np.int64), grad, hess, None, 1)
+    pathmax = np.zeros((1, F), np.float32) if imat is not None else None
+    remaining = params.max_leaves - 1
+    depth = 0
+    trace = []
+    while active and depth < params.max_depth and remaining > 0:
+        M = len(active)
+        if depth == 0:
+            pr = np.zeros(n, np.int64)
+            row_active = np.ones(n, bool)
+        else:
+            node_to_pos = np.full(len(feature), -1, np.int64)
+            node_to_pos[np.array(active)] = np.arange(M)
+            pos = node_to_pos[node_of_row]
+            row_active = pos >= 0
+            pr = np.maximum(pos, 0)
+        boost = None
+        if imat is not None:
+            boost = (f32(1.0) + f32(interaction_boost) * pathmax).astype(np.float32)
+        idx, best_gain, cum = split_scan(hist, lam, gamma, mcw, msl, feature_mask, boost)
+        f, b = idx // B, idx % B
+        do = budget_keep(best_gain, remaining)
+        Gtot = hist[0, :, 0, :].astype(np.float64).sum(-1).astype(np.float32)
+        Htot = hist[1, :, 0, :].astype(np.float64).sum(-1).astype(np.float32)
+        Ctot = hist[2, :, 0, :].astype(np.float64).sum(-1).astype(np.float32)
+        mi = np.arange(M)
+        gL, hL, cL = cum[0][mi, f, b], cum[1][mi, f, b], cum[2][mi, f, b]
+        vL = (f32(-lr) * gL) / (hL + f32(lam))
+        vR = (f32(-lr) * (Gtot - gL)) / ((Htot - hL) + f32(lam))
+        small_left = cL <= (Ctot - cL)
+        trace.append(dict(hist=hist.copy(), f=f.copy(), b=b.copy(), gain=best_gain.copy(),
+                          do=do.copy(), active=list(active)))
+
+        child_l = [-1] * M
+        child_r = [-1] * M
+        nxt: list[int] = []
+        split_pos: list[int] = []
+        d1 = depth + 1
+        for m in range(M):
+            if not do[m]:
+                continue
+            split_pos.append(m)
+            gid, fm, bm = active[m], int(f[m]), int(b[m])
+            feature[gid] = fm
+            e = edges[fm]
+            threshold[gid] = float(e[min(bm, len(e) - 1)])
+            gate[gid] = float(scales_c[fm])
+            sbin[gid] = bm
+            value[gid] = 0.0
+            nl, nr = add_leaf(float(vL[m]), d1), add_leaf(float(vR[m]), d1)
+            left[gid], right[gid] = nl, nr
+            child_l[m], child_r[m] = nl, nr
+            nxt += (nl, nr)
+        remaining -= len(nxt) // 2
+
+        # yabt/tree.py:562-570 repartition
+        cl = np.array(child_l, np.int64)
+        cr = np.array(child_r, np.int64)
+        xb = binned[np.arange(n), f[pr]].astype(np.int64)
+        go_left = xb <= b[pr]
+        newn = np.where(go_left, cl[pr], cr[pr])
+        moved = row_active & do[pr]
+        node_of_row = np.where(moved, newn, node_of_row)
+
+        # yabt/tree.py:576-612 smaller-child histogram + sibling subtraction.
+        # Skipped once the loop cannot run again (the result is never read).
+        more = bool(nxt) and d1 < params.max_depth and remaining > 0
+        if more:
+            sp = np.array(split_pos, np.int64)
+            P = sp.shape[0]
+            pos_to_pair = np.full(M, -1, np.int64)
+            pos_to_pair[sp] = np.arange(P)
+            sil = small_left[sp]
+            pair_row = pos_to_pair[pr]
+            part = row_active & (pair_row >= 0)
+            sil_row = sil[np.maximum(pair_row, 0)]
+            small = part & (go_left == sil_row)
+            rows = np.nonzero(small)[0]
+            hs = scatter_hist(binned[rows], pair_row[rows], grad[rows], hess[rows], None, P)
+            hp = hist[:, sp]
+            ho = hp - hs
+            s4 = sil.reshape(1, P, 1, 1)
+            lh = np.where(s4, hs, ho)
+            rh = np.where(s4, ho, hs)
+            hist = np.empty((3, 2 * P, F, B), np.float32)
+            hist[:, 0::2] = lh
+            hist[:, 1::2] = rh
+            if imat is not None:
+                cpm = np.maximum(pathmax[sp], imat[f[sp]])
+                pathmax = np.repeat(cpm, 2, axis=0)
+        active = nxt if more else []
+        depth = d1
+
+    tree = OTree(
+        feature=np.array(feature, np.int64), threshold=np.array(threshold, np.float32),
+        left=np.array(left, np.int64), right=np.array(right, np.int64),
+        value=np.array(value, np.float32), depth=max(node_depth) + 1,
+        gate_scale=np.array(gate, np.float32), split_bin=np.array(sbin, np.int64))
+    return tree, node_of_row, trace
