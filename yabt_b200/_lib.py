@@ -1,0 +1,108 @@
+"""ctypes binding of libyabt_b200.so (the C ABI declared in include/yabt_b200.h).
+
+The library is built in-tree by ``yabt_b200.build``. There is no fallback:
+if the shared library is missing or a CUDA device is absent, calls raise.
+Loading is guarded by a lock, as the reference guards its C grower loader
+(yabt/grow_c.py:49,215).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libyabt_b200.so")
+_LOCK = threading.Lock()
+_LIB = None
+
+c_ll = ctypes.c_longlong
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+c_vp = ctypes.c_void_p
+
+
+class TreeArgs(ctypes.Structure):
+    """Mirror of ``yabt_tree_args`` (include/yabt_b200.h)."""
+    _fields_ = [
+        ("bins", c_vp), ("grad", c_vp), ("hess", c_vp), ("edges", c_vp), ("edge_off", c_vp),
+        ("edge_cnt", c_vp), ("scales", c_vp), ("feature_mask", c_vp), ("interaction", c_vp),
+        ("reg_lambda", c_float), ("gamma", c_float), ("min_child_weight", c_float),
+        ("learning_rate", c_float), ("interaction_boost", c_float), ("min_samples_leaf", ctypes.c_int32),
+        ("feature", c_vp), ("threshold", c_vp), ("left", c_vp), ("right", c_vp), ("value", c_vp),
+        ("gate_scale", c_vp), ("leaf_of_row", c_vp), ("meta", c_vp),
+    ]
+
+
+# (name, restype, argtypes) of every exported symbol
+SIGNATURES = [
+    ("yabt_version", c_int, []),
+    ("yabt_last_error", c_int, [ctypes.c_char_p, c_int]),
+    ("yabt_bin_matrix_bytes", c_ll, [c_ll, c_int]),
+    ("yabt_bin_address", c_int, [c_ll, c_int, c_int, ctypes.POINTER(c_ll), ctypes.POINTER(c_int),
+                                 ctypes.POINTER(c_int)]),
+    ("yabt_pack_bins", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
+    ("yabt_grower_create", c_int, [c_ll, c_int, c_int, c_int, c_int, ctypes.POINTER(c_vp)]),
+    ("yabt_grower_workspace_bytes", c_ll, [c_vp]),
+    ("yabt_grower_bind", c_int, [c_vp, c_vp, c_ll, c_vp]),
+    ("yabt_grower_destroy", c_int, [c_vp]),
+    ("yabt_grower_max_nodes", c_int, [c_vp]),
+    ("yabt_grower_levels", c_int, [c_vp]),
+    ("yabt_grow_tree", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_begin", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_init", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_hist", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_int, c_vp]),
+    ("yabt_grow_split", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_int, c_vp]),
+    ("yabt_grow_end", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_amax_ptr", c_vp, [c_vp]),
+    ("yabt_grow_small_ptr", c_vp, [c_vp]),
+    ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
+    ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
+]
+
+
+class YabtError(RuntimeError):
+    pass
+
+
+def load():
+    """Load the shared library (once). Raises if it is missing."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        if not os.path.exists(LIB_PATH):
+            raise YabtError(f"{LIB_PATH} is missing: build it with `python -m yabt_b200.build` "
+                            "(the CUDA path has no fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+        return lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    load().yabt_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        raise YabtError(f"{what}: yabt error {rc}: {last_error()}")
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream=None) -> int | None:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream or None

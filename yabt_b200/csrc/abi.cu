@@ -1,0 +1,361 @@
+// C ABI of libyabt_b200.so: error reporting, bin-matrix layout helpers and the
+// level-wise grower context (workspace carving + launch sequencing).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/yabt_b200.h"
+#include "grow.cuh"
+
+namespace yabt {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_level_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
+cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
+cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, int*, cudaStream_t);
+cudaError_t set_hist_smem_attrs();
+
+// ---------------------------------------------------------------- pack kernel
+__global__ void k_pack_bins(const uint8_t* __restrict__ plain, long long n, int F,
+                            uint8_t* __restrict__ tiled) {
+  const long long total = n * F;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long r = e / F;
+    const int f = (int)(e % F);
+    const FeatAddr a = feat_addr(F, n, f);
+    tiled[a.off + r * a.width + a.pos] = plain[e];
+  }
+}
+
+}  // namespace yabt
+
+using namespace yabt;
+
+#define CUDA_TRY(x)                                                              \
+  do {                                                                           \
+    cudaError_t e__ = (x);                                                       \
+    if (e__ != cudaSuccess) {                                                    \
+      set_error("%s failed: %s (%s:%d)", #x, cudaGetErrorString(e__), __FILE__, __LINE__); \
+      return YABT_ERR_CUDA;                                                      \
+    }                                                                            \
+  } while (0)
+
+static std::vector<TileInfo> host_tiles(int F, long long n, long long* bytes) {
+  std::vector<TileInfo> t(tile_count(F) + 1);
+  long long b = make_tiles(F, n, t.data());
+  t.resize(tile_count(F));
+  if (bytes) *bytes = b;
+  return t;
+}
+
+extern "C" {
+
+int yabt_version(void) { return 100; }
+
+int yabt_last_error(char* buf, int len) {
+  if (!buf || len <= 0) return YABT_ERR_ARG;
+  strncpy(buf, g_err, (size_t)len - 1);
+  buf[len - 1] = 0;
+  return YABT_OK;
+}
+
+long long yabt_bin_matrix_bytes(long long n, int F) {
+  if (n < 0 || F <= 0) return -1;
+  long long b = 0;
+  host_tiles(F, n, &b);
+  return b;
+}
+
+int yabt_bin_address(long long n, int F, int feature, long long* tile_off, int* width, int* pos) {
+  if (n < 0 || F <= 0 || feature < 0 || feature >= F) { set_error("bad bin address query"); return YABT_ERR_ARG; }
+  auto t = host_tiles(F, n, nullptr);
+  std::vector<FeatAddr> fa(F);
+  feat_addrs(F, t.data(), (int)t.size(), fa.data());
+  if (tile_off) *tile_off = fa[feature].off;
+  if (width) *width = fa[feature].width;
+  if (pos) *pos = fa[feature].pos;
+  return YABT_OK;
+}
+
+int yabt_pack_bins(const uint8_t* plain, long long n, int F, uint8_t* tiled, void* stream) {
+  if (!plain || !tiled || n < 0 || F <= 0) { set_error("yabt_pack_bins: bad arguments"); return YABT_ERR_ARG; }
+  if (n == 0) return YABT_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  long long bytes = 0;
+  host_tiles(F, n, &bytes);
+  CUDA_TRY(cudaMemsetAsync(tiled, 0, (size_t)bytes, s));
+  const long long total = n * F;
+  const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 32);
+  k_pack_bins<<<grid, 256, 0, s>>>(plain, n, F, tiled);
+  CUDA_TRY(cudaGetLastError());
+  return YABT_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- grower
+struct yabt_grower {
+  GrowParams p;
+  GrowBufs b;
+  long long ws_bytes;
+  int bound;
+  int nsm;
+  int LIMBS;
+  std::vector<UnitDesc> units;
+  std::vector<FeatAddr> faddr;
+  // carve offsets
+  struct Off { const char* name; long long bytes; long long off; };
+  std::vector<Off> offs;
+};
+
+static long long al(long long x) { return (x + 255) & ~255LL; }
+
+extern "C" {
+
+int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int general,
+                       yabt_grower** out) {
+  if (!out || n <= 0 || n >= (1LL << 31) || F <= 0 || max_leaves < 1 || max_depth < 0) {
+    set_error("yabt_grower_create: bad arguments (n=%lld F=%d max_leaves=%d max_depth=%d)", n, F,
+              max_leaves, max_depth);
+    return YABT_ERR_ARG;
+  }
+  yabt_grower* g = new yabt_grower();
+  GrowParams& p = g->p;
+  memset(&p, 0, sizeof(p));
+  p.n = n; p.F = F; p.general = general ? 1 : 0;
+  p.S = general ? 1 : 2; g->LIMBS = general ? 5 : 3; p.C = general ? 3 : 2;
+  p.max_leaves = max_leaves; p.max_depth = max_depth;
+  p.maxa = max_leaves;
+  p.maxn = 2 * max_leaves + 1;
+  p.max_pairs = std::max(1, max_leaves - 1);
+  p.levels_max = std::max(1, std::min(max_depth, max_leaves - 1));
+  // units
+  auto tiles = host_tiles(F, n, nullptr);
+  for (auto& t : tiles) {
+    if (t.wide && p.S == 1) {
+      for (int k0 = 0; k0 < 2; ++k0) {
+        UnitDesc u; memset(&u, 0, sizeof(u));
+        u.off = t.off; u.width = t.width; u.wide = 1; u.k0 = k0; u.nsub = 1;
+        for (int j = 0; j < 32; ++j) { u.feat[0][j] = t.f0 + 32 * k0 + j; u.feat[1][j] = -1; }
+        g->units.push_back(u);
+      }
+    } else {
+      UnitDesc u; memset(&u, 0, sizeof(u));
+      u.off = t.off; u.width = t.width; u.wide = t.wide; u.k0 = 0;
+      u.nsub = t.wide ? 2 : 1;
+      for (int j = 0; j < 32; ++j) {
+        u.feat[0][j] = j < std::min(t.nfeat, 32) ? t.f0 + j : -1;
+        u.feat[1][j] = (t.wide && 32 + j < t.nfeat) ? t.f0 + 32 + j : -1;
+      }
+      g->units.push_back(u);
+    }
+  }
+  p.U = (int)g->units.size();
+  g->faddr.resize(F);
+  feat_addrs(F, tiles.data(), (int)tiles.size(), g->faddr.data());
+  p.max_items = ITEM_TARGET + p.U * (int)(n / CHUNK_MAX + 1) + p.U * (p.max_pairs + 1);
+  p.max_tiles = (int)((n + PART_TILE - 1) / PART_TILE) + p.maxa + 1;
+  // workspace carve list
+  const long long HN = (long long)p.C * F * YABT_NB * 8;
+  const long long words = (long long)g->LIMBS * p.S * YABT_NB * 32;
+  auto add = [&](const char* nm, long long bytes) { g->offs.push_back({nm, bytes, 0}); };
+  add("st", sizeof(GrowState));
+  add("rows0", n * 4); add("rows1", n * 4); add("fin", n * 4);
+  add("segb0", p.maxa * 4); add("segb1", p.maxa * 4);
+  add("segc0", p.maxa * 4); add("segc1", p.maxa * 4);
+  add("gid0", p.maxa * 4); add("gid1", p.maxa * 4);
+  add("hist0", p.maxa * HN); add("hist1", p.maxa * HN);
+  add("small", (long long)p.max_pairs * HN);
+  add("pm0", (long long)p.maxa * F * 4); add("pm1", (long long)p.maxa * F * 4);
+  add("best", (long long)p.maxa * F * sizeof(NodeBest));
+  add("nbest", (long long)p.maxa * sizeof(NodeBest));
+  add("tot", (long long)p.maxa * sizeof(NodeTot));
+  add("pair_pos", p.max_pairs * 4); add("pair_sil", p.max_pairs * 4);
+  add("split_pair", p.maxa * 4); add("split_f", p.maxa * 4); add("split_b", p.maxa * 4);
+  add("tpre", (long long)(std::max(p.maxa, p.max_pairs) + 1) * 4);
+  add("items", (long long)p.max_items * sizeof(HistItem));
+  add("job_first", (long long)p.max_pairs * p.U * 4); add("job_nitems", (long long)p.max_pairs * p.U * 4);
+  add("tiles", (long long)p.max_tiles * sizeof(PartTile));
+  add("tile_status", (long long)p.max_tiles * 8);
+  add("partials", (long long)p.max_items * words * 4);
+  add("units", (long long)p.U * sizeof(UnitDesc));
+  add("faddr", (long long)F * sizeof(FeatAddr));
+  add("leaf_src", p.maxn * 4); add("leaf_begin", p.maxn * 4); add("leaf_count", p.maxn * 4);
+  add("node_depth", p.maxn * 4); add("node_bin", p.maxn * 4);
+  long long off = 0;
+  for (auto& o : g->offs) { o.off = off; off = al(off + o.bytes); }
+  g->ws_bytes = off;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int nsm = YABT_SMS_HINT;
+  if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) nsm = YABT_SMS_HINT;
+  cudaGetLastError();
+  g->nsm = nsm;
+  *out = g;
+  return YABT_OK;
+}
+
+long long yabt_grower_workspace_bytes(const yabt_grower* g) { return g ? g->ws_bytes : -1; }
+int yabt_grower_max_nodes(const yabt_grower* g) { return g ? g->p.maxn : -1; }
+int yabt_grower_levels(const yabt_grower* g) { return g ? g->p.levels_max : -1; }
+
+int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
+  if (!g || !ws) { set_error("yabt_grower_bind: null argument"); return YABT_ERR_ARG; }
+  if (bytes < g->ws_bytes) {
+    set_error("yabt_grower_bind: workspace of %lld bytes < required %lld", bytes, g->ws_bytes);
+    return YABT_ERR_WORKSPACE;
+  }
+  if (((uintptr_t)ws & 255) != 0) { set_error("yabt_grower_bind: workspace not 256-byte aligned"); return YABT_ERR_ARG; }
+  char* base = (char*)ws;
+  auto P = [&](const char* nm) -> char* {
+    for (auto& o : g->offs) if (!strcmp(o.name, nm)) return base + o.off;
+    return nullptr;
+  };
+  GrowBufs& b = g->b;
+  b.st = (GrowState*)P("st");
+  b.rows[0] = (int*)P("rows0"); b.rows[1] = (int*)P("rows1"); b.fin = (int*)P("fin");
+  b.seg_begin[0] = (int*)P("segb0"); b.seg_begin[1] = (int*)P("segb1");
+  b.seg_count[0] = (int*)P("segc0"); b.seg_count[1] = (int*)P("segc1");
+  b.act_gid[0] = (int*)P("gid0"); b.act_gid[1] = (int*)P("gid1");
+  b.hist[0] = (long long*)P("hist0"); b.hist[1] = (long long*)P("hist1");
+  b.small = (long long*)P("small");
+  b.pathmax[0] = (float*)P("pm0"); b.pathmax[1] = (float*)P("pm1");
+  b.best = (NodeBest*)P("best"); b.nbest = (NodeBest*)P("nbest"); b.tot = (NodeTot*)P("tot");
+  b.pair_pos = (int*)P("pair_pos"); b.pair_sil = (int*)P("pair_sil");
+  b.split_pair = (int*)P("split_pair"); b.split_f = (int*)P("split_f"); b.split_b = (int*)P("split_b");
+  b.node_tpre = (int*)P("tpre");
+  b.items = (HistItem*)P("items");
+  b.job_first = (int*)P("job_first"); b.job_nitems = (int*)P("job_nitems");
+  b.tiles = (PartTile*)P("tiles"); b.tile_status = (unsigned long long*)P("tile_status");
+  b.partials = (unsigned*)P("partials");
+  b.units = (UnitDesc*)P("units"); b.faddr = (FeatAddr*)P("faddr");
+  b.leaf_src = (int*)P("leaf_src"); b.leaf_begin = (int*)P("leaf_begin"); b.leaf_count = (int*)P("leaf_count");
+  b.node_depth = (int*)P("node_depth"); b.node_bin = (int*)P("node_bin");
+  cudaStream_t s = (cudaStream_t)stream;
+  CUDA_TRY(set_hist_smem_attrs());
+  CUDA_TRY(cudaMemsetAsync(b.st, 0, sizeof(GrowState), s));
+  CUDA_TRY(cudaMemsetAsync(b.tile_status, 0, (size_t)g->p.max_tiles * 8, s));
+  CUDA_TRY(cudaMemcpyAsync(b.units, g->units.data(), sizeof(UnitDesc) * g->units.size(), cudaMemcpyHostToDevice, s));
+  CUDA_TRY(cudaMemcpyAsync(b.faddr, g->faddr.data(), sizeof(FeatAddr) * g->faddr.size(), cudaMemcpyHostToDevice, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  g->bound = 1;
+  return YABT_OK;
+}
+
+int yabt_grower_destroy(yabt_grower* g) {
+  delete g;
+  return YABT_OK;
+}
+
+}  // extern "C"
+
+static int fill_io(yabt_grower* g, const yabt_tree_args* a, TreeIO* io) {
+  if (!g || !a || !g->bound) { set_error("grower not created/bound"); return YABT_ERR_ARG; }
+  if (!a->bins || !a->grad || (g->p.general && !a->hess) || !a->edges || !a->edge_off || !a->edge_cnt ||
+      !a->scales || !a->feature || !a->threshold || !a->left || !a->right || !a->value ||
+      !a->gate_scale || !a->leaf_of_row || !a->meta) {
+    set_error("yabt_tree_args: null required pointer");
+    return YABT_ERR_ARG;
+  }
+  GrowParams& p = g->p;
+  p.lam = a->reg_lambda; p.gamma = a->gamma; p.mcw = a->min_child_weight; p.lr = a->learning_rate;
+  p.ib = a->interaction_boost; p.msl = a->min_samples_leaf;
+  p.use_imat = a->interaction != nullptr; p.use_fmask = a->feature_mask != nullptr;
+  io->bins = a->bins; io->g = a->grad; io->h = g->p.general ? a->hess : nullptr;
+  io->edges = a->edges; io->edge_off = a->edge_off; io->edge_cnt = a->edge_cnt; io->scales = a->scales;
+  io->fmask = a->feature_mask; io->imat = a->interaction;
+  io->feature = (long long*)a->feature; io->threshold = a->threshold;
+  io->left = (long long*)a->left; io->right = (long long*)a->right;
+  io->value = a->value; io->gate = a->gate_scale; io->leaf_of_row = a->leaf_of_row;
+  return YABT_OK;
+}
+
+extern "C" {
+
+int yabt_grow_begin(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  CUDA_TRY(launch_tree_begin(g->p, g->b, io, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_init(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  CUDA_TRY(launch_tree_init(g->p, g->b, io, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_hist(yabt_grower* g, const yabt_tree_args* a, int level, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (level < 0 || level >= g->p.levels_max) { set_error("level out of range"); return YABT_ERR_ARG; }
+  CUDA_TRY(launch_level_hist(g->p, g->b, io, level, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_split(yabt_grower* g, const yabt_tree_args* a, int level, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (level < 0 || level >= g->p.levels_max) { set_error("level out of range"); return YABT_ERR_ARG; }
+  CUDA_TRY(launch_level_split(g->p, g->b, io, level, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_end(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  CUDA_TRY(launch_tree_finish(g->p, g->b, a->meta, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  int rc;
+  if ((rc = yabt_grow_begin(g, a, stream))) return rc;
+  if ((rc = yabt_grow_init(g, a, stream))) return rc;
+  for (int d = 0; d < g->p.levels_max; ++d) {
+    if ((rc = yabt_grow_hist(g, a, d, stream))) return rc;
+    if ((rc = yabt_grow_split(g, a, d, stream))) return rc;
+  }
+  return yabt_grow_end(g, a, stream);
+}
+
+void* yabt_grow_amax_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->amax_g : nullptr; }
+void* yabt_grow_small_ptr(yabt_grower* g) { return g && g->bound ? (void*)g->b.small : nullptr; }
+
+long long yabt_grow_small_count(const yabt_grower* g, int level) {
+  if (!g) return -1;
+  long long jobs = level == 0 ? 1 : std::min<long long>(1LL << std::min(level - 1, 30), g->p.max_pairs);
+  return jobs * g->p.C * g->p.F * YABT_NB;
+}
+
+int yabt_grow_leaf_rows(yabt_grower* g, void** src, void** begin, void** count, void** fin,
+                        void** list0, void** list1) {
+  if (!g || !g->bound) { set_error("grower not bound"); return YABT_ERR_ARG; }
+  if (src) *src = g->b.leaf_src;
+  if (begin) *begin = g->b.leaf_begin;
+  if (count) *count = g->b.leaf_count;
+  if (fin) *fin = g->b.fin;
+  if (list0) *list0 = g->b.rows[0];
+  if (list1) *list1 = g->b.rows[1];
+  return YABT_OK;
+}
+
+}  // extern "C"

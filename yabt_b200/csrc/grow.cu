@@ -1,0 +1,692 @@
+// Level-wise tree growth on the device: split scan, level finalisation (split
+// choice, leaf budget, node ids), stable row partition and next-level planning.
+//
+// Restates yabt/tree.py:362-625 (grow_tree_levelwise). Per level the host
+// launches a fixed sequence
+//     k_hist -> k_reduce -> [all-reduce hook] -> k_scan -> k_finalize -> k_partition -> k_plan
+// and every kernel reads what it has to do from the device-resident
+// GrowState, so a whole tree needs no host synchronisation.
+//
+// Floating-point semantics of the split scan match the reference CPU
+// execution: left sums are the float32 rounding of exact prefix sums (the
+// reference accumulates cumsum in float64, yabt/tree.py:504), and the gain,
+// validity, boost and leaf values use float32 operations in the reference's
+// operand order with round-to-nearest intrinsics (no FMA contraction).
+#include "grow.cuh"
+
+namespace yabt {
+
+cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
+                                int jobs, int nsm, cudaStream_t s);
+
+__device__ __forceinline__ int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+// Exclusive prefix sum of n ints by one warp (all 32 lanes must call it).
+// `in` and `out` may alias. Returns the total.
+__device__ int warp_excl_scan(const int* in, int* out, int n) {
+  const int lane = threadIdx.x & 31;
+  int carry = 0;
+  for (int base = 0; base < n; base += 32) {
+    const int v = base + lane < n ? in[base + lane] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (base + lane < n) out[base + lane] = carry + x - v;
+    carry += __shfl_sync(0xffffffffu, x, 31);
+  }
+  return carry;
+}
+
+// ------------------------------------------------------------------ per-tree setup
+__global__ void k_absmax(const float* __restrict__ g, const float* __restrict__ h, long long n,
+                         GrowState* st) {
+  unsigned mg = 0, mh = 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    mg = max(mg, f2ord(fabsf(g[i])));
+    if (h) mh = max(mh, f2ord(fabsf(h[i])));
+  }
+  for (int o = 16; o; o >>= 1) {
+    mg = max(mg, __shfl_xor_sync(0xffffffffu, mg, o));
+    mh = max(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&st->amax_g, mg);
+    if (h) atomicMax(&st->amax_h, mh);
+  }
+}
+
+__device__ void quant_scale(unsigned amax_ord, int* qe, float* scale, float* inv) {
+  float a = amax_ord ? ord2f(amax_ord) : 0.f;
+  int e = exp_bound(a);
+  int q = 30 - e;
+  q = max(-100, min(q, 100));
+  *qe = q;
+  *scale = ldexpf(1.f, q);
+  *inv = ldexpf(1.f, -q);
+}
+
+// chunk size (rows per histogram item) for R rows spread over U units
+__device__ __forceinline__ int item_chunk(long long R, int U) {
+  long long c = (R * U + ITEM_TARGET - 1) / ITEM_TARGET;
+  c = max((long long)CHUNK_MIN, min((long long)CHUNK_MAX, c));
+  return (int)c;
+}
+
+__global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
+  GrowState* st = b.st;
+  if (threadIdx.x == 0) {
+    st->level = 0; st->active = 1; st->M = 1; st->P = 0; st->n_nodes = 1;
+    st->remaining = p.max_leaves - 1; st->part_level = -1; st->plan_level = -1;
+    st->depth_max = 0; st->n_leaves = 0; st->err = 0; st->tile_counter = 0; st->n_tiles = 0;
+    quant_scale(st->amax_g, &st->qe_g, &st->gscale, &st->ginv);
+    if (p.general) quant_scale(st->amax_h, &st->qe_h, &st->hscale, &st->hinv);
+    else { st->qe_h = 0; st->hscale = 1.f; st->hinv = 1.f; }
+    b.act_gid[0][0] = 0; b.seg_begin[0][0] = 0; b.seg_count[0][0] = (int)p.n;
+    io.feature[0] = -1; io.threshold[0] = 0.f; io.left[0] = -1; io.right[0] = -1;
+    io.value[0] = 0.f; io.gate[0] = 1.f; b.node_depth[0] = 0; b.node_bin[0] = -1;
+    // root histogram items: all rows, identity list
+    const int chunk = item_chunk(p.n, p.U);
+    const int nch = (int)((p.n + chunk - 1) / chunk);
+    int slot = 0;
+    for (int u = 0; u < p.U; ++u) {
+      b.job_first[u] = slot;
+      b.job_nitems[u] = nch;
+      slot += nch;
+    }
+    if (slot > p.max_items) { atomicOr(&st->err, DERR_ITEM_OVERFLOW); slot = 0; }
+    st->n_items = slot; st->item_counter = 0;
+  }
+  __syncthreads();
+  const int chunk = item_chunk(p.n, p.U);
+  const int nch = (int)((p.n + chunk - 1) / chunk);
+  if (nch * p.U <= p.max_items) {
+    for (int i = threadIdx.x; i < nch * p.U; i += blockDim.x) {
+      const int u = i / nch, c = i % nch;
+      HistItem it;
+      it.begin = c * chunk;
+      it.count = (int)min((long long)chunk, p.n - (long long)c * chunk);
+      it.unit = u; it.job = 0; it.slot = i;
+      it.pad[0] = it.pad[1] = it.pad[2] = 0;
+      b.items[i] = it;
+    }
+  }
+  for (int f = threadIdx.x; f < p.F; f += blockDim.x) b.pathmax[0][f] = 0.f;
+}
+
+// ------------------------------------------------------------------ split scan
+// grid: jobs x ceil(F / SCAN_WARPS); one warp per feature, lane L owns bins 8L..8L+7.
+template <int C>
+__global__ void __launch_bounds__(SCAN_WARPS * 32)
+k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
+  GrowState* st = b.st;
+  if (st->level != level_gate || !st->active) return;
+  const int d = level_gate;
+  const int njobs = d == 0 ? 1 : st->P;
+  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  const int job = blockIdx.x / fblocks;
+  if (job >= njobs) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f = (blockIdx.x % fblocks) * SCAN_WARPS + warp;
+  if (f >= p.F) return;
+  const int cur = d & 1, prv = cur ^ 1;
+  const bool write_hist = d + 1 < p.levels_max;
+  const float ginv = st->ginv, hinv = st->hinv;
+  const float lam = p.lam, gam = p.gamma, mcw = p.mcw, fmsl = (float)p.msl;
+  const bool fok = !(p.use_fmask && io.fmask && !io.fmask[f]);
+  const size_t FB = (size_t)p.F * YABT_NB;
+  const size_t HN = (size_t)C * FB;           // int64 per node histogram
+  const long long* sm = b.small + (size_t)job * HN + (size_t)f * YABT_NB + lane * 8;
+
+  int nchild, pos_small, pos_other = -1;
+  const long long* par = nullptr;
+  if (d == 0) { nchild = 1; pos_small = 0; }
+  else {
+    nchild = 2;
+    const int sil = b.pair_sil[job];
+    pos_small = sil ? 2 * job : 2 * job + 1;
+    pos_other = sil ? 2 * job + 1 : 2 * job;
+    par = b.hist[prv] + (size_t)b.pair_pos[job] * HN + (size_t)f * YABT_NB + lane * 8;
+  }
+  long long vs[C][8];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const longlong2* q = reinterpret_cast<const longlong2*>(sm + c * FB);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { longlong2 t = q[i]; vs[c][2 * i] = t.x; vs[c][2 * i + 1] = t.y; }
+  }
+  for (int ch = 0; ch < nchild; ++ch) {
+    long long v[C][8];
+    const int pos = ch == 0 ? pos_small : pos_other;
+    if (ch == 0) {
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = vs[c][i];
+    } else {
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const longlong2* q = reinterpret_cast<const longlong2*>(par + c * FB);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          longlong2 t = q[i];
+          v[c][2 * i] = t.x - vs[c][2 * i];
+          v[c][2 * i + 1] = t.y - vs[c][2 * i + 1];
+        }
+      }
+    }
+    if (write_hist) {
+      long long* dst = b.hist[cur] + (size_t)pos * HN + (size_t)f * YABT_NB + lane * 8;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        longlong2* q = reinterpret_cast<longlong2*>(dst + c * FB);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = make_longlong2(v[c][2 * i], v[c][2 * i + 1]);
+      }
+    }
+    // inclusive prefix inside the lane, then exclusive scan of lane totals
+    long long lt[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+#pragma unroll
+      for (int i = 1; i < 8; ++i) v[c][i] += v[c][i - 1];
+      long long x = v[c][7];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        long long y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      long long total = __shfl_sync(0xffffffffu, x, 31);
+      long long excl = x - v[c][7];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] += excl;
+      lt[c] = total;
+    }
+    const float G = __fmul_rn(__ll2float_rn(lt[0]), ginv);
+    const float H = (C == 3) ? __fmul_rn(__ll2float_rn(lt[1]), hinv) : __ll2float_rn(lt[C - 1]);
+    const float Cn = __ll2float_rn(lt[C - 1]);
+    const float t3 = __fdiv_rn(__fmul_rn(G, G), __fadd_rn(H, lam));
+    float boost = 1.f;
+    if (p.use_imat) boost = __fadd_rn(1.f, __fmul_rn(p.ib, b.pathmax[cur][(size_t)pos * p.F + f]));
+    float bsel = -INFINITY, bgain = -INFINITY, bGL = 0.f, bHL = 0.f, bCL = 0.f;
+    int bbin = 0;
+    long long bcl = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int bin = lane * 8 + i;
+      const float GL = __fmul_rn(__ll2float_rn(v[0][i]), ginv);
+      const float CL = __ll2float_rn(v[C - 1][i]);
+      const float HL = (C == 3) ? __fmul_rn(__ll2float_rn(v[1][i]), hinv) : CL;
+      const float GR = __fsub_rn(G, GL), HR = __fsub_rn(H, HL), CR = __fsub_rn(Cn, CL);
+      const float t1 = __fdiv_rn(__fmul_rn(GL, GL), __fadd_rn(HL, lam));
+      const float t2 = __fdiv_rn(__fmul_rn(GR, GR), __fadd_rn(HR, lam));
+      float gain = __fsub_rn(__fmul_rn(0.5f, __fsub_rn(__fadd_rn(t1, t2), t3)), gam);
+      const bool valid = fok && bin != YABT_NB - 1 && CL >= fmsl && CR >= fmsl && HL >= mcw && HR >= mcw;
+      if (!valid) gain = -INFINITY;
+      const float sel = p.use_imat ? __fmul_rn(gain, boost) : gain;
+      if (i == 0 || sel > bsel) {
+        bsel = sel; bgain = gain; bGL = GL; bHL = HL; bCL = CL; bbin = bin; bcl = v[C - 1][i];
+      }
+    }
+    // warp argmax: larger sel wins, ties -> lower bin
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float os = __shfl_xor_sync(0xffffffffu, bsel, o);
+      const int ob = __shfl_xor_sync(0xffffffffu, bbin, o);
+      const float og = __shfl_xor_sync(0xffffffffu, bgain, o);
+      const float oGL = __shfl_xor_sync(0xffffffffu, bGL, o);
+      const float oHL = __shfl_xor_sync(0xffffffffu, bHL, o);
+      const float oCL = __shfl_xor_sync(0xffffffffu, bCL, o);
+      const long long ocl = __shfl_xor_sync(0xffffffffu, bcl, o);
+      if (os > bsel || (os == bsel && ob < bbin)) {
+        bsel = os; bbin = ob; bgain = og; bGL = oGL; bHL = oHL; bCL = oCL; bcl = ocl;
+      }
+    }
+    if (lane == 0) {
+      NodeBest nb;
+      nb.sel = bsel; nb.gain = bgain; nb.GL = bGL; nb.HL = bHL; nb.CL = bCL; nb.bin = bbin; nb.cl = bcl;
+      b.best[(size_t)pos * p.F + f] = nb;
+      if (f == 0) {
+        NodeTot t; t.G = G; t.H = H; t.C = Cn; t.pad = 0; t.c = lt[C - 1];
+        b.tot[pos] = t;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ finalize
+// One block. Picks each node's split (first max over features), applies the
+// leaf budget (highest gains, ties -> lower position), numbers the children
+// (ascending position, left then right), writes the tree arrays and plans the
+// partition of this level.
+__global__ void __launch_bounds__(1024)
+k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
+  GrowState* st = b.st;
+  if (st->level != level_gate || !st->active) return;
+  const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
+  const int M = st->M;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __shared__ int s_P, s_ntiles, s_remaining, s_nnodes;
+  // A: per node argmax over features
+  for (int m = warp; m < M; m += nw) {
+    // each lane: first max among its features; then first max across lanes
+    float bs = -INFINITY; int bf = p.F;
+    for (int f = lane; f < p.F; f += 32) {
+      const float s = b.best[(size_t)m * p.F + f].sel;
+      if (s > bs) { bs = s; bf = f; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      const int of = __shfl_xor_sync(0xffffffffu, bf, o);
+      if (os > bs || (os == bs && of < bf)) { bs = os; bf = of; }
+    }
+    if (bf >= p.F) bf = 0;   // every score -inf: argmax of an all -inf row is index 0
+    if (lane == 0) {
+      NodeBest nb = b.best[(size_t)m * p.F + bf];
+      b.nbest[m] = nb;
+      b.split_f[m] = bf;
+      b.split_b[m] = nb.bin;
+    }
+  }
+  __syncthreads();
+  const bool loop_ok = d < p.max_depth && st->remaining > 0;
+  const int remaining = st->remaining;
+  // B: budget rank (parallel) -> split_pair = 1 tentatively
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const float gm = b.nbest[m].gain;
+    int keep = loop_ok && gm > 0.f;
+    if (keep) {
+      int rank = 0;
+      for (int q = 0; q < M; ++q) {
+        const float gq = b.nbest[q].gain;
+        if (gq > 0.f && (gq > gm || (gq == gm && q < m))) ++rank;
+      }
+      keep = rank < remaining;
+    }
+    b.split_pair[m] = keep ? 1 : -1;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // split_pair holds 1 (keep) / -1; number the kept nodes in ascending position
+    int P = 0;
+    for (int base = 0; base < M; base += 32) {
+      const int m = base + lane;
+      const bool k = m < M && b.split_pair[m] > 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, k);
+      if (m < M) {
+        if (k) { const int q = P + __popc(bal & ((1u << lane) - 1u)); b.split_pair[m] = q; b.pair_pos[q] = m; }
+        else b.split_pair[m] = -1;
+      }
+      P += __popc(bal);
+    }
+    if (lane == 0) {
+      s_P = P;
+      s_nnodes = st->n_nodes;
+      s_remaining = remaining - P;
+      if (s_nnodes + 2 * P > p.maxn) atomicOr(&st->err, DERR_NODE_OVERFLOW);
+    }
+  }
+  __syncthreads();
+  const int P = s_P, n0 = s_nnodes;
+  const float lr = p.lr, lam = p.lam;
+  // C: tree arrays, pairs, children, leaf ranges of stopping nodes
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const int gid = b.act_gid[cur][m];
+    const int pr = b.split_pair[m];
+    const NodeTot t = b.tot[m];
+    if (d == 0) {
+      // root value, yabt/tree.py:473 (double arithmetic on the float32 sums)
+      io.value[0] = pr >= 0 ? 0.f : (float)(-(double)lr * (double)t.G / ((double)t.H + (double)lam));
+    }
+    if (pr < 0) {
+      b.leaf_src[gid] = SRC_FIN;
+      b.leaf_begin[gid] = b.seg_begin[cur][m];
+      b.leaf_count[gid] = b.seg_count[cur][m];
+      continue;
+    }
+    const NodeBest nb = b.nbest[m];
+    const int f = b.split_f[m], bin = nb.bin;
+    const int ne = io.edge_cnt[f];
+    io.feature[gid] = f;
+    io.threshold[gid] = io.edges[io.edge_off[f] + min(bin, ne - 1)];
+    io.gate[gid] = fmaxf(io.scales[f], 1e-12f);
+    io.value[gid] = 0.f;
+    b.node_bin[gid] = bin;
+    const int nl = n0 + 2 * pr, nr = nl + 1;
+    io.left[gid] = nl; io.right[gid] = nr;
+    const float nlr = -lr;
+    const float vL = __fdiv_rn(__fmul_rn(nlr, nb.GL), __fadd_rn(nb.HL, lam));
+    const float vR = __fdiv_rn(__fmul_rn(nlr, __fsub_rn(t.G, nb.GL)), __fadd_rn(__fsub_rn(t.H, nb.HL), lam));
+    io.feature[nl] = -1; io.threshold[nl] = 0.f; io.left[nl] = -1; io.right[nl] = -1;
+    io.value[nl] = vL; io.gate[nl] = 1.f; b.node_depth[nl] = d + 1; b.node_bin[nl] = -1;
+    io.feature[nr] = -1; io.threshold[nr] = 0.f; io.left[nr] = -1; io.right[nr] = -1;
+    io.value[nr] = vR; io.gate[nr] = 1.f; b.node_depth[nr] = d + 1; b.node_bin[nr] = -1;
+    b.pair_sil[pr] = nb.cl <= t.c - nb.cl;   // smaller child by (global) row count
+    b.act_gid[nxt][2 * pr] = nl;
+    b.act_gid[nxt][2 * pr + 1] = nr;
+    // child segments: inherit the parent's region; the partition fills in the split point
+    const int B = b.seg_begin[cur][m], cnt = b.seg_count[cur][m];
+    b.seg_begin[nxt][2 * pr] = B; b.seg_count[nxt][2 * pr] = 0;
+    b.seg_begin[nxt][2 * pr + 1] = B; b.seg_count[nxt][2 * pr + 1] = cnt;
+  }
+  // children path max (interaction steering): max(parent, imat[f, :])
+  if (p.use_imat) {
+    for (int e = threadIdx.x; e < P * p.F; e += blockDim.x) {
+      const int pr = e / p.F, j = e % p.F;
+      const int m = b.pair_pos[pr];
+      const int f = b.split_f[m];
+      const float v = fmaxf(b.pathmax[cur][(size_t)m * p.F + j], io.imat[(size_t)f * p.F + j]);
+      b.pathmax[nxt][(size_t)(2 * pr) * p.F + j] = v;
+      b.pathmax[nxt][(size_t)(2 * pr + 1) * p.F + j] = v;
+    }
+  }
+  // D: partition tiles over every active node's rows (stopping nodes move to fin)
+  for (int m = threadIdx.x; m < M; m += blockDim.x)
+    b.node_tpre[m] = P > 0 ? (b.seg_count[cur][m] + PART_TILE - 1) / PART_TILE : 0;
+  __syncthreads();
+  if (warp == 0) {
+    const int nt = warp_excl_scan(b.node_tpre, b.node_tpre, M);
+    if (lane == 0) { b.node_tpre[M] = nt; s_ntiles = nt <= p.max_tiles ? nt : 0; }
+    if (lane == 0 && nt > p.max_tiles) atomicOr(&st->err, DERR_TILE_OVERFLOW);
+  }
+  __syncthreads();
+  const int ntl = s_ntiles;
+  for (int e = threadIdx.x; e < ntl; e += blockDim.x) {
+    int lo = 0, hi = M - 1;            // last node with tpre <= e
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (b.node_tpre[mid] <= e) lo = mid; else hi = mid - 1;
+    }
+    const int m = lo, q = e - b.node_tpre[m];
+    const int k = b.node_tpre[m + 1] - b.node_tpre[m];
+    const int B = b.seg_begin[cur][m], cnt = b.seg_count[cur][m];
+    PartTile t;
+    t.pos = m; t.begin = B + q * PART_TILE; t.end = min(B + cnt, t.begin + PART_TILE);
+    t.last = q == k - 1; t.t_in_node = q;
+    t.pad[0] = t.pad[1] = t.pad[2] = 0;
+    b.tiles[e] = t;
+  }
+  if (P == 0) {
+    // nothing splits: every active node is a final leaf and keeps its rows in place
+    const int src = d == 0 ? SRC_IDENTITY : (cur == 0 ? SRC_LIST0 : SRC_LIST1);
+    for (int m = threadIdx.x; m < M; m += blockDim.x) b.leaf_src[b.act_gid[cur][m]] = src;
+  }
+  if (threadIdx.x == 0) {
+    const int nt = ntl;
+    st->n_tiles = nt; st->tile_counter = 0;
+    st->epoch = st->epoch + 1;
+    st->part_level = P > 0 ? d : -1;
+    st->plan_level = P > 0 ? d : -1;
+    st->P = P;
+    st->n_nodes = n0 + 2 * P;
+    st->remaining = s_remaining;
+    st->M = 2 * P;
+    st->level = d + 1;
+    st->active = (P > 0 && d + 1 < p.max_depth && s_remaining > 0) ? 1 : 0;
+    if (P > 0) st->depth_max = max(st->depth_max, d + 1);
+  }
+}
+
+// ------------------------------------------------------------------ partition
+// Stable partition of each splitting node's rows: left rows ascending from the
+// region start, right rows descending from the region end, with a decoupled
+// look-back over the node's tiles for the running left count. Rows of nodes
+// that stop are copied to `fin` at the same offsets. leaf_of_row is updated.
+__device__ __forceinline__ unsigned long long lb_word(unsigned epoch, unsigned flag, unsigned v) {
+  return ((unsigned long long)(epoch & 0x3fffffffu) << 34) | ((unsigned long long)flag << 32) | v;
+}
+
+__global__ void __launch_bounds__(PART_THREADS)
+k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
+  GrowState* st = b.st;
+  if (st->part_level != level_gate) return;
+  const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
+  const int ntiles = st->n_tiles;
+  const unsigned epoch = st->epoch;
+  const int* src = d == 0 ? nullptr : b.rows[cur];
+  int* dst = b.rows[nxt];
+  __shared__ int s_tile, s_excl;
+  __shared__ int s_wc[8][PART_THREADS / 32];
+  __shared__ int s_wpre[8][PART_THREADS / 32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  constexpr int NW = PART_THREADS / 32;
+  for (;;) {
+    if (t == 0) s_tile = atomicAdd(&st->tile_counter, 1);
+    __syncthreads();
+    const int tile = s_tile;
+    if (tile >= ntiles) break;
+    const PartTile T = b.tiles[tile];
+    const int m = T.pos;
+    const int B = b.seg_begin[cur][m], cnt = b.seg_count[cur][m];
+    const int pr = b.split_pair[m];
+    int row[8];
+    bool ok[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = T.begin + i * PART_THREADS + t;
+      ok[i] = idx < T.end;
+      row[i] = ok[i] ? (src ? src[idx] : idx) : 0;
+    }
+    if (pr < 0) {
+      const int gid = b.act_gid[cur][m];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (!ok[i]) continue;
+        const int idx = T.begin + i * PART_THREADS + t;
+        b.fin[idx] = row[i];
+        io.leaf_of_row[row[i]] = gid;
+      }
+      __syncthreads();
+      continue;
+    }
+    const int f = b.split_f[m];
+    const unsigned thr = (unsigned)b.split_b[m];
+    const FeatAddr fa = b.faddr[f];
+    const uint8_t* col = io.bins + fa.off + fa.pos;
+    bool lf[8];
+    unsigned bal[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lf[i] = ok[i] && (unsigned)__ldg(col + (size_t)row[i] * fa.width) <= thr;
+      bal[i] = __ballot_sync(0xffffffffu, lf[i]);
+      if (lane == 0) s_wc[i][warp] = __popc(bal[i]);
+    }
+    __syncthreads();
+    if (t == 0) {
+      int run = 0;
+      for (int i = 0; i < 8; ++i)
+        for (int w = 0; w < NW; ++w) { s_wpre[i][w] = run; run += s_wc[i][w]; }
+      const unsigned Lt = (unsigned)run;
+      unsigned excl = 0;
+      unsigned long long* stat = b.tile_status;
+      if (T.t_in_node == 0) {
+        atomicExch(&stat[tile], lb_word(epoch, 2u, Lt));
+      } else {
+        atomicExch(&stat[tile], lb_word(epoch, 1u, Lt));
+        int j = tile - 1;
+        long long spins = 0;
+        for (;;) {
+          const unsigned long long w = *(volatile unsigned long long*)&stat[j];
+          const unsigned we = (unsigned)(w >> 34), wf = (unsigned)(w >> 32) & 3u;
+          if (we == (epoch & 0x3fffffffu) && wf != 0u) {
+            excl += (unsigned)(w & 0xffffffffu);
+            if (wf == 2u) break;
+            --j;
+            continue;
+          }
+          if (++spins > (1LL << 24)) { atomicOr(&st->err, DERR_LOOKBACK_TIMEOUT); break; }
+        }
+        atomicExch(&stat[tile], lb_word(epoch, 2u, excl + Lt));
+      }
+      s_excl = (int)excl;
+      if (T.last) {
+        const int Ltot = (int)(excl + Lt);
+        b.seg_begin[nxt][2 * pr] = B; b.seg_count[nxt][2 * pr] = Ltot;
+        b.seg_begin[nxt][2 * pr + 1] = B + Ltot; b.seg_count[nxt][2 * pr + 1] = cnt - Ltot;
+      }
+    }
+    __syncthreads();
+    const int excl = s_excl;
+    const int off_in_node = T.begin - B;
+    const int gl = b.act_gid[nxt][2 * pr], gr = b.act_gid[nxt][2 * pr + 1];
+    const unsigned lt_mask = (1u << lane) - 1u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (!ok[i]) continue;
+      const int rl = s_wpre[i][warp] + __popc(bal[i] & lt_mask);   // left rank in tile
+      int pos;
+      if (lf[i]) pos = B + excl + rl;
+      else {
+        const int rr = off_in_node - excl + (i * PART_THREADS + t - rl);
+        pos = B + cnt - 1 - rr;
+      }
+      if (pos < B || pos >= B + cnt) { atomicOr(&st->err, DERR_SEGMENT_OVERFLOW); continue; }
+      dst[pos] = row[i];
+      io.leaf_of_row[row[i]] = lf[i] ? gl : gr;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ plan next level
+// One block: histogram items for the smaller children (local row counts come
+// from the partition), or the leaf ranges of the children when no level follows.
+// Item slots of pair q, unit u: [U * pre_q + u * nch_q, + nch_q) where nch_q is
+// the pair's chunk count and pre_q its exclusive prefix over pairs.
+__global__ void __launch_bounds__(1024)
+k_plan(GrowParams p, GrowBufs b, int level_gate) {
+  GrowState* st = b.st;
+  if (st->plan_level != level_gate) return;
+  const int d = level_gate, nxt = (d + 1) & 1;
+  const int P = st->P;
+  __shared__ int s_chunk, s_total;
+  if (!st->active) {
+    const int src = nxt == 0 ? SRC_LIST0 : SRC_LIST1;
+    for (int q = threadIdx.x; q < 2 * P; q += blockDim.x) {
+      const int gid = b.act_gid[nxt][q];
+      b.leaf_src[gid] = src;
+      b.leaf_begin[gid] = b.seg_begin[nxt][q];
+      b.leaf_count[gid] = b.seg_count[nxt][q];
+    }
+    if (threadIdx.x == 0) { st->plan_level = -1; st->n_items = 0; }
+    return;
+  }
+  // node_tpre[q] <- chunk count of pair q; job_nitems[q] <- its prefix
+  if ((threadIdx.x >> 5) == 0) {
+    const int lane = threadIdx.x & 31;
+    long long R = 0;
+    for (int q = lane; q < P; q += 32) R += b.seg_count[nxt][b.pair_sil[q] ? 2 * q : 2 * q + 1];
+    for (int o = 16; o; o >>= 1) R += __shfl_xor_sync(0xffffffffu, R, o);
+    const int chunk = item_chunk(R, p.U);
+    for (int q = lane; q < P; q += 32) {
+      const int sc = b.seg_count[nxt][b.pair_sil[q] ? 2 * q : 2 * q + 1];
+      b.node_tpre[q] = (sc + chunk - 1) / chunk;
+    }
+    __syncwarp();
+    const int tot = warp_excl_scan(b.node_tpre, b.job_nitems, P);
+    if (lane == 0) {
+      const int slots = tot * p.U;
+      const bool ok = slots <= p.max_items;
+      if (!ok) atomicOr(&st->err, DERR_ITEM_OVERFLOW);
+      s_chunk = chunk; s_total = ok ? slots : 0;
+      st->n_items = ok ? slots : 0; st->item_counter = 0; st->plan_level = -1;
+    }
+  }
+  __syncthreads();
+  const int chunk = s_chunk;
+  if (s_total == 0) return;
+  // job tables (pair-major, unit-minor)
+  for (int e = threadIdx.x; e < P * p.U; e += blockDim.x) {
+    const int q = e / p.U, u = e % p.U;
+    const int nch = b.node_tpre[q];
+    b.job_first[e] = p.U * b.job_nitems[q] + u * nch;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < P * p.U; e += blockDim.x) {
+    const int q = e / p.U, u = e % p.U;
+    const int sp = b.pair_sil[q] ? 2 * q : 2 * q + 1;
+    const int sb = b.seg_begin[nxt][sp], sc = b.seg_count[nxt][sp];
+    const int first = b.job_first[e], nch = b.node_tpre[q];
+    for (int c = 0; c < nch; ++c) {
+      HistItem it;
+      it.begin = sb + c * chunk;
+      it.count = min(chunk, sc - c * chunk);
+      it.unit = u; it.job = q; it.slot = first + c;
+      it.pad[0] = it.pad[1] = it.pad[2] = 0;
+      b.items[first + c] = it;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < P * p.U; e += blockDim.x) b.job_nitems[e] = b.node_tpre[e / p.U];
+}
+
+__global__ void k_finish(GrowParams p, GrowBufs b, int* meta) {
+  GrowState* st = b.st;
+  if (threadIdx.x == 0) {
+    meta[0] = st->n_nodes;
+    meta[1] = st->depth_max + 1;
+    meta[2] = (int)st->err;
+    meta[3] = st->level;
+    if (st->n_nodes == 1) {   // single-leaf tree: the root owns every row
+      b.leaf_src[0] = SRC_IDENTITY; b.leaf_begin[0] = 0; b.leaf_count[0] = (int)p.n;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+struct HostStep {
+  int S, LIMBS, C;
+};
+
+static inline int jobs_bound(int d, int max_pairs) {
+  if (d == 0) return 1;
+  long long j = 1LL << min(d - 1, 30);
+  return (int)std::min<long long>(j, max_pairs);
+}
+
+// Launches of one level. Returns a CUDA error code (0 on success).
+cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
+                              int nsm, cudaStream_t s) {
+  return launch_hist_kernels(p, b, io, d, jobs_bound(d, p.max_pairs), nsm, s);
+}
+
+cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
+                               int nsm, cudaStream_t s) {
+  const int jobs = jobs_bound(d, p.max_pairs);
+  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  if (!p.general) k_scan<2><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
+  else k_scan<3><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
+  k_finalize<<<1, 1024, 0, s>>>(p, b, io, d);
+  const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
+  k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, d);
+  k_plan<<<1, 1024, 0, s>>>(p, b, d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm,
+                              cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(&b.st->amax_g, 0, 2 * sizeof(unsigned), s);
+  if (e != cudaSuccess) return e;
+  // rows of a root that never splits are never partitioned: start every row at node 0
+  e = cudaMemsetAsync(io.leaf_of_row, 0, (size_t)p.n * sizeof(int), s);
+  if (e != cudaSuccess) return e;
+  const int grid = (int)std::min<long long>((p.n + 255) / 256, 8LL * nsm);
+  k_absmax<<<std::max(grid, 1), 256, 0, s>>>(io.g, p.general ? io.h : nullptr, p.n, b.st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeIO& io, cudaStream_t s) {
+  k_tree_init<<<1, 1024, 0, s>>>(p, b, io);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, int* meta, cudaStream_t s) {
+  k_finish<<<1, 32, 0, s>>>(p, b, meta);
+  return cudaGetLastError();
+}
+
+}  // namespace yabt

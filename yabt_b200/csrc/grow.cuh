@@ -1,0 +1,160 @@
+// Device-side data structures of the level-wise grower (shared by the kernels
+// in hist.cu / grow.cu). All per-tree state lives in device memory so that a
+// whole tree is grown by a fixed sequence of launches with no host sync.
+#pragma once
+#include "common.cuh"
+
+namespace yabt {
+
+constexpr int HIST_THREADS = 1024;    // k_hist block size (one block per SM)
+constexpr int PART_TILE = 4096;       // rows per partition tile
+constexpr int PART_THREADS = 512;     // 8 rows per thread
+constexpr int ITEM_TARGET = 8 * YABT_SMS_HINT;  // histogram work items per level (target)
+constexpr int CHUNK_MIN = 4096;       // rows per histogram item (lower bound)
+constexpr int CHUNK_MAX = 65536;      // rows per item (u32 limb overflow bound)
+constexpr int SCAN_WARPS = 8;         // k_scan: one warp per feature
+
+// leaf row sources
+enum : int { SRC_FIN = 0, SRC_LIST0 = 1, SRC_LIST1 = 2, SRC_IDENTITY = 3 };
+
+// A column unit = the features one histogram block accumulates: up to S
+// sub-groups ("subs") of 32 features, lane j of sub s <-> feature feat[s][j].
+struct UnitDesc {
+  long long off;  // tile block byte offset in the bin matrix
+  int width;      // tile row width in bytes
+  int wide;       // 64-wide interleaved tile
+  int k0;         // byte (0/1) of a wide tile handled by this unit when S == 1
+  int nsub;       // subs actually present (1 or 2)
+  int feat[2][32];
+};
+
+struct HistItem {       // one histogram work item: rows [begin, begin+count) of a list
+  int begin;
+  int count;
+  int unit;
+  int job;              // pair index (or 0 for the root)
+  int slot;             // partial-histogram slot
+  int pad[3];
+};
+
+struct PartTile {       // one partition tile: rows [begin, end) of active node `pos`
+  int pos;
+  int begin;
+  int end;
+  int last;             // 1 if this is the node's last tile
+  int t_in_node;
+  int pad[3];
+};
+
+struct NodeBest {       // best split of one (node, feature)
+  float sel;            // selection score (gain * boost)
+  float gain;           // true gain
+  float GL, HL, CL;     // left sums at the chosen bin (float32 of exact sums)
+  int bin;
+  long long cl;         // exact left row count (global)
+};
+
+struct NodeTot {        // node totals
+  float G, H, C;
+  int pad;
+  long long c;          // exact row count (global)
+};
+
+struct GrowState {
+  int level;            // level the next level-kernels will process
+  int active;           // 1 while the level loop continues
+  int M;                // active nodes at `level`
+  int P;                // pairs produced by the last finalize
+  int n_nodes;          // nodes in the tree so far
+  int remaining;        // leaf budget: splits still allowed
+  int part_level;       // level whose partition is pending (-1 none)
+  int plan_level;       // level whose plan is pending (-1 none)
+  int n_items;
+  int item_counter;
+  int n_tiles;
+  int tile_counter;
+  unsigned epoch;       // look-back epoch, bumped by every partition launch
+  unsigned err;         // device error bits
+  int qe_g, qe_h;       // quantisation exponents
+  float gscale, hscale; // 2^qe
+  float ginv, hinv;     // 2^-qe
+  int depth_max;        // deepest node depth so far
+  unsigned amax_g, amax_h;  // ordered-float max |g|, max h
+  int n_leaves;
+  int pad[2];
+};
+
+// Per-call grower parameters (copied by value into kernels).
+struct GrowParams {
+  long long n;
+  int F, U, S, C;       // features, units, subs per unit, hist channels (2 or 3)
+  int general;          // 1: hessian channel present (else hessian == 1 for every row)
+  int maxa;             // max active nodes per level (= max_leaves)
+  int maxn;             // max nodes
+  int max_pairs;
+  int max_items;
+  int max_tiles;
+  int max_leaves, max_depth;
+  int levels_max;
+  float lam, gamma, mcw, lr, ib;
+  int msl;
+  int use_imat;
+  int use_fmask;
+};
+
+// Device pointers of one grower workspace.
+struct GrowBufs {
+  GrowState* st;
+  int* rows[2];          // active row lists (ping-pong by level parity)
+  int* fin;              // rows of nodes that stopped (same offsets as the lists)
+  int* seg_begin[2];     // [maxa] per level parity
+  int* seg_count[2];
+  int* act_gid[2];
+  long long* hist[2];    // [maxa][C][F][256] int64 full histograms per level parity
+  long long* small;      // [max_pairs][C][F][256] small-child (or root) histograms
+  float* pathmax[2];     // [maxa][F] max over path features p of imat[p][f]
+  NodeBest* best;        // [maxa][F]
+  NodeBest* nbest;       // [maxa] chosen split per active node
+  NodeTot* tot;          // [maxa]
+  int* pair_pos;         // [max_pairs] active position of the parent of pair p
+  int* pair_sil;         // [max_pairs] small child is the left one
+  int* split_pair;       // [maxa] pair index of an active node, -1 if it stops
+  int* split_f;          // [maxa]
+  int* split_b;          // [maxa]
+  int* node_tpre;        // [max(maxa, max_pairs) + 1] scratch for per-node / per-pair prefixes
+  HistItem* items;       // [max_items]
+  int* job_first;        // [max_pairs * U]
+  int* job_nitems;       // [max_pairs * U]
+  PartTile* tiles;       // [max_tiles]
+  unsigned long long* tile_status;  // [max_tiles]
+  unsigned* partials;    // [max_items][LIMBS][S][256][32]
+  UnitDesc* units;       // [U]
+  FeatAddr* faddr;       // [F]
+  int* leaf_src;         // [maxn] SRC_*
+  int* leaf_begin;       // [maxn]
+  int* leaf_count;       // [maxn]
+  int* node_depth;       // [maxn]
+  int* node_bin;         // [maxn] split bin of internal nodes, -1 at leaves
+};
+
+// Caller-owned inputs / outputs of one tree.
+struct TreeIO {
+  const uint8_t* bins;       // tiled bin matrix
+  const float* g;
+  const float* h;            // nullptr on the unit-hessian path
+  const float* edges;        // concatenated per-feature interior edges
+  const int* edge_off;       // [F]
+  const int* edge_cnt;       // [F]
+  const float* scales;       // [F]
+  const unsigned char* fmask;  // [F] or nullptr
+  const float* imat;         // [F][F] or nullptr
+  long long* feature;        // [maxn]
+  float* threshold;
+  long long* left;
+  long long* right;
+  float* value;
+  float* gate;
+  int* leaf_of_row;          // [n]
+};
+
+}  // namespace yabt

@@ -1,0 +1,176 @@
+"""Host side of the level-wise grower: workspace management and the drop-in
+``grow_tree_levelwise`` (yabt/tree.py:362-625).
+
+A ``Grower`` owns one device workspace (a torch uint8 tensor) sized by the C
+ABI for a problem shape, and grows trees with no host synchronisation: the
+tree arrays are written into caller-provided device tensors. The drop-in
+function ``grow_tree_levelwise`` returns a ``Tree`` sized to its node count
+(one small device-to-host read, as the reference's per-level ``.tolist()``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .tree import Tree, TreeParams
+
+
+def _i32(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.int32).contiguous()
+
+
+class EdgePack:
+    """Per-feature interior edges packed for the device (concatenated values,
+    offsets, counts) plus scales."""
+
+    def __init__(self, edges: list[torch.Tensor], scales: torch.Tensor, device):
+        cnt = torch.tensor([int(len(e)) for e in edges], dtype=torch.int32)
+        off = torch.zeros_like(cnt)
+        if cnt.numel() > 1:
+            off[1:] = torch.cumsum(cnt, 0)[:-1].to(torch.int32)
+        self.values = torch.cat([torch.as_tensor(e, dtype=torch.float32).reshape(-1).cpu()
+                                 for e in edges]).to(device)
+        self.off = off.to(device)
+        self.cnt = cnt.to(device)
+        self.scales = torch.as_tensor(scales, dtype=torch.float32).to(device).contiguous()
+        self.F = len(edges)
+
+
+class Grower:
+    """One grower context (C ABI ``yabt_grower``) bound to a workspace tensor."""
+
+    def __init__(self, n: int, F: int, max_leaves: int, max_depth: int, general: bool,
+                 device: torch.device | str = "cuda"):
+        self.lib = _lib.load()
+        self.device = torch.device(device)
+        self.n, self.F, self.general = int(n), int(F), bool(general)
+        self.max_leaves, self.max_depth = int(max_leaves), int(max_depth)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.yabt_grower_create(self.n, self.F, self.max_leaves, self.max_depth,
+                                                   1 if general else 0, ctypes.byref(h)),
+                       "yabt_grower_create")
+            self.h = h
+            nbytes = int(self.lib.yabt_grower_workspace_bytes(h))
+            self.ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            _lib.check(self.lib.yabt_grower_bind(h, self.ws.data_ptr(), nbytes, _lib.stream_ptr()),
+                       "yabt_grower_bind")
+        self.max_nodes = int(self.lib.yabt_grower_max_nodes(h))
+        self.levels = int(self.lib.yabt_grower_levels(h))
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None) is not None:
+                self.lib.yabt_grower_destroy(self.h)
+        except Exception:
+            pass
+
+    def new_outputs(self) -> dict:
+        dev, m = self.device, self.max_nodes
+        return dict(
+            feature=torch.empty(m, dtype=torch.int64, device=dev),
+            threshold=torch.empty(m, dtype=torch.float32, device=dev),
+            left=torch.empty(m, dtype=torch.int64, device=dev),
+            right=torch.empty(m, dtype=torch.int64, device=dev),
+            value=torch.empty(m, dtype=torch.float32, device=dev),
+            gate_scale=torch.empty(m, dtype=torch.float32, device=dev),
+            leaf_of_row=torch.empty(self.n, dtype=torch.int32, device=dev),
+            meta=torch.zeros(4, dtype=torch.int32, device=dev),
+        )
+
+    def args(self, bins: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor | None,
+             edges: EdgePack, params: TreeParams, out: dict,
+             feature_mask: torch.Tensor | None = None,
+             interaction: torch.Tensor | None = None, interaction_boost: float = 0.5) -> _lib.TreeArgs:
+        a = _lib.TreeArgs()
+        a.bins = bins.data_ptr()
+        a.grad = grad.data_ptr()
+        a.hess = hess.data_ptr() if (hess is not None and self.general) else None
+        a.edges, a.edge_off, a.edge_cnt = edges.values.data_ptr(), edges.off.data_ptr(), edges.cnt.data_ptr()
+        a.scales = edges.scales.data_ptr()
+        a.feature_mask = feature_mask.data_ptr() if feature_mask is not None else None
+        a.interaction = interaction.data_ptr() if interaction is not None else None
+        a.reg_lambda = float(params.reg_lambda)
+        a.gamma = float(params.gamma)
+        a.min_child_weight = float(params.min_child_weight)
+        a.learning_rate = float(params.learning_rate)
+        a.interaction_boost = float(interaction_boost)
+        a.min_samples_leaf = int(params.min_samples_leaf)
+        for k in ("feature", "threshold", "left", "right", "value", "gate_scale", "leaf_of_row", "meta"):
+            setattr(a, k, out[k].data_ptr())
+        return a
+
+    def grow(self, a: _lib.TreeArgs, stream=None) -> None:
+        _lib.check(self.lib.yabt_grow_tree(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
+                   "yabt_grow_tree")
+
+    def leaf_rows(self) -> dict:
+        ptrs = [ctypes.c_void_p() for _ in range(6)]
+        _lib.check(self.lib.yabt_grow_leaf_rows(self.h, *[ctypes.byref(p) for p in ptrs]),
+                   "yabt_grow_leaf_rows")
+        return dict(zip(("src", "begin", "count", "fin", "list0", "list1"), [p.value for p in ptrs]))
+
+
+def bin_matrix_bytes(n: int, F: int) -> int:
+    return int(_lib.load().yabt_bin_matrix_bytes(int(n), int(F)))
+
+
+def pack_bins(binned: torch.Tensor) -> torch.Tensor:
+    """Plain row-major (n, F) uint8 -> tiled layout (device)."""
+    binned = binned.contiguous()
+    n, F = binned.shape
+    out = torch.empty(bin_matrix_bytes(n, F), dtype=torch.uint8, device=binned.device)
+    _lib.check(_lib.load().yabt_pack_bins(binned.data_ptr(), n, F, out.data_ptr(), _lib.stream_ptr()),
+               "yabt_pack_bins")
+    return out
+
+
+def trim_tree(out: dict, n_nodes: int, depth: int) -> Tree:
+    k = n_nodes
+    return Tree(feature=out["feature"][:k], threshold=out["threshold"][:k], left=out["left"][:k],
+                right=out["right"][:k], value=out["value"][:k], depth=depth,
+                gate_scale=out["gate_scale"][:k])
+
+
+_GROWERS: dict = {}
+
+
+def grow_tree_levelwise(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor, binner,
+                        params: TreeParams, feature_mask: torch.Tensor | None = None,
+                        interaction_matrix: torch.Tensor | None = None,
+                        interaction_boost: float = 0.5, *, return_leaf: bool = False):
+    """Drop-in for yabt/tree.py:362-625 on a CUDA device.
+
+    ``binned`` is the plain (n, F) uint8 bin matrix (it is packed into the
+    tiled layout on the device). The hessian channel is dropped when every
+    hessian equals 1 (squared loss), which the reference's float32 sums of
+    ones reproduce exactly. Returns the ``Tree`` (and the leaf of every row
+    when ``return_leaf``)."""
+    if binned.device.type != "cuda":
+        raise ValueError("grow_tree_levelwise (yabt_b200) needs CUDA tensors")
+    n, F = binned.shape
+    dev = binned.device
+    general = not bool(torch.all(hess == 1.0))
+    key = (n, F, params.max_leaves, params.max_depth, general, dev.index)
+    gr = _GROWERS.get(key)
+    if gr is None:
+        gr = _GROWERS[key] = Grower(n, F, params.max_leaves, params.max_depth, general, dev)
+    tiled = pack_bins(binned)
+    ep = EdgePack(list(binner.edges_), binner.scales_, dev)
+    out = gr.new_outputs()
+    fm = feature_mask.to(device=dev, dtype=torch.uint8).contiguous() if feature_mask is not None else None
+    im = interaction_matrix.to(device=dev, dtype=torch.float32).contiguous() if interaction_matrix is not None else None
+    g = grad.to(torch.float32).contiguous()
+    h = hess.to(torch.float32).contiguous()
+    a = gr.args(tiled, g, h, ep, params, out, fm, im, interaction_boost)
+    gr.grow(a)
+    meta = out["meta"].tolist()
+    if meta[2] != 0:
+        raise _lib.YabtError(f"device error bits 0x{meta[2]:x} while growing a tree")
+    tree = trim_tree(out, meta[0], meta[1])
+    if return_leaf:
+        return tree, out["leaf_of_row"].to(torch.int64)
+    return tree
