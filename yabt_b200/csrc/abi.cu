@@ -23,7 +23,7 @@ cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&,
 cudaError_t launch_level_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
-cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, int*, cudaStream_t);
+cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, int*, int*, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
 
 // ---------------------------------------------------------------- pack kernel
@@ -322,7 +322,7 @@ int yabt_grow_end(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   TreeIO io;
   int rc = fill_io(g, a, &io);
   if (rc) return rc;
-  CUDA_TRY(launch_tree_finish(g->p, g->b, a->meta, (cudaStream_t)stream));
+  CUDA_TRY(launch_tree_finish(g->p, g->b, a->meta, a->leaf_of_row, g->nsm, (cudaStream_t)stream));
   return YABT_OK;
 }
 

@@ -74,31 +74,38 @@ struct FeatAddr {
   int pos;        // byte position within the tile row
 };
 
+// Tile plan of F features: full 64-wide tiles; a remainder r >= 32 becomes a
+// 32-wide tile (r -= 32); a remaining r' > 16 a 32-wide tile padded with
+// zero bytes, r' in 1..16 a 16-wide padded tile. Every tile row is 64, 32 or
+// 16 bytes, so rows are always moved with 16-byte copies.
 __host__ __device__ inline int tile_count(int F) {
-  int full = F / YABT_TILE, r = F % YABT_TILE, t = full;
+  int t = F / YABT_TILE, r = F % YABT_TILE;
   if (r >= 32) { t += 1; r -= 32; }
   if (r > 0) t += 1;
   return t;
+}
+
+__host__ __device__ inline long long tile_block_bytes(long long n, int width) {
+  return (n * width + 255) & ~255LL;
 }
 
 // fill tiles[0..ntiles) for F features and n rows; returns total bytes
 inline long long make_tiles(int F, long long n, TileInfo* tiles) {
   int t = 0, f = 0;
   long long off = 0;
-  auto align = [](long long x) { return (x + 255) & ~255LL; };
   for (; f + YABT_TILE <= F; f += YABT_TILE) {
     tiles[t] = TileInfo{f, YABT_TILE, YABT_TILE, 1, off};
-    off = align(off + n * YABT_TILE); ++t;
+    off += tile_block_bytes(n, YABT_TILE); ++t;
   }
   int r = F - f;
   if (r >= 32) {
     tiles[t] = TileInfo{f, 32, 32, 0, off};
-    off = align(off + n * 32); ++t; f += 32; r -= 32;
+    off += tile_block_bytes(n, 32); ++t; f += 32; r -= 32;
   }
   if (r > 0) {
-    int w = (r + 3) & ~3;
+    const int w = r > 16 ? 32 : 16;
     tiles[t] = TileInfo{f, r, w, 0, off};
-    off = align(off + n * w); ++t;
+    off += tile_block_bytes(n, w); ++t;
   }
   return off;
 }
@@ -116,7 +123,7 @@ inline void feat_addrs(int F, const TileInfo* tiles, int ntiles, FeatAddr* out) 
 // Address of feature f in the tiled layout, computed analytically (matches
 // make_tiles / feat_addrs).
 __host__ __device__ inline FeatAddr feat_addr(int F, long long n, int f) {
-  const long long a64 = (n * YABT_TILE + 255) & ~255LL;
+  const long long a64 = tile_block_bytes(n, YABT_TILE);
   const int nfull = F / YABT_TILE;
   if (f < nfull * YABT_TILE) {
     const int t = f / YABT_TILE, i = f % YABT_TILE;
@@ -126,9 +133,9 @@ __host__ __device__ inline FeatAddr feat_addr(int F, long long n, int f) {
   int r = F - nfull * YABT_TILE, f0 = nfull * YABT_TILE;
   if (r >= 32) {
     if (f < f0 + 32) return FeatAddr{off, 32, f - f0};
-    off += (n * 32 + 255) & ~255LL; f0 += 32; r -= 32;
+    off += tile_block_bytes(n, 32); f0 += 32; r -= 32;
   }
-  return FeatAddr{off, (r + 3) & ~3, f - f0};
+  return FeatAddr{off, r > 16 ? 32 : 16, f - f0};
 }
 
 // ---------------------------------------------------------------- misc device helpers

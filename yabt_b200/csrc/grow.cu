@@ -435,7 +435,7 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
 // Stable partition of each splitting node's rows: left rows ascending from the
 // region start, right rows descending from the region end, with a decoupled
 // look-back over the node's tiles for the running left count. Rows of nodes
-// that stop are copied to `fin` at the same offsets. leaf_of_row is updated.
+// that stop are copied to `fin` at the same offsets.
 __device__ __forceinline__ unsigned long long lb_word(unsigned epoch, unsigned flag, unsigned v) {
   return ((unsigned long long)(epoch & 0x3fffffffu) << 34) | ((unsigned long long)flag << 32) | v;
 }
@@ -472,13 +472,11 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
       row[i] = ok[i] ? (src ? src[idx] : idx) : 0;
     }
     if (pr < 0) {
-      const int gid = b.act_gid[cur][m];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         if (!ok[i]) continue;
         const int idx = T.begin + i * PART_THREADS + t;
         b.fin[idx] = row[i];
-        io.leaf_of_row[row[i]] = gid;
       }
       __syncthreads();
       continue;
@@ -532,7 +530,6 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     __syncthreads();
     const int excl = s_excl;
     const int off_in_node = T.begin - B;
-    const int gl = b.act_gid[nxt][2 * pr], gr = b.act_gid[nxt][2 * pr + 1];
     const unsigned lt_mask = (1u << lane) - 1u;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -546,7 +543,6 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
       }
       if (pos < B || pos >= B + cnt) { atomicOr(&st->err, DERR_SEGMENT_OVERFLOW); continue; }
       dst[pos] = row[i];
-      io.leaf_of_row[row[i]] = lf[i] ? gl : gr;
     }
     __syncthreads();
   }
@@ -624,16 +620,71 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
   for (int e = threadIdx.x; e < P * p.U; e += blockDim.x) b.job_nitems[e] = b.node_tpre[e / p.U];
 }
 
-__global__ void k_finish(GrowParams p, GrowBufs b, int* meta) {
+// One block: tree metadata, and the leaves' row intervals sorted by start.
+// The leaf row ranges (in `fin` or a final list; they share one offset space
+// and are disjoint) tile [0, n), so k_leaf_assign can map every position to
+// its leaf with a binary search.
+__global__ void __launch_bounds__(1024)
+k_finish(GrowParams p, GrowBufs b, int* meta) {
   GrowState* st = b.st;
+  const int nn = st->n_nodes;
+  __shared__ int s_nl;
   if (threadIdx.x == 0) {
-    meta[0] = st->n_nodes;
+    meta[0] = nn;
     meta[1] = st->depth_max + 1;
     meta[2] = (int)st->err;
     meta[3] = st->level;
-    if (st->n_nodes == 1) {   // single-leaf tree: the root owns every row
+    if (nn == 1) {   // single-leaf tree: the root owns every row
       b.leaf_src[0] = SRC_IDENTITY; b.leaf_begin[0] = 0; b.leaf_count[0] = (int)p.n;
     }
+    s_nl = 0;
+  }
+  __syncthreads();
+  // rank leaves (feature < 0 is not visible here; leaves are nodes with node_bin < 0)
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    if (b.node_bin[g] >= 0) continue;
+    // order by (begin, non-empty, id): an empty range sorts before the
+    // non-empty range that starts at the same position
+    const int bg = b.leaf_begin[g], ng = b.leaf_count[g] > 0;
+    int rank = 0;
+    for (int q = 0; q < nn; ++q) {
+      if (b.node_bin[q] >= 0) continue;
+      const int bq = b.leaf_begin[q], nq = b.leaf_count[q] > 0;
+      if (bq < bg || (bq == bg && (nq < ng || (nq == ng && q < g)))) ++rank;
+    }
+    b.split_f[rank] = g;            // reuse per-node scratch: sorted leaf gids
+    atomicAdd(&s_nl, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) st->n_leaves = s_nl;
+}
+
+// Writes leaf_of_row[row] = leaf for every position of the final leaf ranges.
+__global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_of_row) {
+  GrowState* st = b.st;
+  const int nl = st->n_leaves;
+  extern __shared__ int sm_leaf[];          // [nl] begins, [nl] gids, [nl] srcs
+  int* sb = sm_leaf;
+  int* sg = sm_leaf + nl;
+  int* ss = sm_leaf + 2 * nl;
+  for (int i = threadIdx.x; i < nl; i += blockDim.x) {
+    const int g = b.split_f[i];
+    sb[i] = b.leaf_begin[g]; sg[i] = g; ss[i] = b.leaf_src[g];
+  }
+  __syncthreads();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n;
+       i += (long long)gridDim.x * blockDim.x) {
+    int lo = 0, hi = nl - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sb[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    const int src = ss[lo];
+    int row;
+    if (src == SRC_IDENTITY) row = (int)i;
+    else if (src == SRC_FIN) row = b.fin[i];
+    else row = b.rows[src == SRC_LIST0 ? 0 : 1][i];
+    leaf_of_row[row] = sg[lo];
   }
 }
 
@@ -671,9 +722,7 @@ cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const Tree
                               cudaStream_t s) {
   cudaError_t e = cudaMemsetAsync(&b.st->amax_g, 0, 2 * sizeof(unsigned), s);
   if (e != cudaSuccess) return e;
-  // rows of a root that never splits are never partitioned: start every row at node 0
-  e = cudaMemsetAsync(io.leaf_of_row, 0, (size_t)p.n * sizeof(int), s);
-  if (e != cudaSuccess) return e;
+
   const int grid = (int)std::min<long long>((p.n + 255) / 256, 8LL * nsm);
   k_absmax<<<std::max(grid, 1), 256, 0, s>>>(io.g, p.general ? io.h : nullptr, p.n, b.st);
   return cudaGetLastError();
@@ -684,8 +733,11 @@ cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeI
   return cudaGetLastError();
 }
 
-cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, int* meta, cudaStream_t s) {
-  k_finish<<<1, 32, 0, s>>>(p, b, meta);
+cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, int* meta, int* leaf_of_row,
+                               int nsm, cudaStream_t s) {
+  k_finish<<<1, 1024, 0, s>>>(p, b, meta);
+  const int grid = (int)std::min<long long>((p.n + 511) / 512, 4LL * nsm);
+  k_leaf_assign<<<std::max(grid, 1), 512, 3 * (p.max_leaves + 1) * sizeof(int), s>>>(p, b, leaf_of_row);
   return cudaGetLastError();
 }
 

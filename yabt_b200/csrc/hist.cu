@@ -58,21 +58,118 @@ __device__ __forceinline__ void acc_row(unsigned* sh, unsigned b0, unsigned b1, 
   }
 }
 
-// rows: the active row list (nullptr = identity, row = begin + i)
+// ---------------------------------------------------------------- async copy helpers
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// Block geometry and shared-memory budget of k_hist: the histogram plus a
+// per-warp ring of STG stages of 512 bytes (one 16-byte async copy per lane).
 template <int S, int LIMBS>
-__global__ void __launch_bounds__(HIST_THREADS, 1)
+struct HistPipe {
+  static constexpr int WARPS = (S == 2) ? 16 : 32;
+  static constexpr int THREADS = WARPS * 32;
+  static constexpr int STG = 4;
+  static constexpr int STAGE_BYTES = 512;
+  static constexpr int SMEM = HistCfg<S, LIMBS>::SMEM + WARPS * STG * STAGE_BYTES;
+};
+
+// One work item of one warp: rows [w0, w1) of the item (positions in the row
+// list), tile rows of TW bytes. Stage s holds RPS = 512/TW rows; lane copies
+// 16 bytes (row lane/LPR, piece lane%LPR). Row ids are loaded one iteration
+// ahead of their copy and gradients travel with the copy, so a warp keeps
+// STG-1 stages (1.5 KB) in flight while it consumes one.
+template <int S, int LIMBS, int TW>
+__device__ __forceinline__ void hist_warp(unsigned* __restrict__ sh, uint8_t* __restrict__ ring,
+                                          const uint8_t* __restrict__ tb, const int* __restrict__ lst,
+                                          int base, int nrow, const float* __restrict__ g,
+                                          const float* __restrict__ h, float gs, float hs,
+                                          int k0, bool ok0, bool ok1, int lane) {
+  constexpr int LPR = TW / 16;
+  constexpr int RPS = 32 / LPR;
+  constexpr int STG = HistPipe<S, LIMBS>::STG;
+  const int rr = lane / LPR, piece = lane % LPR;
+  const int nst = (nrow + RPS - 1) / RPS;
+  auto rid_of = [&](int s) -> int {
+    const int k = s * RPS + rr;
+    if (k >= nrow) return -1;
+    return lst ? __ldg(lst + base + k) : base + k;
+  };
+  auto copy = [&](int s, int r) {
+    if (r >= 0) cp_async16(ring + (s % STG) * 512 + lane * 16, tb + (size_t)r * TW + piece * 16);
+  };
+  float gq[STG], hq[STG];
+#pragma unroll
+  for (int s = 0; s < STG - 1; ++s) {
+    const int r = rid_of(s);
+    gq[s] = r >= 0 ? __ldg(g + r) : 0.f;
+    hq[s] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    if (s < nst) copy(s, r);
+    cp_commit();
+  }
+  int rnext = rid_of(STG - 1);
+  for (int s = 0; s < nst; ++s) {
+    const int r = rnext;
+    rnext = rid_of(s + STG);
+    gq[STG - 1] = r >= 0 ? __ldg(g + r) : 0.f;
+    hq[STG - 1] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    if (s + STG - 1 < nst) copy(s + STG - 1, r);
+    cp_commit();
+    cp_wait<STG - 1>();
+    __syncwarp();
+    const int vgl = __float2int_rn(gq[0] * gs);
+    const int vhl = (LIMBS == 5) ? __float2int_rn(hq[0] * hs) : 0;
+    const uint8_t* stg = ring + (s % STG) * 512;
+#pragma unroll
+    for (int q = 0; q < RPS; ++q) {
+      const int vg = __shfl_sync(0xffffffffu, vgl, q * LPR);
+      int vh = 0;
+      if constexpr (LIMBS == 5) vh = __shfl_sync(0xffffffffu, vhl, q * LPR);
+      if (s * RPS + q < nrow) {
+        unsigned wv = 0;
+        if constexpr (TW == 64) {
+          if constexpr (S == 2) wv = *reinterpret_cast<const unsigned short*>(stg + q * 64 + 2 * lane);
+          else wv = stg[q * 64 + 2 * lane + k0];
+        } else {
+          if (TW == 32 || lane < 16) wv = stg[q * TW + (lane & (TW - 1))];
+        }
+        acc_row<S, LIMBS>(sh, wv & 0xFFu, (wv >> 8) & 0xFFu, ok0, ok1, lane, vg, vh);
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int t = 0; t < STG - 1; ++t) { gq[t] = gq[t + 1]; hq[t] = hq[t + 1]; }
+  }
+  cp_wait<0>();
+}
+
+// rows: the active row list (nullptr = identity, row = begin + i)
+// Persistent: one block per SM takes histogram work items from a device
+// counter; each item's shared histogram is zeroed, filled by the warps (each
+// streams a contiguous share of the item's rows) and flushed to its partial slot.
+template <int S, int LIMBS>
+__global__ void __launch_bounds__(HistPipe<S, LIMBS>::THREADS, 1)
 k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
        const float* __restrict__ g, const float* __restrict__ h,
        const HistItem* __restrict__ items, const UnitDesc* __restrict__ units,
        GrowState* st, unsigned* __restrict__ partials, int level_gate) {
   using Cfg = HistCfg<S, LIMBS>;
+  using Pipe = HistPipe<S, LIMBS>;
   extern __shared__ __align__(16) unsigned sh[];
   __shared__ int s_item;
   if (st->level != level_gate || !st->active) return;
   const int nitems = st->n_items;
   const float gs = st->gscale, hs = st->hscale;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  constexpr int UNR = 8;
+  uint8_t* ring = reinterpret_cast<uint8_t*>(sh + Cfg::WORDS) + warp * Pipe::STG * Pipe::STAGE_BYTES;
   for (;;) {
     if (threadIdx.x == 0) s_item = atomicAdd(&st->item_counter, 1);
     __syncthreads();
@@ -83,52 +180,19 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
     for (int i = threadIdx.x * 4; i < Cfg::WORDS; i += blockDim.x * 4)
       *reinterpret_cast<uint4*>(sh + i) = make_uint4(0, 0, 0, 0);
     __syncthreads();
-
     const uint8_t* tb = bins + ud.off;
-    const int width = ud.width;
-    const bool wide = ud.wide;
-    const int k0 = ud.k0;
     const bool ok0 = ud.feat[0][lane] >= 0;
     const bool ok1 = (S == 2) && ud.nsub > 1 && ud.feat[S == 2 ? 1 : 0][lane] >= 0;
+    const int per = (item.count + nw - 1) / nw;
+    const int w0 = min(item.count, warp * per), w1 = min(item.count, w0 + per);
     const int* lst = rows ? rows + item.begin : nullptr;
-    const int cnt = item.count;
-    for (int base = warp * 32; base < cnt; base += nw * 32) {
-      const int k = base + lane;
-      const bool okr = k < cnt;
-      int r = 0, vg = 0, vh = 0;
-      if (okr) {
-        r = lst ? __ldg(lst + k) : item.begin + k;
-        vg = __float2int_rn(__ldg(g + r) * gs);
-        if constexpr (LIMBS == 5) vh = __float2int_rn(__ldg(h + r) * hs);
-      }
-      const int nr = min(32, cnt - base);
-      for (int u0 = 0; u0 < nr; u0 += UNR) {
-        unsigned wv[UNR];
-        int gv[UNR], hv[UNR];
-#pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-          const int rr = __shfl_sync(0xffffffffu, r, u0 + u);
-          gv[u] = __shfl_sync(0xffffffffu, vg, u0 + u);
-          if constexpr (LIMBS == 5) hv[u] = __shfl_sync(0xffffffffu, vh, u0 + u);
-          else hv[u] = 0;
-          wv[u] = 0;
-          if (u0 + u < nr) {
-            const uint8_t* rp = tb + (size_t)rr * width;
-            if (wide) {
-              if constexpr (S == 2) wv[u] = __ldg(reinterpret_cast<const unsigned short*>(rp) + lane);
-              else wv[u] = __ldg(rp + 2 * lane + k0);
-            } else if (ok0) {
-              wv[u] = __ldg(rp + lane);
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-          if (u0 + u < nr)
-            acc_row<S, LIMBS>(sh, wv[u] & 0xFFu, (wv[u] >> 8) & 0xFFu, ok0, ok1, lane, gv[u], hv[u]);
-        }
-      }
-    }
+    const int base = rows ? w0 : item.begin + w0;
+    if (ud.width == 64)
+      hist_warp<S, LIMBS, 64>(sh, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+    else if (ud.width == 32)
+      hist_warp<S, LIMBS, 32>(sh, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+    else
+      hist_warp<S, LIMBS, 16>(sh, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
     __syncthreads();
     unsigned* dst = partials + (size_t)item.slot * Cfg::WORDS;
     for (int i = threadIdx.x * 4; i < Cfg::WORDS; i += blockDim.x * 4)
@@ -137,19 +201,22 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
 }
 
 // One block per (job, unit, sub, bin-part): sums the u32-limb partials of the
-// job's items for 32 bins x 32 lanes into exact int64 and writes
-// [job][c][f][bin] (c = 0 g, 1 h (general path), last = count) through a small
-// shared-memory transpose.
-constexpr int RED_PARTS = 8;   // bins are split into 8 parts of 32
+// job's items for 16 bins x 32 lanes (one word per thread) into exact int64
+// and writes [job][c][f][bin] (c = 0 g, 1 h (general path), last = count)
+// through a small shared-memory transpose. The item loop is unrolled so that
+// 8 items' limbs are in flight per thread.
+constexpr int RED_PARTS = 16;   // bins are split into 16 parts of 16
+constexpr int RED_THREADS = 512;
 template <int S, int LIMBS>
-__global__ void __launch_bounds__(512)
+__global__ void __launch_bounds__(RED_THREADS)
 k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_first,
          const int* __restrict__ job_nitems, const HistItem* __restrict__ items,
          const UnitDesc* __restrict__ units, GrowState* st, long long* __restrict__ out,
          int F, int U, int level_gate) {
   using Cfg = HistCfg<S, LIMBS>;
   constexpr int C = (LIMBS == 5) ? 3 : 2;
-  __shared__ long long tsm[C][32][33];
+  constexpr int BPP = YABT_NB / RED_PARTS;     // bins per part (16)
+  __shared__ long long tsm[C][32][BPP + 1];
   if (st->level != level_gate || !st->active) return;
   const int njobs = (level_gate == 0) ? 1 : st->P;
   int b = blockIdx.x;
@@ -162,21 +229,37 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   if (sub >= ud.nsub) return;
   const int first = job_first[job * U + unit];
   const int nit = job_nitems[job * U + unit];
-  // 1024 words (32 bins x 32 lanes) per block; thread t handles words t and t+512
-  for (int w = threadIdx.x; w < 32 * 32; w += blockDim.x) {
-    const int word = part * 32 * 32 + w;      // (bin, j) word inside the sub
-    long long ag = 0, ah = 0;
-    unsigned long long ac = 0;
-    for (int q = 0; q < nit; ++q) {
-      const unsigned* p = partials + (size_t)items[first + q].slot * Cfg::WORDS + sub * YABT_NB * 32 + word;
-      const unsigned glo = __ldg(p), ghi = __ldg(p + Cfg::LIMB_STRIDE);
-      ag += (long long)(int)ghi * 65536LL + (long long)glo;
-      if constexpr (LIMBS == 5) {
-        const unsigned hlo = __ldg(p + 2 * Cfg::LIMB_STRIDE), hhi = __ldg(p + 3 * Cfg::LIMB_STRIDE);
-        ah += (long long)(int)hhi * 65536LL + (long long)hlo;
-      }
-      ac += __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE);
+  const int w = threadIdx.x;                               // (bin-in-part, lane)
+  const size_t woff = (size_t)sub * YABT_NB * 32 + (size_t)part * BPP * 32 + w;
+  long long ag = 0, ah = 0;
+  unsigned long long ac = 0;
+  constexpr int UNR = 8;
+  int q = 0;
+  for (; q + UNR <= nit; q += UNR) {
+    unsigned lo[UNR], hi[UNR], cn[UNR], hlo[UNR], hhi[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const unsigned* p = partials + (size_t)__ldg(&items[first + q + u].slot) * Cfg::WORDS + woff;
+      lo[u] = __ldg(p);
+      hi[u] = __ldg(p + Cfg::LIMB_STRIDE);
+      if constexpr (LIMBS == 5) { hlo[u] = __ldg(p + 2 * Cfg::LIMB_STRIDE); hhi[u] = __ldg(p + 3 * Cfg::LIMB_STRIDE); }
+      cn[u] = __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE);
     }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      ag += (long long)(int)hi[u] * 65536LL + (long long)lo[u];
+      if constexpr (LIMBS == 5) ah += (long long)(int)hhi[u] * 65536LL + (long long)hlo[u];
+      ac += cn[u];
+    }
+  }
+  for (; q < nit; ++q) {
+    const unsigned* p = partials + (size_t)__ldg(&items[first + q].slot) * Cfg::WORDS + woff;
+    ag += (long long)(int)__ldg(p + Cfg::LIMB_STRIDE) * 65536LL + (long long)__ldg(p);
+    if constexpr (LIMBS == 5)
+      ah += (long long)(int)__ldg(p + 3 * Cfg::LIMB_STRIDE) * 65536LL + (long long)__ldg(p + 2 * Cfg::LIMB_STRIDE);
+    ac += __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE);
+  }
+  {
     const int bl = w >> 5, j = w & 31;
     tsm[0][j][bl] = ag;
     if constexpr (C == 3) tsm[1][j][bl] = ah;
@@ -184,11 +267,11 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   }
   __syncthreads();
   const long long job_base = (long long)job * C * F * YABT_NB;
-  for (int e = threadIdx.x; e < C * 32 * 32; e += blockDim.x) {
-    const int bl = e & 31, j = (e >> 5) & 31, c = e >> 10;
+  for (int e = threadIdx.x; e < C * 32 * BPP; e += blockDim.x) {
+    const int bl = e % BPP, j = (e / BPP) & 31, c = e / (BPP * 32);
     const int f = ud.feat[sub][j];
     if (f < 0) continue;
-    out[job_base + ((long long)c * F + f) * YABT_NB + part * 32 + bl] = tsm[c][j][bl];
+    out[job_base + ((long long)c * F + f) * YABT_NB + part * BPP + bl] = tsm[c][j][bl];
   }
 }
 
@@ -196,16 +279,14 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
                                 int jobs, int nsm, cudaStream_t s) {
   const int* rows = d == 0 ? nullptr : b.rows[d & 1];
   if (!p.general) {
-    using Cfg = HistCfg<2, 3>;
-    k_hist<2, 3><<<nsm, HIST_THREADS, Cfg::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+    k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
-    k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS, 512, 0, s>>>(b.partials, b.job_first, b.job_nitems,
+    k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS, RED_THREADS, 0, s>>>(b.partials, b.job_first, b.job_nitems,
                                                               b.items, b.units, b.st, b.small, p.F, p.U, d);
   } else {
-    using Cfg = HistCfg<1, 5>;
-    k_hist<1, 5><<<nsm, HIST_THREADS, Cfg::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+    k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
-    k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS, 512, 0, s>>>(b.partials, b.job_first, b.job_nitems,
+    k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS, RED_THREADS, 0, s>>>(b.partials, b.job_first, b.job_nitems,
                                                               b.items, b.units, b.st, b.small, p.F, p.U, d);
   }
   return cudaGetLastError();
@@ -213,10 +294,10 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
 
 cudaError_t set_hist_smem_attrs() {
   cudaError_t e = cudaFuncSetAttribute(k_hist<2, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       HistCfg<2, 3>::SMEM);
+                                       HistPipe<2, 3>::SMEM);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(k_hist<1, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              HistCfg<1, 5>::SMEM);
+                              HistPipe<1, 5>::SMEM);
 }
 
 }  // namespace yabt
