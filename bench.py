@@ -1,0 +1,335 @@
+#!/usr/bin/env python
+"""Benchmark of the YABT per-tree growth path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4]
+
+A step is one boosting iteration (gradients, level-wise tree growth, ridge-
+linear neural leaves, interaction-score update, margin update) on the
+configuration's synthetic data. The default workload is BASELINE config 4
+(10M x 200 correlated features, 255 leaves, max depth 10, squared loss,
+neural leaves and interaction steering on). Prints one JSON line.
+
+value   trees/s over all GPUs with the inputs resident in HBM (CUDA events,
+        max over ranks).
+e2e     trees/s through the public estimator API (YABTRegressor.fit) from host
+        memory: host->device copy of X and y, binning and K trees per fit.
+impl=reference  the reference's own CPU implementation of the path (its OpenMP
+        C grower yabt/_cgrow/grow.c, built under oracle/_ref, plus the oracle
+        restatement of its leaf models) on a row sample, scaled to the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (n, F, leaves, max_depth, loss, lr)
+    "c1": (20_000, 20, 31, 64, "mse", 0.1),
+    "c2": (100_000, 50, 63, 64, "logloss", 0.05),
+    "c3": (1_000_000, 100, 127, 64, "mse", 0.1),
+    "c4": (10_000_000, 200, 255, 10, "mse", 0.1),
+    "c5": (5_000_000, 128, 63, 64, "logloss", 0.1),
+}
+
+
+def make_data(cfg: str, n: int, F: int, device, seed: int = 0):
+    """Seeded synthetic data with the configuration's shapes and distributions
+    (generated on the device with torch's Philox generator)."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    if cfg == "c4":
+        X = torch.randn(n, F, generator=g, device=device).mul_(0.7 ** 0.5)
+        zb = torch.randn(n, F // 10, generator=g, device=device).mul_(0.3 ** 0.5)
+        X.view(n, F // 10, 10).add_(zb.unsqueeze(2))
+        del zb
+        w = torch.randn(50, generator=g, device=device)
+        y = torch.tanh(X[:, :50]) @ w
+        for k in range(10):
+            y += X[:, 2 * k] * X[:, 2 * k + 1]
+        y += torch.randn(n, generator=g, device=device)
+    elif cfg == "c1":
+        X = torch.randn(n, F, generator=g, device=device)
+        y = torch.sin(X[:, 0]) + X[:, 1] * X[:, 2] + 0.5 * X[:, 3] ** 2 + 0.2 * X[:, 4:10].sum(1)
+        y += 0.1 * torch.randn(n, generator=g, device=device)
+    elif cfg == "c3":
+        X = torch.randn(n, F, generator=g, device=device)
+        X[:, 80:] = torch.exp(X[:, 80:])
+        w = torch.randn(20, generator=g, device=device)
+        y = X[:, :20] @ w + 0.5 * X[:, 20] * X[:, 21] + 0.5 * torch.randn(n, generator=g, device=device)
+        X[torch.rand(n, F, generator=g, device=device) < 0.05] = float("nan")
+    else:   # c2 / c5 (binary / multiclass-as-binary for timing)
+        X = torch.randn(n, F, generator=g, device=device)
+        if cfg == "c5":
+            X[torch.rand(n, F, generator=g, device=device) < 0.3] = 0.0
+        logit = 0.8 * X[:, 0] - 0.5 * X[:, 1] + X[:, 2] * X[:, 3] + 0.3 * X[:, 4:15].sum(1)
+        y = (torch.rand(n, generator=g, device=device) < torch.sigmoid(logit)).float()
+    return X.contiguous(), y.contiguous()
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = [ln.split(",") for ln in open(self.f.name).read().strip().splitlines() if ln.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        load = [v for v in sm if v > 500] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference(cfg: str, steps: int, warmup: int, threads: int, sample_rows: int, X_src=None, y_src=None):
+    """The reference's CPU path (C grower + C apply + leaf models) on a row
+    sample of the workload; returns (trees/s scaled to the full workload,
+    seconds per sample step, sample description)."""
+    from oracle import cgrow
+    from oracle.binning import Binner as OBinner
+    n, F, leaves, depth, loss, lr = CONFIGS[cfg]
+    if X_src is None:
+        rng = np.random.default_rng(0)
+        X = rng.standard_normal((sample_rows, F), dtype=np.float32)
+        y = (np.tanh(X[:, :min(50, F)]) @ rng.standard_normal(min(50, F)).astype(np.float32)).astype(np.float32)
+    else:
+        X, y = X_src, y_src
+    b = OBinner().fit(X)
+    bins_fm = np.ascontiguousarray(b.transform(X).T)
+    Xi = b.impute(X)
+    margin = np.full(X.shape[0], float(y.mean()), np.float32)
+    times = []
+    for s in range(warmup + steps):
+        dt, margin = cgrow.boosting_step_seconds(bins_fm, Xi, y, margin, b.edges_, leaves, depth, lr, threads)
+        if s >= warmup:
+            times.append(dt)
+    per = statistics.median(times)
+    scale = X.shape[0] / n
+    return scale / per, per, f"{X.shape[0]} of {n} rows x {F} features, {leaves} leaves; trees/s scaled by rows"
+
+
+def run_reference(args):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = args.config
+    n, F, leaves, depth, loss, lr = CONFIGS[cfg]
+    threads = os.cpu_count() or 1
+    from oracle import cgrow
+    if not cgrow.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libcgrow.so not built"}))
+        return
+    sample = min(n, args.ref_rows)
+    X = y = None
+    if torch.cuda.is_available():
+        Xd, yd = make_data(cfg, sample, F, "cuda", seed=0)
+        X, y = Xd.cpu().numpy(), yd.cpu().numpy()
+    tps, per, desc = cpu_reference(cfg, args.steps, args.warmup, threads, sample, X, y)
+    line = {"impl": "reference", "metric": "trees_per_sec", "value": tps, "unit": "trees/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{cfg}: {n}x{F}, {leaves} leaves, max_depth {depth}, {loss}, "
+                                   "neural leaves, interaction steering"},
+            "cpu_baseline": {"value": tps, "unit": "trees/s", "cores": threads, "kind": "reference",
+                             "sample": desc},
+            "e2e": {"value": tps, "unit": "trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from yabt_b200 import _lib
+    from yabt_b200.boosting import Booster, BoostParams, DeviceData, LogLoss, MSELoss
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    cfg = args.config
+    n, F, leaves, depth, loss_name, lr = CONFIGS[cfg]
+    n_local = n  # weak scaling: every rank grows the full per-GPU workload
+    lib = _lib.load()
+    X, y = make_data(cfg, n_local, F, dev, seed=1000 + rank)
+    loss = MSELoss() if loss_name == "mse" else LogLoss()
+    W, K = args.warmup, args.steps
+    params = BoostParams(n_estimators=W + K, max_leaves=leaves, max_depth=depth, learning_rate=lr)
+    data = DeviceData(X, params.max_bins, dev)
+    y_host = y.cpu().numpy()
+    del X
+    torch.cuda.synchronize()
+
+    ev = {}
+    marks = {}
+
+    def cb(t, grower):
+        if t == 0:
+            grower.set_timing(K * grower.levels)      # create the event pool early
+        if t == W - 1:
+            grower.set_timing(K * grower.levels)      # restart recording (no allocation)
+            grower.acc_reset()
+            ev["start"] = torch.cuda.Event(enable_timing=True)
+            ev["start"].record()
+            marks["launches0"] = int(lib.yabt_launch_count())
+            if sampler:
+                sampler.start()
+        if t == W + K - 1:
+            ev["stop"] = torch.cuda.Event(enable_timing=True)
+            ev["stop"].record()
+            marks["launches1"] = int(lib.yabt_launch_count())
+
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    booster = Booster(params, loss)
+    booster.fit(None, y_host, data=data, tree_callback=cb)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = ev["start"].elapsed_time(ev["stop"])
+    hist_ms = booster.grower_.hist_times()
+    root_rows, child_rows, hist_launches = booster.grower_.acc_read()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    trees_per_s = world * K / (ms / 1000.0)
+
+    # Roofline of the histogram kernel (k_hist): algorithmic bytes of the timed
+    # trees = rows histogrammed x (F bin bytes + 4 B gradient [+ 4 B hessian]
+    # [+ 4 B row id below the root]); achieved = bytes / summed k_hist time.
+    gh = 4 + (4 if loss_name != "mse" else 0)
+    alg_bytes = root_rows * (F + gh) + child_rows * (F + gh + 4)
+    hist_total_ms = sum(hist_ms)
+    achieved = alg_bytes / (hist_total_ms / 1000.0) / 1e9 if hist_total_ms > 0 else float("nan")
+    alg_per_launch = alg_bytes / max(hist_launches, 1)
+    avg_hist_ms = hist_total_ms / max(hist_launches, 1)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    bin_reads_per_s = world * (root_rows + child_rows) * F / (ms / 1000.0)
+
+    # e2e through the public estimator API from host memory (rank 0 fits alone)
+    e2e = None
+    if rank == 0 and not args.no_e2e:
+        from yabt_b200 import YABTRegressor, YABTClassifier
+        Xh = make_data(cfg, n_local, F, dev, seed=1000 + rank)[0].cpu().pin_memory()
+        est_cls = YABTRegressor if loss_name == "mse" else YABTClassifier
+        kw = dict(max_leaves=leaves, max_depth=depth, learning_rate=lr)
+        est_cls(n_estimators=1, **kw).fit(Xh[:4096], y_host[:4096])   # warm-up (context, library)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        est = est_cls(n_estimators=K, **kw).fit(Xh, y_host)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        e2e = {"value": K / dt, "unit": "trees/s",
+               "h2d_bytes_per_step": int((Xh.numel() * 4 + y_host.nbytes) / K),
+               "d2h_bytes_per_step": int(K * 4 * 4 / K + 4)}
+        del Xh, est
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import cgrow
+        if cgrow.available():
+            sample = min(n, args.ref_rows)
+            Xs, ys = make_data(cfg, sample, F, dev, seed=0)
+            tps, per, desc = cpu_reference(cfg, 1, 1, os.cpu_count() or 1, sample, Xs.cpu().numpy(),
+                                           ys.cpu().numpy())
+            cpu = {"value": tps, "unit": "trees/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": "trees_per_sec", "value": trees_per_s, "unit": "trees/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch Philox, config shapes)",
+            "config": {"workload": f"{cfg}: {n_local}x{F} per GPU, {leaves} leaves, max_depth {depth}, "
+                                   f"{loss_name}, neural leaves, interaction steering",
+                       "global_rows": n_local * world, "l2": "inputs larger than L2 (bin matrix "
+                       f"{data.bins.numel() / 1e9:.2f} GB)", "parallelism": f"rows x{world}"},
+            "bin_reads_per_sec": bin_reads_per_s,
+            "gpu_launches": marks.get("launches1", 0) - marks.get("launches0", 0),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "k_hist", "alg_bytes_per_launch": alg_per_launch,
+                         "avg_launch_ms": avg_hist_ms, "launches_timed": hist_launches,
+                         "hist_share_of_step": hist_total_ms / ms,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
+    ap.add_argument("--ref-rows", type=int, default=500_000)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 1:
+        args.warmup = 1
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

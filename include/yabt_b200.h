@@ -33,6 +33,9 @@ int yabt_version(void);
 /* Copy the last error message of this thread into buf (NUL-terminated). */
 int yabt_last_error(char* buf, int len);
 
+/* Number of kernels the library has launched so far in this process. */
+long long yabt_launch_count(void);
+
 /* ------------------------------------------------------------------ bin matrix
  * The tiled bin-matrix layout (see DESIGN.md "Data layout"): size in bytes for
  * n rows x F features, and the byte address of (row, feature).            */
@@ -66,6 +69,17 @@ int yabt_grower_destroy(yabt_grower* g);
 int yabt_grower_max_nodes(const yabt_grower* g);
 /* Levels the host must drive (yabt_grow_hist / yabt_grow_split calls). */
 int yabt_grower_levels(const yabt_grower* g);
+/* Per-launch timing of the histogram kernel: record CUDA events around up to
+ * max_launches histogram launches (0 disables); yabt_grower_hist_times returns
+ * their durations in ms (synchronising) and resets the pool.              */
+int yabt_grower_set_timing(yabt_grower* g, int max_launches);
+int yabt_grower_hist_times(yabt_grower* g, float* ms, int cap, int* count);
+/* Rows histogrammed at each level of the last tree (synchronising copy). */
+int yabt_grower_hist_rows(yabt_grower* g, long long* rows, int cap);
+/* Accumulators since the last reset: root-level rows, deeper-level smaller-
+ * child rows, histogram levels that did work (reset is stream-ordered).    */
+int yabt_grower_acc_reset(yabt_grower* g, void* stream);
+int yabt_grower_acc_read(yabt_grower* g, long long* out3);
 
 typedef struct {
   /* inputs (device) */
@@ -111,6 +125,115 @@ long long yabt_grow_small_count(const yabt_grower* g, int level);
  * src (0 fin, 1 list0, 2 list1, 3 identity), begin, count; plus list bases. */
 int yabt_grow_leaf_rows(yabt_grower* g, void** src, void** begin, void** count,
                         void** fin, void** list0, void** list1);
+
+
+/* ------------------------------------------------------------------ binning
+ * Quantile binner, bit-exact with the numpy path of Binner.fit / transform
+ * (yabt/binning.py:29-112).                                               */
+
+/* X (n, F) row-major float32 -> Xfm (F, n) feature-major. */
+int yabt_transpose(const float* X, long long n, int F, float* Xfm, void* stream);
+long long yabt_bin_fit_workspace_bytes(long long n, int F, long long nq);
+/* Medians over all rows; edges / scales from the sample rows sample_idx[nq]
+ * (NULL: rows 0..nq-1). edges is [F][255] (first edge_cnt[f] valid).
+ * Replaces Binner.fit (yabt/binning.py:29-69).                           */
+int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
+                 int max_bins, void* workspace, long long ws_bytes, float* medians, float* edges,
+                 int32_t* edge_cnt, float* scales, void* stream);
+/* NaN -> median in Xfm (in place), bins = #{edges < x} into the tiled layout
+ * (and, if plain_out != NULL, the plain (n, F) matrix).
+ * Replaces Binner.transform / impute (yabt/binning.py:97-124).           */
+int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, const float* edges,
+                       const int32_t* edge_cnt, uint8_t* tiled, uint8_t* plain_out, void* stream);
+
+/* ------------------------------------------------------------------ neural leaves
+ * Ridge-linear leaf models of one grown tree (fit_leaf_networks with
+ * leaf_net_hidden == 0, yabt/neural_leaves.py:131-184).                  */
+typedef struct {
+  const int64_t* feature;         /* [max_nodes] tree arrays from yabt_grow_* */
+  float* value;                   /* [max_nodes] updated in place (folded bias) */
+  int32_t max_nodes;
+  const int32_t* meta;            /* grower meta (n_nodes first) */
+  const int32_t* leaf_src;        /* leaf row ranges (yabt_grow_leaf_rows) */
+  const int32_t* leaf_begin;
+  const int32_t* leaf_count;
+  const int32_t* fin;
+  const int32_t* list0;
+  const int32_t* list1;
+  const int32_t* leaf_of_row;     /* [n] */
+  const float* Xfm;               /* [F][n] imputed features */
+  const float* col_mean;          /* [F] column means (yabt_column_stats) */
+  const float* col_std;           /* [F] unbiased column std */
+  const float* margin;            /* [n] ensemble margin excluding this tree */
+  const float* y;                 /* [n] */
+  long long n;
+  int32_t F;
+  int32_t K;                      /* min(leaf_net_features, F), 1..8 */
+  int32_t loss;                   /* 0 squared error, 1 logistic */
+  int32_t min_samples;            /* leaf_net_min_samples */
+  float l2;                       /* leaf_net_l2 */
+  float learning_rate;
+  int64_t* feats;                 /* out [K] */
+  float* linear;                  /* out [max_nodes][K] */
+  float* lo;                      /* out [max_nodes][K] */
+  float* hi;                      /* out [max_nodes][K] */
+  int32_t* has_nets;              /* out [1]: 0 when no leaf is eligible */
+} yabt_leafnet_args;
+
+long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes);
+int yabt_leafnet_fit(const yabt_leafnet_args* a, void* workspace, long long ws_bytes, void* stream);
+
+/* Margin update of one tree and the next tree's gradients
+ * (yabt/boosting.py:36-38,53-54,511-514; Tree.net_contribution yabt/tree.py:118-128). */
+typedef struct {
+  const int32_t* leaf_of_row;
+  const float* value;
+  const float* linear;            /* NULL: constant leaves */
+  const float* lo;
+  const float* hi;
+  const int64_t* feats;
+  const int32_t* has_nets;
+  int32_t K;
+  const float* Xfm;
+  long long n;
+  float* margin;                  /* in/out */
+  const float* y;
+  float* grad;                    /* out, or NULL */
+  float* hess;                    /* out, or NULL (unit hessian) */
+  int32_t loss;
+} yabt_update_args;
+
+int yabt_update_margin(const yabt_update_args* a, void* stream);
+int yabt_grad_init(const float* margin, const float* y, long long n, int loss, float* grad, float* hess,
+                   void* stream);
+/* Column means and unbiased stds of Xfm (fp64 accumulation). */
+int yabt_column_stats(const float* Xfm, long long n, int F, float* mean, float* std, void* stream);
+
+/* ------------------------------------------------------------------ interaction steering
+ * FeatureInteractionDetector.update_from_path_pairs / normalized_matrix
+ * (yabt/adaptive_features.py:129-160) on the device.                     */
+int yabt_interaction_update(const int64_t* feature, const int64_t* left, const int64_t* right,
+                            const int32_t* meta, int F, int max_nodes, float* scores,
+                            int32_t* parent_scratch, void* stream);
+int yabt_interaction_normalize(const float* scores, int F, float* imat, void* stream);
+
+/* ------------------------------------------------------------------ inference
+ * Batched prediction of a packed forest (Booster._margin / Tree.predict,
+ * yabt/boosting.py:542-550, yabt/tree.py:82-135). X is the imputed raw
+ * (n, F) row-major matrix; node arrays of all trees are concatenated, tree t
+ * starting at tree_off[t], child indices local to the tree. has_nets[t] = 0
+ * (or has_nets == NULL) means constant leaves.                           */
+int yabt_predict_forest(const float* X, long long n, int F, int ntrees, const int64_t* tree_off,
+                        const int32_t* feature, const float* threshold, const int32_t* left,
+                        const int32_t* right, const float* value, const int32_t* has_nets,
+                        const int64_t* feats, int K, const float* linear, const float* lo, const float* hi,
+                        float base, float* out, void* stream);
+/* Leaf index per row for one tree (Tree.apply, yabt/tree.py:82-116; the
+ * reference's C variant capply, yabt/_cgrow/grow.c:223-239).              */
+int yabt_apply_tree(const float* X, long long n, int F, const int64_t* feature, const float* threshold,
+                    const int64_t* left, const int64_t* right, int64_t* out, void* stream);
+/* NaN -> medians[f] in a row-major (n, F) matrix (Binner.impute, yabt/binning.py:121-124). */
+int yabt_impute_rows(float* X, long long n, int F, const float* medians, void* stream);
 
 #ifdef __cplusplus
 }

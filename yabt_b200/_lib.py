@@ -35,10 +35,38 @@ class TreeArgs(ctypes.Structure):
     ]
 
 
+class LeafNetArgs(ctypes.Structure):
+    """Mirror of ``yabt_leafnet_args``."""
+    _fields_ = [
+        ("feature", c_vp), ("value", c_vp), ("max_nodes", ctypes.c_int32), ("meta", c_vp),
+        ("leaf_src", c_vp), ("leaf_begin", c_vp), ("leaf_count", c_vp), ("fin", c_vp),
+        ("list0", c_vp), ("list1", c_vp), ("leaf_of_row", c_vp), ("Xfm", c_vp), ("col_mean", c_vp),
+        ("col_std", c_vp), ("margin", c_vp), ("y", c_vp), ("n", c_ll), ("F", ctypes.c_int32),
+        ("K", ctypes.c_int32), ("loss", ctypes.c_int32), ("min_samples", ctypes.c_int32),
+        ("l2", c_float), ("learning_rate", c_float), ("feats", c_vp), ("linear", c_vp),
+        ("lo", c_vp), ("hi", c_vp), ("has_nets", c_vp),
+    ]
+
+
+class UpdateArgs(ctypes.Structure):
+    """Mirror of ``yabt_update_args``."""
+    _fields_ = [
+        ("leaf_of_row", c_vp), ("value", c_vp), ("linear", c_vp), ("lo", c_vp), ("hi", c_vp),
+        ("feats", c_vp), ("has_nets", c_vp), ("K", ctypes.c_int32), ("Xfm", c_vp), ("n", c_ll),
+        ("margin", c_vp), ("y", c_vp), ("grad", c_vp), ("hess", c_vp), ("loss", ctypes.c_int32),
+    ]
+
+
 # (name, restype, argtypes) of every exported symbol
 SIGNATURES = [
     ("yabt_version", c_int, []),
     ("yabt_last_error", c_int, [ctypes.c_char_p, c_int]),
+    ("yabt_launch_count", c_ll, []),
+    ("yabt_grower_set_timing", c_int, [c_vp, c_int]),
+    ("yabt_grower_hist_times", c_int, [c_vp, ctypes.POINTER(c_float), c_int, ctypes.POINTER(c_int)]),
+    ("yabt_grower_hist_rows", c_int, [c_vp, ctypes.POINTER(c_ll), c_int]),
+    ("yabt_grower_acc_reset", c_int, [c_vp, c_vp]),
+    ("yabt_grower_acc_read", c_int, [c_vp, ctypes.POINTER(c_ll)]),
     ("yabt_bin_matrix_bytes", c_ll, [c_ll, c_int]),
     ("yabt_bin_address", c_int, [c_ll, c_int, c_int, ctypes.POINTER(c_ll), ctypes.POINTER(c_int),
                                  ctypes.POINTER(c_int)]),
@@ -59,6 +87,21 @@ SIGNATURES = [
     ("yabt_grow_small_ptr", c_vp, [c_vp]),
     ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
     ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
+    ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
+    ("yabt_bin_fit_workspace_bytes", c_ll, [c_ll, c_int, c_ll]),
+    ("yabt_bin_fit", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    ("yabt_bin_transform", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    ("yabt_leafnet_workspace_bytes", c_ll, [c_ll, c_int, c_int]),
+    ("yabt_leafnet_fit", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, c_vp]),
+    ("yabt_update_margin", c_int, [ctypes.POINTER(UpdateArgs), c_vp]),
+    ("yabt_grad_init", c_int, [c_vp, c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),
+    ("yabt_column_stats", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),
+    ("yabt_interaction_update", c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    ("yabt_interaction_normalize", c_int, [c_vp, c_int, c_vp, c_vp]),
+    ("yabt_predict_forest", c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                    c_vp, c_int, c_vp, c_vp, c_vp, c_float, c_vp, c_vp]),
+    ("yabt_apply_tree", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    ("yabt_impute_rows", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
 ]
 
 

@@ -1,5 +1,6 @@
 // C ABI of libyabt_b200.so: error reporting, bin-matrix layout helpers and the
 // level-wise grower context (workspace carving + launch sequencing).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -11,6 +12,9 @@
 namespace yabt {
 
 static thread_local char g_err[512] = "";
+static std::atomic<long long> g_launches{0};
+
+void count_launches(int k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -19,7 +23,8 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
-cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t,
+                              cudaEvent_t after_hist);
 cudaError_t launch_level_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
@@ -64,6 +69,8 @@ extern "C" {
 
 int yabt_version(void) { return 100; }
 
+long long yabt_launch_count(void) { return g_launches.load(); }
+
 int yabt_last_error(char* buf, int len) {
   if (!buf || len <= 0) return YABT_ERR_ARG;
   strncpy(buf, g_err, (size_t)len - 1);
@@ -99,6 +106,7 @@ int yabt_pack_bins(const uint8_t* plain, long long n, int F, uint8_t* tiled, voi
   const long long total = n * F;
   const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 32);
   k_pack_bins<<<grid, 256, 0, s>>>(plain, n, F, tiled);
+  count_launches(1);
   CUDA_TRY(cudaGetLastError());
   return YABT_OK;
 }
@@ -115,6 +123,10 @@ struct yabt_grower {
   int LIMBS;
   std::vector<UnitDesc> units;
   std::vector<FeatAddr> faddr;
+  // optional per-launch timing of the histogram kernel
+  int timing = 0;
+  std::vector<cudaEvent_t> ev;   // pairs (start, stop)
+  int ev_used = 0;
   // carve offsets
   struct Off { const char* name; long long bytes; long long off; };
   std::vector<Off> offs;
@@ -255,7 +267,50 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
 }
 
 int yabt_grower_destroy(yabt_grower* g) {
+  if (g) for (auto e : g->ev) cudaEventDestroy(e);
   delete g;
+  return YABT_OK;
+}
+
+int yabt_grower_set_timing(yabt_grower* g, int max_launches) {
+  if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
+  g->ev_used = 0;
+  g->timing = max_launches > 0;
+  while ((int)g->ev.size() < 2 * max_launches) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreate(&e));
+    g->ev.push_back(e);
+  }
+  return YABT_OK;
+}
+
+int yabt_grower_acc_reset(yabt_grower* g, void* stream) {
+  if (!g || !g->bound) { set_error("grower not bound"); return YABT_ERR_ARG; }
+  CUDA_TRY(cudaMemsetAsync(&g->b.st->acc_root_rows, 0, 3 * sizeof(long long), (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grower_acc_read(yabt_grower* g, long long* out3) {
+  if (!g || !g->bound || !out3) { set_error("grower not bound"); return YABT_ERR_ARG; }
+  CUDA_TRY(cudaMemcpy(out3, &g->b.st->acc_root_rows, 3 * sizeof(long long), cudaMemcpyDeviceToHost));
+  return YABT_OK;
+}
+
+int yabt_grower_hist_rows(yabt_grower* g, long long* rows, int cap) {
+  if (!g || !g->bound || !rows) { set_error("null argument"); return YABT_ERR_ARG; }
+  CUDA_TRY(cudaMemcpy(rows, g->b.st->hist_rows, sizeof(long long) * std::min(cap, 64), cudaMemcpyDeviceToHost));
+  return YABT_OK;
+}
+
+int yabt_grower_hist_times(yabt_grower* g, float* ms, int cap, int* count) {
+  if (!g || !count) { set_error("null argument"); return YABT_ERR_ARG; }
+  const int k = g->ev_used / 2;
+  for (int i = 0; i < k && i < cap; ++i) {
+    CUDA_TRY(cudaEventSynchronize(g->ev[2 * i + 1]));
+    CUDA_TRY(cudaEventElapsedTime(&ms[i], g->ev[2 * i], g->ev[2 * i + 1]));
+  }
+  *count = k;
+  g->ev_used = 0;
   return YABT_OK;
 }
 
@@ -305,7 +360,11 @@ int yabt_grow_hist(yabt_grower* g, const yabt_tree_args* a, int level, void* str
   int rc = fill_io(g, a, &io);
   if (rc) return rc;
   if (level < 0 || level >= g->p.levels_max) { set_error("level out of range"); return YABT_ERR_ARG; }
-  CUDA_TRY(launch_level_hist(g->p, g->b, io, level, g->nsm, (cudaStream_t)stream));
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool tm = g->timing && g->ev_used + 2 <= (int)g->ev.size();
+  if (tm) CUDA_TRY(cudaEventRecord(g->ev[g->ev_used], s));
+  CUDA_TRY(launch_level_hist(g->p, g->b, io, level, g->nsm, s, tm ? g->ev[g->ev_used + 1] : nullptr));
+  if (tm) g->ev_used += 2;
   return YABT_OK;
 }
 

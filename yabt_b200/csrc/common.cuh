@@ -48,6 +48,8 @@ enum : unsigned {
 };
 
 void set_error(const char* fmt, ...);
+// host-side count of kernel launches issued by the library (gpu_launches)
+void count_launches(int k);
 
 // ---------------------------------------------------------------- layout
 struct TileInfo {

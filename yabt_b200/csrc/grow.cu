@@ -17,7 +17,7 @@
 namespace yabt {
 
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                                int jobs, int nsm, cudaStream_t s);
+                                int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist);
 
 __device__ __forceinline__ int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
@@ -99,6 +99,10 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
     }
     if (slot > p.max_items) { atomicOr(&st->err, DERR_ITEM_OVERFLOW); slot = 0; }
     st->n_items = slot; st->item_counter = 0;
+    for (int l = 0; l < 64; ++l) st->hist_rows[l] = 0;
+    st->hist_rows[0] = p.n;
+    st->acc_root_rows += p.n;
+    st->acc_launches += 1;
   }
   __syncthreads();
   const int chunk = item_chunk(p.n, p.U);
@@ -578,6 +582,11 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
     for (int q = lane; q < P; q += 32) R += b.seg_count[nxt][b.pair_sil[q] ? 2 * q : 2 * q + 1];
     for (int o = 16; o; o >>= 1) R += __shfl_xor_sync(0xffffffffu, R, o);
     const int chunk = item_chunk(R, p.U);
+    if (lane == 0) {
+      st->hist_rows[min(d + 1, 63)] = R;
+      st->acc_child_rows += R;
+      st->acc_launches += 1;
+    }
     for (int q = lane; q < P; q += 32) {
       const int sc = b.seg_count[nxt][b.pair_sil[q] ? 2 * q : 2 * q + 1];
       b.node_tpre[q] = (sc + chunk - 1) / chunk;
@@ -701,8 +710,8 @@ static inline int jobs_bound(int d, int max_pairs) {
 
 // Launches of one level. Returns a CUDA error code (0 on success).
 cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                              int nsm, cudaStream_t s) {
-  return launch_hist_kernels(p, b, io, d, jobs_bound(d, p.max_pairs), nsm, s);
+                              int nsm, cudaStream_t s, cudaEvent_t after_hist) {
+  return launch_hist_kernels(p, b, io, d, jobs_bound(d, p.max_pairs), nsm, s, after_hist);
 }
 
 cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
@@ -715,6 +724,7 @@ cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const Tre
   const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
   k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, d);
   k_plan<<<1, 1024, 0, s>>>(p, b, d);
+  count_launches(4);
   return cudaGetLastError();
 }
 
@@ -725,11 +735,13 @@ cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const Tree
 
   const int grid = (int)std::min<long long>((p.n + 255) / 256, 8LL * nsm);
   k_absmax<<<std::max(grid, 1), 256, 0, s>>>(io.g, p.general ? io.h : nullptr, p.n, b.st);
+  count_launches(1);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeIO& io, cudaStream_t s) {
   k_tree_init<<<1, 1024, 0, s>>>(p, b, io);
+  count_launches(1);
   return cudaGetLastError();
 }
 
@@ -738,6 +750,7 @@ cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, int* meta
   k_finish<<<1, 1024, 0, s>>>(p, b, meta);
   const int grid = (int)std::min<long long>((p.n + 511) / 512, 4LL * nsm);
   k_leaf_assign<<<std::max(grid, 1), 512, 3 * (p.max_leaves + 1) * sizeof(int), s>>>(p, b, leaf_of_row);
+  count_launches(2);
   return cudaGetLastError();
 }
 

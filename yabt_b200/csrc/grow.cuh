@@ -82,6 +82,10 @@ struct GrowState {
   unsigned amax_g, amax_h;  // ordered-float max |g|, max h
   int n_leaves;
   int pad[2];
+  long long hist_rows[64];   // rows histogrammed at each level (algorithmic-traffic accounting)
+  long long acc_root_rows;   // accumulated since the last yabt_grower_acc_reset: root-level rows,
+  long long acc_child_rows;  // smaller-child rows of deeper levels,
+  long long acc_launches;    // histogram levels that did work
 };
 
 // Per-call grower parameters (copied by value into kernels).

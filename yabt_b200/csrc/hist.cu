@@ -276,19 +276,22 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
 }
 
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                                int jobs, int nsm, cudaStream_t s) {
+                                int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist) {
   const int* rows = d == 0 ? nullptr : b.rows[d & 1];
   if (!p.general) {
     k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
+    if (after_hist) cudaEventRecord(after_hist, s);
     k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS, RED_THREADS, 0, s>>>(b.partials, b.job_first, b.job_nitems,
                                                               b.items, b.units, b.st, b.small, p.F, p.U, d);
   } else {
     k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
+    if (after_hist) cudaEventRecord(after_hist, s);
     k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS, RED_THREADS, 0, s>>>(b.partials, b.job_first, b.job_nitems,
                                                               b.items, b.units, b.st, b.small, p.F, p.U, d);
   }
+  count_launches(2);
   return cudaGetLastError();
 }
 

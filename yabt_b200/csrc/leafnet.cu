@@ -1,0 +1,694 @@
+// Ridge-linear neural leaves, the fused margin update + loss gradients, and
+// the interaction detector, all on the device.
+//
+// Restates fit_leaf_networks with leaf_net_hidden == 0
+// (yabt/neural_leaves.py:131-184, _select_features :21-39, _fit_linear :42-90),
+// the loss gradients (yabt/boosting.py:36-38,53-54), the margin update
+// (yabt/boosting.py:511-514, Tree.net_contribution yabt/tree.py:118-128) and
+// FeatureInteractionDetector (yabt/adaptive_features.py:129-160).
+//
+// Per tree, with no host synchronisation:
+//   k_ln_select   split-feature use counts -> top-K (count desc, feature asc);
+//                 flags whether gradient-correlation padding is needed
+//   k_ln_corr     (only if padding is needed) |X^T g - mean * sum g| / std
+//   k_ln_pad      completes the feature list
+//   k_ln_rows     natural row order: per-row record (x_norm[K], g, h), per-leaf
+//                 min/max envelope of the raw inputs
+//   k_ln_gram     per leaf segment chunk: fp64 normal-equation partial sums
+//                 M = sum h x1 x1^T (upper triangle), b = -sum g x1, one lane
+//                 per entry, fixed order (deterministic)
+//   k_ln_solve    per leaf: reduce chunk partials in order, add the ridge,
+//                 Cholesky solve, fold normalisation + learning rate
+//   k_update      margin += value[leaf] + sum_k linear * clamp(x, lo, hi);
+//                 next tree's gradient / hessian
+#include <algorithm>
+#include <cstdint>
+
+#include "common.cuh"
+#include "../../include/yabt_b200.h"
+
+namespace yabt {
+
+constexpr int KMAX = 8;                 // leaf-model inputs (leaf_net_features <= 8)
+constexpr int NE = (KMAX + 1) * (KMAX + 2) / 2 + (KMAX + 1);   // 45 + 9 = 54 accumulators
+constexpr int GRAM_CHUNK = 8192;        // rows per Gram partial
+
+struct LeafNetArgs {
+  // tree (device)
+  const long long* feature;   // [maxn]
+  float* value;               // [maxn] updated in place (fold)
+  int n_nodes_cap;            // maxn
+  const int* meta;            // [4] from the grower: n_nodes, ...
+  // leaf ranges (grower workspace)
+  const int* leaf_src;
+  const int* leaf_begin;
+  const int* leaf_count;
+  const int* fin;
+  const int* list0;
+  const int* list1;
+  const int* leaf_of_row;
+  // data
+  const float* Xfm;           // [F][n] imputed
+  const float* col_mean;      // [F]
+  const float* col_std;       // [F] unbiased, unclamped
+  const float* margin;        // [n] ensemble margin excluding this tree
+  const float* y;             // [n]
+  long long n;
+  int F;
+  int K;                      // min(leaf_net_features, F)
+  int loss;                   // 0 squared error, 1 logistic
+  int min_samples;
+  float l2;
+  float lr;
+  // outputs (device)
+  long long* feats;           // [K]
+  float* linear;              // [maxn][K]
+  float* lo;                  // [maxn][K]
+  float* hi;                  // [maxn][K]
+  int* has_nets;              // [1]
+  // scratch (device)
+  int* fcount;                // [F]
+  int* flags;                 // [4]: n_used, need_pad, n_chunks, n_eligible
+  double* corr;               // [F]
+  double* gsum;               // [1]
+  float* rec;                 // [n][REC] records
+  unsigned* lo_ord;           // [maxn][K]
+  unsigned* hi_ord;           // [maxn][K]
+  int* counts;                // [maxn]
+  int* chunk_leaf;            // [max_chunks]
+  int* chunk_begin;           // [max_chunks]
+  int* chunk_end;             // [max_chunks]
+  double* partial;            // [max_chunks][NE]
+  int max_chunks;
+};
+
+constexpr int REC = 12;   // floats per row record: x_norm[8], g, h, pad[2] (48 bytes)
+
+__device__ __forceinline__ void loss_gh(int loss, float m, float y, float* g, float* h) {
+  if (loss == 0) { *g = __fsub_rn(m, y); *h = 1.f; return; }
+  // p = sigmoid(m) = 1 / (1 + exp(-m)), g = p - y, h = max(p (1 - p), 1e-6)
+  const float p = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-m)));
+  *g = __fsub_rn(p, y);
+  *h = fmaxf(__fmul_rn(p, __fsub_rn(1.f, p)), 1e-6f);
+}
+
+// ------------------------------------------------------------------ feature choice
+__global__ void __launch_bounds__(1024) k_ln_select(LeafNetArgs a) {
+  __shared__ int s_used;
+  const int nn = a.meta[0];
+  for (int f = threadIdx.x; f < a.F; f += blockDim.x) a.fcount[f] = 0;
+  __syncthreads();
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    const long long f = a.feature[g];
+    if (f >= 0) atomicAdd(&a.fcount[f], 1);
+  }
+  if (threadIdx.x == 0) s_used = 0;
+  __syncthreads();
+  // rank used features by (count desc, feature asc)
+  for (int f = threadIdx.x; f < a.F; f += blockDim.x) {
+    const int c = a.fcount[f];
+    if (c <= 0) continue;
+    atomicAdd(&s_used, 1);
+    int rank = 0;
+    for (int q = 0; q < a.F; ++q) {
+      const int cq = a.fcount[q];
+      if (cq > c || (cq == c && cq > 0 && q < f)) ++rank;
+    }
+    if (rank < a.K) a.feats[rank] = f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int used = min(s_used, a.K);
+    a.flags[0] = used;
+    a.flags[1] = used < a.K;
+    a.gsum[0] = 0.0;
+  }
+  for (int f = threadIdx.x; f < a.F; f += blockDim.x) a.corr[f] = 0.0;
+}
+
+// grid (chunks, ceil(F/8)): sum_i x_fi g_i and sum g (only when padding is needed)
+__global__ void k_ln_corr(LeafNetArgs a) {
+  if (!a.flags[1]) return;
+  __shared__ double s[8][33];
+  const int f0 = blockIdx.y * 8;
+  double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  double gs = 0.0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < a.n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int l = a.leaf_of_row[i];
+    float g, h;
+    loss_gh(a.loss, __fadd_rn(a.margin[i], a.value[l]), a.y[i], &g, &h);
+    gs += (double)g;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (f0 + q < a.F) acc[q] += (double)a.Xfm[(long long)(f0 + q) * a.n + i] * (double)g;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    double v = acc[q];
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) atomicAdd(&a.corr[min(f0 + q, a.F - 1)], f0 + q < a.F ? v : 0.0);
+  }
+  for (int o = 16; o; o >>= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+  if (lane == 0 && blockIdx.y == 0) atomicAdd(a.gsum, gs);
+  (void)warp; (void)s;
+}
+
+__global__ void __launch_bounds__(1024) k_ln_pad(LeafNetArgs a) {
+  if (!a.flags[1]) return;
+  // score = |X^T g - mean * sum g| / max(std, 1e-6); used features excluded
+  __shared__ int s_base;
+  if (threadIdx.x == 0) s_base = a.flags[0];
+  __syncthreads();
+  const int need = a.K - s_base;
+  for (int f = threadIdx.x; f < a.F; f += blockDim.x) {
+    if (a.fcount[f] > 0) continue;
+    const float sf = (float)(fabs(a.corr[f] - (double)a.col_mean[f] * a.gsum[0]) /
+                             fmax((double)a.col_std[f], 1e-6));
+    int rank = 0;
+    for (int q = 0; q < a.F; ++q) {
+      if (a.fcount[q] > 0) continue;
+      const float sq = (float)(fabs(a.corr[q] - (double)a.col_mean[q] * a.gsum[0]) /
+                               fmax((double)a.col_std[q], 1e-6));
+      if (sq > sf || (sq == sf && q < f)) ++rank;
+    }
+    if (rank < need) a.feats[s_base + rank] = f;
+  }
+}
+
+// ------------------------------------------------------------------ per-row records + envelope
+// grid-stride over rows; per block shared min/max per (leaf, k) flushed with atomics
+__global__ void __launch_bounds__(256) k_ln_rows(LeafNetArgs a) {
+  extern __shared__ unsigned smm[];       // [2][maxn][K]
+  const int K = a.K;
+  const int nn = a.meta[0];
+  const int M = nn * K;
+  unsigned* slo = smm;
+  unsigned* shi = smm + M;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) { slo[i] = 0xFFFFFFFFu; shi[i] = 0u; }
+  __syncthreads();
+  int fk[KMAX];
+  float mu[KMAX], sd[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    if (k < K) {
+      fk[k] = (int)a.feats[k];
+      mu[k] = a.col_mean[fk[k]];
+      sd[k] = fmaxf(a.col_std[fk[k]], 1e-6f);
+    } else { fk[k] = 0; mu[k] = 0.f; sd[k] = 1.f; }
+  }
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < a.n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int l = a.leaf_of_row[i];
+    float g, h;
+    loss_gh(a.loss, __fadd_rn(a.margin[i], a.value[l]), a.y[i], &g, &h);
+    float r[REC];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      float xn = 0.f;
+      if (k < K) {
+        const float x = a.Xfm[(long long)fk[k] * a.n + i];
+        xn = __fdiv_rn(__fsub_rn(x, mu[k]), sd[k]);
+        const unsigned o = f2ord(x);
+        atomicMin(&slo[l * K + k], o);
+        atomicMax(&shi[l * K + k], o);
+      }
+      r[k] = xn;
+    }
+    r[KMAX] = g; r[KMAX + 1] = h; r[KMAX + 2] = 0.f; r[KMAX + 3] = 0.f;
+    float4* dst = reinterpret_cast<float4*>(a.rec + i * REC);
+    dst[0] = make_float4(r[0], r[1], r[2], r[3]);
+    dst[1] = make_float4(r[4], r[5], r[6], r[7]);
+    dst[2] = make_float4(r[8], r[9], r[10], r[11]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < M; i += blockDim.x) {
+    if (slo[i] != 0xFFFFFFFFu) atomicMin(&a.lo_ord[i], slo[i]);
+    if (shi[i] != 0u) atomicMax(&a.hi_ord[i], shi[i]);
+  }
+}
+
+// one block: counts, eligibility and the Gram chunk plan
+__global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
+  const int nn = a.meta[0];
+  __shared__ int s_ne;
+  if (threadIdx.x == 0) s_ne = 0;
+  __syncthreads();
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    const bool leaf = a.feature[g] < 0;
+    const int c = leaf ? a.leaf_count[g] : 0;
+    a.counts[g] = c;
+    if (leaf && c >= a.min_samples) atomicAdd(&s_ne, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int nc = 0;
+    for (int g = 0; g < nn; ++g) {
+      if (a.feature[g] >= 0 || a.counts[g] < a.min_samples) continue;
+      const int c = a.counts[g];
+      for (int b = 0; b < c; b += GRAM_CHUNK) {
+        if (nc < a.max_chunks) {
+          a.chunk_leaf[nc] = g;
+          a.chunk_begin[nc] = a.leaf_begin[g] + b;
+          a.chunk_end[nc] = a.leaf_begin[g] + min(c, b + GRAM_CHUNK);
+        }
+        ++nc;
+      }
+    }
+    a.flags[2] = min(nc, a.max_chunks);
+    a.flags[3] = s_ne;
+    a.has_nets[0] = s_ne > 0;
+  }
+}
+
+// one block (8 warps) per chunk; each warp takes rows, lane e accumulates
+// entries e and e + 32 in fp64 in row order; warps are reduced in order.
+__global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
+  __shared__ double sp[8][NE];
+  const int c = blockIdx.x;
+  if (c >= a.flags[2]) return;
+  const int g = a.chunk_leaf[c];
+  const int src = a.leaf_src[g];
+  const int* lst = src == 0 ? a.fin : (src == 1 ? a.list0 : (src == 2 ? a.list1 : nullptr));
+  const int b0 = a.chunk_begin[c], b1 = a.chunk_end[c];
+  const int K = a.K, D = K + 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // entry e -> (ia, ib) of the upper triangle of the D x D matrix, then rhs
+  int ea[2], eb[2];
+  bool ev[2];
+  const int ntri = D * (D + 1) / 2;
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int e = lane + 32 * q;
+    ev[q] = e < ntri + D;
+    int ia = 0, ib = 0;
+    if (e < ntri) {
+      int rem = e, row = 0;
+      while (rem >= D - row) { rem -= D - row; ++row; }
+      ia = row; ib = row + rem;
+    } else { ia = e - ntri; ib = -1; }
+    ea[q] = ia; eb[q] = ib;
+  }
+  double acc[2] = {0.0, 0.0};
+  const int per = (b1 - b0 + 7) / 8;
+  const int w0 = b0 + warp * per, w1 = min(b1, w0 + per);
+  for (int p = w0; p < w1; ++p) {
+    const int row = lst ? lst[p] : p;
+    const float4* r4 = reinterpret_cast<const float4*>(a.rec + (long long)row * REC);
+    const float4 v0 = __ldg(r4), v1 = __ldg(r4 + 1), v2 = __ldg(r4 + 2);
+    const float xr[KMAX + 2] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, v2.x, v2.y};
+    const double hh = (double)xr[KMAX + 1], gg = (double)xr[KMAX];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (!ev[q]) continue;
+      const double xa = ea[q] < K ? (double)xr[ea[q]] : 1.0;
+      if (eb[q] >= 0) {
+        const double xb = eb[q] < K ? (double)xr[eb[q]] : 1.0;
+        // M_ab += x1_a * (x1_b * h)   (yabt/neural_leaves.py:71,82)
+        acc[q] = __dadd_rn(acc[q], __dmul_rn(xa, __dmul_rn(xb, hh)));
+      } else {
+        // b_a += -(x1_a * g)          (yabt/neural_leaves.py:72,83)
+        acc[q] = __dadd_rn(acc[q], -__dmul_rn(xa, gg));
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int e = lane + 32 * q;
+    if (e < NE) sp[warp][e] = ev[q] ? acc[q] : 0.0;
+  }
+  __syncthreads();
+  if (threadIdx.x < NE) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t = __dadd_rn(t, sp[w][threadIdx.x]);
+    a.partial[(long long)c * NE + threadIdx.x] = t;
+  }
+}
+
+// one thread per eligible leaf: reduce partials in chunk order, ridge,
+// Cholesky, fold (yabt/neural_leaves.py:85-89,180-184)
+__global__ void k_ln_solve(LeafNetArgs a) {
+  const int nn = a.meta[0];
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= nn) return;
+  const int K = a.K, D = K + 1;
+  const bool leaf = a.feature[g] < 0;
+  const bool elig = leaf && a.counts[g] >= a.min_samples;
+  float W[KMAX], db = 0.f;
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) W[k] = 0.f;
+  if (elig) {
+    double e[NE];
+    for (int q = 0; q < NE; ++q) e[q] = 0.0;
+    const int nc = a.flags[2];
+    for (int c = 0; c < nc; ++c) {
+      if (a.chunk_leaf[c] != g) continue;
+      for (int q = 0; q < NE; ++q) e[q] = __dadd_rn(e[q], a.partial[(long long)c * NE + q]);
+    }
+    double M[KMAX + 1][KMAX + 1], bv[KMAX + 1];
+    int idx = 0;
+    for (int i = 0; i < D; ++i)
+      for (int j = i; j < D; ++j) { M[i][j] = e[idx]; M[j][i] = e[idx]; ++idx; }
+    for (int i = 0; i < D; ++i) bv[i] = e[idx + i];
+    for (int i = 0; i < K; ++i) M[i][i] = __dadd_rn(M[i][i], (double)a.l2);
+    M[K][K] = __dadd_rn(M[K][K], 1e-8);
+    // Cholesky M = L L^T (in place, lower)
+    bool ok = true;
+    for (int j = 0; j < D && ok; ++j) {
+      double s = M[j][j];
+      for (int k = 0; k < j; ++k) s -= M[j][k] * M[j][k];
+      if (!(s > 0.0)) { ok = false; break; }
+      const double d = sqrt(s);
+      M[j][j] = d;
+      for (int i = j + 1; i < D; ++i) {
+        double t = M[i][j];
+        for (int k = 0; k < j; ++k) t -= M[i][k] * M[j][k];
+        M[i][j] = t / d;
+      }
+    }
+    if (ok) {
+      double z[KMAX + 1], th[KMAX + 1];
+      for (int i = 0; i < D; ++i) {
+        double t = bv[i];
+        for (int k = 0; k < i; ++k) t -= M[i][k] * z[k];
+        z[i] = t / M[i][i];
+      }
+      for (int i = D - 1; i >= 0; --i) {
+        double t = z[i];
+        for (int k = i + 1; k < D; ++k) t -= M[k][i] * th[k];
+        th[i] = t / M[i][i];
+      }
+      for (int k = 0; k < K; ++k) W[k] = (float)th[k];
+      db = (float)th[K];
+    }
+  }
+  // fold: value += lr * (db - sum_k W_k * (mu_k / sd_k)); linear = lr * W / sd
+  float s = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const int f = (int)a.feats[k];
+    const float sd = fmaxf(a.col_std[f], 1e-6f);
+    const float mu = a.col_mean[f];
+    s = __fadd_rn(s, __fmul_rn(W[k], __fdiv_rn(mu, sd)));
+    a.linear[(long long)g * K + k] = __fdiv_rn(__fmul_rn(a.lr, W[k]), sd);
+    const unsigned lo = a.lo_ord[(long long)g * K + k], hi = a.hi_ord[(long long)g * K + k];
+    a.lo[(long long)g * K + k] = lo == 0xFFFFFFFFu ? INFINITY : ord2f(lo);
+    a.hi[(long long)g * K + k] = hi == 0u ? -INFINITY : ord2f(hi);
+  }
+  if (a.flags[3] > 0) a.value[g] = __fadd_rn(a.value[g], __fmul_rn(a.lr, __fsub_rn(db, s)));
+}
+
+// ------------------------------------------------------------------ margin update + gradients
+struct UpdateArgs {
+  const int* leaf_of_row;
+  const float* value;         // [maxn] (leaf values incl. folded bias)
+  const float* linear;        // [maxn][K] or nullptr
+  const float* lo;
+  const float* hi;
+  const long long* feats;     // [K]
+  const int* has_nets;        // [1] or nullptr
+  int K;
+  const float* Xfm;
+  long long n;
+  float* margin;
+  const float* y;
+  float* grad;                // next tree's gradient (or nullptr)
+  float* hess;                // next tree's hessian (or nullptr: unit hessian)
+  int loss;
+};
+
+__global__ void __launch_bounds__(256) k_update(UpdateArgs u) {
+  const bool nets = u.linear && u.has_nets && u.has_nets[0];
+  int fk[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) fk[k] = (nets && k < u.K) ? (int)u.feats[k] : 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < u.n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int l = u.leaf_of_row[i];
+    float c = u.value[l];
+    if (nets) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) {
+        if (k < u.K) {
+          const long long o = (long long)l * u.K + k;
+          const float x = u.Xfm[(long long)fk[k] * u.n + i];
+          const float xc = fminf(fmaxf(x, u.lo[o]), u.hi[o]);
+          s = __fadd_rn(s, __fmul_rn(u.linear[o], xc));
+        }
+      }
+      c = __fadd_rn(c, s);
+    }
+    const float m = __fadd_rn(u.margin[i], c);
+    u.margin[i] = m;
+    if (u.grad) {
+      float g, h;
+      loss_gh(u.loss, m, u.y[i], &g, &h);
+      u.grad[i] = g;
+      if (u.hess) u.hess[i] = h;
+    }
+  }
+}
+
+__global__ void k_grad_init(const float* margin, const float* y, long long n, int loss, float* grad, float* hess) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float g, h;
+    loss_gh(loss, margin[i], y[i], &g, &h);
+    grad[i] = g;
+    if (hess) hess[i] = h;
+  }
+}
+
+// ------------------------------------------------------------------ column moments
+// mean and unbiased std of every feature column (fp64 two-pass), float32 results
+__global__ void __launch_bounds__(512) k_colstats(const float* __restrict__ Xfm, long long n, float* mean, float* std) {
+  __shared__ double s[512];
+  const int f = blockIdx.x;
+  const float* col = Xfm + (long long)f * n;
+  double acc = 0.0;
+  for (long long i = threadIdx.x; i < n; i += blockDim.x) acc += (double)col[i];
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = 256; o; o >>= 1) { if (threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o]; __syncthreads(); }
+  const double mu = s[0] / (double)n;
+  __syncthreads();
+  acc = 0.0;
+  for (long long i = threadIdx.x; i < n; i += blockDim.x) { const double d = (double)col[i] - mu; acc += d * d; }
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = 256; o; o >>= 1) { if (threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o]; __syncthreads(); }
+  if (threadIdx.x == 0) {
+    mean[f] = (float)mu;
+    std[f] = (float)sqrt(s[0] / (double)(n > 1 ? n - 1 : 1));
+  }
+}
+
+// ------------------------------------------------------------------ interaction detector
+// scores (F x F, float counts) += 1 for every (ancestor feature, node feature)
+// pair with a != f along root-to-node paths, both directions
+// (yabt/tree.py:186-203, yabt/adaptive_features.py:129-145)
+__global__ void __launch_bounds__(512) k_ia_update(const long long* feature, const long long* left,
+                                                   const long long* right, const int* meta, int F,
+                                                   float* scores, int* parent) {
+  const int nn = meta[0];
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) parent[g] = -1;
+  __syncthreads();
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    if (feature[g] >= 0) { parent[left[g]] = g; parent[right[g]] = g; }
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    const long long f = feature[g];
+    if (f < 0) continue;
+    for (int p = parent[g]; p >= 0; p = parent[p]) {
+      const long long a = feature[p];
+      if (a == f) continue;
+      atomicAdd(&scores[a * F + f], 1.f);
+      atomicAdd(&scores[f * F + a], 1.f);
+    }
+  }
+}
+
+// normalized_matrix (yabt/adaptive_features.py:147-160): one block
+__global__ void __launch_bounds__(1024) k_ia_normalize(const float* scores, int F, float* imat) {
+  __shared__ float s_mx[32];
+  __shared__ double s_sum[32];
+  __shared__ long long s_cnt[32];
+  const long long FF = (long long)F * F;
+  float mx = 0.f;
+  double sum = 0.0;
+  long long cnt = 0;
+  for (long long i = threadIdx.x; i < FF; i += blockDim.x) {
+    const float v = scores[i];
+    mx = fmaxf(mx, v);
+    if (v > 0.f) { sum += (double)v; ++cnt; }
+  }
+  for (int o = 16; o; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  }
+  if ((threadIdx.x & 31) == 0) { s_mx[threadIdx.x >> 5] = mx; s_sum[threadIdx.x >> 5] = sum; s_cnt[threadIdx.x >> 5] = cnt; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) { s_mx[0] = fmaxf(s_mx[0], s_mx[w]); s_sum[0] += s_sum[w]; s_cnt[0] += s_cnt[w]; }
+  }
+  __syncthreads();
+  mx = s_mx[0];
+  if (!(mx > 0.f)) {
+    for (long long i = threadIdx.x; i < FF; i += blockDim.x) imat[i] = scores[i];
+    return;
+  }
+  // bg = mean of the positive entries: float32 sum (exact for integer counts) / count
+  const float bg = __fdiv_rn((float)s_sum[0], (float)s_cnt[0]);
+  const float den = __fadd_rn(__fsub_rn(mx, bg), 1e-8f);
+  for (long long i = threadIdx.x; i < FF; i += blockDim.x)
+    imat[i] = fmaxf(__fdiv_rn(__fsub_rn(scores[i], bg), den), 0.f);
+}
+
+}  // namespace yabt
+
+// ------------------------------------------------------------------ C ABI
+using namespace yabt;
+
+#define LCUDA(x)                                                                         \
+  do {                                                                                   \
+    cudaError_t e__ = (x);                                                               \
+    if (e__ != cudaSuccess) {                                                            \
+      set_error("%s: %s (%s:%d)", #x, cudaGetErrorString(e__), __FILE__, __LINE__);      \
+      return YABT_ERR_CUDA;                                                              \
+    }                                                                                    \
+  } while (0)
+
+extern "C" {
+
+long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes) {
+  auto al = [](long long x) { return (x + 255) & ~255LL; };
+  const long long max_chunks = n / GRAM_CHUNK + max_nodes + 1;
+  long long b = 0;
+  b += al((long long)F * 4);                 // fcount
+  b += al(16);                               // flags
+  b += al((long long)F * 8);                 // corr
+  b += al(8);                                // gsum
+  b += al(n * REC * 4);                      // rec
+  b += 2 * al((long long)max_nodes * KMAX * 4);   // lo_ord, hi_ord
+  b += al((long long)max_nodes * 4);         // counts
+  b += 3 * al(max_chunks * 4);               // chunk arrays
+  b += al(max_chunks * NE * 8);              // partials
+  return b;
+}
+
+// Fit ridge-linear leaf models for one grown tree and fold them into
+// value / linear / lo / hi (yabt/neural_leaves.py:131-184).
+int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, void* stream) {
+  if (!p || !workspace || p->K < 1 || p->K > KMAX || p->n <= 0 || p->F <= 0) {
+    set_error("yabt_leafnet_fit: bad arguments (K must be in [1, %d])", KMAX);
+    return YABT_ERR_ARG;
+  }
+  if (ws_bytes < yabt_leafnet_workspace_bytes(p->n, p->F, p->max_nodes)) {
+    set_error("yabt_leafnet_fit: workspace too small");
+    return YABT_ERR_WORKSPACE;
+  }
+  auto al = [](long long x) { return (x + 255) & ~255LL; };
+  cudaStream_t s = (cudaStream_t)stream;
+  LeafNetArgs a;
+  a.feature = (const long long*)p->feature; a.value = p->value; a.n_nodes_cap = p->max_nodes; a.meta = p->meta;
+  a.leaf_src = p->leaf_src; a.leaf_begin = p->leaf_begin; a.leaf_count = p->leaf_count;
+  a.fin = p->fin; a.list0 = p->list0; a.list1 = p->list1; a.leaf_of_row = p->leaf_of_row;
+  a.Xfm = p->Xfm; a.col_mean = p->col_mean; a.col_std = p->col_std; a.margin = p->margin; a.y = p->y;
+  a.n = p->n; a.F = p->F; a.K = p->K; a.loss = p->loss; a.min_samples = p->min_samples;
+  a.l2 = p->l2; a.lr = p->learning_rate;
+  a.feats = (long long*)p->feats; a.linear = p->linear; a.lo = p->lo; a.hi = p->hi; a.has_nets = p->has_nets;
+  const long long max_chunks = p->n / GRAM_CHUNK + p->max_nodes + 1;
+  char* w = (char*)workspace;
+  a.fcount = (int*)w; w += al((long long)p->F * 4);
+  a.flags = (int*)w; w += al(16);
+  a.corr = (double*)w; w += al((long long)p->F * 8);
+  a.gsum = (double*)w; w += al(8);
+  a.rec = (float*)w; w += al(p->n * REC * 4);
+  a.lo_ord = (unsigned*)w; w += al((long long)p->max_nodes * KMAX * 4);
+  a.hi_ord = (unsigned*)w; w += al((long long)p->max_nodes * KMAX * 4);
+  a.counts = (int*)w; w += al((long long)p->max_nodes * 4);
+  a.chunk_leaf = (int*)w; w += al(max_chunks * 4);
+  a.chunk_begin = (int*)w; w += al(max_chunks * 4);
+  a.chunk_end = (int*)w; w += al(max_chunks * 4);
+  a.partial = (double*)w;
+  a.max_chunks = (int)max_chunks;
+  const int nsm = 148;
+  LCUDA(cudaMemsetAsync(a.lo_ord, 0xFF, (size_t)p->max_nodes * KMAX * 4, s));
+  LCUDA(cudaMemsetAsync(a.hi_ord, 0x00, (size_t)p->max_nodes * KMAX * 4, s));
+  k_ln_select<<<1, 1024, 0, s>>>(a);
+  {
+    dim3 grid((unsigned)std::min<long long>((p->n + 255) / 256, 4LL * nsm), (unsigned)((p->F + 7) / 8));
+    k_ln_corr<<<grid, 256, 0, s>>>(a);
+  }
+  k_ln_pad<<<1, 1024, 0, s>>>(a);
+  {
+    const size_t smem = (size_t)2 * p->max_nodes * p->K * 4;
+    const int grid = (int)std::min<long long>((p->n + 255) / 256, 4LL * nsm);
+    k_ln_rows<<<grid, 256, smem, s>>>(a);
+  }
+  k_ln_plan<<<1, 1024, 0, s>>>(a);
+  k_ln_gram<<<(unsigned)max_chunks, 256, 0, s>>>(a);
+  k_ln_solve<<<(p->max_nodes + 127) / 128, 128, 0, s>>>(a);
+  count_launches(7);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_update_margin(const yabt_update_args* p, void* stream) {
+  if (!p || !p->leaf_of_row || !p->value || !p->margin || p->n < 0) { set_error("yabt_update_margin: bad arguments"); return YABT_ERR_ARG; }
+  UpdateArgs u;
+  u.leaf_of_row = p->leaf_of_row; u.value = p->value; u.linear = p->linear; u.lo = p->lo; u.hi = p->hi;
+  u.feats = (const long long*)p->feats; u.has_nets = p->has_nets; u.K = p->K; u.Xfm = p->Xfm; u.n = p->n;
+  u.margin = p->margin; u.y = p->y; u.grad = p->grad; u.hess = p->hess; u.loss = p->loss;
+  if (p->n == 0) return YABT_OK;
+  const int grid = (int)std::min<long long>((p->n + 255) / 256, 148LL * 8);
+  k_update<<<grid, 256, 0, (cudaStream_t)stream>>>(u);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_grad_init(const float* margin, const float* y, long long n, int loss, float* grad, float* hess, void* stream) {
+  if (!margin || !y || !grad || n < 0) { set_error("yabt_grad_init: bad arguments"); return YABT_ERR_ARG; }
+  if (n == 0) return YABT_OK;
+  const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 8);
+  k_grad_init<<<grid, 256, 0, (cudaStream_t)stream>>>(margin, y, n, loss, grad, hess);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_column_stats(const float* Xfm, long long n, int F, float* mean, float* std, void* stream) {
+  if (!Xfm || n <= 0 || F <= 0 || !mean || !std) { set_error("yabt_column_stats: bad arguments"); return YABT_ERR_ARG; }
+  k_colstats<<<F, 512, 0, (cudaStream_t)stream>>>(Xfm, n, mean, std);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_interaction_update(const int64_t* feature, const int64_t* left, const int64_t* right, const int32_t* meta,
+                            int F, int max_nodes, float* scores, int32_t* parent_scratch, void* stream) {
+  if (!feature || !left || !right || !meta || !scores || !parent_scratch || F <= 0) {
+    set_error("yabt_interaction_update: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  (void)max_nodes;
+  k_ia_update<<<1, 512, 0, (cudaStream_t)stream>>>((const long long*)feature, (const long long*)left,
+                                                   (const long long*)right, meta, F, scores, parent_scratch);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_interaction_normalize(const float* scores, int F, float* imat, void* stream) {
+  if (!scores || !imat || F <= 0) { set_error("yabt_interaction_normalize: bad arguments"); return YABT_ERR_ARG; }
+  k_ia_normalize<<<1, 1024, 0, (cudaStream_t)stream>>>(scores, F, imat);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+}  // extern "C"

@@ -107,6 +107,29 @@ class Grower:
         _lib.check(self.lib.yabt_grow_tree(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
                    "yabt_grow_tree")
 
+    def set_timing(self, max_launches: int) -> None:
+        """Record CUDA events around up to max_launches histogram launches."""
+        _lib.check(self.lib.yabt_grower_set_timing(self.h, int(max_launches)), "yabt_grower_set_timing")
+
+    def hist_times(self, cap: int = 4096) -> list[float]:
+        buf = (ctypes.c_float * cap)()
+        cnt = ctypes.c_int()
+        _lib.check(self.lib.yabt_grower_hist_times(self.h, buf, cap, ctypes.byref(cnt)), "yabt_grower_hist_times")
+        return [buf[i] for i in range(min(cnt.value, cap))]
+
+    def acc_reset(self) -> None:
+        _lib.check(self.lib.yabt_grower_acc_reset(self.h, _lib.stream_ptr()), "yabt_grower_acc_reset")
+
+    def acc_read(self) -> tuple[int, int, int]:
+        buf = (ctypes.c_longlong * 3)()
+        _lib.check(self.lib.yabt_grower_acc_read(self.h, buf), "yabt_grower_acc_read")
+        return int(buf[0]), int(buf[1]), int(buf[2])
+
+    def hist_rows(self) -> list[int]:
+        buf = (ctypes.c_longlong * 64)()
+        _lib.check(self.lib.yabt_grower_hist_rows(self.h, buf, 64), "yabt_grower_hist_rows")
+        return [int(buf[i]) for i in range(64)]
+
     def leaf_rows(self) -> dict:
         ptrs = [ctypes.c_void_p() for _ in range(6)]
         _lib.check(self.lib.yabt_grow_leaf_rows(self.h, *[ctypes.byref(p) for p in ptrs]),

@@ -1,0 +1,114 @@
+"""scikit-learn estimators (yabt/sklearn_api.py:250-366) over the device
+boosting loop. Same constructor parameters (every ``BoostParams`` field plus
+``cat_smoothing``), same target handling: the regressor standardises y
+(:356-363), the classifier maps binary labels to {0, 1} and uses one-vs-rest
+for more classes (:307-331); predict_proba is expit / softmax of the margins.
+"""
+
+from __future__ import annotations
+
+from dataclasses import fields
+
+import numpy as np
+from scipy.special import expit
+from sklearn.base import BaseEstimator, ClassifierMixin, RegressorMixin
+
+from .boosting import Booster, BoostParams, LogLoss, MSELoss
+from .multiclass import MulticlassBooster
+
+_PARAM_NAMES = [f.name for f in fields(BoostParams)]
+
+
+def _require_single_target(y: np.ndarray) -> np.ndarray:
+    if y.ndim == 2 and y.shape[1] == 1:
+        return y.ravel()
+    if y.ndim > 1:
+        raise ValueError(f"y has shape {y.shape}; this estimator predicts a single target.")
+    return y
+
+
+class _YABTBase(BaseEstimator):
+    def __init__(self, **kwargs):
+        defaults = BoostParams()
+        for name in _PARAM_NAMES:
+            setattr(self, name, kwargs.pop(name, getattr(defaults, name)))
+        self.cat_smoothing = kwargs.pop("cat_smoothing", 10.0)
+        if kwargs:
+            raise TypeError(f"Unknown parameters: {sorted(kwargs)}")
+
+    @classmethod
+    def _get_param_names(cls):
+        return sorted(_PARAM_NAMES + ["cat_smoothing"])
+
+    def _boost_params(self) -> BoostParams:
+        return BoostParams(**{n: getattr(self, n) for n in _PARAM_NAMES})
+
+    @staticmethod
+    def _check_cats(categorical_features):
+        if categorical_features:
+            raise NotImplementedError("categorical target encoding is host preprocessing outside the "
+                                      "GPU tree-growth path; encode categorical columns before fit")
+
+    def fit(self, X, y, eval_set=None, categorical_features=None):
+        self._check_cats(categorical_features)
+        y = _require_single_target(np.asarray(y, dtype=np.float32))
+        yt = self._transform_y(y, fit=True)
+        ev = None
+        if eval_set is not None:
+            ev = (eval_set[0], self._transform_y(np.asarray(eval_set[1], dtype=np.float32), fit=False))
+        self.booster_ = Booster(self._boost_params(), self._loss())
+        self.booster_.fit(X, yt, eval_set=ev)
+        return self
+
+    def _margin(self, X) -> np.ndarray:
+        return self.booster_.predict_margin(X)
+
+
+class YABTClassifier(_YABTBase, ClassifierMixin):
+    """Binary and multiclass classifier (one-vs-rest for multiclass)."""
+
+    def fit(self, X, y, eval_set=None, categorical_features=None):
+        self._check_cats(categorical_features)
+        y = np.asarray(y, dtype=np.float32)
+        self.classes_ = np.unique(y)
+        self.n_classes_ = len(self.classes_)
+        self._is_binary = self.n_classes_ == 2
+        if self._is_binary:
+            yt = (y == self.classes_[1]).astype(np.float32)
+            ev = None
+            if eval_set is not None:
+                ye = (np.asarray(eval_set[1], dtype=np.float32) == self.classes_[1]).astype(np.float32)
+                ev = (eval_set[0], ye)
+            self.booster_ = Booster(self._boost_params(), LogLoss())
+            self.booster_.fit(X, yt, eval_set=ev)
+        else:
+            self.booster_ = MulticlassBooster(self._boost_params())
+            self.booster_.fit(X, y, eval_set=eval_set)
+        return self
+
+    def predict_proba(self, X) -> np.ndarray:
+        if self._is_binary:
+            p = expit(self.booster_.predict_margin(X))
+            return np.stack([1 - p, p], axis=1)
+        return self.booster_.predict_proba(X)
+
+    def predict(self, X) -> np.ndarray:
+        if self._is_binary:
+            return self.classes_[(self.booster_.predict_margin(X) > 0).astype(int)]
+        return self.booster_.predict(X)
+
+
+class YABTRegressor(_YABTBase, RegressorMixin):
+    """Regressor; standardises the target internally."""
+
+    def _loss(self):
+        return MSELoss()
+
+    def _transform_y(self, y, fit):
+        if fit:
+            self._y_mean = float(y.mean())
+            self._y_std = float(y.std()) or 1.0
+        return (y - self._y_mean) / self._y_std
+
+    def predict(self, X) -> np.ndarray:
+        return self._margin(X) * self._y_std + self._y_mean
