@@ -187,6 +187,7 @@ int yabt_leafnet_fit(const yabt_leafnet_args* a, void* workspace, long long ws_b
  * (yabt/boosting.py:36-38,53-54,511-514; Tree.net_contribution yabt/tree.py:118-128). */
 typedef struct {
   const int32_t* leaf_of_row;
+  int32_t max_nodes;              /* length of the per-node tables */
   const float* value;
   const float* linear;            /* NULL: constant leaves */
   const float* lo;

@@ -51,8 +51,9 @@ class LeafNetArgs(ctypes.Structure):
 class UpdateArgs(ctypes.Structure):
     """Mirror of ``yabt_update_args``."""
     _fields_ = [
-        ("leaf_of_row", c_vp), ("value", c_vp), ("linear", c_vp), ("lo", c_vp), ("hi", c_vp),
-        ("feats", c_vp), ("has_nets", c_vp), ("K", ctypes.c_int32), ("Xfm", c_vp), ("n", c_ll),
+        ("leaf_of_row", c_vp), ("max_nodes", ctypes.c_int32), ("value", c_vp), ("linear", c_vp),
+        ("lo", c_vp), ("hi", c_vp), ("feats", c_vp), ("has_nets", c_vp), ("K", ctypes.c_int32),
+        ("Xfm", c_vp), ("n", c_ll),
         ("margin", c_vp), ("y", c_vp), ("grad", c_vp), ("hess", c_vp), ("loss", ctypes.c_int32),
     ]
 

@@ -319,6 +319,7 @@ class Booster:
                                                        s), "yabt_interaction_update")
             u = _lib.UpdateArgs()
             u.leaf_of_row = leaf_of_row.data_ptr(); u.value = forest.value[t].data_ptr()
+            u.max_nodes = grower.max_nodes
             if p.neural_leaves:
                 u.linear = forest.linear[t].data_ptr(); u.lo = forest.lo[t].data_ptr()
                 u.hi = forest.hi[t].data_ptr(); u.feats = forest.feats[t].data_ptr()

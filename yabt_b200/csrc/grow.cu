@@ -498,37 +498,60 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
       if (lane == 0) s_wc[i][warp] = __popc(bal[i]);
     }
     __syncthreads();
-    if (t == 0) {
+    // warp 0: tile total, then a warp-wide decoupled look-back over up to 32
+    // predecessor tiles of the same node per step
+    if (warp == 0) {
       int run = 0;
-      for (int i = 0; i < 8; ++i)
-        for (int w = 0; w < NW; ++w) { s_wpre[i][w] = run; run += s_wc[i][w]; }
-      const unsigned Lt = (unsigned)run;
-      unsigned excl = 0;
+      if (t == 0) {
+        for (int i = 0; i < 8; ++i)
+          for (int w = 0; w < NW; ++w) { s_wpre[i][w] = run; run += s_wc[i][w]; }
+      }
+      const unsigned Lt = (unsigned)__shfl_sync(0xffffffffu, run, 0);
       unsigned long long* stat = b.tile_status;
+      const unsigned ep = epoch & 0x3fffffffu;
+      unsigned excl = 0;
       if (T.t_in_node == 0) {
-        atomicExch(&stat[tile], lb_word(epoch, 2u, Lt));
+        if (lane == 0) atomicExch(&stat[tile], lb_word(epoch, 2u, Lt));
       } else {
-        atomicExch(&stat[tile], lb_word(epoch, 1u, Lt));
-        int j = tile - 1;
+        if (lane == 0) atomicExch(&stat[tile], lb_word(epoch, 1u, Lt));
+        int base = tile - 1;                // window [base-31, base], lane j <-> tile base-j
+        const int first = tile - T.t_in_node;
         long long spins = 0;
         for (;;) {
-          const unsigned long long w = *(volatile unsigned long long*)&stat[j];
-          const unsigned we = (unsigned)(w >> 34), wf = (unsigned)(w >> 32) & 3u;
-          if (we == (epoch & 0x3fffffffu) && wf != 0u) {
-            excl += (unsigned)(w & 0xffffffffu);
-            if (wf == 2u) break;
-            --j;
+          const int j = base - lane;
+          unsigned long long w = 0;
+          unsigned wf = 2u;                 // tiles before the node's first count as "inclusive 0"
+          unsigned wv = 0;
+          if (j >= first) {
+            w = *(volatile unsigned long long*)&stat[j];
+            const bool cur = (unsigned)(w >> 34) == ep;
+            wf = cur ? (unsigned)(w >> 32) & 3u : 0u;
+            wv = (unsigned)(w & 0xffffffffu);
+          }
+          const unsigned notready = __ballot_sync(0xffffffffu, wf == 0u);
+          const unsigned incl = __ballot_sync(0xffffffffu, wf == 2u);
+          // lanes up to the first inclusive tile must all be ready
+          const int stop = incl ? __ffs(incl) - 1 : 31;
+          const unsigned need = stop >= 31 ? 0xffffffffu : ((1u << (stop + 1)) - 1u);
+          if (notready & need) {
+            if (++spins > (1LL << 22)) { if (lane == 0) atomicOr(&st->err, DERR_LOOKBACK_TIMEOUT); break; }
             continue;
           }
-          if (++spins > (1LL << 24)) { atomicOr(&st->err, DERR_LOOKBACK_TIMEOUT); break; }
+          unsigned v = (lane <= stop && j >= first) ? wv : 0u;
+          for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          excl += v;
+          if (incl) break;
+          base -= 32;
         }
-        atomicExch(&stat[tile], lb_word(epoch, 2u, excl + Lt));
+        if (lane == 0) atomicExch(&stat[tile], lb_word(epoch, 2u, excl + Lt));
       }
-      s_excl = (int)excl;
-      if (T.last) {
-        const int Ltot = (int)(excl + Lt);
-        b.seg_begin[nxt][2 * pr] = B; b.seg_count[nxt][2 * pr] = Ltot;
-        b.seg_begin[nxt][2 * pr + 1] = B + Ltot; b.seg_count[nxt][2 * pr + 1] = cnt - Ltot;
+      if (lane == 0) {
+        s_excl = (int)excl;
+        if (T.last) {
+          const int Ltot = (int)(excl + Lt);
+          b.seg_begin[nxt][2 * pr] = B; b.seg_count[nxt][2 * pr] = Ltot;
+          b.seg_begin[nxt][2 * pr + 1] = B + Ltot; b.seg_count[nxt][2 * pr + 1] = cnt - Ltot;
+        }
       }
     }
     __syncthreads();

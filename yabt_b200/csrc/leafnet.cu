@@ -72,9 +72,11 @@ struct LeafNetArgs {
   double* corr;               // [F]
   double* gsum;               // [1]
   float* rec;                 // [n][REC] records
-  unsigned* lo_ord;           // [maxn][K]
-  unsigned* hi_ord;           // [maxn][K]
+  float* pmin;                // [max_chunks][KMAX] chunk envelope
+  float* pmax;                // [max_chunks][KMAX]
   int* counts;                // [maxn]
+  int* leaf_first;            // [maxn] first chunk of a leaf
+  int* leaf_nch;              // [maxn] chunks of a leaf
   int* chunk_leaf;            // [max_chunks]
   int* chunk_begin;           // [max_chunks]
   int* chunk_end;             // [max_chunks]
@@ -82,7 +84,7 @@ struct LeafNetArgs {
   int max_chunks;
 };
 
-constexpr int REC = 12;   // floats per row record: x_norm[8], g, h, pad[2] (48 bytes)
+constexpr int REC = 12;   // floats per row record: raw x[8], g, h, pad[2] (48 bytes)
 
 __device__ __forceinline__ void loss_gh(int loss, float m, float y, float* g, float* h) {
   if (loss == 0) { *g = __fsub_rn(m, y); *h = 1.f; return; }
@@ -177,27 +179,13 @@ __global__ void __launch_bounds__(1024) k_ln_pad(LeafNetArgs a) {
   }
 }
 
-// ------------------------------------------------------------------ per-row records + envelope
-// grid-stride over rows; per block shared min/max per (leaf, k) flushed with atomics
+// ------------------------------------------------------------------ per-row records
+// Natural row order, streaming: record = (raw x[K], g, h) at margin + value[leaf].
 __global__ void __launch_bounds__(256) k_ln_rows(LeafNetArgs a) {
-  extern __shared__ unsigned smm[];       // [2][maxn][K]
   const int K = a.K;
-  const int nn = a.meta[0];
-  const int M = nn * K;
-  unsigned* slo = smm;
-  unsigned* shi = smm + M;
-  for (int i = threadIdx.x; i < M; i += blockDim.x) { slo[i] = 0xFFFFFFFFu; shi[i] = 0u; }
-  __syncthreads();
   int fk[KMAX];
-  float mu[KMAX], sd[KMAX];
 #pragma unroll
-  for (int k = 0; k < KMAX; ++k) {
-    if (k < K) {
-      fk[k] = (int)a.feats[k];
-      mu[k] = a.col_mean[fk[k]];
-      sd[k] = fmaxf(a.col_std[fk[k]], 1e-6f);
-    } else { fk[k] = 0; mu[k] = 0.f; sd[k] = 1.f; }
-  }
+  for (int k = 0; k < KMAX; ++k) fk[k] = k < K ? (int)a.feats[k] : 0;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < a.n;
        i += (long long)gridDim.x * blockDim.x) {
     const int l = a.leaf_of_row[i];
@@ -205,31 +193,17 @@ __global__ void __launch_bounds__(256) k_ln_rows(LeafNetArgs a) {
     loss_gh(a.loss, __fadd_rn(a.margin[i], a.value[l]), a.y[i], &g, &h);
     float r[REC];
 #pragma unroll
-    for (int k = 0; k < KMAX; ++k) {
-      float xn = 0.f;
-      if (k < K) {
-        const float x = a.Xfm[(long long)fk[k] * a.n + i];
-        xn = __fdiv_rn(__fsub_rn(x, mu[k]), sd[k]);
-        const unsigned o = f2ord(x);
-        atomicMin(&slo[l * K + k], o);
-        atomicMax(&shi[l * K + k], o);
-      }
-      r[k] = xn;
-    }
+    for (int k = 0; k < KMAX; ++k) r[k] = k < K ? a.Xfm[(long long)fk[k] * a.n + i] : 0.f;
     r[KMAX] = g; r[KMAX + 1] = h; r[KMAX + 2] = 0.f; r[KMAX + 3] = 0.f;
     float4* dst = reinterpret_cast<float4*>(a.rec + i * REC);
     dst[0] = make_float4(r[0], r[1], r[2], r[3]);
     dst[1] = make_float4(r[4], r[5], r[6], r[7]);
     dst[2] = make_float4(r[8], r[9], r[10], r[11]);
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < M; i += blockDim.x) {
-    if (slo[i] != 0xFFFFFFFFu) atomicMin(&a.lo_ord[i], slo[i]);
-    if (shi[i] != 0u) atomicMax(&a.hi_ord[i], shi[i]);
-  }
 }
 
-// one block: counts, eligibility and the Gram chunk plan
+// one block: counts, eligibility and the chunk plan (every non-empty leaf;
+// chunks of a leaf are contiguous: leaf_first[g], leaf_nch[g])
 __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
   const int nn = a.meta[0];
   __shared__ int s_ne;
@@ -239,42 +213,66 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
     const bool leaf = a.feature[g] < 0;
     const int c = leaf ? a.leaf_count[g] : 0;
     a.counts[g] = c;
+    a.leaf_nch[g] = (c + GRAM_CHUNK - 1) / GRAM_CHUNK;
     if (leaf && c >= a.min_samples) atomicAdd(&s_ne, 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int nc = 0;
-    for (int g = 0; g < nn; ++g) {
-      if (a.feature[g] >= 0 || a.counts[g] < a.min_samples) continue;
-      const int c = a.counts[g];
-      for (int b = 0; b < c; b += GRAM_CHUNK) {
-        if (nc < a.max_chunks) {
-          a.chunk_leaf[nc] = g;
-          a.chunk_begin[nc] = a.leaf_begin[g] + b;
-          a.chunk_end[nc] = a.leaf_begin[g] + min(c, b + GRAM_CHUNK);
-        }
-        ++nc;
-      }
+  if ((threadIdx.x >> 5) == 0) {
+    const int lane = threadIdx.x & 31;
+    int carry = 0;
+    for (int base = 0; base < nn; base += 32) {
+      const int g = base + lane;
+      const int v = g < nn ? a.leaf_nch[g] : 0;
+      int x = v;
+      for (int o = 1; o < 32; o <<= 1) { const int y = __shfl_up_sync(0xffffffffu, x, o); if (lane >= o) x += y; }
+      if (g < nn) a.leaf_first[g] = carry + x - v;
+      carry += __shfl_sync(0xffffffffu, x, 31);
     }
-    a.flags[2] = min(nc, a.max_chunks);
-    a.flags[3] = s_ne;
-    a.has_nets[0] = s_ne > 0;
+    if (lane == 0) {
+      a.flags[2] = min(carry, a.max_chunks);
+      a.flags[3] = s_ne;
+      a.has_nets[0] = s_ne > 0;
+    }
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    const int c = a.counts[g], f0 = a.leaf_first[g];
+    for (int q = 0; q < a.leaf_nch[g]; ++q) {
+      const int idx = f0 + q;
+      if (idx >= a.max_chunks) break;
+      a.chunk_leaf[idx] = g;
+      a.chunk_begin[idx] = a.leaf_begin[g] + q * GRAM_CHUNK;
+      a.chunk_end[idx] = a.leaf_begin[g] + min(c, (q + 1) * GRAM_CHUNK);
+    }
   }
 }
 
-// one block (8 warps) per chunk; each warp takes rows, lane e accumulates
-// entries e and e + 32 in fp64 in row order; warps are reduced in order.
+// One block (8 warps) per chunk of a leaf's rows. Each warp stages 32-row
+// batches through shared memory (lane k gathers row k's record; the next
+// batch is prefetched into registers while the current one is consumed),
+// normalises x, tracks the raw-x envelope, and lane e accumulates Gram /
+// rhs entries e and e+32 in fp64 over the rows in order. Warps are reduced in
+// order, so the chunk partial is deterministic.
 __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
   __shared__ double sp[8][NE];
+  __shared__ float stage[8][32][REC];
+  __shared__ float smin[8][KMAX], smax[8][KMAX];
   const int c = blockIdx.x;
   if (c >= a.flags[2]) return;
   const int g = a.chunk_leaf[c];
+  const bool elig = a.counts[g] >= a.min_samples;
   const int src = a.leaf_src[g];
   const int* lst = src == 0 ? a.fin : (src == 1 ? a.list0 : (src == 2 ? a.list1 : nullptr));
   const int b0 = a.chunk_begin[c], b1 = a.chunk_end[c];
   const int K = a.K, D = K + 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // entry e -> (ia, ib) of the upper triangle of the D x D matrix, then rhs
+  float mu[KMAX], sd[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    const int f = k < K ? (int)a.feats[k] : 0;
+    mu[k] = k < K ? a.col_mean[f] : 0.f;
+    sd[k] = k < K ? fmaxf(a.col_std[f], 1e-6f) : 1.f;
+  }
   int ea[2], eb[2];
   bool ev[2];
   const int ntri = D * (D + 1) / 2;
@@ -291,27 +289,67 @@ __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
     ea[q] = ia; eb[q] = ib;
   }
   double acc[2] = {0.0, 0.0};
+  float mn[KMAX], mx[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) { mn[k] = INFINITY; mx[k] = -INFINITY; }
   const int per = (b1 - b0 + 7) / 8;
   const int w0 = b0 + warp * per, w1 = min(b1, w0 + per);
-  for (int p = w0; p < w1; ++p) {
-    const int row = lst ? lst[p] : p;
-    const float4* r4 = reinterpret_cast<const float4*>(a.rec + (long long)row * REC);
-    const float4 v0 = __ldg(r4), v1 = __ldg(r4 + 1), v2 = __ldg(r4 + 2);
-    const float xr[KMAX + 2] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, v2.x, v2.y};
-    const double hh = (double)xr[KMAX + 1], gg = (double)xr[KMAX];
+  float4 n0, n1, n2;   // prefetched record of this lane's row in the next batch
+  auto fetch = [&](int p0) {
+    const int p = p0 + lane;
+    if (p < w1) {
+      const int row = lst ? lst[p] : p;
+      const float4* r4 = reinterpret_cast<const float4*>(a.rec + (long long)row * REC);
+      n0 = __ldg(r4); n1 = __ldg(r4 + 1); n2 = __ldg(r4 + 2);
+    }
+  };
+  fetch(w0);
+  for (int p0 = w0; p0 < w1; p0 += 32) {
+    const int nb = min(32, w1 - p0);
+    {
+      // stage this lane's row: normalised x, g, h; envelope of raw x
+      float xr[KMAX] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+      float* st = stage[warp][lane];
+      if (lane < nb) {
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      if (!ev[q]) continue;
-      const double xa = ea[q] < K ? (double)xr[ea[q]] : 1.0;
-      if (eb[q] >= 0) {
-        const double xb = eb[q] < K ? (double)xr[eb[q]] : 1.0;
-        // M_ab += x1_a * (x1_b * h)   (yabt/neural_leaves.py:71,82)
-        acc[q] = __dadd_rn(acc[q], __dmul_rn(xa, __dmul_rn(xb, hh)));
-      } else {
-        // b_a += -(x1_a * g)          (yabt/neural_leaves.py:72,83)
-        acc[q] = __dadd_rn(acc[q], -__dmul_rn(xa, gg));
+        for (int k = 0; k < KMAX; ++k) {
+          if (k < K) { mn[k] = fminf(mn[k], xr[k]); mx[k] = fmaxf(mx[k], xr[k]); }
+          st[k] = __fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]);
+        }
+        st[KMAX] = n2.x; st[KMAX + 1] = n2.y;
       }
     }
+    __syncwarp();
+    fetch(p0 + 32);   // next batch in flight while this one is consumed
+    if (elig) {
+      for (int r = 0; r < nb; ++r) {
+        const float* st = stage[warp][r];
+        const double hh = (double)st[KMAX + 1], gg = (double)st[KMAX];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          if (!ev[q]) continue;
+          const double xa = ea[q] < K ? (double)st[ea[q]] : 1.0;
+          if (eb[q] >= 0) {
+            const double xb = eb[q] < K ? (double)st[eb[q]] : 1.0;
+            // M_ab += x1_a * (x1_b * h)   (yabt/neural_leaves.py:71,82)
+            acc[q] = __dadd_rn(acc[q], __dmul_rn(xa, __dmul_rn(xb, hh)));
+          } else {
+            // b_a += -(x1_a * g)          (yabt/neural_leaves.py:72,83)
+            acc[q] = __dadd_rn(acc[q], -__dmul_rn(xa, gg));
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    float a0 = mn[k], a1 = mx[k];
+    for (int o = 16; o; o >>= 1) {
+      a0 = fminf(a0, __shfl_xor_sync(0xffffffffu, a0, o));
+      a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, o));
+    }
+    if (lane == 0) { smin[warp][k] = a0; smax[warp][k] = a1; }
   }
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
@@ -323,29 +361,51 @@ __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
     double t = 0.0;
     for (int w = 0; w < 8; ++w) t = __dadd_rn(t, sp[w][threadIdx.x]);
     a.partial[(long long)c * NE + threadIdx.x] = t;
+  } else if (threadIdx.x >= 64 && threadIdx.x < 64 + KMAX) {
+    const int k = threadIdx.x - 64;
+    float a0 = INFINITY, a1 = -INFINITY;
+    for (int w = 0; w < 8; ++w) { a0 = fminf(a0, smin[w][k]); a1 = fmaxf(a1, smax[w][k]); }
+    a.pmin[(long long)c * KMAX + k] = a0;
+    a.pmax[(long long)c * KMAX + k] = a1;
   }
 }
 
-// one thread per eligible leaf: reduce partials in chunk order, ridge,
-// Cholesky, fold (yabt/neural_leaves.py:85-89,180-184)
-__global__ void k_ln_solve(LeafNetArgs a) {
+// One warp per node: lanes reduce the node's chunk partials (contiguous, in
+// chunk order) and envelope, lane 0 adds the ridge, solves by Cholesky and
+// folds (yabt/neural_leaves.py:85-89,180-184).
+__global__ void __launch_bounds__(128) k_ln_solve(LeafNetArgs a) {
+  __shared__ double se[4][NE];
   const int nn = a.meta[0];
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x * 4 + warp;
   if (g >= nn) return;
   const int K = a.K, D = K + 1;
   const bool leaf = a.feature[g] < 0;
   const bool elig = leaf && a.counts[g] >= a.min_samples;
+  const int c0 = leaf ? a.leaf_first[g] : 0, nc = leaf ? a.leaf_nch[g] : 0;
+  // envelope over the node's chunks (lanes 0..K-1)
+  if (lane < K) {
+    float lo = INFINITY, hi = -INFINITY;
+    for (int c = c0; c < c0 + nc; ++c) {
+      lo = fminf(lo, a.pmin[(long long)c * KMAX + lane]);
+      hi = fmaxf(hi, a.pmax[(long long)c * KMAX + lane]);
+    }
+    a.lo[(long long)g * K + lane] = lo;
+    a.hi[(long long)g * K + lane] = hi;
+  }
+  for (int e = lane; e < NE; e += 32) {
+    double t = 0.0;
+    if (elig)
+      for (int c = c0; c < c0 + nc; ++c) t = __dadd_rn(t, a.partial[(long long)c * NE + e]);
+    se[warp][e] = t;
+  }
+  __syncwarp();
+  if (lane != 0) return;
   float W[KMAX], db = 0.f;
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) W[k] = 0.f;
   if (elig) {
-    double e[NE];
-    for (int q = 0; q < NE; ++q) e[q] = 0.0;
-    const int nc = a.flags[2];
-    for (int c = 0; c < nc; ++c) {
-      if (a.chunk_leaf[c] != g) continue;
-      for (int q = 0; q < NE; ++q) e[q] = __dadd_rn(e[q], a.partial[(long long)c * NE + q]);
-    }
+    const double* e = se[warp];
     double M[KMAX + 1][KMAX + 1], bv[KMAX + 1];
     int idx = 0;
     for (int i = 0; i < D; ++i)
@@ -353,7 +413,6 @@ __global__ void k_ln_solve(LeafNetArgs a) {
     for (int i = 0; i < D; ++i) bv[i] = e[idx + i];
     for (int i = 0; i < K; ++i) M[i][i] = __dadd_rn(M[i][i], (double)a.l2);
     M[K][K] = __dadd_rn(M[K][K], 1e-8);
-    // Cholesky M = L L^T (in place, lower)
     bool ok = true;
     for (int j = 0; j < D && ok; ++j) {
       double s = M[j][j];
@@ -391,9 +450,6 @@ __global__ void k_ln_solve(LeafNetArgs a) {
     const float mu = a.col_mean[f];
     s = __fadd_rn(s, __fmul_rn(W[k], __fdiv_rn(mu, sd)));
     a.linear[(long long)g * K + k] = __fdiv_rn(__fmul_rn(a.lr, W[k]), sd);
-    const unsigned lo = a.lo_ord[(long long)g * K + k], hi = a.hi_ord[(long long)g * K + k];
-    a.lo[(long long)g * K + k] = lo == 0xFFFFFFFFu ? INFINITY : ord2f(lo);
-    a.hi[(long long)g * K + k] = hi == 0u ? -INFINITY : ord2f(hi);
   }
   if (a.flags[3] > 0) a.value[g] = __fadd_rn(a.value[g], __fmul_rn(a.lr, __fsub_rn(db, s)));
 }
@@ -417,24 +473,35 @@ struct UpdateArgs {
   int loss;
 };
 
-__global__ void __launch_bounds__(256) k_update(UpdateArgs u) {
+// Per-leaf tables (value, linear, lo, hi) are staged in shared memory; rows
+// stream in natural order.
+__global__ void __launch_bounds__(256) k_update(UpdateArgs u, int nn) {
+  extern __shared__ float tb[];            // value[nn], linear/lo/hi[nn][K]
   const bool nets = u.linear && u.has_nets && u.has_nets[0];
+  const int K = nets ? u.K : 0;
+  float* sval = tb;
+  float* slin = tb + nn;
+  float* slo = slin + nn * K;
+  float* shi = slo + nn * K;
+  for (int i = threadIdx.x; i < nn; i += blockDim.x) sval[i] = u.value[i];
+  for (int i = threadIdx.x; i < nn * K; i += blockDim.x) { slin[i] = u.linear[i]; slo[i] = u.lo[i]; shi[i] = u.hi[i]; }
+  __syncthreads();
   int fk[KMAX];
 #pragma unroll
-  for (int k = 0; k < KMAX; ++k) fk[k] = (nets && k < u.K) ? (int)u.feats[k] : 0;
+  for (int k = 0; k < KMAX; ++k) fk[k] = (k < K) ? (int)u.feats[k] : 0;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < u.n;
        i += (long long)gridDim.x * blockDim.x) {
     const int l = u.leaf_of_row[i];
-    float c = u.value[l];
+    float c = sval[l];
     if (nets) {
       float s = 0.f;
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
-        if (k < u.K) {
-          const long long o = (long long)l * u.K + k;
+        if (k < K) {
+          const int o = l * K + k;
           const float x = u.Xfm[(long long)fk[k] * u.n + i];
-          const float xc = fminf(fmaxf(x, u.lo[o]), u.hi[o]);
-          s = __fadd_rn(s, __fmul_rn(u.linear[o], xc));
+          const float xc = fminf(fmaxf(x, slo[o]), shi[o]);
+          s = __fadd_rn(s, __fmul_rn(slin[o], xc));
         }
       }
       c = __fadd_rn(c, s);
@@ -572,8 +639,8 @@ long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes) {
   b += al((long long)F * 8);                 // corr
   b += al(8);                                // gsum
   b += al(n * REC * 4);                      // rec
-  b += 2 * al((long long)max_nodes * KMAX * 4);   // lo_ord, hi_ord
-  b += al((long long)max_nodes * 4);         // counts
+  b += 2 * al(max_chunks * KMAX * 4);        // pmin, pmax
+  b += 3 * al((long long)max_nodes * 4);     // counts, leaf_first, leaf_nch
   b += 3 * al(max_chunks * 4);               // chunk arrays
   b += al(max_chunks * NE * 8);              // partials
   return b;
@@ -607,17 +674,17 @@ int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_b
   a.corr = (double*)w; w += al((long long)p->F * 8);
   a.gsum = (double*)w; w += al(8);
   a.rec = (float*)w; w += al(p->n * REC * 4);
-  a.lo_ord = (unsigned*)w; w += al((long long)p->max_nodes * KMAX * 4);
-  a.hi_ord = (unsigned*)w; w += al((long long)p->max_nodes * KMAX * 4);
+  a.pmin = (float*)w; w += al(max_chunks * KMAX * 4);
+  a.pmax = (float*)w; w += al(max_chunks * KMAX * 4);
   a.counts = (int*)w; w += al((long long)p->max_nodes * 4);
+  a.leaf_first = (int*)w; w += al((long long)p->max_nodes * 4);
+  a.leaf_nch = (int*)w; w += al((long long)p->max_nodes * 4);
   a.chunk_leaf = (int*)w; w += al(max_chunks * 4);
   a.chunk_begin = (int*)w; w += al(max_chunks * 4);
   a.chunk_end = (int*)w; w += al(max_chunks * 4);
   a.partial = (double*)w;
   a.max_chunks = (int)max_chunks;
   const int nsm = 148;
-  LCUDA(cudaMemsetAsync(a.lo_ord, 0xFF, (size_t)p->max_nodes * KMAX * 4, s));
-  LCUDA(cudaMemsetAsync(a.hi_ord, 0x00, (size_t)p->max_nodes * KMAX * 4, s));
   k_ln_select<<<1, 1024, 0, s>>>(a);
   {
     dim3 grid((unsigned)std::min<long long>((p->n + 255) / 256, 4LL * nsm), (unsigned)((p->F + 7) / 8));
@@ -625,13 +692,12 @@ int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_b
   }
   k_ln_pad<<<1, 1024, 0, s>>>(a);
   {
-    const size_t smem = (size_t)2 * p->max_nodes * p->K * 4;
-    const int grid = (int)std::min<long long>((p->n + 255) / 256, 4LL * nsm);
-    k_ln_rows<<<grid, 256, smem, s>>>(a);
+    const int grid = (int)std::min<long long>((p->n + 255) / 256, 16LL * nsm);
+    k_ln_rows<<<grid, 256, 0, s>>>(a);
   }
   k_ln_plan<<<1, 1024, 0, s>>>(a);
   k_ln_gram<<<(unsigned)max_chunks, 256, 0, s>>>(a);
-  k_ln_solve<<<(p->max_nodes + 127) / 128, 128, 0, s>>>(a);
+  k_ln_solve<<<(p->max_nodes + 3) / 4, 128, 0, s>>>(a);
   count_launches(7);
   LCUDA(cudaGetLastError());
   return YABT_OK;
@@ -644,8 +710,15 @@ int yabt_update_margin(const yabt_update_args* p, void* stream) {
   u.feats = (const long long*)p->feats; u.has_nets = p->has_nets; u.K = p->K; u.Xfm = p->Xfm; u.n = p->n;
   u.margin = p->margin; u.y = p->y; u.grad = p->grad; u.hess = p->hess; u.loss = p->loss;
   if (p->n == 0) return YABT_OK;
+  if (p->max_nodes <= 0) { set_error("yabt_update_margin: max_nodes must be > 0"); return YABT_ERR_ARG; }
   const int grid = (int)std::min<long long>((p->n + 255) / 256, 148LL * 8);
-  k_update<<<grid, 256, 0, (cudaStream_t)stream>>>(u);
+  const int K = p->linear ? p->K : 0;
+  const size_t smem = (size_t)p->max_nodes * (1 + 3 * K) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) { set_error("k_update smem: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  }
+  k_update<<<grid, 256, smem, (cudaStream_t)stream>>>(u, p->max_nodes);
   count_launches(1);
   LCUDA(cudaGetLastError());
   return YABT_OK;
