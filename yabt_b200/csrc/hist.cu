@@ -29,82 +29,100 @@ struct HistCfg {
   static constexpr int SMEM = WORDS * 4;
 };
 
-__device__ __forceinline__ void red_add(unsigned* p, unsigned v) {
-  atomicAdd(p, v);   // result unused -> shared-memory reduction (RED)
+// Shared-memory reductions with explicit 32-bit shared addresses; the limb
+// offsets are immediates, so each update is one red instruction.
+template <int OFF>
+__device__ __forceinline__ void red_s(unsigned addr, unsigned v) {
+  asm volatile("red.shared.add.u32 [%0+%1], %2;\n" ::"r"(addr), "n"(OFF), "r"(v) : "memory");
 }
 
-template <int S, int LIMBS>
-__device__ __forceinline__ void acc_row(unsigned* sh, unsigned b0, unsigned b1, bool ok0, bool ok1,
-                                        int lane, int vg, int vh) {
-  using Cfg = HistCfg<S, LIMBS>;
+// Row contribution of one lane: feature sub 0 at bin b0, sub 1 at bin b1.
+// lb is the shared address of word (bin 0, lane) of limb 0. FULL: every lane
+// owns a feature of every sub (no per-lane predicates).
+template <int S, int LIMBS, bool FULL>
+__device__ __forceinline__ void acc_row(unsigned lb, unsigned b0, unsigned b1, bool ok0, bool ok1,
+                                        int vg, int vh) {
+  constexpr int LS = HistCfg<S, LIMBS>::LIMB_STRIDE * 4;   // bytes between limbs
   const unsigned glo = (unsigned)vg & 0xFFFFu, ghi = (unsigned)(vg >> 16);
-  if (ok0) {
-    unsigned* w = sh + ((b0 << 5) | lane);
-    red_add(w, glo);
-    red_add(w + Cfg::LIMB_STRIDE, ghi);
+  if (FULL || ok0) {
+    const unsigned a0 = lb + (b0 << 7);
+    red_s<0>(a0, glo);
+    red_s<LS>(a0, ghi);
     if constexpr (LIMBS == 5) {
-      red_add(w + 2 * Cfg::LIMB_STRIDE, (unsigned)vh & 0xFFFFu);
-      red_add(w + 3 * Cfg::LIMB_STRIDE, (unsigned)(vh >> 16));
+      red_s<2 * LS>(a0, (unsigned)vh & 0xFFFFu);
+      red_s<3 * LS>(a0, (unsigned)(vh >> 16));
     }
-    red_add(w + (LIMBS - 1) * Cfg::LIMB_STRIDE, 1u);
+    red_s<(LIMBS - 1) * LS>(a0, 1u);
   }
   if constexpr (S == 2) {
-    if (ok1) {
-      unsigned* w = sh + (((YABT_NB + b1) << 5) | lane);
-      red_add(w, glo);
-      red_add(w + Cfg::LIMB_STRIDE, ghi);
-      red_add(w + (LIMBS - 1) * Cfg::LIMB_STRIDE, 1u);
+    if (FULL || ok1) {
+      const unsigned a1 = lb + (b1 << 7) + YABT_NB * 32 * 4;
+      red_s<0>(a1, glo);
+      red_s<LS>(a1, ghi);
+      red_s<(LIMBS - 1) * LS>(a1, 1u);
     }
   }
 }
 
-// ---------------------------------------------------------------- async copy helpers
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+// ---------------------------------------------------------------- async copy / shared helpers
+__device__ __forceinline__ void cp_async16s(unsigned saddr, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gmem));
 }
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+__device__ __forceinline__ unsigned lds_u16(unsigned a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ unsigned lds_u8(unsigned a) {
+  unsigned short v;
+  asm volatile("ld.shared.u8 %0, [%1];\n" : "=h"(v) : "r"(a));
+  return v;
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 // Block geometry and shared-memory budget of k_hist: the histogram plus a
-// per-warp ring of STG stages of 512 bytes (one 16-byte async copy per lane).
+// per-warp ring of STG stages of RPS row slots (64 bytes each).
 template <int S, int LIMBS>
 struct HistPipe {
-  static constexpr int WARPS = (S == 2) ? 16 : 32;
+  static constexpr int WARPS = 32;
   static constexpr int THREADS = WARPS * 32;
   static constexpr int STG = 4;
-  static constexpr int STAGE_BYTES = 512;
+  static constexpr int RPS = 4;                         // rows per stage
+  static constexpr int STAGE_BYTES = RPS * 64;
   static constexpr int SMEM = HistCfg<S, LIMBS>::SMEM + WARPS * STG * STAGE_BYTES;
 };
 
-// One work item of one warp: rows [w0, w1) of the item (positions in the row
-// list), tile rows of TW bytes. Stage s holds RPS = 512/TW rows; lane copies
-// 16 bytes (row lane/LPR, piece lane%LPR). Row ids are loaded one iteration
-// ahead of their copy and gradients travel with the copy, so a warp keeps
-// STG-1 stages (1.5 KB) in flight while it consumes one.
-template <int S, int LIMBS, int TW>
-__device__ __forceinline__ void hist_warp(unsigned* __restrict__ sh, uint8_t* __restrict__ ring,
-                                          const uint8_t* __restrict__ tb, const int* __restrict__ lst,
-                                          int base, int nrow, const float* __restrict__ g,
-                                          const float* __restrict__ h, float gs, float hs,
-                                          int k0, bool ok0, bool ok1, int lane) {
+// One work item of one warp: rows [0, nrow) of its share (positions in the row
+// list), tile rows of TW bytes. Stage s holds RPS rows; the first RPS*LPR lanes
+// copy 16 bytes each (row lane/LPR, piece lane%LPR) with cp.async; the row's
+// gradient is loaded with the copy. Row ids are loaded one iteration ahead of
+// their copy, so a warp keeps STG-1 stages in flight while it consumes one.
+// The loads and shuffles of a stage's rows are issued before their shared-
+// memory reductions, and full stages need no per-row bounds checks.
+template <int S, int LIMBS, int TW, bool FULL>
+__device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, const uint8_t* __restrict__ tb,
+                                          const int* __restrict__ lst, int base, int nrow,
+                                          const float* __restrict__ g, const float* __restrict__ h,
+                                          float gs, float hs, int k0, bool ok0, bool ok1, int lane) {
+  using Pipe = HistPipe<S, LIMBS>;
   constexpr int LPR = TW / 16;
-  constexpr int RPS = 32 / LPR;
-  constexpr int STG = HistPipe<S, LIMBS>::STG;
+  constexpr int SB = Pipe::STAGE_BYTES;
+  constexpr int RPS = Pipe::RPS;
+  constexpr int STG = Pipe::STG;
+  constexpr int CL = RPS * LPR;                 // copying lanes (<= 32)
+  static_assert(CL <= 32, "stage geometry");
   const int rr = lane / LPR, piece = lane % LPR;
+  const bool copier = lane < CL;
   const int nst = (nrow + RPS - 1) / RPS;
   auto rid_of = [&](int s) -> int {
     const int k = s * RPS + rr;
-    if (k >= nrow) return -1;
+    if (!copier || k >= nrow) return -1;
     return lst ? __ldg(lst + base + k) : base + k;
   };
   auto copy = [&](int s, int r) {
-    if (r >= 0) cp_async16(ring + (s % STG) * 512 + lane * 16, tb + (size_t)r * TW + piece * 16);
+    if (r >= 0) cp_async16s(ring + (s % STG) * SB + rr * 64 + piece * 16, tb + (size_t)r * TW + piece * 16);
   };
   float gq[STG], hq[STG];
 #pragma unroll
@@ -116,6 +134,8 @@ __device__ __forceinline__ void hist_warp(unsigned* __restrict__ sh, uint8_t* __
     cp_commit();
   }
   int rnext = rid_of(STG - 1);
+  // byte offset of this lane's bin(s) inside a row slot
+  const unsigned boff = (TW == 64) ? (S == 2 ? 2u * lane : 2u * lane + k0) : (unsigned)(lane & (TW - 1));
   for (int s = 0; s < nst; ++s) {
     const int r = rnext;
     rnext = rid_of(s + STG);
@@ -127,22 +147,25 @@ __device__ __forceinline__ void hist_warp(unsigned* __restrict__ sh, uint8_t* __
     __syncwarp();
     const int vgl = __float2int_rn(gq[0] * gs);
     const int vhl = (LIMBS == 5) ? __float2int_rn(hq[0] * hs) : 0;
-    const uint8_t* stg = ring + (s % STG) * 512;
+    const unsigned stg = ring + (s % STG) * SB;   // row q at stg + 64 q
+    const int nr = min(RPS, nrow - s * RPS);
+    unsigned wv[RPS];
+    int vg[RPS], vh[RPS];
 #pragma unroll
     for (int q = 0; q < RPS; ++q) {
-      const int vg = __shfl_sync(0xffffffffu, vgl, q * LPR);
-      int vh = 0;
-      if constexpr (LIMBS == 5) vh = __shfl_sync(0xffffffffu, vhl, q * LPR);
-      if (s * RPS + q < nrow) {
-        unsigned wv = 0;
-        if constexpr (TW == 64) {
-          if constexpr (S == 2) wv = *reinterpret_cast<const unsigned short*>(stg + q * 64 + 2 * lane);
-          else wv = stg[q * 64 + 2 * lane + k0];
-        } else {
-          if (TW == 32 || lane < 16) wv = stg[q * TW + (lane & (TW - 1))];
-        }
-        acc_row<S, LIMBS>(sh, wv & 0xFFu, (wv >> 8) & 0xFFu, ok0, ok1, lane, vg, vh);
-      }
+      vg[q] = __shfl_sync(0xffffffffu, vgl, q * LPR);
+      vh[q] = (LIMBS == 5) ? __shfl_sync(0xffffffffu, vhl, q * LPR) : 0;
+      if constexpr (TW == 64 && S == 2) wv[q] = lds_u16(stg + q * 64 + boff);
+      else wv[q] = lds_u8(stg + q * 64 + boff);
+    }
+    if (nr == RPS) {
+#pragma unroll
+      for (int q = 0; q < RPS; ++q)
+        acc_row<S, LIMBS, FULL>(lb, wv[q] & 0xFFu, wv[q] >> 8, ok0, ok1, vg[q], vh[q]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < RPS; ++q)
+        if (q < nr) acc_row<S, LIMBS, FULL>(lb, wv[q] & 0xFFu, wv[q] >> 8, ok0, ok1, vg[q], vh[q]);
     }
     __syncwarp();
 #pragma unroll
@@ -169,7 +192,9 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
   const int nitems = st->n_items;
   const float gs = st->gscale, hs = st->hscale;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  uint8_t* ring = reinterpret_cast<uint8_t*>(sh + Cfg::WORDS) + warp * Pipe::STG * Pipe::STAGE_BYTES;
+  const unsigned sh_s = (unsigned)__cvta_generic_to_shared(sh);
+  const unsigned lb = sh_s + lane * 4;                       // word (bin 0, lane) of limb 0
+  const unsigned ring = sh_s + Cfg::WORDS * 4 + warp * Pipe::STG * Pipe::STAGE_BYTES;
   for (;;) {
     if (threadIdx.x == 0) s_item = atomicAdd(&st->item_counter, 1);
     __syncthreads();
@@ -181,18 +206,21 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
       *reinterpret_cast<uint4*>(sh + i) = make_uint4(0, 0, 0, 0);
     __syncthreads();
     const uint8_t* tb = bins + ud.off;
-    const bool ok0 = ud.feat[0][lane] >= 0;
+    const bool ok0 = ud.feat[0][lane] >= 0 && (ud.width != 16 || lane < 16);
     const bool ok1 = (S == 2) && ud.nsub > 1 && ud.feat[S == 2 ? 1 : 0][lane] >= 0;
     const int per = (item.count + nw - 1) / nw;
     const int w0 = min(item.count, warp * per), w1 = min(item.count, w0 + per);
     const int* lst = rows ? rows + item.begin : nullptr;
     const int base = rows ? w0 : item.begin + w0;
-    if (ud.width == 64)
-      hist_warp<S, LIMBS, 64>(sh, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+    const bool full = ud.width == 64 && (S == 1 || ud.nsub == 2);
+    if (full)
+      hist_warp<S, LIMBS, 64, true>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+    else if (ud.width == 64)
+      hist_warp<S, LIMBS, 64, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
     else if (ud.width == 32)
-      hist_warp<S, LIMBS, 32>(sh, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+      hist_warp<S, LIMBS, 32, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
     else
-      hist_warp<S, LIMBS, 16>(sh, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+      hist_warp<S, LIMBS, 16, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
     __syncthreads();
     unsigned* dst = partials + (size_t)item.slot * Cfg::WORDS;
     for (int i = threadIdx.x * 4; i < Cfg::WORDS; i += blockDim.x * 4)
