@@ -140,6 +140,26 @@ long long yabt_bin_fit_workspace_bytes(long long n, int F, long long nq);
 int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
                  int max_bins, void* workspace, long long ws_bytes, float* medians, float* edges,
                  int32_t* edge_cnt, float* scales, void* stream);
+/* Allocation-free variant of yabt_bin_fit (no counterpart in the reference).
+ * For callers that cannot allocate device memory when they fit -- e.g. a
+ * process whose GPU memory is reserved up front by another framework's caching
+ * allocator, or a latency-critical loop where cudaMalloc (which may
+ * synchronise the device and can fail under memory pressure) is not allowed.
+ * Same inputs, outputs and results as yabt_bin_fit; the scratch lives in a
+ * fixed device array of yabt_bin_fit_static_capacity() bytes (8 MiB) that
+ * every GPU loading the library holds until the process exits. Fits whose
+ * scratch (yabt_bin_fit_workspace_bytes) exceeds it are rejected with
+ * YABT_ERR_UNSUPPORTED (e.g. F = 64 features with up to 16384 sample rows fit,
+ * the default 200000-row sample of 200 features does not). The first call on
+ * each device looks up the array's device address; make that first call before
+ * any stream capture. All calls on a device share the one array: calls whose
+ * work overlaps on the GPU (different streams, or host threads) race and
+ * corrupt each other's results -- serialise them. The function allocates
+ * nothing.                                                                */
+long long yabt_bin_fit_static_capacity(void);
+int yabt_bin_fit_static(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
+                        int max_bins, float* medians, float* edges, int32_t* edge_cnt, float* scales,
+                        void* stream);
 /* NaN -> median in Xfm (in place), bins = #{edges < x} into the tiled layout
  * (and, if plain_out != NULL, the plain (n, F) matrix).
  * Replaces Binner.transform / impute (yabt/binning.py:97-124).           */

@@ -91,6 +91,8 @@ SIGNATURES = [
     ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
     ("yabt_bin_fit_workspace_bytes", c_ll, [c_ll, c_int, c_ll]),
     ("yabt_bin_fit", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    ("yabt_bin_fit_static_capacity", c_ll, []),
+    ("yabt_bin_fit_static", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_bin_transform", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_leafnet_workspace_bytes", c_ll, [c_ll, c_int, c_int]),
     ("yabt_leafnet_fit", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, c_vp]),

@@ -503,3 +503,74 @@ int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, con
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free variant
+// yabt_bin_fit_static: the same bin fit with its scratch in a fixed array that
+// lives in the library's device image instead of a caller workspace. It is for
+// callers that cannot allocate device memory at fit time -- for example a
+// process whose GPU memory is reserved up front by another framework's caching
+// allocator, or a latency-critical loop where cudaMalloc (which may
+// synchronise the device and can fail under memory pressure) is not allowed.
+// The array is BIN_FIT_STATIC_BYTES per GPU that loads the library, held until
+// the process exits.
+#include <mutex>
+
+namespace yabt {
+
+constexpr long long BIN_FIT_STATIC_BYTES = 8LL << 20;   // 8 MiB per device
+static __device__ __align__(256) unsigned char g_bin_fit_scratch[BIN_FIT_STATIC_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+static std::mutex g_static_mu;
+static void* g_static_ptr[MAX_DEVICES] = {};
+
+// Device address of the scratch array on the current device, looked up once per
+// device (host code must not pass the symbol itself: in host code its name is
+// only a stand-in, not a device address).
+static int bin_fit_scratch_ptr(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) { set_error("yabt_bin_fit_static: cudaGetDevice: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  if (dev < 0 || dev >= MAX_DEVICES) { set_error("yabt_bin_fit_static: device %d out of range", dev); return YABT_ERR_ARG; }
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_bin_fit_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("yabt_bin_fit_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return YABT_ERR_CUDA;
+    }
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return YABT_OK;
+}
+
+}  // namespace yabt
+
+extern "C" {
+
+long long yabt_bin_fit_static_capacity(void) { return BIN_FIT_STATIC_BYTES; }
+
+int yabt_bin_fit_static(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
+                        int max_bins, float* medians, float* edges, int32_t* edge_cnt, float* scales,
+                        void* stream) {
+  if (!Xfm || n <= 0 || F <= 0 || nq <= 0) { set_error("yabt_bin_fit_static: bad arguments"); return YABT_ERR_ARG; }
+  const long long need = yabt_bin_fit_workspace_bytes(n, F, nq);
+  if (need > BIN_FIT_STATIC_BYTES) {
+    set_error("yabt_bin_fit_static: this fit needs %lld bytes of scratch but the static buffer holds %lld "
+              "(F=%d, sample rows=%lld); use yabt_bin_fit with a caller workspace",
+              need, BIN_FIT_STATIC_BYTES, F, nq);
+    return YABT_ERR_UNSUPPORTED;
+  }
+  void* ws = nullptr;
+  int rc = bin_fit_scratch_ptr(&ws);
+  if (rc) return rc;
+  // yabt_bin_fit clears every scratch region it accumulates into before use
+  // (NaN counts, digit histograms) and fully writes the rest, so the contents
+  // left by an earlier call do not matter.
+  return yabt_bin_fit(Xfm, n, F, sample_idx, nq, max_bins, ws, BIN_FIT_STATIC_BYTES, medians, edges,
+                      edge_cnt, scales, stream);
+}
+
+}  // extern "C"
