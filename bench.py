@@ -215,8 +215,6 @@ def run_ours(args):
             ev["start"] = torch.cuda.Event(enable_timing=True)
             ev["start"].record()
             marks["launches0"] = int(lib.yabt_launch_count())
-            if sampler:
-                sampler.start()
         if t == W + K - 1:
             ev["stop"] = torch.cuda.Event(enable_timing=True)
             ev["stop"].record()
@@ -227,6 +225,8 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     booster = Booster(params, loss)
+    if sampler:
+        sampler.start()     # nvidia-smi needs ~0.1 s to start: begin before the warm-up trees
     booster.fit(None, y_host, data=data, tree_callback=cb)
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
@@ -271,7 +271,8 @@ def run_ours(args):
         dt = time.perf_counter() - t0
         e2e = {"value": K / dt, "unit": "trees/s",
                "h2d_bytes_per_step": int((Xh.numel() * 4 + y_host.nbytes) / K),
-               "d2h_bytes_per_step": int(K * 4 * 4 / K + 4)}
+               # fit reads back each tree's meta row (4 int32) and leaf-model flag (int32)
+               "d2h_bytes_per_step": 4 * 4 + 4}
         del Xh, est
 
     cpu = None
@@ -322,7 +323,12 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=500_000)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the configuration's row count (small cases for profiling)")
     args = ap.parse_args()
+    if args.rows > 0:
+        n, *rest = CONFIGS[args.config]
+        CONFIGS[args.config] = (args.rows, *rest)
     if args.warmup < 1:
         args.warmup = 1
     if args.impl == "reference":

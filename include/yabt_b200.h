@@ -37,8 +37,12 @@ int yabt_last_error(char* buf, int len);
 long long yabt_launch_count(void);
 
 /* ------------------------------------------------------------------ bin matrix
- * The tiled bin-matrix layout (see DESIGN.md "Data layout"): size in bytes for
- * n rows x F features, and the byte address of (row, feature).            */
+ * The tiled bin-matrix layout: features in column tiles (64-wide tiles, then
+ * a 32-wide tile if >= 32 features remain, then a 16- or 32-wide padded
+ * tile), each tile an (n x width) row-major uint8 block starting on a 256-byte
+ * boundary; in a 64-wide tile byte 2j+k of a row holds feature f0+j+32k.
+ * Size in bytes for n rows x F features, and the address of a feature: tile
+ * block offset, tile row width and byte position within the tile row.     */
 long long yabt_bin_matrix_bytes(long long n, int F);
 int yabt_bin_address(long long n, int F, int feature, long long* tile_off, int* width, int* pos);
 
@@ -46,6 +50,23 @@ int yabt_bin_address(long long n, int F, int feature, long long* tile_off, int* 
  * Replaces the layout contract of yabt/cuda_hist.py:79-89 (row-major (n, F)
  * uint8 input) for callers that hold plain bin matrices.                  */
 int yabt_pack_bins(const uint8_t* plain, long long n, int F, uint8_t* tiled, void* stream);
+
+/* ------------------------------------------------------------------ histogram FFI
+ * Replaces the reference's fused histogram build, build_hist
+ * (yabt/cuda_hist.py:79-89 -> hist_build in yabt/_cuda/hist.cu:105-133):
+ * row i of the plain row-major (n, F) uint8 matrix `binned` adds
+ * (g[i], h[i], w[i]) into bin binned[i, f] of node slot slot[i] (int64, in
+ * [0, K)) for every feature f; `out` is the (3, K, F, B) float32 histogram
+ * (channels g, h, w). Sums are exact fixed-point integers rounded once to
+ * float32, so the result is deterministic. Rows with a slot outside [0, K) or
+ * a bin >= B are skipped, and non-finite g/h/w values are rejected: each sets
+ * a bit in the device word *err_out (0 = clean; may be NULL). No host
+ * synchronisation; the workspace (yabt_hist_build_workspace_bytes) is
+ * caller-owned.                                                            */
+long long yabt_hist_build_workspace_bytes(long long n, int K, int F);
+int yabt_hist_build(const uint8_t* binned, const int64_t* slot, const float* g, const float* h,
+                    const float* w, long long n, int K, int F, int B, float* out, int32_t* err_out,
+                    void* workspace, long long ws_bytes, void* stream);
 
 /* ------------------------------------------------------------------ grower
  * Level-wise tree grower. Replaces grow_tree_levelwise

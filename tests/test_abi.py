@@ -1,0 +1,109 @@
+"""The C ABI boundary on the CPU: the shared library loads without a GPU,
+exports every function ``include/yabt_b200.h`` declares, the ctypes table in
+``yabt_b200/_lib.py`` binds each one with the declared number of arguments, and
+the host-only layout functions agree with an independent restatement of the
+tiled bin-matrix layout. No compute entry point is called here."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "yabt_b200.h")
+
+
+def _declarations():
+    """(name, n_params) of every function declared in the header."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", " ", text)
+    out = {}
+    for m in re.finditer(r"\b(yabt_[A-Za-z0-9_]+)\s*\(([^;{)]*)\)\s*;", text):
+        name, params = m.group(1), m.group(2).strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        out[name] = n
+    return out
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from yabt_b200 import _lib, build
+    if not os.path.exists(_lib.LIB_PATH) or not build.up_to_date():
+        build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_path():
+    decl = _declarations()
+    for name in ("yabt_bin_fit", "yabt_bin_transform", "yabt_grow_tree", "yabt_grow_hist",
+                 "yabt_grow_split", "yabt_leafnet_fit", "yabt_update_margin", "yabt_predict_forest",
+                 "yabt_hist_build"):
+        assert name in decl, name
+    assert len(decl) >= 40
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [name for name in _declarations() if not hasattr(lib, name)]
+    assert not missing, f"declared in the header but not exported: {missing}"
+
+
+def test_ctypes_table_matches_header(lib):
+    from yabt_b200 import _lib
+    decl = _declarations()
+    table = {name: args for name, _res, args in _lib.SIGNATURES}
+    assert set(table) == set(decl), (set(decl) ^ set(table))
+    for name, n in decl.items():
+        assert len(table[name]) == n, f"{name}: header has {n} parameters, ctypes table {len(table[name])}"
+
+
+def test_host_only_queries(lib):
+    assert lib.yabt_version() > 0
+    assert lib.yabt_bin_fit_static_capacity() == 8 << 20
+    # workspace queries are pure arithmetic
+    assert lib.yabt_bin_fit_workspace_bytes(200_000, 200, 200_000) > lib.yabt_bin_fit_static_capacity()
+    assert lib.yabt_leafnet_workspace_bytes(10_000, 8, 511) > 0
+    assert lib.yabt_hist_build_workspace_bytes(20_000, 31, 24) >= 3 * 31 * 24 * 256 * 8 + 20_000 * 4
+    assert lib.yabt_hist_build_workspace_bytes(10, 0, 4) < 0
+    buf = ctypes.create_string_buffer(64)
+    assert lib.yabt_last_error(buf, 64) >= 0
+
+
+def _expected_layout(n, F):
+    """Independent restatement of the tiled layout: 64-feature tiles (lane j of
+    a warp reads bytes 2j, 2j+1 = features j and j+32), then one 32-wide tile if
+    at least 32 features remain, then a 16- or 32-wide padded tile; every tile
+    block starts on a 256-byte boundary."""
+    def blk(w):
+        return (n * w + 255) // 256 * 256
+    addr, off, f = {}, 0, 0
+    while F - f >= 64:
+        for i in range(64):
+            addr[f + i] = (off, 64, 2 * (i % 32) + i // 32)
+        off += blk(64)
+        f += 64
+    if F - f >= 32:
+        for i in range(32):
+            addr[f + i] = (off, 32, i)
+        off += blk(32)
+        f += 32
+    r = F - f
+    if r:
+        w = 32 if r > 16 else 16
+        for i in range(r):
+            addr[f + i] = (off, w, i)
+        off += blk(w)
+    return addr, off
+
+
+@pytest.mark.parametrize("n,F", [(1, 1), (1000, 7), (4097, 16), (333, 17), (10_000, 48),
+                                 (100, 64), (12345, 100), (10_000_000, 200), (5, 255)])
+def test_tiled_layout_addresses(lib, n, F):
+    from yabt_b200 import _lib
+    addr, total = _expected_layout(n, F)
+    assert lib.yabt_bin_matrix_bytes(n, F) == total
+    off, width, pos = _lib.c_ll(), ctypes.c_int(), ctypes.c_int()
+    for f in range(F):
+        assert lib.yabt_bin_address(n, F, f, ctypes.byref(off), ctypes.byref(width), ctypes.byref(pos)) == 0
+        assert (off.value, width.value, pos.value) == addr[f], f

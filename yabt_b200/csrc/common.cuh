@@ -4,8 +4,8 @@
 // -------------------------------------------
 // * Bin matrix ("tiled layout"): features are grouped into column tiles. A
 //   full tile holds 64 features; the remainder of F mod 64 becomes a 32-wide
-//   tile (if >= 32 features remain) and then a narrow tile of width
-//   roundup(r, 4). Each tile is its own (n x width) row-major uint8 block, the
+//   tile (if >= 32 features remain) and then a tile of width 32 (more than
+//   16 features left) or 16, padded. Each tile is its own (n x width) row-major uint8 block, the
 //   blocks stored one after another (each starting on a 256-byte boundary).
 //   Within a 64-wide tile, byte 2*j + k of a row holds feature f0 + j + 32*k,
 //   so lane j of a warp loads one u16 and receives features j and j+32: the
@@ -45,6 +45,7 @@ enum : unsigned {
   DERR_TILE_OVERFLOW = 1u << 3,
   DERR_BAD_INDEX = 1u << 4,
   DERR_NODE_OVERFLOW = 1u << 5,
+  DERR_NONFINITE = 1u << 6,
 };
 
 void set_error(const char* fmt, ...);
