@@ -45,6 +45,16 @@ CONFIGS = {
 }
 
 
+def workload_config(cfg: str, world: int) -> dict:
+    """The ``config`` object of the JSON line (both arms)."""
+    n, F, leaves, depth, loss, lr = CONFIGS[cfg]
+    return {"workload": f"{cfg}: {n}x{F} sharded by rows over {world} GPU(s), {leaves} leaves, "
+                        f"max_depth {depth}, {loss}, neural leaves, interaction steering",
+            "global_rows": n, "rows_per_gpu": n // world,
+            "l2": "inputs larger than L2 (bin matrix of C4: 2.08 GB)" if n * F > 10 ** 9 else "see workload",
+            "parallelism": f"row shards x{world}, NCCL all-reduce of level histograms"}
+
+
 def make_data(cfg: str, n: int, F: int, device, seed: int = 0):
     """Seeded synthetic data with the configuration's shapes and distributions
     (generated on the device with torch's Philox generator)."""
@@ -82,7 +92,7 @@ def make_data(cfg: str, n: int, F: int, device, seed: int = 0):
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -99,7 +109,9 @@ class ClockSampler:
         except Exception:
             self.p = None
 
-    def stop(self) -> dict:
+    def stop(self, window: tuple[float, float] | None = None) -> dict:
+        """Summary of the samples taken inside ``window`` (wall-clock seconds;
+        all samples if none falls inside it)."""
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -108,16 +120,30 @@ class ClockSampler:
         except Exception:
             self.p.kill()
         self.f.flush()
-        rows = [ln.split(",") for ln in open(self.f.name).read().strip().splitlines() if ln.strip()]
+        rows = [[c.strip() for c in ln.split(",")] for ln in open(self.f.name).read().strip().splitlines()
+                if ln.strip()]
         os.unlink(self.f.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        rows = [r for r in rows if len(r) >= 10 and r[2].replace(".", "").isdigit()]
+
+        def stamp(r):
+            try:
+                return time.mktime(time.strptime(r[0].split(".")[0], "%Y/%m/%d %H:%M:%S")) + \
+                    float("0." + r[0].split(".")[1]) if "." in r[0] else 0.0
+            except Exception:
+                return None
+        inside = rows
+        if window is not None:
+            sel = [r for r in rows if (t := stamp(r)) is not None and window[0] - 0.05 <= t <= window[1] + 0.05]
+            if sel:
+                inside = sel
+        sm = [float(r[2]) for r in inside]
+        mx = [float(r[3]) for r in inside if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
-                          if r[5 + i].strip().lower() == "active"})
+        reasons = sorted({names[i] for r in inside for i in range(4) if r[6 + i].lower() == "active"})
         load = [v for v in sm if v > 500] or sm
         return {"sm_mhz": statistics.median(load) if load else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(inside),
+                "in_timed_region": len(inside) if inside is not rows else 0}
 
 
 def cpu_reference(cfg: str, steps: int, warmup: int, threads: int, sample_rows: int, X_src=None, y_src=None):
@@ -167,10 +193,9 @@ def run_reference(args):
     tps, per, desc = cpu_reference(cfg, args.steps, args.warmup, threads, sample, X, y)
     line = {"impl": "reference", "metric": "trees_per_sec", "value": tps, "unit": "trees/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{cfg}: {n}x{F}, {leaves} leaves, max_depth {depth}, {loss}, "
-                                   "neural leaves, interaction steering"},
+            "config": workload_config(cfg, args.gpus),
             "cpu_baseline": {"value": tps, "unit": "trees/s", "cores": threads, "kind": "reference",
                              "sample": desc},
             "e2e": {"value": tps, "unit": "trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -188,17 +213,33 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # clock sampling runs from here (nvidia-smi takes a moment to start); the
+    # summary keeps the samples that fall inside the timed region
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    comm = None
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        from yabt_b200.distributed import ShardComm
+        comm = ShardComm()
     cfg = args.config
     n, F, leaves, depth, loss_name, lr = CONFIGS[cfg]
-    n_local = n  # weak scaling: every rank grows the full per-GPU workload
+    # strong scaling: the configuration's n rows are sharded across the ranks in
+    # contiguous blocks (the same data set, and so the same model, for every N)
+    bounds = [n * r // world for r in range(world + 1)]
+    lo, hi = bounds[rank], bounds[rank + 1]
+    n_local = hi - lo
     lib = _lib.load()
-    X, y = make_data(cfg, n_local, F, dev, seed=1000 + rank)
+    X, y = make_data(cfg, n, F, dev, seed=1000)
+    if world > 1:
+        X, y = X[lo:hi].clone(), y[lo:hi].clone()
+        torch.cuda.empty_cache()
     loss = MSELoss() if loss_name == "mse" else LogLoss()
     W, K = args.warmup, args.steps
     params = BoostParams(n_estimators=W + K, max_leaves=leaves, max_depth=depth, learning_rate=lr)
-    data = DeviceData(X, params.max_bins, dev)
+    data = DeviceData(X, params.max_bins, dev, comm=comm)
     y_host = y.cpu().numpy()
     del X
     torch.cuda.synchronize()
@@ -215,21 +256,19 @@ def run_ours(args):
             ev["start"] = torch.cuda.Event(enable_timing=True)
             ev["start"].record()
             marks["launches0"] = int(lib.yabt_launch_count())
+            marks["t0"] = time.time()
         if t == W + K - 1:
             ev["stop"] = torch.cuda.Event(enable_timing=True)
             ev["stop"].record()
             marks["launches1"] = int(lib.yabt_launch_count())
 
-    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     booster = Booster(params, loss)
-    if sampler:
-        sampler.start()     # nvidia-smi needs ~0.1 s to start: begin before the warm-up trees
-    booster.fit(None, y_host, data=data, tree_callback=cb)
+    booster.fit(None, y_host, data=data, tree_callback=cb, comm=comm)
     torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop((marks["t0"], time.time())) if sampler else None
     ms = ev["start"].elapsed_time(ev["stop"])
     hist_ms = booster.grower_.hist_times()
     root_rows, child_rows, hist_launches = booster.grower_.acc_read()
@@ -237,7 +276,7 @@ def run_ours(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    trees_per_s = world * K / (ms / 1000.0)
+    trees_per_s = K / (ms / 1000.0)
 
     # Roofline of the histogram kernel (k_hist): algorithmic bytes of the timed
     # trees = rows histogrammed x (F bin bytes + 4 B gradient [+ 4 B hessian]
@@ -254,23 +293,35 @@ def run_ours(args):
     except Exception:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    bin_reads_per_s = world * (root_rows + child_rows) * F / (ms / 1000.0)
+    rows_hist = torch.tensor([float(root_rows + child_rows)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(rows_hist)
+    bin_reads_per_s = float(rows_hist.item()) * F / (ms / 1000.0)
 
-    # e2e through the public estimator API from host memory (rank 0 fits alone)
+    # e2e through the public estimator API from host memory (every rank fits
+    # its host shard; the slowest rank's wall time counts)
     e2e = None
-    if rank == 0 and not args.no_e2e:
+    if not args.no_e2e:
         from yabt_b200 import YABTRegressor, YABTClassifier
-        Xh = make_data(cfg, n_local, F, dev, seed=1000 + rank)[0].cpu().pin_memory()
+        del data, booster
+        torch.cuda.empty_cache()
+        Xh = make_data(cfg, n, F, dev, seed=1000)[0][lo:hi].cpu().pin_memory()
         est_cls = YABTRegressor if loss_name == "mse" else YABTClassifier
         kw = dict(max_leaves=leaves, max_depth=depth, learning_rate=lr)
         est_cls(n_estimators=1, **kw).fit(Xh[:4096], y_host[:4096])   # warm-up (context, library)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
-        est = est_cls(n_estimators=K, **kw).fit(Xh, y_host)
+        est = est_cls(n_estimators=K, **kw).fit(Xh, y_host, comm=comm)
         torch.cuda.synchronize()
         dt = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([dt], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
         e2e = {"value": K / dt, "unit": "trees/s",
-               "h2d_bytes_per_step": int((Xh.numel() * 4 + y_host.nbytes) / K),
+               "h2d_bytes_per_step": int(n * (F + 1) * 4 / K),   # X and y of every rank, once per fit
                # fit reads back each tree's meta row (4 int32) and leaf-model flag (int32)
                "d2h_bytes_per_step": 4 * 4 + 4}
         del Xh, est
@@ -289,12 +340,9 @@ def run_ours(args):
     if rank == 0:
         line = {
             "metric": "trees_per_sec", "value": trees_per_s, "unit": "trees/s", "n_gpus": world,
-            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch Philox, config shapes)",
-            "config": {"workload": f"{cfg}: {n_local}x{F} per GPU, {leaves} leaves, max_depth {depth}, "
-                                   f"{loss_name}, neural leaves, interaction steering",
-                       "global_rows": n_local * world, "l2": "inputs larger than L2 (bin matrix "
-                       f"{data.bins.numel() / 1e9:.2f} GB)", "parallelism": f"rows x{world}"},
+            "config": workload_config(cfg, world),
             "bin_reads_per_sec": bin_reads_per_s,
             "gpu_launches": marks.get("launches1", 0) - marks.get("launches0", 0),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -316,7 +364,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))

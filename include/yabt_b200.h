@@ -140,6 +140,12 @@ int yabt_grow_hist(yabt_grower* g, const yabt_tree_args* a, int level, void* str
 int yabt_grow_split(yabt_grower* g, const yabt_tree_args* a, int level, void* stream);
 int yabt_grow_end(yabt_grower* g, const yabt_tree_args* a, void* stream);
 void* yabt_grow_amax_ptr(yabt_grower* g);
+/* Device address of four int32 words of the level state: level, active,
+ * active node count, pairs split by the last yabt_grow_split. After
+ * yabt_grow_split(level d) the pairs count is the number of jobs of level d+1
+ * (the small-child histograms to reduce are then pairs * small_count(0)
+ * int64 values), and active = 0 means the tree is complete.              */
+void* yabt_grow_level_ptr(yabt_grower* g);
 void* yabt_grow_small_ptr(yabt_grower* g);
 long long yabt_grow_small_count(const yabt_grower* g, int level);
 /* Per-leaf row ranges of the last tree (device arrays inside the workspace):
@@ -161,6 +167,24 @@ long long yabt_bin_fit_workspace_bytes(long long n, int F, long long nq);
 int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
                  int max_bins, void* workspace, long long ws_bytes, float* medians, float* edges,
                  int32_t* edge_cnt, float* scales, void* stream);
+/* yabt_bin_fit in steps, for a fit over rows sharded across GPUs
+ * (yabt/binning.py:29-69 on the concatenation of every rank's rows). The
+ * medians are a 3-pass radix selection: for pass = 0, 1, 2 each rank calls
+ * yabt_bin_median_hist on its rows, the caller sums the digit histogram
+ * (hist_words uint32 counts) and, after pass 0, the per-feature NaN counts
+ * (F uint64) over the ranks in place (yabt_bin_median_bufs gives both
+ * addresses), then every rank calls yabt_bin_median_pick with the total row
+ * count; yabt_bin_median_final writes the medians. The workspace is sized by
+ * yabt_bin_fit_workspace_bytes(n_local, F, 1). yabt_bin_fit_edges fits the
+ * edges and scales on a gathered (F, nq) feature-major sample matrix
+ * (workspace yabt_bin_fit_workspace_bytes(nq, F, nq)).                    */
+int yabt_bin_median_hist(const float* Xfm, long long n, int F, int pass, void* workspace, long long ws_bytes,
+                         void* stream);
+int yabt_bin_median_pick(long long n_total, int F, int pass, void* workspace, long long ws_bytes, void* stream);
+int yabt_bin_median_final(int F, void* workspace, long long ws_bytes, float* medians, void* stream);
+int yabt_bin_median_bufs(int F, void* workspace, void** hist, long long* hist_words, void** nan_count);
+int yabt_bin_fit_edges(const float* Xs, long long nq, int F, int max_bins, void* workspace, long long ws_bytes,
+                       float* edges, int32_t* edge_cnt, float* scales, void* stream);
 /* Allocation-free variant of yabt_bin_fit (no counterpart in the reference).
  * For callers that cannot allocate device memory when they fit -- e.g. a
  * process whose GPU memory is reserved up front by another framework's caching
@@ -223,6 +247,17 @@ typedef struct {
 
 long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes);
 int yabt_leafnet_fit(const yabt_leafnet_args* a, void* workspace, long long ws_bytes, void* stream);
+/* yabt_leafnet_fit in four stages for rows sharded across GPUs
+ * (fit_leaf_networks over every rank's rows). Between the stages the caller
+ * reduces over the ranks, in place:
+ *   after stage 0: sum of corr[0..F] (float64; X^T g and sum g);
+ *   after stage 1: sum of counts[0..max_nodes) (int32 leaf row counts);
+ *   after stage 2: sum of totals[0..max_nodes * per_node) (float64 normal
+ *                  equations), min of lo and max of hi (the envelopes).
+ * Stage 3 solves and folds. yabt_leafnet_bufs gives the three addresses.  */
+int yabt_leafnet_stage(const yabt_leafnet_args* a, int stage, void* workspace, long long ws_bytes, void* stream);
+int yabt_leafnet_bufs(const yabt_leafnet_args* a, void* workspace, long long ws_bytes, void** corr, void** counts,
+                      void** totals, int* per_node);
 
 /* Margin update of one tree and the next tree's gradients
  * (yabt/boosting.py:36-38,53-54,511-514; Tree.net_contribution yabt/tree.py:118-128). */
@@ -250,6 +285,12 @@ int yabt_grad_init(const float* margin, const float* y, long long n, int loss, f
                    void* stream);
 /* Column means and unbiased stds of Xfm (fp64 accumulation). */
 int yabt_column_stats(const float* Xfm, long long n, int F, float* mean, float* std, void* stream);
+/* The same moments over rows sharded across GPUs: pass 0 writes acc[f] = sum x
+ * of this rank's rows; once acc[0..F) holds the sum over all ranks, pass 1
+ * writes acc[F+f] = sum (x - mean)^2; once that is summed too,
+ * yabt_column_finish writes mean and std. acc is [2F] float64.          */
+int yabt_column_sums(const float* Xfm, long long n, long long n_total, int F, int pass, double* acc, void* stream);
+int yabt_column_finish(const double* acc, long long n_total, int F, float* mean, float* std, void* stream);
 
 /* ------------------------------------------------------------------ interaction steering
  * FeatureInteractionDetector.update_from_path_pairs / normalized_matrix

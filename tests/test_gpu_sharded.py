@@ -1,0 +1,137 @@
+"""GPU parity of the row-sharded fit: ranks that each hold a block of the
+rows (contiguous blocks in rank order) must end with the model a single-GPU
+fit builds on the concatenated rows.
+
+Two ranks run as two processes on GPU 0 over gloo (the collectives are staged
+through host memory and no kernel waits on another process), so the test needs
+one GPU; with two or more GPUs the same check also runs over NCCL, one rank
+per GPU. Binning (medians, edges, scales) and, without leaf models, every tree
+are bit-identical; with leaf models the float64 normal equations are summed in
+a different order, so leaf values and predictions are compared within 1e-5 /
+1e-4 relative, the first tree's structure exactly."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+N, F = 8192, 10          # a power of two: the mean of dyadic targets is exact either way
+SPLIT = (5000, 3192)
+
+
+def _data():
+    rng = np.random.default_rng(7)
+    X = rng.normal(size=(N, F)).astype(np.float32)
+    X[:, 3] = np.exp(X[:, 3])
+    X[rng.random(size=X.shape) < 0.02] = np.nan
+    z = np.nan_to_num(X)
+    y = np.sin(z[:, 0]) + z[:, 1] * z[:, 2] + 0.5 * z[:, 4] + 0.1 * rng.normal(size=N)
+    y = (np.round(np.clip(y, -7, 7) * 4) / 4).astype(np.float32)   # dyadic: the mean is exact in float32
+    return X, y
+
+
+def _params(neural: bool):
+    from yabt_b200.boosting import BoostParams
+    return BoostParams(n_estimators=4, max_leaves=15, max_depth=5, learning_rate=0.3, neural_leaves=neural,
+                       leaf_net_min_samples=50, min_samples_leaf=20)
+
+
+def _summary(b, Xt):
+    med, edges, ecnt, scales = b.binner._dev
+    trees = [dict(feature=t.feature.cpu().numpy(), threshold=t.threshold.cpu().numpy(),
+                  left=t.left.cpu().numpy(), right=t.right.cpu().numpy(), value=t.value.cpu().numpy())
+             for t in b.trees]
+    return dict(med=med.cpu().numpy(), edges=edges.cpu().numpy(), ecnt=ecnt.cpu().numpy(),
+                scales=scales.cpu().numpy(), trees=trees, pred=b.predict_margin(Xt))
+
+
+def _worker(rank, world, port, backend, neural, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = rank if backend == "nccl" else 0
+    torch.cuda.set_device(dev)
+    kw = dict(device_id=torch.device("cuda", dev)) if backend == "nccl" else {}
+    dist.init_process_group(backend, rank=rank, world_size=world, **kw)
+    try:
+        from yabt_b200.boosting import Booster, MSELoss
+        from yabt_b200.distributed import ShardComm
+        X, y = _data()
+        off = sum(SPLIT[:rank])
+        sl = slice(off, off + SPLIT[rank])
+        b = Booster(_params(neural), MSELoss())
+        b.fit(X[sl], y[sl], comm=ShardComm())
+        torch.cuda.synchronize()
+        q.put((rank, _summary(b, X[:1500])))
+    except Exception as e:          # report instead of hanging the parent
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_sharded(backend, neural):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert isinstance(res[r], dict), res[r]
+    return res
+
+
+def _single(neural):
+    from yabt_b200.boosting import Booster, MSELoss
+    X, y = _data()
+    b = Booster(_params(neural), MSELoss())
+    b.fit(X, y)
+    return _summary(b, X[:1500])
+
+
+def _compare(res, ref, neural):
+    for r in (0, 1):
+        got = res[r]
+        np.testing.assert_array_equal(got["med"], ref["med"])
+        np.testing.assert_array_equal(got["ecnt"], ref["ecnt"])
+        for f in range(F):
+            c = ref["ecnt"][f]
+            np.testing.assert_array_equal(got["edges"][f, :c], ref["edges"][f, :c])
+        np.testing.assert_array_equal(got["scales"], ref["scales"])
+        assert len(got["trees"]) == len(ref["trees"])
+        for t, (a, b) in enumerate(zip(got["trees"], ref["trees"])):
+            if neural and t > 0:
+                continue
+            for k in ("feature", "threshold", "left", "right"):
+                np.testing.assert_array_equal(a[k], b[k], err_msg=f"tree {t} {k}")
+            if neural:
+                np.testing.assert_allclose(a["value"], b["value"], rtol=1e-5, atol=1e-6)
+            else:
+                np.testing.assert_array_equal(a["value"], b["value"], err_msg=f"tree {t} value")
+        if neural:
+            np.testing.assert_allclose(got["pred"], ref["pred"], rtol=1e-4, atol=1e-4)
+        else:
+            np.testing.assert_array_equal(got["pred"], ref["pred"])
+    # both ranks hold the same model
+    np.testing.assert_array_equal(res[0]["pred"], res[1]["pred"])
+
+
+@pytest.mark.parametrize("neural", [False, True])
+def test_two_ranks_one_gpu_gloo(neural):
+    _compare(_run_sharded("gloo", neural), _single(neural), neural)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_nccl():
+    _compare(_run_sharded("nccl", True), _single(True), True)

@@ -86,6 +86,7 @@ SIGNATURES = [
     ("yabt_grow_end", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
     ("yabt_grow_amax_ptr", c_vp, [c_vp]),
     ("yabt_grow_small_ptr", c_vp, [c_vp]),
+    ("yabt_grow_level_ptr", c_vp, [c_vp]),
     ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
     ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
     ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
@@ -96,12 +97,22 @@ SIGNATURES = [
     ("yabt_bin_fit", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_bin_fit_static_capacity", c_ll, []),
     ("yabt_bin_fit_static", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    ("yabt_bin_median_hist", c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_ll, c_vp]),
+    ("yabt_bin_median_pick", c_int, [c_ll, c_int, c_int, c_vp, c_ll, c_vp]),
+    ("yabt_bin_median_final", c_int, [c_int, c_vp, c_ll, c_vp, c_vp]),
+    ("yabt_bin_median_bufs", c_int, [c_int, c_vp, ctypes.POINTER(c_vp), ctypes.POINTER(c_ll), ctypes.POINTER(c_vp)]),
+    ("yabt_bin_fit_edges", c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_bin_transform", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_leafnet_workspace_bytes", c_ll, [c_ll, c_int, c_int]),
     ("yabt_leafnet_fit", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, c_vp]),
+    ("yabt_leafnet_stage", c_int, [ctypes.POINTER(LeafNetArgs), c_int, c_vp, c_ll, c_vp]),
+    ("yabt_leafnet_bufs", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp),
+                                  ctypes.POINTER(c_vp), ctypes.POINTER(c_int)]),
     ("yabt_update_margin", c_int, [ctypes.POINTER(UpdateArgs), c_vp]),
     ("yabt_grad_init", c_int, [c_vp, c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),
     ("yabt_column_stats", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),
+    ("yabt_column_sums", c_int, [c_vp, c_ll, c_ll, c_int, c_int, c_vp, c_vp]),
+    ("yabt_column_finish", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),
     ("yabt_interaction_update", c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("yabt_interaction_normalize", c_int, [c_vp, c_int, c_vp, c_vp]),
     ("yabt_predict_forest", c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

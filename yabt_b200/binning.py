@@ -74,6 +74,17 @@ class Binner:
         _lib.check(lib.yabt_bin_fit(Xfm.data_ptr(), n, F, idx.data_ptr() if idx is not None else None, nq,
                                     self.max_bins, ws.data_ptr(), ws.numel(), med.data_ptr(),
                                     edges.data_ptr(), ecnt.data_ptr(), scales.data_ptr(), s), "yabt_bin_fit")
+        return self._set_state(med, edges, ecnt, scales)
+
+    def fit_device_sharded(self, Xfm: torch.Tensor, n: int, comm) -> "Binner":
+        """Fit over the rows of every rank of ``comm`` (a ``ShardComm``): this
+        rank holds the feature-major (F, n) block of its rows. The result equals
+        a fit on the concatenation of every rank's rows."""
+        from .distributed import fit_binner
+        return self._set_state(*fit_binner(Xfm, n, self.max_bins, comm))
+
+    def _set_state(self, med, edges, ecnt, scales) -> "Binner":
+        F = med.shape[0]
         self._dev = (med, edges, ecnt, scales)
         # host views of the fitted state (the reference's attribute layout)
         med_h = med.cpu().numpy()

@@ -42,6 +42,11 @@ class LogLoss:
         return float(np.log(p / (1 - p)))
 
     @staticmethod
+    def base_from_mean(m: float) -> float:
+        p = float(np.clip(np.float32(m), np.float32(1e-6), np.float32(1 - 1e-6)))
+        return float(np.log(p / (1 - p)))
+
+    @staticmethod
     def grad_hess(margin: torch.Tensor, y: torch.Tensor):
         p = torch.sigmoid(margin)
         return p - y, (p * (1 - p)).clamp_min(1e-6)
@@ -59,6 +64,10 @@ class MSELoss:
     @staticmethod
     def base_score(y: torch.Tensor) -> float:
         return float(y.mean())
+
+    @staticmethod
+    def base_from_mean(m: float) -> float:
+        return float(np.float32(m))
 
     @staticmethod
     def grad_hess(margin: torch.Tensor, y: torch.Tensor):
@@ -157,7 +166,9 @@ class DeviceData:
     imputed feature-major features and their column moments. Shared by the
     one-vs-rest boosters of a multiclass fit."""
 
-    def __init__(self, X, max_bins: int, device: torch.device):
+    def __init__(self, X, max_bins: int, device: torch.device, comm=None):
+        """``comm`` (a ``distributed.ShardComm``): X holds this rank's rows of a
+        row-sharded training set; binning and column moments cover every rank."""
         lib = _lib.load()
         Xd = to_device_f32(X, device)
         self.n, self.F = int(Xd.shape[0]), int(Xd.shape[1])
@@ -166,12 +177,20 @@ class DeviceData:
         _lib.check(lib.yabt_transpose(Xd.data_ptr(), n, F, self.Xfm.data_ptr(), _lib.stream_ptr()),
                    "yabt_transpose")
         del Xd
-        self.binner = Binner(max_bins).fit_device(self.Xfm, n)
+        self.comm = comm
+        if comm is None:
+            self.binner = Binner(max_bins).fit_device(self.Xfm, n)
+        else:
+            self.binner = Binner(max_bins).fit_device_sharded(self.Xfm, n, comm)
         self.bins, _ = self.binner.transform_device(self.Xfm, n)   # imputes Xfm in place
-        self.col_mean = torch.empty(F, dtype=torch.float32, device=device)
-        self.col_std = torch.empty(F, dtype=torch.float32, device=device)
-        _lib.check(lib.yabt_column_stats(self.Xfm.data_ptr(), n, F, self.col_mean.data_ptr(),
-                                         self.col_std.data_ptr(), _lib.stream_ptr()), "yabt_column_stats")
+        if comm is None:
+            self.col_mean = torch.empty(F, dtype=torch.float32, device=device)
+            self.col_std = torch.empty(F, dtype=torch.float32, device=device)
+            _lib.check(lib.yabt_column_stats(self.Xfm.data_ptr(), n, F, self.col_mean.data_ptr(),
+                                             self.col_std.data_ptr(), _lib.stream_ptr()), "yabt_column_stats")
+        else:
+            from .distributed import column_stats
+            self.col_mean, self.col_std = column_stats(self.Xfm, n, comm)
         med, edges, ecnt, scales = self.binner._dev
         self.edges = edges                      # [F][255]
         self.edge_off = (torch.arange(F, dtype=torch.int32, device=device) * 255).contiguous()
@@ -216,30 +235,43 @@ class Booster:
         self._packed = None
 
     # ------------------------------------------------------------------ fit
-    def fit(self, X, y, eval_set=None, data: DeviceData | None = None, tree_callback=None) -> "Booster":
+    def fit(self, X, y, eval_set=None, data: DeviceData | None = None, tree_callback=None,
+            comm=None) -> "Booster":
         """yabt/boosting.py:271-534. ``tree_callback(t, grower)``, if given, is
-        called after the launches of tree t are queued (no synchronisation)."""
+        called after the launches of tree t are queued (no synchronisation).
+
+        ``comm`` (a ``distributed.ShardComm``): X and y hold this rank's rows of
+        a row-sharded training set; every rank must call ``fit`` with the same
+        parameters and ends with the same model."""
         p = self.p
         _check_supported(p)
+        if comm is not None and (eval_set is not None or p.min_split_gain_rel > 0.0):
+            raise NotImplementedError("row-sharded fits support neither eval_set nor min_split_gain_rel")
         dev = torch.device(p.resolve_device())
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
         self.device_ = str(dev)
         if data is None:
-            data = DeviceData(X, p.max_bins, dev)
+            data = DeviceData(X, p.max_bins, dev, comm=comm)
+        elif comm is not None and data.comm is None:
+            raise ValueError("a row-sharded fit needs DeviceData built with the same comm")
         self.binner = data.binner
         n, F = data.n, data.F
+        n_total = n if comm is None else sum(comm.int_values(n))
         lib = _lib.load()
         s = _lib.stream_ptr()
         yt = torch.as_tensor(np.asarray(y, dtype=np.float32)).to(dev)
         general = self.loss.kind != 0
         gen = torch.Generator(device="cpu").manual_seed(p.seed)
 
-        use_ia = p.interaction_aware and n >= _INTERACTION_MIN_ROWS
+        use_ia = p.interaction_aware and n_total >= _INTERACTION_MIN_ROWS
         scores = torch.zeros(F, F, dtype=torch.float32, device=dev) if (use_ia or p.detect_interactions) else None
         imat = torch.empty(F, F, dtype=torch.float32, device=dev) if use_ia else None
 
-        self.base_score = self.loss.base_score(yt)
+        if comm is None:
+            self.base_score = self.loss.base_score(yt)
+        else:
+            self.base_score = self.loss.base_from_mean(comm.sum_float(float(yt.double().sum())) / n_total)
         margin = torch.full((n,), self.base_score, dtype=torch.float32, device=dev)
         grad = torch.empty(n, dtype=torch.float32, device=dev)
         hess = torch.empty(n, dtype=torch.float32, device=dev) if general else None
@@ -295,7 +327,11 @@ class Booster:
                        right=forest.right[t], value=forest.value[t], gate_scale=forest.gate[t],
                        leaf_of_row=leaf_of_row, meta=forest.meta[t])
             a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost)
-            grower.grow(a)
+            if comm is None:
+                grower.grow(a)
+            else:
+                from .distributed import grow_tree
+                grow_tree(grower, a, comm)
             if p.neural_leaves:
                 la = _lib.LeafNetArgs()
                 la.feature = forest.feature[t].data_ptr(); la.value = forest.value[t].data_ptr()
@@ -310,8 +346,12 @@ class Booster:
                 la.feats = forest.feats[t].data_ptr(); la.linear = forest.linear[t].data_ptr()
                 la.lo = forest.lo[t].data_ptr(); la.hi = forest.hi[t].data_ptr()
                 la.has_nets = forest.has_nets[t:t + 1].data_ptr()
-                _lib.check(lib.yabt_leafnet_fit(ctypes.byref(la), ln_ws.data_ptr(), ln_ws.numel(), s),
-                           "yabt_leafnet_fit")
+                if comm is None:
+                    _lib.check(lib.yabt_leafnet_fit(ctypes.byref(la), ln_ws.data_ptr(), ln_ws.numel(), s),
+                               "yabt_leafnet_fit")
+                else:
+                    from .distributed import fit_leaf_models
+                    fit_leaf_models(la, ln_ws, forest.lo[t], forest.hi[t], comm)
             if scores is not None:
                 _lib.check(lib.yabt_interaction_update(forest.feature[t].data_ptr(), forest.left[t].data_ptr(),
                                                        forest.right[t].data_ptr(), forest.meta[t].data_ptr(),

@@ -398,6 +398,7 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
 
 void* yabt_grow_amax_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->amax_g : nullptr; }
 void* yabt_grow_small_ptr(yabt_grower* g) { return g && g->bound ? (void*)g->b.small : nullptr; }
+void* yabt_grow_level_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->level : nullptr; }
 
 long long yabt_grow_small_count(const yabt_grower* g, int level) {
   if (!g) return -1;

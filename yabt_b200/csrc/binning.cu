@@ -426,37 +426,68 @@ int yabt_transpose(const float* X, long long n, int F, float* Xfm, void* stream)
   return YABT_OK;
 }
 
-int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
-                 int max_bins, void* workspace, long long ws_bytes, float* medians, float* edges,
-                 int32_t* edge_cnt, float* scales, void* stream) {
-  if (!Xfm || n <= 0 || F <= 0 || nq <= 0 || max_bins < 2 || max_bins > 256 || !workspace || !medians ||
-      !edges || !edge_cnt || !scales) {
-    set_error("yabt_bin_fit: bad arguments");
-    return YABT_ERR_ARG;
-  }
-  if (ws_bytes < yabt_bin_fit_workspace_bytes(n, F, nq)) { set_error("yabt_bin_fit: workspace too small"); return YABT_ERR_WORKSPACE; }
-  cudaStream_t s = (cudaStream_t)stream;
-  const long long P = pow2_at_least(std::max(nq, 2LL));
+}  // extern "C"
+
+// ---------------------------------------------------------------- fit steps
+// The bin fit in steps: the median selection passes (a digit histogram over
+// the caller's rows, then a pick on the -- possibly all-reduced -- histogram),
+// and the edge fit on a row sample. yabt_bin_fit runs them back to back; a
+// row-sharded fit all-reduces the histograms and NaN counts between the steps
+// and fits the edges on the gathered sample.
+namespace yabt {
+
+struct FitWs {
+  SelState* sel;
+  unsigned* hist;               // [F][2][2048]
+  unsigned long long* nanc;     // [F]
+  unsigned* keys;               // [F][P]
+};
+
+static FitWs carve_fit(void* workspace, int F) {
   char* w = (char*)workspace;
-  SelState* sel = (SelState*)w; w += ((long long)F * sizeof(SelState) + 255) & ~255LL;
-  unsigned* hist = (unsigned*)w; w += ((long long)F * 2 * 2048 * 4 + 255) & ~255LL;
-  unsigned long long* nanc = (unsigned long long*)w; w += ((long long)F * 8 + 255) & ~255LL;
-  unsigned* keys = (unsigned*)w;
-  // medians: radix select over all rows
-  BCUDA(cudaMemsetAsync(nanc, 0, (size_t)F * 8, s));
-  const int chunks = (int)std::max(1LL, std::min(64LL, (n + 65535) / 65536));
-  for (int pass = 0; pass < 3; ++pass) {
-    BCUDA(cudaMemsetAsync(hist, 0, (size_t)F * 2 * 2048 * 4, s));
-    k_sel_hist<<<dim3(chunks, F), 512, 0, s>>>(Xfm, n, pass, sel, hist, nanc);
-    k_sel_pick<<<(F * 32 + 255) / 256, 256, 0, s>>>(n, F, pass, sel, hist, nanc);
+  FitWs r;
+  r.sel = (SelState*)w; w += ((long long)F * sizeof(SelState) + 255) & ~255LL;
+  r.hist = (unsigned*)w; w += ((long long)F * 2 * 2048 * 4 + 255) & ~255LL;
+  r.nanc = (unsigned long long*)w; w += ((long long)F * 8 + 255) & ~255LL;
+  r.keys = (unsigned*)w;
+  return r;
+}
+
+static cudaError_t median_hist(const float* Xfm, long long n, int F, int pass, const FitWs& w, cudaStream_t s) {
+  cudaError_t e = cudaSuccess;
+  if (pass == 0) e = cudaMemsetAsync(w.nanc, 0, (size_t)F * 8, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w.hist, 0, (size_t)F * 2 * 2048 * 4, s);
+  if (e != cudaSuccess) return e;
+  if (n > 0) {
+    const int chunks = (int)std::max(1LL, std::min(64LL, (n + 65535) / 65536));
+    k_sel_hist<<<dim3(chunks, F), 512, 0, s>>>(Xfm, n, pass, w.sel, w.hist, w.nanc);
+    count_launches(1);
   }
-  k_sel_final<<<(F + 255) / 256, 256, 0, s>>>(F, sel, medians);
-  BCUDA(cudaGetLastError());
-  // edges: sample keys, bitonic sort per column, quantiles
+  return cudaGetLastError();
+}
+
+static cudaError_t median_pick(long long n_total, int F, int pass, const FitWs& w, cudaStream_t s) {
+  k_sel_pick<<<(F * 32 + 255) / 256, 256, 0, s>>>(n_total, F, pass, w.sel, w.hist, w.nanc);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+static cudaError_t median_final(int F, const FitWs& w, float* medians, cudaStream_t s) {
+  k_sel_final<<<(F + 255) / 256, 256, 0, s>>>(F, w.sel, medians);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+// edges and scales from the sample rows idx[0..nq) of Xfm (all of its first nq
+// columns when idx is NULL)
+static cudaError_t fit_edges(const float* Xfm, long long n, int F, const int32_t* idx, long long nq, int max_bins,
+                             const FitWs& w, float* edges, int32_t* edge_cnt, float* scales, cudaStream_t s) {
+  const long long P = pow2_at_least(std::max(nq, 2LL));
+  unsigned* keys = w.keys;
   {
     const long long total = (long long)F * P;
     const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
-    k_sample_keys<<<grid, 256, 0, s>>>(Xfm, n, F, sample_idx, nq, P, keys);
+    k_sample_keys<<<grid, 256, 0, s>>>(Xfm, n, F, idx, nq, P, keys);
     count_launches(2);   // sample keys + first bitonic pass
   }
   if (P <= BL) {
@@ -474,10 +505,98 @@ int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx
       count_launches(1);
     }
   }
-  BCUDA(cudaGetLastError());
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   k_quantiles<<<F, 256, 0, s>>>(keys, P, max_bins, edges, edge_cnt, scales);
-  count_launches(8);   // selection (7) + quantiles; the bitonic launches are counted below
-  BCUDA(cudaGetLastError());
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace yabt
+
+extern "C" {
+
+int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
+                 int max_bins, void* workspace, long long ws_bytes, float* medians, float* edges,
+                 int32_t* edge_cnt, float* scales, void* stream) {
+  if (!Xfm || n <= 0 || F <= 0 || nq <= 0 || max_bins < 2 || max_bins > 256 || !workspace || !medians ||
+      !edges || !edge_cnt || !scales) {
+    set_error("yabt_bin_fit: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  if (ws_bytes < yabt_bin_fit_workspace_bytes(n, F, nq)) { set_error("yabt_bin_fit: workspace too small"); return YABT_ERR_WORKSPACE; }
+  cudaStream_t s = (cudaStream_t)stream;
+  const FitWs w = carve_fit(workspace, F);
+  // medians: radix select over all rows
+  for (int pass = 0; pass < 3; ++pass) {
+    BCUDA(median_hist(Xfm, n, F, pass, w, s));
+    BCUDA(median_pick(n, F, pass, w, s));
+  }
+  BCUDA(median_final(F, w, medians, s));
+  // edges: sample keys, bitonic sort per column, quantiles
+  BCUDA(fit_edges(Xfm, n, F, sample_idx, nq, max_bins, w, edges, edge_cnt, scales, s));
+  return YABT_OK;
+}
+
+int yabt_bin_median_hist(const float* Xfm, long long n, int F, int pass, void* workspace, long long ws_bytes,
+                         void* stream) {
+  if ((n > 0 && !Xfm) || n < 0 || F <= 0 || pass < 0 || pass > 2 || !workspace) {
+    set_error("yabt_bin_median_hist: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  if (ws_bytes < yabt_bin_fit_workspace_bytes(std::max(n, 1LL), F, 1)) {
+    set_error("yabt_bin_median_hist: workspace too small");
+    return YABT_ERR_WORKSPACE;
+  }
+  BCUDA(median_hist(Xfm, n, F, pass, carve_fit(workspace, F), (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_bin_median_pick(long long n_total, int F, int pass, void* workspace, long long ws_bytes, void* stream) {
+  if (n_total <= 0 || F <= 0 || pass < 0 || pass > 2 || !workspace) {
+    set_error("yabt_bin_median_pick: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  if (ws_bytes < yabt_bin_fit_workspace_bytes(1, F, 1)) {
+    set_error("yabt_bin_median_pick: workspace too small");
+    return YABT_ERR_WORKSPACE;
+  }
+  BCUDA(median_pick(n_total, F, pass, carve_fit(workspace, F), (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_bin_median_final(int F, void* workspace, long long ws_bytes, float* medians, void* stream) {
+  if (F <= 0 || !workspace || !medians) { set_error("yabt_bin_median_final: bad arguments"); return YABT_ERR_ARG; }
+  if (ws_bytes < yabt_bin_fit_workspace_bytes(1, F, 1)) {
+    set_error("yabt_bin_median_final: workspace too small");
+    return YABT_ERR_WORKSPACE;
+  }
+  BCUDA(median_final(F, carve_fit(workspace, F), medians, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_bin_median_bufs(int F, void* workspace, void** hist, long long* hist_words, void** nan_count) {
+  if (F <= 0 || !workspace) { set_error("yabt_bin_median_bufs: bad arguments"); return YABT_ERR_ARG; }
+  const FitWs w = carve_fit(workspace, F);
+  if (hist) *hist = w.hist;
+  if (hist_words) *hist_words = (long long)F * 2 * 2048;
+  if (nan_count) *nan_count = w.nanc;
+  return YABT_OK;
+}
+
+int yabt_bin_fit_edges(const float* Xs, long long nq, int F, int max_bins, void* workspace, long long ws_bytes,
+                       float* edges, int32_t* edge_cnt, float* scales, void* stream) {
+  if (!Xs || nq <= 0 || F <= 0 || max_bins < 2 || max_bins > 256 || !workspace || !edges || !edge_cnt ||
+      !scales) {
+    set_error("yabt_bin_fit_edges: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  if (ws_bytes < yabt_bin_fit_workspace_bytes(nq, F, nq)) {
+    set_error("yabt_bin_fit_edges: workspace too small");
+    return YABT_ERR_WORKSPACE;
+  }
+  BCUDA(fit_edges(Xs, nq, F, nullptr, nq, max_bins, carve_fit(workspace, F), edges, edge_cnt, scales,
+                  (cudaStream_t)stream));
   return YABT_OK;
 }
 

@@ -69,8 +69,8 @@ struct LeafNetArgs {
   // scratch (device)
   int* fcount;                // [F]
   int* flags;                 // [4]: n_used, need_pad, n_chunks, n_eligible
-  double* corr;               // [F]
-  double* gsum;               // [1]
+  double* corr;               // [F + 1]: sum_i x_fi g_i, then sum g at [F]
+  double* gsum;               // corr + F
   float* rec;                 // [n][REC] records
   float* pmin;                // [max_chunks][KMAX] chunk envelope
   float* pmax;                // [max_chunks][KMAX]
@@ -81,6 +81,7 @@ struct LeafNetArgs {
   int* chunk_begin;           // [max_chunks]
   int* chunk_end;             // [max_chunks]
   double* partial;            // [max_chunks][NE]
+  double* totals;             // [maxn][NE] per-node sums of the chunk partials
   int max_chunks;
 };
 
@@ -131,7 +132,6 @@ __global__ void __launch_bounds__(1024) k_ln_select(LeafNetArgs a) {
 // grid (chunks, ceil(F/8)): sum_i x_fi g_i and sum g (only when padding is needed)
 __global__ void k_ln_corr(LeafNetArgs a) {
   if (!a.flags[1]) return;
-  __shared__ double s[8][33];
   const int f0 = blockIdx.y * 8;
   double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   double gs = 0.0;
@@ -145,7 +145,7 @@ __global__ void k_ln_corr(LeafNetArgs a) {
     for (int q = 0; q < 8; ++q)
       if (f0 + q < a.F) acc[q] += (double)a.Xfm[(long long)(f0 + q) * a.n + i] * (double)g;
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     double v = acc[q];
@@ -154,7 +154,6 @@ __global__ void k_ln_corr(LeafNetArgs a) {
   }
   for (int o = 16; o; o >>= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
   if (lane == 0 && blockIdx.y == 0) atomicAdd(a.gsum, gs);
-  (void)warp; (void)s;
 }
 
 __global__ void __launch_bounds__(1024) k_ln_pad(LeafNetArgs a) {
@@ -371,19 +370,15 @@ __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
 }
 
 // One warp per node: lanes reduce the node's chunk partials (contiguous, in
-// chunk order) and envelope, lane 0 adds the ridge, solves by Cholesky and
-// folds (yabt/neural_leaves.py:85-89,180-184).
-__global__ void __launch_bounds__(128) k_ln_solve(LeafNetArgs a) {
-  __shared__ double se[4][NE];
+// chunk order) into its totals and its envelope into lo / hi.
+__global__ void __launch_bounds__(128) k_ln_total(LeafNetArgs a) {
   const int nn = a.meta[0];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x * 4 + warp;
   if (g >= nn) return;
-  const int K = a.K, D = K + 1;
+  const int K = a.K;
   const bool leaf = a.feature[g] < 0;
-  const bool elig = leaf && a.counts[g] >= a.min_samples;
   const int c0 = leaf ? a.leaf_first[g] : 0, nc = leaf ? a.leaf_nch[g] : 0;
-  // envelope over the node's chunks (lanes 0..K-1)
   if (lane < K) {
     float lo = INFINITY, hi = -INFINITY;
     for (int c = c0; c < c0 + nc; ++c) {
@@ -395,10 +390,35 @@ __global__ void __launch_bounds__(128) k_ln_solve(LeafNetArgs a) {
   }
   for (int e = lane; e < NE; e += 32) {
     double t = 0.0;
-    if (elig)
-      for (int c = c0; c < c0 + nc; ++c) t = __dadd_rn(t, a.partial[(long long)c * NE + e]);
-    se[warp][e] = t;
+    for (int c = c0; c < c0 + nc; ++c) t = __dadd_rn(t, a.partial[(long long)c * NE + e]);
+    a.totals[(long long)g * NE + e] = t;
   }
+}
+
+// eligibility from the (all-ranks) leaf counts: eligible-leaf count and has_nets
+__global__ void __launch_bounds__(1024) k_ln_elig(LeafNetArgs a) {
+  __shared__ int s_ne;
+  const int nn = a.meta[0];
+  if (threadIdx.x == 0) s_ne = 0;
+  __syncthreads();
+  for (int g = threadIdx.x; g < nn; g += blockDim.x)
+    if (a.feature[g] < 0 && a.counts[g] >= a.min_samples) atomicAdd(&s_ne, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) { a.flags[3] = s_ne; a.has_nets[0] = s_ne > 0; }
+}
+
+// One warp per node: lane 0 adds the ridge to the node's totals, solves by
+// Cholesky and folds (yabt/neural_leaves.py:85-89,180-184).
+__global__ void __launch_bounds__(128) k_ln_solve(LeafNetArgs a) {
+  __shared__ double se[4][NE];
+  const int nn = a.meta[0];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x * 4 + warp;
+  if (g >= nn) return;
+  const int K = a.K, D = K + 1;
+  const bool leaf = a.feature[g] < 0;
+  const bool elig = leaf && a.counts[g] >= a.min_samples;
+  for (int e = lane; e < NE; e += 32) se[warp][e] = elig ? a.totals[(long long)g * NE + e] : 0.0;
   __syncwarp();
   if (lane != 0) return;
   float W[KMAX], db = 0.f;
@@ -551,6 +571,32 @@ __global__ void __launch_bounds__(512) k_colstats(const float* __restrict__ Xfm,
   }
 }
 
+// Row-sharded column moments: pass 0 writes acc[f] = sum x over this rank's
+// rows; after acc[0..F) holds the all-ranks sum, pass 1 writes
+// acc[F + f] = sum (x - mu)^2 with mu = acc[f] / n_total. Same block reduction
+// as k_colstats, so one rank reproduces it exactly.
+__global__ void __launch_bounds__(512) k_colsum(const float* __restrict__ Xfm, long long n, long long n_total,
+                                                int F, int pass, double* acc) {
+  __shared__ double s[512];
+  const int f = blockIdx.x;
+  const float* col = Xfm + (long long)f * n;
+  const double mu = pass == 0 ? 0.0 : acc[f] / (double)n_total;
+  double v = 0.0;
+  if (pass == 0) for (long long i = threadIdx.x; i < n; i += blockDim.x) v += (double)col[i];
+  else for (long long i = threadIdx.x; i < n; i += blockDim.x) { const double d = (double)col[i] - mu; v += d * d; }
+  s[threadIdx.x] = v;
+  __syncthreads();
+  for (int o = 256; o; o >>= 1) { if (threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o]; __syncthreads(); }
+  if (threadIdx.x == 0) acc[pass * F + f] = s[0];
+}
+
+__global__ void k_colfinish(const double* acc, long long n_total, int F, float* mean, float* std) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= F) return;
+  mean[f] = (float)(acc[f] / (double)n_total);
+  std[f] = (float)sqrt(acc[F + f] / (double)(n_total > 1 ? n_total - 1 : 1));
+}
+
 // ------------------------------------------------------------------ interaction detector
 // scores (F x F, float counts) += 1 for every (ancestor feature, node feature)
 // pair with a != f along root-to-node paths, both directions
@@ -636,29 +682,31 @@ long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes) {
   long long b = 0;
   b += al((long long)F * 4);                 // fcount
   b += al(16);                               // flags
-  b += al((long long)F * 8);                 // corr
-  b += al(8);                                // gsum
+  b += al((long long)(F + 1) * 8);           // corr, gsum
   b += al(n * REC * 4);                      // rec
   b += 2 * al(max_chunks * KMAX * 4);        // pmin, pmax
   b += 3 * al((long long)max_nodes * 4);     // counts, leaf_first, leaf_nch
   b += 3 * al(max_chunks * 4);               // chunk arrays
   b += al(max_chunks * NE * 8);              // partials
+  b += al((long long)max_nodes * NE * 8);    // totals
   return b;
 }
 
-// Fit ridge-linear leaf models for one grown tree and fold them into
-// value / linear / lo / hi (yabt/neural_leaves.py:131-184).
-int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, void* stream) {
-  if (!p || !workspace || p->K < 1 || p->K > KMAX || p->n <= 0 || p->F <= 0) {
-    set_error("yabt_leafnet_fit: bad arguments (K must be in [1, %d])", KMAX);
+}  // extern "C"
+
+namespace yabt {
+
+static int leafnet_carve(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, LeafNetArgs* out,
+                         const char* who) {
+  if (!p || !workspace || p->K < 1 || p->K > KMAX || p->n < 0 || p->F <= 0) {
+    set_error("%s: bad arguments (K must be in [1, %d])", who, KMAX);
     return YABT_ERR_ARG;
   }
   if (ws_bytes < yabt_leafnet_workspace_bytes(p->n, p->F, p->max_nodes)) {
-    set_error("yabt_leafnet_fit: workspace too small");
+    set_error("%s: workspace too small", who);
     return YABT_ERR_WORKSPACE;
   }
   auto al = [](long long x) { return (x + 255) & ~255LL; };
-  cudaStream_t s = (cudaStream_t)stream;
   LeafNetArgs a;
   a.feature = (const long long*)p->feature; a.value = p->value; a.n_nodes_cap = p->max_nodes; a.meta = p->meta;
   a.leaf_src = p->leaf_src; a.leaf_begin = p->leaf_begin; a.leaf_count = p->leaf_count;
@@ -671,8 +719,8 @@ int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_b
   char* w = (char*)workspace;
   a.fcount = (int*)w; w += al((long long)p->F * 4);
   a.flags = (int*)w; w += al(16);
-  a.corr = (double*)w; w += al((long long)p->F * 8);
-  a.gsum = (double*)w; w += al(8);
+  a.corr = (double*)w; w += al((long long)(p->F + 1) * 8);
+  a.gsum = a.corr + p->F;
   a.rec = (float*)w; w += al(p->n * REC * 4);
   a.pmin = (float*)w; w += al(max_chunks * KMAX * 4);
   a.pmax = (float*)w; w += al(max_chunks * KMAX * 4);
@@ -682,24 +730,88 @@ int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_b
   a.chunk_leaf = (int*)w; w += al(max_chunks * 4);
   a.chunk_begin = (int*)w; w += al(max_chunks * 4);
   a.chunk_end = (int*)w; w += al(max_chunks * 4);
-  a.partial = (double*)w;
+  a.partial = (double*)w; w += al(max_chunks * NE * 8);
+  a.totals = (double*)w;
   a.max_chunks = (int)max_chunks;
+  *out = a;
+  return YABT_OK;
+}
+
+// Stage s of the leaf-model fit (see yabt_leafnet_stage in the header).
+static cudaError_t leafnet_launch(const LeafNetArgs& a, int stage, cudaStream_t s) {
   const int nsm = 148;
-  k_ln_select<<<1, 1024, 0, s>>>(a);
-  {
-    dim3 grid((unsigned)std::min<long long>((p->n + 255) / 256, 4LL * nsm), (unsigned)((p->F + 7) / 8));
-    k_ln_corr<<<grid, 256, 0, s>>>(a);
+  const int nblk = (a.n_nodes_cap + 3) / 4;
+  switch (stage) {
+    case 0: {
+      k_ln_select<<<1, 1024, 0, s>>>(a);
+      if (a.n > 0) {
+        dim3 grid((unsigned)std::min<long long>((a.n + 255) / 256, 4LL * nsm), (unsigned)((a.F + 7) / 8));
+        k_ln_corr<<<grid, 256, 0, s>>>(a);
+        count_launches(1);
+      }
+      count_launches(1);
+      break;
+    }
+    case 1: {
+      k_ln_pad<<<1, 1024, 0, s>>>(a);
+      if (a.n > 0) {
+        const int grid = (int)std::min<long long>((a.n + 255) / 256, 16LL * nsm);
+        k_ln_rows<<<grid, 256, 0, s>>>(a);
+        count_launches(1);
+      }
+      k_ln_plan<<<1, 1024, 0, s>>>(a);
+      count_launches(2);
+      break;
+    }
+    case 2: {
+      k_ln_elig<<<1, 1024, 0, s>>>(a);
+      k_ln_gram<<<(unsigned)a.max_chunks, 256, 0, s>>>(a);
+      k_ln_total<<<nblk, 128, 0, s>>>(a);
+      count_launches(3);
+      break;
+    }
+    default: {
+      k_ln_solve<<<nblk, 128, 0, s>>>(a);
+      count_launches(1);
+      break;
+    }
   }
-  k_ln_pad<<<1, 1024, 0, s>>>(a);
-  {
-    const int grid = (int)std::min<long long>((p->n + 255) / 256, 16LL * nsm);
-    k_ln_rows<<<grid, 256, 0, s>>>(a);
-  }
-  k_ln_plan<<<1, 1024, 0, s>>>(a);
-  k_ln_gram<<<(unsigned)max_chunks, 256, 0, s>>>(a);
-  k_ln_solve<<<(p->max_nodes + 3) / 4, 128, 0, s>>>(a);
-  count_launches(7);
-  LCUDA(cudaGetLastError());
+  return cudaGetLastError();
+}
+
+}  // namespace yabt
+
+extern "C" {
+
+// Fit ridge-linear leaf models for one grown tree and fold them into
+// value / linear / lo / hi (yabt/neural_leaves.py:131-184).
+int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, void* stream) {
+  LeafNetArgs a;
+  int rc = leafnet_carve(p, workspace, ws_bytes, &a, "yabt_leafnet_fit");
+  if (rc) return rc;
+  if (p->n <= 0) { set_error("yabt_leafnet_fit: n must be > 0"); return YABT_ERR_ARG; }
+  for (int st = 0; st < 4; ++st) LCUDA(leafnet_launch(a, st, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_leafnet_stage(const yabt_leafnet_args* p, int stage, void* workspace, long long ws_bytes, void* stream) {
+  LeafNetArgs a;
+  int rc = leafnet_carve(p, workspace, ws_bytes, &a, "yabt_leafnet_stage");
+  if (rc) return rc;
+  if (stage < 0 || stage > 3) { set_error("yabt_leafnet_stage: stage must be 0..3"); return YABT_ERR_ARG; }
+  LCUDA(leafnet_launch(a, stage, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_leafnet_bufs(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, void** corr, void** counts,
+                      void** totals, int* per_node) {
+  LeafNetArgs a;
+  int rc = leafnet_carve(p, workspace, ws_bytes, &a, "yabt_leafnet_bufs");
+  if (rc) return rc;
+  if (corr) *corr = a.corr;
+  if (counts) *counts = a.counts;
+  if (totals) *totals = a.totals;
+  if (per_node) *per_node = NE;
   return YABT_OK;
 }
 
@@ -737,6 +849,25 @@ int yabt_grad_init(const float* margin, const float* y, long long n, int loss, f
 int yabt_column_stats(const float* Xfm, long long n, int F, float* mean, float* std, void* stream) {
   if (!Xfm || n <= 0 || F <= 0 || !mean || !std) { set_error("yabt_column_stats: bad arguments"); return YABT_ERR_ARG; }
   k_colstats<<<F, 512, 0, (cudaStream_t)stream>>>(Xfm, n, mean, std);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_column_sums(const float* Xfm, long long n, long long n_total, int F, int pass, double* acc, void* stream) {
+  if ((n > 0 && !Xfm) || n < 0 || n_total <= 0 || F <= 0 || pass < 0 || pass > 1 || !acc) {
+    set_error("yabt_column_sums: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  k_colsum<<<F, 512, 0, (cudaStream_t)stream>>>(Xfm, n, n_total, F, pass, acc);
+  count_launches(1);
+  LCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_column_finish(const double* acc, long long n_total, int F, float* mean, float* std, void* stream) {
+  if (!acc || n_total <= 0 || F <= 0 || !mean || !std) { set_error("yabt_column_finish: bad arguments"); return YABT_ERR_ARG; }
+  k_colfinish<<<(F + 255) / 256, 256, 0, (cudaStream_t)stream>>>(acc, n_total, F, mean, std);
   count_launches(1);
   LCUDA(cudaGetLastError());
   return YABT_OK;

@@ -1,0 +1,255 @@
+"""Row-sharded fitting over several GPUs, one process per GPU.
+
+Each rank holds a contiguous block of the training rows (its shard) and runs
+the same sequence of kernels as a single-GPU fit on its own rows. Wherever the
+reference's fit reads statistics of ALL rows, the ranks reduce their partial
+statistics with ``torch.distributed`` collectives (NCCL over NVLink on GPUs;
+gloo, staged through host memory, in the CPU tests), so that every rank takes
+identical decisions and holds an identical model:
+
+* binning (yabt/binning.py:29-69): the three radix-selection passes of the
+  medians sum their digit histograms and NaN counts; the quantile sample is the
+  reference's own draw over the global row count, gathered from the ranks
+  that own the rows;
+* column moments for the leaf models: sums, then centred sums of squares;
+* per tree: the max |g| / max h quantisation words (max), every level's
+  smaller-child histograms (exact int64 sums, so split decisions are
+  bit-identical to a single-GPU fit on the concatenated rows), and the leaf
+  models' statistics (gradient correlations, leaf counts, normal equations,
+  input envelopes);
+* the base score (sum of y).
+
+Margins, gradients, row partitions and leaf assignments stay rank-local.
+Float64 sums of the leaf-model statistics change order with the rank count,
+so leaf values agree with a single-GPU fit to rounding, not bit for bit.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+
+QUANTILE_SAMPLE = 200_000
+
+
+class ShardComm:
+    """Collectives of one process group. With the NCCL backend tensors are
+    reduced in place on the device; with any other backend (gloo) they are
+    staged through host memory."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        if not dist.is_initialized():
+            raise RuntimeError("ShardComm needs an initialised torch.distributed process group")
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.on_device = dist.get_backend(group) == "nccl"
+
+    # in-place reductions -------------------------------------------------
+    def _reduce(self, t: torch.Tensor, op) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        if self.on_device or t.device.type == "cpu":
+            self.dist.all_reduce(t, op=op, group=self.group)
+            return t
+        h = t.cpu()
+        self.dist.all_reduce(h, op=op, group=self.group)
+        t.copy_(h)
+        return t
+
+    def sum_(self, t: torch.Tensor) -> torch.Tensor:
+        return self._reduce(t, self.dist.ReduceOp.SUM)
+
+    def max_(self, t: torch.Tensor) -> torch.Tensor:
+        return self._reduce(t, self.dist.ReduceOp.MAX)
+
+    def min_(self, t: torch.Tensor) -> torch.Tensor:
+        return self._reduce(t, self.dist.ReduceOp.MIN)
+
+    def unsigned_max_(self, words: torch.Tensor) -> torch.Tensor:
+        """Max of uint32 words held in an int32 tensor (order-preserving
+        float encodings have the top bit set, so a signed max would be
+        wrong): widened to int64 for the reduction."""
+        t = words.to(torch.int64) & 0xFFFFFFFF
+        self.max_(t)
+        words.copy_(torch.where(t >= 2 ** 31, t - 2 ** 32, t).to(torch.int32))
+        return words
+
+    # scalars and gathers -------------------------------------------------
+    def int_values(self, v: int) -> list[int]:
+        """Every rank's value of an integer, in rank order."""
+        dev = "cuda" if self.on_device else "cpu"
+        mine = torch.tensor([int(v)], dtype=torch.int64, device=dev)
+        out = [torch.empty_like(mine) for _ in range(self.world)]
+        self.dist.all_gather(out, mine, group=self.group)
+        return [int(x.item()) for x in out]
+
+    def sum_float(self, v: float) -> float:
+        dev = "cuda" if self.on_device else "cpu"
+        t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+        self.sum_(t)
+        return float(t.item())
+
+    def gather_columns(self, x: torch.Tensor) -> torch.Tensor:
+        """Concatenate every rank's (F, m_r) float32 block along columns, in
+        rank order; the result is on x's device."""
+        F, m = x.shape
+        sizes = self.int_values(m)
+        mx = max(max(sizes), 1)
+        dev = x.device if self.on_device else torch.device("cpu")
+        pad = torch.zeros(F, mx, dtype=x.dtype, device=dev)
+        pad[:, :m] = x.to(dev)
+        parts = [torch.empty_like(pad) for _ in range(self.world)]
+        self.dist.all_gather(parts, pad, group=self.group)
+        return torch.cat([p[:, :s] for p, s in zip(parts, sizes)], dim=1).to(x.device).contiguous()
+
+
+def _view(base: torch.Tensor, ptr: int, count: int, dtype: torch.dtype) -> torch.Tensor:
+    """``count`` elements of ``dtype`` at device address ``ptr`` inside the
+    uint8 workspace tensor ``base``."""
+    size = torch.empty(0, dtype=dtype).element_size()
+    off = int(ptr) - base.data_ptr()
+    if off < 0 or off + count * size > base.numel() or off % size:
+        raise _lib.YabtError("buffer outside its workspace")
+    return base[off:off + count * size].view(dtype)
+
+
+def shard_layout(comm: ShardComm, n_local: int) -> tuple[int, int]:
+    """(first global row of this rank, total rows): ranks hold contiguous
+    blocks in rank order."""
+    sizes = comm.int_values(n_local)
+    return sum(sizes[:comm.rank]), sum(sizes)
+
+
+def sample_rows(n_total: int) -> np.ndarray:
+    """Global quantile-sample rows: the reference's draw (yabt/binning.py:36-40)."""
+    if n_total > QUANTILE_SAMPLE:
+        return np.random.default_rng(0).choice(n_total, QUANTILE_SAMPLE, replace=False)
+    return np.arange(n_total)
+
+
+def local_sample(rows: np.ndarray, offset: int, n_local: int) -> np.ndarray:
+    """The sample rows this rank owns, as local row indices (draw order)."""
+    mine = rows[(rows >= offset) & (rows < offset + n_local)]
+    return (mine - offset).astype(np.int64)
+
+
+def fit_binner(Xfm: torch.Tensor, n_local: int, max_bins: int, comm: ShardComm):
+    """Device binner state (medians, edges [F][255], edge counts, scales)
+    fitted over the rows of every rank."""
+    lib = _lib.load()
+    F = Xfm.shape[0]
+    dev = Xfm.device
+    s = _lib.stream_ptr()
+    offset, n_total = shard_layout(comm, n_local)
+    ws = torch.empty(int(lib.yabt_bin_fit_workspace_bytes(max(n_local, 1), F, 1)), dtype=torch.uint8, device=dev)
+    hp, words, nanp = ctypes.c_void_p(), ctypes.c_longlong(), ctypes.c_void_p()
+    _lib.check(lib.yabt_bin_median_bufs(F, ws.data_ptr(), ctypes.byref(hp), ctypes.byref(words),
+                                        ctypes.byref(nanp)), "yabt_bin_median_bufs")
+    hist = _view(ws, hp.value, words.value, torch.int32)
+    nanc = _view(ws, nanp.value, F, torch.int64)
+    for p in range(3):
+        _lib.check(lib.yabt_bin_median_hist(Xfm.data_ptr(), n_local, F, p, ws.data_ptr(), ws.numel(), s),
+                   "yabt_bin_median_hist")
+        comm.sum_(hist)                      # uint32 counts: int32 sums wrap identically
+        if p == 0:
+            comm.sum_(nanc)
+        _lib.check(lib.yabt_bin_median_pick(n_total, F, p, ws.data_ptr(), ws.numel(), s), "yabt_bin_median_pick")
+    med = torch.empty(F, dtype=torch.float32, device=dev)
+    _lib.check(lib.yabt_bin_median_final(F, ws.data_ptr(), ws.numel(), med.data_ptr(), s), "yabt_bin_median_final")
+    del ws
+    idx = torch.from_numpy(local_sample(sample_rows(n_total), offset, n_local)).to(dev)
+    Xs = comm.gather_columns(Xfm.index_select(1, idx))
+    nq = Xs.shape[1]
+    ws = torch.empty(int(lib.yabt_bin_fit_workspace_bytes(nq, F, nq)), dtype=torch.uint8, device=dev)
+    edges = torch.empty(F, 255, dtype=torch.float32, device=dev)
+    ecnt = torch.empty(F, dtype=torch.int32, device=dev)
+    scales = torch.empty(F, dtype=torch.float32, device=dev)
+    _lib.check(lib.yabt_bin_fit_edges(Xs.data_ptr(), nq, F, max_bins, ws.data_ptr(), ws.numel(), edges.data_ptr(),
+                                      ecnt.data_ptr(), scales.data_ptr(), s), "yabt_bin_fit_edges")
+    return med, edges, ecnt, scales
+
+
+def column_stats(Xfm: torch.Tensor, n_local: int, comm: ShardComm) -> tuple[torch.Tensor, torch.Tensor]:
+    """Column means and unbiased stds over the rows of every rank."""
+    lib = _lib.load()
+    F = Xfm.shape[0]
+    dev = Xfm.device
+    s = _lib.stream_ptr()
+    _, n_total = shard_layout(comm, n_local)
+    acc = torch.zeros(2 * F, dtype=torch.float64, device=dev)
+    for p in range(2):
+        _lib.check(lib.yabt_column_sums(Xfm.data_ptr(), n_local, n_total, F, p, acc.data_ptr(), s), "yabt_column_sums")
+        comm.sum_(acc[p * F:(p + 1) * F])
+    mean = torch.empty(F, dtype=torch.float32, device=dev)
+    std = torch.empty(F, dtype=torch.float32, device=dev)
+    _lib.check(lib.yabt_column_finish(acc.data_ptr(), n_total, F, mean.data_ptr(), std.data_ptr(), s),
+               "yabt_column_finish")
+    return mean, std
+
+
+def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
+    """One tree over the rows of every rank: the grower's step API with the
+    quantisation words and each level's smaller-child histograms summed
+    between the steps. The level state (pairs, active) of the previous split
+    is copied to host memory while the next level's histogram kernels run, so
+    each all-reduce covers exactly that level's histograms and the loop stops
+    with the tree; the state is identical on every rank, so every rank makes
+    the same collective calls."""
+    lib = grower.lib
+    h = grower.h
+    s = _lib.stream_ptr()
+    ref = ctypes.byref(a)
+    if not hasattr(grower, "_level_host"):
+        grower._level_host = torch.zeros(4, dtype=torch.int32).pin_memory()
+        grower._level_event = torch.cuda.Event()
+    info, ev = grower._level_host, grower._level_event
+    state = _view(grower.ws, lib.yabt_grow_level_ptr(h), 4, torch.int32)
+    per_job = int(lib.yabt_grow_small_count(h, 0))
+    small = _view(grower.ws, lib.yabt_grow_small_ptr(h), int(lib.yabt_grow_small_count(h, grower.levels - 1)),
+                  torch.int64)
+    _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
+    comm.unsigned_max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))
+    _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
+    jobs = 1
+    for d in range(grower.levels):
+        _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
+        if d > 0:
+            ev.synchronize()                 # the previous split's state; level d's histogram runs meanwhile
+            _, active, _, jobs = info.tolist()
+            if not active:
+                break
+        comm.sum_(small[:jobs * per_job])
+        _lib.check(lib.yabt_grow_split(h, ref, d, s), "yabt_grow_split")
+        info.copy_(state, non_blocking=True)
+        ev.record()
+    _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
+
+
+def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, lo: torch.Tensor, hi: torch.Tensor,
+                    comm: ShardComm) -> None:
+    """Leaf models of one tree over the rows of every rank (the four stages
+    of yabt_leafnet_stage with the statistics reduced in between)."""
+    lib = _lib.load()
+    s = _lib.stream_ptr()
+    ref = ctypes.byref(la)
+    cp, np_, tp, per = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int()
+    _lib.check(lib.yabt_leafnet_bufs(ref, ws.data_ptr(), ws.numel(), ctypes.byref(cp), ctypes.byref(np_),
+                                     ctypes.byref(tp), ctypes.byref(per)), "yabt_leafnet_bufs")
+    maxn = int(la.max_nodes)
+    stage = lambda k: _lib.check(lib.yabt_leafnet_stage(ref, k, ws.data_ptr(), ws.numel(), s), "yabt_leafnet_stage")
+    stage(0)
+    comm.sum_(_view(ws, cp.value, int(la.F) + 1, torch.float64))
+    stage(1)
+    comm.sum_(_view(ws, np_.value, maxn, torch.int32))
+    stage(2)
+    comm.sum_(_view(ws, tp.value, maxn * per.value, torch.float64))
+    comm.min_(lo)
+    comm.max_(hi)
+    stage(3)

@@ -49,15 +49,18 @@ class _YABTBase(BaseEstimator):
             raise NotImplementedError("categorical target encoding is host preprocessing outside the "
                                       "GPU tree-growth path; encode categorical columns before fit")
 
-    def fit(self, X, y, eval_set=None, categorical_features=None):
+    def fit(self, X, y, eval_set=None, categorical_features=None, comm=None):
+        """``comm`` (a ``yabt_b200.distributed.ShardComm``): X and y are this
+        rank's rows of a row-sharded training set; every rank calls ``fit``
+        with the same parameters and ends with the same model."""
         self._check_cats(categorical_features)
         y = _require_single_target(np.asarray(y, dtype=np.float32))
-        yt = self._transform_y(y, fit=True)
+        yt = self._transform_y(y, fit=True, comm=comm)
         ev = None
         if eval_set is not None:
             ev = (eval_set[0], self._transform_y(np.asarray(eval_set[1], dtype=np.float32), fit=False))
         self.booster_ = Booster(self._boost_params(), self._loss())
-        self.booster_.fit(X, yt, eval_set=ev)
+        self.booster_.fit(X, yt, eval_set=ev, comm=comm)
         return self
 
     def _margin(self, X) -> np.ndarray:
@@ -67,10 +70,15 @@ class _YABTBase(BaseEstimator):
 class YABTClassifier(_YABTBase, ClassifierMixin):
     """Binary and multiclass classifier (one-vs-rest for multiclass)."""
 
-    def fit(self, X, y, eval_set=None, categorical_features=None):
+    def fit(self, X, y, eval_set=None, categorical_features=None, comm=None):
+        """``comm``: row-sharded fit (binary targets), as for YABTRegressor.fit."""
         self._check_cats(categorical_features)
         y = np.asarray(y, dtype=np.float32)
         self.classes_ = np.unique(y)
+        if comm is not None:
+            import torch
+            u = torch.from_numpy(self.classes_.reshape(1, -1).astype(np.float32))
+            self.classes_ = np.unique(comm.gather_columns(u).numpy())
         self.n_classes_ = len(self.classes_)
         self._is_binary = self.n_classes_ == 2
         if self._is_binary:
@@ -80,7 +88,9 @@ class YABTClassifier(_YABTBase, ClassifierMixin):
                 ye = (np.asarray(eval_set[1], dtype=np.float32) == self.classes_[1]).astype(np.float32)
                 ev = (eval_set[0], ye)
             self.booster_ = Booster(self._boost_params(), LogLoss())
-            self.booster_.fit(X, yt, eval_set=ev)
+            self.booster_.fit(X, yt, eval_set=ev, comm=comm)
+        elif comm is not None:
+            raise NotImplementedError("row-sharded fits support binary classification only")
         else:
             self.booster_ = MulticlassBooster(self._boost_params())
             self.booster_.fit(X, y, eval_set=eval_set)
@@ -104,10 +114,16 @@ class YABTRegressor(_YABTBase, RegressorMixin):
     def _loss(self):
         return MSELoss()
 
-    def _transform_y(self, y, fit):
-        if fit:
+    def _transform_y(self, y, fit, comm=None):
+        if fit and comm is None:
             self._y_mean = float(y.mean())
             self._y_std = float(y.std()) or 1.0
+        elif fit:
+            n = sum(comm.int_values(len(y)))
+            mean = comm.sum_float(float(y.astype(np.float64).sum())) / n
+            var = comm.sum_float(float(((y.astype(np.float64) - mean) ** 2).sum())) / n
+            self._y_mean = float(np.float32(mean))
+            self._y_std = float(np.float32(np.sqrt(var))) or 1.0
         return (y - self._y_mean) / self._y_std
 
     def predict(self, X) -> np.ndarray:
