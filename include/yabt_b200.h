@@ -129,11 +129,12 @@ typedef struct {
 /* Grow one tree (single device): all levels, no host synchronisation. */
 int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream);
 
-/* Step-wise driving for row-sharded multi-GPU growth: the caller may
- * all-reduce (max) the two words at yabt_grow_amax_ptr() after
- * yabt_grow_begin, and all-reduce (sum, int64) the small-child histograms at
- * yabt_grow_small_ptr() between yabt_grow_hist and yabt_grow_split of each
- * level (count = yabt_grow_small_count(level) int64 values).             */
+/* Step-wise driving for row-sharded multi-GPU growth: the caller reduces
+ * (max, as int32) the two words at yabt_grow_amax_ptr() -- bit patterns of
+ * max |g| and max |h| -- after yabt_grow_begin, and sums (int64) the
+ * small-child histograms at yabt_grow_small_ptr() between yabt_grow_hist and
+ * yabt_grow_split of each level: at most yabt_grow_small_count(level) values,
+ * exactly pairs * yabt_grow_small_count(0) (see yabt_grow_level_ptr).     */
 int yabt_grow_begin(yabt_grower* g, const yabt_tree_args* a, void* stream);
 int yabt_grow_init(yabt_grower* g, const yabt_tree_args* a, void* stream);
 int yabt_grow_hist(yabt_grower* g, const yabt_tree_args* a, int level, void* stream);
@@ -247,17 +248,17 @@ typedef struct {
 
 long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes);
 int yabt_leafnet_fit(const yabt_leafnet_args* a, void* workspace, long long ws_bytes, void* stream);
-/* yabt_leafnet_fit in four stages for rows sharded across GPUs
+/* yabt_leafnet_fit in three stages for rows sharded across GPUs
  * (fit_leaf_networks over every rank's rows). Between the stages the caller
  * reduces over the ranks, in place:
- *   after stage 0: sum of corr[0..F] (float64; X^T g and sum g);
- *   after stage 1: sum of counts[0..max_nodes) (int32 leaf row counts);
- *   after stage 2: sum of totals[0..max_nodes * per_node) (float64 normal
- *                  equations), min of lo and max of hi (the envelopes).
- * Stage 3 solves and folds. yabt_leafnet_bufs gives the three addresses.  */
+ *   after stage 0: sum of stats (float64: X^T g, sum g, leaf row counts);
+ *   after stage 1: sum of totals (float64 per-leaf normal equations) and max
+ *                  of envelope (float32: -min x, max x per leaf input).
+ * Stage 2 solves and folds. yabt_leafnet_bufs gives addresses and counts.  */
 int yabt_leafnet_stage(const yabt_leafnet_args* a, int stage, void* workspace, long long ws_bytes, void* stream);
-int yabt_leafnet_bufs(const yabt_leafnet_args* a, void* workspace, long long ws_bytes, void** corr, void** counts,
-                      void** totals, int* per_node);
+int yabt_leafnet_bufs(const yabt_leafnet_args* a, void* workspace, long long ws_bytes, void** stats,
+                      long long* stats_count, void** totals, long long* totals_count, void** envelope,
+                      long long* envelope_count);
 
 /* Margin update of one tree and the next tree's gradients
  * (yabt/boosting.py:36-38,53-54,511-514; Tree.net_contribution yabt/tree.py:118-128). */

@@ -1,5 +1,5 @@
 """Host logic of the row-sharded fit on CPU: two gloo ranks exercise the
-collectives wrapper (sums, signed and unsigned maxima, minima, gathers of
+collectives wrapper (sums, maxima, minima, gathers of
 ragged column blocks), the shard layout and the split of the reference's
 quantile sample across ranks. No GPU is used."""
 
@@ -34,10 +34,10 @@ def _worker(rank, world, port, q):
         f = torch.tensor([1.5, -2.0, float("inf")]) * (1 if rank == 0 else -1)
         out["max"] = c.max_(f.clone()).tolist()
         out["min"] = c.min_(f.clone()).tolist()
-        # order-preserving float words (top bit set for positives) and a zero word
-        w = torch.tensor([0x80000000 + 5 * (rank + 1) - 2 ** 32, 0 if rank == 0 else 0x3F000000],
+        # bit patterns of non-negative floats (the quantisation words) order as int32
+        w = torch.tensor([np.float32(1.5 * (rank + 1)).view(np.int32), 0 if rank == 0 else 0x3F000000],
                          dtype=torch.int32)
-        out["umax"] = (c.unsigned_max_(w).to(torch.int64) & 0xFFFFFFFF).tolist()
+        out["fmax"] = c.max_(w).tolist()
         n_local = [7, 3][rank]
         out["layout"] = shard_layout(c, n_local)
         blk = torch.full((2, n_local), float(rank)) + torch.arange(n_local).float()
@@ -64,7 +64,7 @@ def test_collectives_two_gloo_ranks():
         assert o["sum"] == [3 * i for i in range(6)]
         assert o["max"] == [1.5, 2.0, float("inf")]
         assert o["min"] == [-1.5, -2.0, float("-inf")]
-        assert o["umax"] == [0x80000000 + 10, 0x3F000000]
+        assert o["fmax"] == [int(np.float32(3.0).view(np.int32)), 0x3F000000]
         assert o["layout"] == ((0, 10) if r == 0 else (7, 10))
         assert o["gather"] == [[0, 1, 2, 3, 4, 5, 6, 1, 2, 3], [0, 1, 2, 3, 4, 5, 6, 1, 2, 3]]
         assert o["fsum"] == 0.75

@@ -106,8 +106,9 @@ SIGNATURES = [
     ("yabt_leafnet_workspace_bytes", c_ll, [c_ll, c_int, c_int]),
     ("yabt_leafnet_fit", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, c_vp]),
     ("yabt_leafnet_stage", c_int, [ctypes.POINTER(LeafNetArgs), c_int, c_vp, c_ll, c_vp]),
-    ("yabt_leafnet_bufs", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp),
-                                  ctypes.POINTER(c_vp), ctypes.POINTER(c_int)]),
+    ("yabt_leafnet_bufs", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, ctypes.POINTER(c_vp), ctypes.POINTER(c_ll),
+                                  ctypes.POINTER(c_vp), ctypes.POINTER(c_ll), ctypes.POINTER(c_vp),
+                                  ctypes.POINTER(c_ll)]),
     ("yabt_update_margin", c_int, [ctypes.POINTER(UpdateArgs), c_vp]),
     ("yabt_grad_init", c_int, [c_vp, c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),
     ("yabt_column_stats", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp]),

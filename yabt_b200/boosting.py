@@ -351,7 +351,7 @@ class Booster:
                                "yabt_leafnet_fit")
                 else:
                     from .distributed import fit_leaf_models
-                    fit_leaf_models(la, ln_ws, forest.lo[t], forest.hi[t], comm)
+                    fit_leaf_models(la, ln_ws, comm)
             if scores is not None:
                 _lib.check(lib.yabt_interaction_update(forest.feature[t].data_ptr(), forest.left[t].data_ptr(),
                                                        forest.right[t].data_ptr(), forest.meta[t].data_ptr(),

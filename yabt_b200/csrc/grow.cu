@@ -46,8 +46,10 @@ __global__ void k_absmax(const float* __restrict__ g, const float* __restrict__ 
   unsigned mg = 0, mh = 0;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
-    mg = max(mg, f2ord(fabsf(g[i])));
-    if (h) mh = max(mh, f2ord(fabsf(h[i])));
+    // bit patterns of non-negative floats order like the values, as signed and
+    // as unsigned 32-bit integers (so ranks can combine them with an int max)
+    mg = max(mg, __float_as_uint(fabsf(g[i])));
+    if (h) mh = max(mh, __float_as_uint(fabsf(h[i])));
   }
   for (int o = 16; o; o >>= 1) {
     mg = max(mg, __shfl_xor_sync(0xffffffffu, mg, o));
@@ -59,8 +61,8 @@ __global__ void k_absmax(const float* __restrict__ g, const float* __restrict__ 
   }
 }
 
-__device__ void quant_scale(unsigned amax_ord, int* qe, float* scale, float* inv) {
-  float a = amax_ord ? ord2f(amax_ord) : 0.f;
+__device__ void quant_scale(unsigned amax_bits, int* qe, float* scale, float* inv) {
+  float a = __uint_as_float(amax_bits);
   int e = exp_bound(a);
   int q = 30 - e;
   q = max(-100, min(q, 100));

@@ -79,7 +79,7 @@ struct GrowState {
   float gscale, hscale; // 2^qe
   float ginv, hinv;     // 2^-qe
   int depth_max;        // deepest node depth so far
-  unsigned amax_g, amax_h;  // ordered-float max |g|, max h
+  unsigned amax_g, amax_h;  // bit patterns of max |g| and max |h|
   int n_leaves;
   int pad[2];
   long long hist_rows[64];   // rows histogrammed at each level (algorithmic-traffic accounting)

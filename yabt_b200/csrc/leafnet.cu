@@ -69,8 +69,10 @@ struct LeafNetArgs {
   // scratch (device)
   int* fcount;                // [F]
   int* flags;                 // [4]: n_used, need_pad, n_chunks, n_eligible
-  double* corr;               // [F + 1]: sum_i x_fi g_i, then sum g at [F]
-  double* gsum;               // corr + F
+  double* stats;              // [F + 1 + maxn]: sum_i x_fi g_i [F], sum g, leaf row counts [maxn]
+  double* corr;               // stats
+  double* gsum;               // stats + F
+  float* env;                 // [maxn][2 * KMAX]: -min x, max x (the leaf input envelopes)
   float* rec;                 // [n][REC] records
   float* pmin;                // [max_chunks][KMAX] chunk envelope
   float* pmax;                // [max_chunks][KMAX]
@@ -127,6 +129,10 @@ __global__ void __launch_bounds__(1024) k_ln_select(LeafNetArgs a) {
     a.gsum[0] = 0.0;
   }
   for (int f = threadIdx.x; f < a.F; f += blockDim.x) a.corr[f] = 0.0;
+  // this rank's leaf row counts, summed over the ranks with the correlations
+  double* cnt = a.stats + a.F + 1;
+  for (int g = threadIdx.x; g < a.n_nodes_cap; g += blockDim.x)
+    cnt[g] = (g < nn && a.feature[g] < 0) ? (double)a.leaf_count[g] : 0.0;
 }
 
 // grid (chunks, ceil(F/8)): sum_i x_fi g_i and sum g (only when padding is needed)
@@ -385,8 +391,8 @@ __global__ void __launch_bounds__(128) k_ln_total(LeafNetArgs a) {
       lo = fminf(lo, a.pmin[(long long)c * KMAX + lane]);
       hi = fmaxf(hi, a.pmax[(long long)c * KMAX + lane]);
     }
-    a.lo[(long long)g * K + lane] = lo;
-    a.hi[(long long)g * K + lane] = hi;
+    a.env[(long long)g * 2 * KMAX + lane] = -lo;
+    a.env[(long long)g * 2 * KMAX + KMAX + lane] = hi;
   }
   for (int e = lane; e < NE; e += 32) {
     double t = 0.0;
@@ -395,14 +401,19 @@ __global__ void __launch_bounds__(128) k_ln_total(LeafNetArgs a) {
   }
 }
 
-// eligibility from the (all-ranks) leaf counts: eligible-leaf count and has_nets
+// eligibility from the (all-ranks) leaf counts: counts, eligible-leaf count and has_nets
 __global__ void __launch_bounds__(1024) k_ln_elig(LeafNetArgs a) {
   __shared__ int s_ne;
   const int nn = a.meta[0];
+  const double* cnt = a.stats + a.F + 1;
   if (threadIdx.x == 0) s_ne = 0;
   __syncthreads();
-  for (int g = threadIdx.x; g < nn; g += blockDim.x)
-    if (a.feature[g] < 0 && a.counts[g] >= a.min_samples) atomicAdd(&s_ne, 1);
+  for (int g = threadIdx.x; g < nn; g += blockDim.x) {
+    const bool leaf = a.feature[g] < 0;
+    const int c = leaf ? (int)cnt[g] : 0;
+    a.counts[g] = c;
+    if (leaf && c >= a.min_samples) atomicAdd(&s_ne, 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0) { a.flags[3] = s_ne; a.has_nets[0] = s_ne > 0; }
 }
@@ -418,6 +429,10 @@ __global__ void __launch_bounds__(128) k_ln_solve(LeafNetArgs a) {
   const int K = a.K, D = K + 1;
   const bool leaf = a.feature[g] < 0;
   const bool elig = leaf && a.counts[g] >= a.min_samples;
+  if (lane < K) {
+    a.lo[(long long)g * K + lane] = -a.env[(long long)g * 2 * KMAX + lane];
+    a.hi[(long long)g * K + lane] = a.env[(long long)g * 2 * KMAX + KMAX + lane];
+  }
   for (int e = lane; e < NE; e += 32) se[warp][e] = elig ? a.totals[(long long)g * NE + e] : 0.0;
   __syncwarp();
   if (lane != 0) return;
@@ -682,13 +697,14 @@ long long yabt_leafnet_workspace_bytes(long long n, int F, int max_nodes) {
   long long b = 0;
   b += al((long long)F * 4);                 // fcount
   b += al(16);                               // flags
-  b += al((long long)(F + 1) * 8);           // corr, gsum
+  b += al((long long)(F + 1 + max_nodes) * 8);   // stats: corr, gsum, leaf counts
   b += al(n * REC * 4);                      // rec
   b += 2 * al(max_chunks * KMAX * 4);        // pmin, pmax
   b += 3 * al((long long)max_nodes * 4);     // counts, leaf_first, leaf_nch
   b += 3 * al(max_chunks * 4);               // chunk arrays
   b += al(max_chunks * NE * 8);              // partials
   b += al((long long)max_nodes * NE * 8);    // totals
+  b += al((long long)max_nodes * 2 * KMAX * 4);   // envelopes
   return b;
 }
 
@@ -719,8 +735,9 @@ static int leafnet_carve(const yabt_leafnet_args* p, void* workspace, long long 
   char* w = (char*)workspace;
   a.fcount = (int*)w; w += al((long long)p->F * 4);
   a.flags = (int*)w; w += al(16);
-  a.corr = (double*)w; w += al((long long)(p->F + 1) * 8);
-  a.gsum = a.corr + p->F;
+  a.stats = (double*)w; w += al((long long)(p->F + 1 + p->max_nodes) * 8);
+  a.corr = a.stats;
+  a.gsum = a.stats + p->F;
   a.rec = (float*)w; w += al(p->n * REC * 4);
   a.pmin = (float*)w; w += al(max_chunks * KMAX * 4);
   a.pmax = (float*)w; w += al(max_chunks * KMAX * 4);
@@ -731,7 +748,8 @@ static int leafnet_carve(const yabt_leafnet_args* p, void* workspace, long long 
   a.chunk_begin = (int*)w; w += al(max_chunks * 4);
   a.chunk_end = (int*)w; w += al(max_chunks * 4);
   a.partial = (double*)w; w += al(max_chunks * NE * 8);
-  a.totals = (double*)w;
+  a.totals = (double*)w; w += al((long long)p->max_nodes * NE * 8);
+  a.env = (float*)w;
   a.max_chunks = (int)max_chunks;
   *out = a;
   return YABT_OK;
@@ -760,14 +778,10 @@ static cudaError_t leafnet_launch(const LeafNetArgs& a, int stage, cudaStream_t 
         count_launches(1);
       }
       k_ln_plan<<<1, 1024, 0, s>>>(a);
-      count_launches(2);
-      break;
-    }
-    case 2: {
       k_ln_elig<<<1, 1024, 0, s>>>(a);
       k_ln_gram<<<(unsigned)a.max_chunks, 256, 0, s>>>(a);
       k_ln_total<<<nblk, 128, 0, s>>>(a);
-      count_launches(3);
+      count_launches(5);
       break;
     }
     default: {
@@ -790,7 +804,7 @@ int yabt_leafnet_fit(const yabt_leafnet_args* p, void* workspace, long long ws_b
   int rc = leafnet_carve(p, workspace, ws_bytes, &a, "yabt_leafnet_fit");
   if (rc) return rc;
   if (p->n <= 0) { set_error("yabt_leafnet_fit: n must be > 0"); return YABT_ERR_ARG; }
-  for (int st = 0; st < 4; ++st) LCUDA(leafnet_launch(a, st, (cudaStream_t)stream));
+  for (int st = 0; st < 3; ++st) LCUDA(leafnet_launch(a, st, (cudaStream_t)stream));
   return YABT_OK;
 }
 
@@ -798,20 +812,23 @@ int yabt_leafnet_stage(const yabt_leafnet_args* p, int stage, void* workspace, l
   LeafNetArgs a;
   int rc = leafnet_carve(p, workspace, ws_bytes, &a, "yabt_leafnet_stage");
   if (rc) return rc;
-  if (stage < 0 || stage > 3) { set_error("yabt_leafnet_stage: stage must be 0..3"); return YABT_ERR_ARG; }
+  if (stage < 0 || stage > 2) { set_error("yabt_leafnet_stage: stage must be 0..2"); return YABT_ERR_ARG; }
   LCUDA(leafnet_launch(a, stage, (cudaStream_t)stream));
   return YABT_OK;
 }
 
-int yabt_leafnet_bufs(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, void** corr, void** counts,
-                      void** totals, int* per_node) {
+int yabt_leafnet_bufs(const yabt_leafnet_args* p, void* workspace, long long ws_bytes, void** stats,
+                      long long* stats_count, void** totals, long long* totals_count, void** envelope,
+                      long long* envelope_count) {
   LeafNetArgs a;
   int rc = leafnet_carve(p, workspace, ws_bytes, &a, "yabt_leafnet_bufs");
   if (rc) return rc;
-  if (corr) *corr = a.corr;
-  if (counts) *counts = a.counts;
+  if (stats) *stats = a.stats;
+  if (stats_count) *stats_count = (long long)p->F + 1 + p->max_nodes;
   if (totals) *totals = a.totals;
-  if (per_node) *per_node = NE;
+  if (totals_count) *totals_count = (long long)p->max_nodes * NE;
+  if (envelope) *envelope = a.env;
+  if (envelope_count) *envelope_count = (long long)p->max_nodes * 2 * KMAX;
   return YABT_OK;
 }
 

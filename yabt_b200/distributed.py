@@ -12,7 +12,7 @@ identical decisions and holds an identical model:
   reference's own draw over the global row count, gathered from the ranks
   that own the rows;
 * column moments for the leaf models: sums, then centred sums of squares;
-* per tree: the max |g| / max h quantisation words (max), every level's
+* per tree: the max |g| / max |h| quantisation words (max), every level's
   smaller-child histograms (exact int64 sums, so split decisions are
   bit-identical to a single-GPU fit on the concatenated rows), and the leaf
   models' statistics (gradient correlations, leaf counts, normal equations,
@@ -71,15 +71,6 @@ class ShardComm:
 
     def min_(self, t: torch.Tensor) -> torch.Tensor:
         return self._reduce(t, self.dist.ReduceOp.MIN)
-
-    def unsigned_max_(self, words: torch.Tensor) -> torch.Tensor:
-        """Max of uint32 words held in an int32 tensor (order-preserving
-        float encodings have the top bit set, so a signed max would be
-        wrong): widened to int64 for the reduction."""
-        t = words.to(torch.int64) & 0xFFFFFFFF
-        self.max_(t)
-        words.copy_(torch.where(t >= 2 ** 31, t - 2 ** 32, t).to(torch.int32))
-        return words
 
     # scalars and gathers -------------------------------------------------
     def int_values(self, v: int) -> list[int]:
@@ -215,7 +206,7 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     small = _view(grower.ws, lib.yabt_grow_small_ptr(h), int(lib.yabt_grow_small_count(h, grower.levels - 1)),
                   torch.int64)
     _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
-    comm.unsigned_max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))
+    comm.max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
     _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
     jobs = 1
     for d in range(grower.levels):
@@ -232,24 +223,26 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
 
 
-def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, lo: torch.Tensor, hi: torch.Tensor,
-                    comm: ShardComm) -> None:
-    """Leaf models of one tree over the rows of every rank (the four stages
-    of yabt_leafnet_stage with the statistics reduced in between)."""
+def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, comm: ShardComm) -> None:
+    """Leaf models of one tree over the rows of every rank: the three stages
+    of yabt_leafnet_stage with the statistics reduced in between."""
     lib = _lib.load()
     s = _lib.stream_ptr()
     ref = ctypes.byref(la)
-    cp, np_, tp, per = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int()
-    _lib.check(lib.yabt_leafnet_bufs(ref, ws.data_ptr(), ws.numel(), ctypes.byref(cp), ctypes.byref(np_),
-                                     ctypes.byref(tp), ctypes.byref(per)), "yabt_leafnet_bufs")
-    maxn = int(la.max_nodes)
-    stage = lambda k: _lib.check(lib.yabt_leafnet_stage(ref, k, ws.data_ptr(), ws.numel(), s), "yabt_leafnet_stage")
+    ptr = [ctypes.c_void_p() for _ in range(3)]
+    cnt = [ctypes.c_longlong() for _ in range(3)]
+    _lib.check(lib.yabt_leafnet_bufs(ref, ws.data_ptr(), ws.numel(), ctypes.byref(ptr[0]), ctypes.byref(cnt[0]),
+                                     ctypes.byref(ptr[1]), ctypes.byref(cnt[1]), ctypes.byref(ptr[2]),
+                                     ctypes.byref(cnt[2])), "yabt_leafnet_bufs")
+    stats = _view(ws, ptr[0].value, cnt[0].value, torch.float64)
+    totals = _view(ws, ptr[1].value, cnt[1].value, torch.float64)
+    env = _view(ws, ptr[2].value, cnt[2].value, torch.float32)
+
+    def stage(k):
+        _lib.check(lib.yabt_leafnet_stage(ref, k, ws.data_ptr(), ws.numel(), s), "yabt_leafnet_stage")
     stage(0)
-    comm.sum_(_view(ws, cp.value, int(la.F) + 1, torch.float64))
+    comm.sum_(stats)
     stage(1)
-    comm.sum_(_view(ws, np_.value, maxn, torch.int32))
+    comm.sum_(totals)
+    comm.max_(env)
     stage(2)
-    comm.sum_(_view(ws, tp.value, maxn * per.value, torch.float64))
-    comm.min_(lo)
-    comm.max_(hi)
-    stage(3)
