@@ -116,7 +116,7 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
       it.begin = c * chunk;
       it.count = (int)min((long long)chunk, p.n - (long long)c * chunk);
       it.unit = u; it.job = 0; it.slot = i;
-      it.pad[0] = it.pad[1] = it.pad[2] = 0;
+      it.used = 0; it.pad[0] = it.pad[1] = 0;
       b.items[i] = it;
     }
   }
@@ -646,7 +646,7 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
       it.begin = sb + c * chunk;
       it.count = min(chunk, sc - c * chunk);
       it.unit = u; it.job = q; it.slot = first + c;
-      it.pad[0] = it.pad[1] = it.pad[2] = 0;
+      it.used = 0; it.pad[0] = it.pad[1] = 0;
       b.items[first + c] = it;
     }
   }

@@ -11,7 +11,8 @@ constexpr int PART_TILE = 4096;       // rows per partition tile
 constexpr int PART_THREADS = 512;     // 8 rows per thread
 constexpr int ITEM_TARGET = 8 * YABT_SMS_HINT;  // histogram work items per level (target)
 constexpr int CHUNK_MIN = 4096;       // rows per histogram item (lower bound)
-constexpr int CHUNK_MAX = 65536;      // rows per item (u32 limb overflow bound)
+constexpr int CHUNK_MAX = 65536;      // rows per item and per flushed segment (u32 limb overflow bound)
+constexpr int RUN_MAX = 16;          // items per claimed run (k_hist)
 constexpr int SCAN_WARPS = 8;         // k_scan: one warp per feature
 
 // leaf row sources
@@ -34,7 +35,8 @@ struct HistItem {       // one histogram work item: rows [begin, begin+count) of
   int unit;
   int job;              // pair index (or 0 for the root)
   int slot;             // partial-histogram slot
-  int pad[3];
+  int used;             // set by k_hist: 1 if the slot holds a flushed partial
+  int pad[2];
 };
 
 struct PartTile {       // one partition tile: rows [begin, end) of active node `pos`

@@ -175,19 +175,19 @@ __device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, const uint
 }
 
 // rows: the active row list (nullptr = identity, row = begin + i)
-// Persistent: one block per SM takes histogram work items from a device
-// counter; each item's shared histogram is zeroed, filled by the warps (each
-// streams a contiguous share of the item's rows) and flushed to its partial slot.
+// Persistent: one block per SM claims runs of consecutive work items from a
+// device counter; the warps stream contiguous shares of each item's rows into
+// a shared histogram that is flushed once per (job, unit) segment of the run.
 template <int S, int LIMBS>
 __global__ void __launch_bounds__(HistPipe<S, LIMBS>::THREADS, 1)
 k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
        const float* __restrict__ g, const float* __restrict__ h,
-       const HistItem* __restrict__ items, const UnitDesc* __restrict__ units,
+       HistItem* __restrict__ items, const UnitDesc* __restrict__ units,
        GrowState* st, unsigned* __restrict__ partials, int level_gate) {
   using Cfg = HistCfg<S, LIMBS>;
   using Pipe = HistPipe<S, LIMBS>;
   extern __shared__ __align__(16) unsigned sh[];
-  __shared__ int s_item;
+  __shared__ int s_a, s_e;
   if (st->level != level_gate || !st->active) return;
   const int nitems = st->n_items;
   const float gs = st->gscale, hs = st->hscale;
@@ -195,36 +195,62 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
   const unsigned sh_s = (unsigned)__cvta_generic_to_shared(sh);
   const unsigned lb = sh_s + lane * 4;                       // word (bin 0, lane) of limb 0
   const unsigned ring = sh_s + Cfg::WORDS * 4 + warp * Pipe::STG * Pipe::STAGE_BYTES;
-  for (;;) {
-    if (threadIdx.x == 0) s_item = atomicAdd(&st->item_counter, 1);
+  auto flush = [&](int seg_item) {
     __syncthreads();
-    const int it = s_item;
-    if (it >= nitems) break;
-    const HistItem item = items[it];
-    const UnitDesc& ud = units[item.unit];
-    for (int i = threadIdx.x * 4; i < Cfg::WORDS; i += blockDim.x * 4)
-      *reinterpret_cast<uint4*>(sh + i) = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    const uint8_t* tb = bins + ud.off;
-    const bool ok0 = ud.feat[0][lane] >= 0 && (ud.width != 16 || lane < 16);
-    const bool ok1 = (S == 2) && ud.nsub > 1 && ud.feat[S == 2 ? 1 : 0][lane] >= 0;
-    const int per = (item.count + nw - 1) / nw;
-    const int w0 = min(item.count, warp * per), w1 = min(item.count, w0 + per);
-    const int* lst = rows ? rows + item.begin : nullptr;
-    const int base = rows ? w0 : item.begin + w0;
-    const bool full = ud.width == 64 && (S == 1 || ud.nsub == 2);
-    if (full)
-      hist_warp<S, LIMBS, 64, true>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
-    else if (ud.width == 64)
-      hist_warp<S, LIMBS, 64, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
-    else if (ud.width == 32)
-      hist_warp<S, LIMBS, 32, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
-    else
-      hist_warp<S, LIMBS, 16, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
-    __syncthreads();
-    unsigned* dst = partials + (size_t)item.slot * Cfg::WORDS;
+    unsigned* dst = partials + (size_t)items[seg_item].slot * Cfg::WORDS;
     for (int i = threadIdx.x * 4; i < Cfg::WORDS; i += blockDim.x * 4)
       *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(sh + i);
+    __syncthreads();
+  };
+  for (;;) {
+    // guided runs: a claim of up to RUN_MAX consecutive items, shrinking as the
+    // level's work runs out so that the blocks finish together
+    if (threadIdx.x == 0) {
+      const int cur = *(volatile int*)&st->item_counter;
+      const int k = max(1, min(RUN_MAX, (nitems - cur) / (int)gridDim.x));
+      const int a = atomicAdd(&st->item_counter, k);
+      s_a = a;
+      s_e = min(a + k, nitems);
+    }
+    __syncthreads();
+    const int a = s_a, e = s_e;
+    if (a >= nitems) break;
+    // consecutive items of one (job, unit) accumulate into one shared histogram
+    // (at most CHUNK_MAX rows, the limb bound) and are flushed once, into the
+    // partial slot of the segment's first item; `used` marks those slots
+    int seg = -1, seg_rows = 0, seg_job = -1, seg_unit = -1;
+    for (int it = a; it < e; ++it) {
+      const HistItem item = items[it];
+      const bool cont = seg >= 0 && item.job == seg_job && item.unit == seg_unit &&
+                        seg_rows + item.count <= CHUNK_MAX;
+      if (!cont) {
+        if (seg >= 0) flush(seg);
+        for (int i = threadIdx.x * 4; i < Cfg::WORDS; i += blockDim.x * 4)
+          *reinterpret_cast<uint4*>(sh + i) = make_uint4(0, 0, 0, 0);
+        __syncthreads();
+        seg = it; seg_rows = 0; seg_job = item.job; seg_unit = item.unit;
+      }
+      if (threadIdx.x == 0) items[it].used = cont ? 0 : 1;
+      seg_rows += item.count;
+      const UnitDesc& ud = units[item.unit];
+      const uint8_t* tb = bins + ud.off;
+      const bool ok0 = ud.feat[0][lane] >= 0 && (ud.width != 16 || lane < 16);
+      const bool ok1 = (S == 2) && ud.nsub > 1 && ud.feat[S == 2 ? 1 : 0][lane] >= 0;
+      const int per = (item.count + nw - 1) / nw;
+      const int w0 = min(item.count, warp * per), w1 = min(item.count, w0 + per);
+      const int* lst = rows ? rows + item.begin : nullptr;
+      const int base = rows ? w0 : item.begin + w0;
+      const bool full = ud.width == 64 && (S == 1 || ud.nsub == 2);
+      if (full)
+        hist_warp<S, LIMBS, 64, true>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+      else if (ud.width == 64)
+        hist_warp<S, LIMBS, 64, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+      else if (ud.width == 32)
+        hist_warp<S, LIMBS, 32, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+      else
+        hist_warp<S, LIMBS, 16, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+    }
+    flush(seg);
   }
 }
 
@@ -263,15 +289,21 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   unsigned long long ac = 0;
   constexpr int UNR = 8;
   int q = 0;
+  // only slots that received a flush (`used`) hold partials; merged items' slots are skipped
   for (; q + UNR <= nit; q += UNR) {
     unsigned lo[UNR], hi[UNR], cn[UNR], hlo[UNR], hhi[UNR];
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      const unsigned* p = partials + (size_t)__ldg(&items[first + q + u].slot) * Cfg::WORDS + woff;
-      lo[u] = __ldg(p);
-      hi[u] = __ldg(p + Cfg::LIMB_STRIDE);
-      if constexpr (LIMBS == 5) { hlo[u] = __ldg(p + 2 * Cfg::LIMB_STRIDE); hhi[u] = __ldg(p + 3 * Cfg::LIMB_STRIDE); }
-      cn[u] = __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE);
+      const HistItem* ip = items + first + q + u;
+      const bool used = __ldg(&ip->used) != 0;
+      const unsigned* p = partials + (size_t)__ldg(&ip->slot) * Cfg::WORDS + woff;
+      lo[u] = used ? __ldg(p) : 0u;
+      hi[u] = used ? __ldg(p + Cfg::LIMB_STRIDE) : 0u;
+      if constexpr (LIMBS == 5) {
+        hlo[u] = used ? __ldg(p + 2 * Cfg::LIMB_STRIDE) : 0u;
+        hhi[u] = used ? __ldg(p + 3 * Cfg::LIMB_STRIDE) : 0u;
+      }
+      cn[u] = used ? __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE) : 0u;
     }
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
@@ -281,7 +313,9 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
     }
   }
   for (; q < nit; ++q) {
-    const unsigned* p = partials + (size_t)__ldg(&items[first + q].slot) * Cfg::WORDS + woff;
+    const HistItem* ip = items + first + q;
+    if (__ldg(&ip->used) == 0) continue;
+    const unsigned* p = partials + (size_t)__ldg(&ip->slot) * Cfg::WORDS + woff;
     ag += (long long)(int)__ldg(p + Cfg::LIMB_STRIDE) * 65536LL + (long long)__ldg(p);
     if constexpr (LIMBS == 5)
       ah += (long long)(int)__ldg(p + 3 * Cfg::LIMB_STRIDE) * 65536LL + (long long)__ldg(p + 2 * Cfg::LIMB_STRIDE);
