@@ -133,8 +133,10 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream);
  * (max, as int32) the two words at yabt_grow_amax_ptr() -- bit patterns of
  * max |g| and max |h| -- after yabt_grow_begin, and sums (int64) the
  * small-child histograms at yabt_grow_small_ptr() between yabt_grow_hist and
- * yabt_grow_split of each level: at most yabt_grow_small_count(level) values,
- * exactly pairs * yabt_grow_small_count(0) (see yabt_grow_level_ptr).     */
+ * yabt_grow_split of each level: at most yabt_grow_small_count(level) int64
+ * words, exactly pairs * yabt_grow_small_count(0) (see yabt_grow_level_ptr).
+ * Per job: the value channels, then the counts two bins per word (low / high
+ * 32 bits; they add without carries while the total row count is < 2^32). */
 int yabt_grow_begin(yabt_grower* g, const yabt_tree_args* a, void* stream);
 int yabt_grow_init(yabt_grower* g, const yabt_tree_args* a, void* stream);
 int yabt_grow_hist(yabt_grower* g, const yabt_tree_args* a, int level, void* stream);

@@ -189,7 +189,7 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
   add("segc0", p.maxa * 4); add("segc1", p.maxa * 4);
   add("gid0", p.maxa * 4); add("gid1", p.maxa * 4);
   add("hist0", p.maxa * HN); add("hist1", p.maxa * HN);
-  add("small", (long long)p.max_pairs * HN);
+  add("small", (long long)p.max_pairs * small_job_words(p.C, F) * 8);
   add("pm0", (long long)p.maxa * F * 4); add("pm1", (long long)p.maxa * F * 4);
   add("best", (long long)p.maxa * F * sizeof(NodeBest));
   add("nbest", (long long)p.maxa * sizeof(NodeBest));
@@ -403,7 +403,7 @@ void* yabt_grow_level_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.
 long long yabt_grow_small_count(const yabt_grower* g, int level) {
   if (!g) return -1;
   long long jobs = level == 0 ? 1 : std::min<long long>(1LL << std::min(level - 1, 30), g->p.max_pairs);
-  return jobs * g->p.C * g->p.F * YABT_NB;
+  return jobs * small_job_words(g->p.C, g->p.F);
 }
 
 int yabt_grow_leaf_rows(yabt_grower* g, void** src, void** begin, void** count, void** fin,

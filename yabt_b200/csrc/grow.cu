@@ -145,7 +145,9 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   const bool fok = !(p.use_fmask && io.fmask && !io.fmask[f]);
   const size_t FB = (size_t)p.F * YABT_NB;
   const size_t HN = (size_t)C * FB;           // int64 per node histogram
-  const long long* sm = b.small + (size_t)job * HN + (size_t)f * YABT_NB + lane * 8;
+  const long long* sjob = b.small + (size_t)job * small_job_words(C, p.F);
+  const long long* sm = sjob + (size_t)f * YABT_NB + lane * 8;
+  const long long* scnt = sjob + (size_t)(C - 1) * FB + (size_t)f * (YABT_NB / 2) + lane * 4;
 
   int nchild, pos_small, pos_other = -1;
   const long long* par = nullptr;
@@ -159,10 +161,21 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   }
   long long vs[C][8];
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
+  for (int c = 0; c < C - 1; ++c) {
     const longlong2* q = reinterpret_cast<const longlong2*>(sm + c * FB);
 #pragma unroll
     for (int i = 0; i < 4; ++i) { longlong2 t = q[i]; vs[c][2 * i] = t.x; vs[c][2 * i + 1] = t.y; }
+  }
+  {
+    const longlong2* q = reinterpret_cast<const longlong2*>(scnt);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const longlong2 t = q[i];
+      vs[C - 1][4 * i + 0] = (long long)((unsigned long long)t.x & 0xffffffffULL);
+      vs[C - 1][4 * i + 1] = (long long)((unsigned long long)t.x >> 32);
+      vs[C - 1][4 * i + 2] = (long long)((unsigned long long)t.y & 0xffffffffULL);
+      vs[C - 1][4 * i + 3] = (long long)((unsigned long long)t.y >> 32);
+    }
   }
   for (int ch = 0; ch < nchild; ++ch) {
     long long v[C][8];

@@ -13,6 +13,13 @@ constexpr int ITEM_TARGET = 8 * YABT_SMS_HINT;  // histogram work items per leve
 constexpr int CHUNK_MIN = 4096;       // rows per histogram item (lower bound)
 constexpr int CHUNK_MAX = 65536;      // rows per item and per flushed segment (u32 limb overflow bound)
 constexpr int RUN_MAX = 16;          // items per claimed run (k_hist)
+
+// int64 words of one job's small-child histogram: C-1 value channels of F x 256
+// bins, then the count channel with two bins per word (per-bin counts stay
+// below 2^32 even summed over ranks, so packed words add without carries)
+__host__ __device__ constexpr long long small_job_words(int C, int F) {
+  return (long long)(C - 1) * F * YABT_NB + (long long)F * (YABT_NB / 2);
+}
 constexpr int SCAN_WARPS = 8;         // k_scan: one warp per feature
 
 // leaf row sources
@@ -117,7 +124,9 @@ struct GrowBufs {
   int* seg_count[2];
   int* act_gid[2];
   long long* hist[2];    // [maxa][C][F][256] int64 full histograms per level parity
-  long long* small;      // [max_pairs][C][F][256] small-child (or root) histograms
+  long long* small;      // [max_pairs][small_job_words(C, F)] small-child (or root) histograms:
+                         // value channels [C-1][F][256], then counts [F][128] with bins
+                         // 2k, 2k+1 packed in the low / high 32 bits of one int64
   float* pathmax[2];     // [maxa][F] max over path features p of imat[p][f]
   NodeBest* best;        // [maxa][F]
   NodeBest* nbest;       // [maxa] chosen split per active node

@@ -328,12 +328,19 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
     tsm[C - 1][j][bl] = (long long)ac;
   }
   __syncthreads();
-  const long long job_base = (long long)job * C * F * YABT_NB;
+  const long long job_base = (long long)job * small_job_words(C, F);
   for (int e = threadIdx.x; e < C * 32 * BPP; e += blockDim.x) {
     const int bl = e % BPP, j = (e / BPP) & 31, c = e / (BPP * 32);
     const int f = ud.feat[sub][j];
     if (f < 0) continue;
-    out[job_base + ((long long)c * F + f) * YABT_NB + part * BPP + bl] = tsm[c][j][bl];
+    if (c < C - 1) {
+      out[job_base + ((long long)c * F + f) * YABT_NB + part * BPP + bl] = tsm[c][j][bl];
+    } else if ((bl & 1) == 0) {   // counts: bins 2k, 2k+1 in one word
+      const unsigned long long lo = (unsigned long long)tsm[c][j][bl] & 0xffffffffULL;
+      const unsigned long long hi = (unsigned long long)tsm[c][j][bl + 1] << 32;
+      out[job_base + (long long)(C - 1) * F * YABT_NB + (long long)f * (YABT_NB / 2) + (part * BPP + bl) / 2] =
+          (long long)(lo | hi);
+    }
   }
 }
 

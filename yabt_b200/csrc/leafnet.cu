@@ -31,7 +31,7 @@ namespace yabt {
 
 constexpr int KMAX = 8;                 // leaf-model inputs (leaf_net_features <= 8)
 constexpr int NE = (KMAX + 1) * (KMAX + 2) / 2 + (KMAX + 1);   // 45 + 9 = 54 accumulators
-constexpr int GRAM_CHUNK = 8192;        // rows per Gram partial
+constexpr int GRAM_CHUNK = 2048;        // rows per Gram partial (small: enough blocks at small n)
 
 struct LeafNetArgs {
   // tree (device)
