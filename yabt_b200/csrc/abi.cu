@@ -193,6 +193,7 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
   add("pm0", (long long)p.maxa * F * 4); add("pm1", (long long)p.maxa * F * 4);
   add("best", (long long)p.maxa * F * sizeof(NodeBest));
   add("nbest", (long long)p.maxa * sizeof(NodeBest));
+  add("nkey", (long long)p.maxa * 8);
   add("tot", (long long)p.maxa * sizeof(NodeTot));
   add("pair_pos", p.max_pairs * 4); add("pair_sil", p.max_pairs * 4);
   add("split_pair", p.maxa * 4); add("split_f", p.maxa * 4); add("split_b", p.maxa * 4);
@@ -243,6 +244,7 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
   b.act_gid[0] = (int*)P("gid0"); b.act_gid[1] = (int*)P("gid1");
   b.hist[0] = (long long*)P("hist0"); b.hist[1] = (long long*)P("hist1");
   b.small = (long long*)P("small");
+  b.node_key = (unsigned long long*)P("nkey");
   b.pathmax[0] = (float*)P("pm0"); b.pathmax[1] = (float*)P("pm1");
   b.best = (NodeBest*)P("best"); b.nbest = (NodeBest*)P("nbest"); b.tot = (NodeTot*)P("tot");
   b.pair_pos = (int*)P("pair_pos"); b.pair_sil = (int*)P("pair_sil");

@@ -80,6 +80,7 @@ __device__ __forceinline__ int item_chunk(long long R, int U) {
 
 __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
   GrowState* st = b.st;
+  for (int m = threadIdx.x; m < p.maxa; m += blockDim.x) b.node_key[m] = 0ULL;
   if (threadIdx.x == 0) {
     st->level = 0; st->active = 1; st->M = 1; st->P = 0; st->n_nodes = 1;
     st->remaining = p.max_leaves - 1; st->part_level = -1; st->plan_level = -1;
@@ -268,6 +269,8 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
       NodeBest nb;
       nb.sel = bsel; nb.gain = bgain; nb.GL = bGL; nb.HL = bHL; nb.CL = bCL; nb.bin = bbin; nb.cl = bcl;
       b.best[(size_t)pos * p.F + f] = nb;
+      // node argmax over features: larger sel, ties -> lower feature
+      atomicMax(&b.node_key[pos], ((unsigned long long)f2ord(bsel) << 32) | (0xffffffffu - (unsigned)f));
       if (f == 0) {
         NodeTot t; t.G = G; t.H = H; t.C = Cn; t.pad = 0; t.c = lt[C - 1];
         b.tot[pos] = t;
@@ -287,30 +290,19 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   if (st->level != level_gate || !st->active) return;
   const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
   const int M = st->M;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __shared__ int s_P, s_ntiles, s_remaining, s_nnodes;
-  // A: per node argmax over features
-  for (int m = warp; m < M; m += nw) {
-    // each lane: first max among its features; then first max across lanes
-    float bs = -INFINITY; int bf = p.F;
-    for (int f = lane; f < p.F; f += 32) {
-      const float s = b.best[(size_t)m * p.F + f].sel;
-      if (s > bs) { bs = s; bf = f; }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      const int of = __shfl_xor_sync(0xffffffffu, bf, o);
-      if (os > bs || (os == bs && of < bf)) { bs = os; bf = of; }
-    }
-    if (bf >= p.F) bf = 0;   // every score -inf: argmax of an all -inf row is index 0
-    if (lane == 0) {
-      NodeBest nb = b.best[(size_t)m * p.F + bf];
-      b.nbest[m] = nb;
-      b.split_f[m] = bf;
-      b.split_b[m] = nb.bin;
-    }
+  // A: per node argmax over features (k_scan left the winner in node_key)
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const int bf = (int)(0xffffffffu - (unsigned)(b.node_key[m] & 0xffffffffULL));
+    const NodeBest nb = b.best[(size_t)m * p.F + bf];
+    b.nbest[m] = nb;
+    b.split_f[m] = bf;
+    b.split_b[m] = nb.bin;
   }
+  __syncthreads();
+  // the next level's scan accumulates into node_key again
+  for (int m = threadIdx.x; m < p.maxa; m += blockDim.x) b.node_key[m] = 0ULL;
   __syncthreads();
   const bool loop_ok = d < p.max_depth && st->remaining > 0;
   const int remaining = st->remaining;

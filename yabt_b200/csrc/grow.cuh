@@ -130,6 +130,7 @@ struct GrowBufs {
   float* pathmax[2];     // [maxa][F] max over path features p of imat[p][f]
   NodeBest* best;        // [maxa][F]
   NodeBest* nbest;       // [maxa] chosen split per active node
+  unsigned long long* node_key;   // [maxa] max over features of (ordered sel << 32 | ~feature)
   NodeTot* tot;          // [maxa]
   int* pair_pos;         // [max_pairs] active position of the parent of pair p
   int* pair_sil;         // [max_pairs] small child is the left one
