@@ -149,6 +149,31 @@ void* yabt_grow_amax_ptr(yabt_grower* g);
  * (the small-child histograms to reduce are then pairs * small_count(0)
  * int64 values), and active = 0 means the tree is complete.              */
 void* yabt_grow_level_ptr(yabt_grower* g);
+
+/* Cross-GPU level reduction over NVLink peer memory for row-sharded growth,
+ * instead of a host-driven all-reduce between yabt_grow_hist and
+ * yabt_grow_split (replaces, like the hooks above, the single-process
+ * histogram of yabt/tree.py:425-452 for sharded rows). Each rank allocates an
+ * exchange buffer (yabt_xchg_alloc: cudaMalloc of bytes + header, zeroed, and
+ * its 64-byte CUDA IPC handle), makes it the grower's small-child histogram
+ * buffer (yabt_grower_set_small(g, buf + yabt_xchg_header_bytes(), bytes)),
+ * shares the handle with the other ranks and maps theirs (yabt_xchg_open).
+ * Then yabt_grow_xreduce(level) after yabt_grow_hist sums the level's
+ * histograms of all ranks in place in every rank's buffer, sized from the
+ * grower's device state (no host synchronisation). `bufs` are the exchange
+ * buffers of ranks 0..nranks-1 as mapped in this process (this rank's own
+ * pointer at index rank); `epoch` must differ between consecutive calls and
+ * be the same on every rank. Ranks must be on distinct GPUs of one node (at
+ * most 8); every wait is bounded, and a timeout sets a device error bit that
+ * the tree's meta reports.                                                */
+long long yabt_xchg_header_bytes(void);
+int yabt_xchg_alloc(long long bytes, void** ptr, void* ipc_handle);
+int yabt_xchg_open(const void* ipc_handle, void** ptr);
+int yabt_xchg_close(void* ptr);
+int yabt_xchg_free(void* ptr);
+int yabt_grower_set_small(yabt_grower* g, void* ptr, long long bytes);
+int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                      void* stream);
 void* yabt_grow_small_ptr(yabt_grower* g);
 long long yabt_grow_small_count(const yabt_grower* g, int level);
 /* Per-leaf row ranges of the last tree (device arrays inside the workspace):

@@ -87,6 +87,13 @@ SIGNATURES = [
     ("yabt_grow_amax_ptr", c_vp, [c_vp]),
     ("yabt_grow_small_ptr", c_vp, [c_vp]),
     ("yabt_grow_level_ptr", c_vp, [c_vp]),
+    ("yabt_xchg_header_bytes", c_ll, []),
+    ("yabt_xchg_alloc", c_int, [c_ll, ctypes.POINTER(c_vp), c_vp]),
+    ("yabt_xchg_open", c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    ("yabt_xchg_close", c_int, [c_vp]),
+    ("yabt_xchg_free", c_int, [c_vp]),
+    ("yabt_grower_set_small", c_int, [c_vp, c_vp, c_ll]),
+    ("yabt_grow_xreduce", c_int, [c_vp, ctypes.POINTER(c_vp), c_int, c_int, c_int, ctypes.c_uint, c_vp]),
     ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
     ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
     ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),

@@ -382,6 +382,9 @@ class Booster:
                     print(f"[{t}] train={float(self.loss.loss(margin, yt)):.5f} val={vl:.5f}")
                 if p.early_stopping_rounds and rounds_since_best >= p.early_stopping_rounds:
                     break
+        if comm is not None and getattr(grower, "_exchange", None) is not None:
+            grower._exchange.close()
+            grower._exchange = None
         self._forest = forest
         self._margin_train = margin
         self.interaction_scores_ = scores

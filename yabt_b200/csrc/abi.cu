@@ -134,6 +134,10 @@ struct yabt_grower {
 
 static long long al(long long x) { return (x + 255) & ~255LL; }
 
+namespace yabt {
+GrowState* grower_state(yabt_grower* g) { return g && g->bound ? g->b.st : nullptr; }
+}  // namespace yabt
+
 extern "C" {
 
 int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int general,
@@ -401,6 +405,17 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
 void* yabt_grow_amax_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->amax_g : nullptr; }
 void* yabt_grow_small_ptr(yabt_grower* g) { return g && g->bound ? (void*)g->b.small : nullptr; }
 void* yabt_grow_level_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->level : nullptr; }
+
+int yabt_grower_set_small(yabt_grower* g, void* ptr, long long bytes) {
+  if (!g || !g->bound || !ptr || ((uintptr_t)ptr & 255)) {
+    set_error("yabt_grower_set_small: needs a bound grower and a 256-byte aligned buffer");
+    return YABT_ERR_ARG;
+  }
+  const long long need = (long long)g->p.max_pairs * small_job_words(g->p.C, g->p.F) * 8;
+  if (bytes < need) { set_error("yabt_grower_set_small: %lld bytes, %lld needed", bytes, need); return YABT_ERR_ARG; }
+  g->b.small = static_cast<long long*>(ptr);
+  return YABT_OK;
+}
 
 long long yabt_grow_small_count(const yabt_grower* g, int level) {
   if (!g) return -1;

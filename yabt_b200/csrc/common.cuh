@@ -46,6 +46,7 @@ enum : unsigned {
   DERR_BAD_INDEX = 1u << 4,
   DERR_NODE_OVERFLOW = 1u << 5,
   DERR_NONFINITE = 1u << 6,
+  DERR_XCHG_TIMEOUT = 1u << 7,    // a cross-GPU exchange gave up waiting for a peer
 };
 
 void set_error(const char* fmt, ...);

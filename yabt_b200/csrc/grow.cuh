@@ -173,4 +173,7 @@ struct TreeIO {
   int* leaf_of_row;          // [n]
 };
 
+// the device state of a bound grower (C ABI handle), or nullptr
+GrowState* grower_state(struct yabt_grower* g);
+
 }  // namespace yabt

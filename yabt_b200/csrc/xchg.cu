@@ -1,0 +1,189 @@
+// Cross-GPU sum of the level histograms over NVLink peer memory.
+//
+// Row-sharded growth needs, at every level, the sum over the ranks of each
+// rank's smaller-child histograms (int64 words). The exchange buffers of all
+// ranks are mapped into every rank's address space (CUDA IPC, plain peer
+// loads and stores -- no multicast objects), and k_xreduce sums them in place
+// with a two-shot scheme: rank r owns slice r of the words, reads that slice
+// from every rank, adds the N values in rank order and stores the sum into
+// every rank's buffer. The word count comes from the grower's device state
+// (pairs split by the previous level), so the host neither waits for the
+// level nor moves a byte more than the level's histograms: this replaces an
+// NCCL all-reduce whose size the host would have to read back first.
+//
+// Ordering: (1) each rank's block 0 tells every rank "my histograms are
+// written" (fence, then a flag store); every block waits for all N flags
+// before reading peers; (2) after its stores, each block fences and counts
+// itself done; the last block tells every rank "your slice r is written" and
+// waits for all N of those flags, so the kernel ends only when this rank's
+// buffer holds the full sums. Every wait is bounded: on timeout the kernel
+// sets an error bit in the grower state and returns.
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/yabt_b200.h"
+#include "grow.cuh"
+
+namespace yabt {
+
+constexpr int XR_MAX = 8;                 // ranks
+constexpr long long XCHG_HEADER = 256;    // bytes before the data words
+constexpr long long XSPIN_LIMIT = 1LL << 24;   // polls of ~64 ns (about 1 s)
+
+struct XHeader {                          // at the start of every rank's exchange buffer
+  unsigned ready[XR_MAX];                 // epoch when rank q's histograms were written
+  unsigned done[XR_MAX];                  // epoch when rank q's slice of this buffer was summed
+  unsigned blocks;                        // blocks of this rank's kernel that finished their stores
+};
+static_assert(sizeof(XHeader) <= XCHG_HEADER, "exchange header");
+
+struct XArgs {
+  char* buf[XR_MAX];                      // every rank's exchange buffer, mapped here
+  int rank, nranks;
+  unsigned epoch;
+  int level;
+  long long per_job;                      // int64 words per job
+};
+
+__device__ __forceinline__ void st_flag(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_flag(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until flags[q] == epoch for every rank q; false on timeout.
+__device__ bool wait_all(const unsigned* flags, int nranks, unsigned epoch) {
+  for (int q = 0; q < nranks; ++q) {
+    long long spins = 0;
+    while (ld_flag(flags + q) != epoch) {
+      if (++spins > XSPIN_LIMIT) return false;
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(512) k_xreduce(XArgs a, GrowState* st) {
+  __shared__ int s_ok, s_last;
+  if (st->level != a.level || !st->active) return;   // the same on every rank
+  const long long jobs = a.level == 0 ? 1 : st->P;
+  const long long words = jobs * a.per_job;
+  XHeader* mine = reinterpret_cast<XHeader*>(a.buf[a.rank]);
+  if (blockIdx.x == 0 && threadIdx.x < a.nranks) {
+    __threadfence_system();                          // this rank's histograms (k_reduce) first
+    st_flag(&reinterpret_cast<XHeader*>(a.buf[threadIdx.x])->ready[a.rank], a.epoch);
+  }
+  if (threadIdx.x == 0) s_ok = wait_all(mine->ready, a.nranks, a.epoch) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) {
+    if (threadIdx.x == 0) atomicOr(&st->err, DERR_XCHG_TIMEOUT);
+    return;
+  }
+  // slice of this rank: words [lo, hi), in pairs of int64
+  const long long lo = words * a.rank / a.nranks & ~1LL;
+  const long long hi = a.rank + 1 == a.nranks ? words : (words * (a.rank + 1) / a.nranks & ~1LL);
+  for (long long i = lo + 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 2LL * gridDim.x * blockDim.x) {
+    const bool pair = i + 1 < hi;
+    long long s0 = 0, s1 = 0;
+    for (int q = 0; q < a.nranks; ++q) {             // rank order: the same sum everywhere
+      const long long* src = reinterpret_cast<const long long*>(a.buf[q] + XCHG_HEADER) + i;
+      if (pair) {
+        const longlong2 v = __ldcv(reinterpret_cast<const longlong2*>(src));
+        s0 += v.x; s1 += v.y;
+      } else {
+        s0 += __ldcv(src);
+      }
+    }
+    for (int q = 0; q < a.nranks; ++q) {
+      long long* dst = reinterpret_cast<long long*>(a.buf[q] + XCHG_HEADER) + i;
+      if (pair) *reinterpret_cast<longlong2*>(dst) = make_longlong2(s0, s1);
+      else *dst = s0;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&mine->blocks, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x == 0) mine->blocks = 0;
+  if (threadIdx.x < a.nranks) {
+    __threadfence_system();
+    st_flag(&reinterpret_cast<XHeader*>(a.buf[threadIdx.x])->done[a.rank], a.epoch);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !wait_all(mine->done, a.nranks, a.epoch)) atomicOr(&st->err, DERR_XCHG_TIMEOUT);
+}
+
+}  // namespace yabt
+
+using namespace yabt;
+
+extern "C" {
+
+long long yabt_xchg_header_bytes(void) { return XCHG_HEADER; }
+
+int yabt_xchg_alloc(long long bytes, void** ptr, void* ipc_handle) {
+  if (bytes <= 0 || !ptr || !ipc_handle) { set_error("yabt_xchg_alloc: bad arguments"); return YABT_ERR_ARG; }
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)(bytes + XCHG_HEADER));
+  if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)(bytes + XCHG_HEADER));
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    set_error("yabt_xchg_alloc: %s", cudaGetErrorString(e));
+    return YABT_ERR_CUDA;
+  }
+  *ptr = p;
+  return YABT_OK;
+}
+
+int yabt_xchg_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) { set_error("yabt_xchg_open: bad arguments"); return YABT_ERR_ARG; }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) { set_error("yabt_xchg_open: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int yabt_xchg_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) { set_error("yabt_xchg_close: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int yabt_xchg_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) { set_error("yabt_xchg_free: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                      void* stream) {
+  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks || level < 0) {
+    set_error("yabt_grow_xreduce: bad arguments (at most %d ranks)", XR_MAX);
+    return YABT_ERR_ARG;
+  }
+  XArgs a;
+  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
+  for (int q = 0; q < nranks; ++q)
+    if (!a.buf[q]) { set_error("yabt_grow_xreduce: missing buffer of rank %d", q); return YABT_ERR_ARG; }
+  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level;
+  a.per_job = yabt_grow_small_count(g, 0);
+  GrowState* st = grower_state(g);
+  if (!st) { set_error("yabt_grow_xreduce: grower not bound"); return YABT_ERR_ARG; }
+  int dev = 0, nsm = YABT_SMS_HINT;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  // one block per SM: every block waits on the flags, so all must be resident
+  k_xreduce<<<nsm, 512, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("yabt_grow_xreduce: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+}  // extern "C"

@@ -41,7 +41,10 @@ class ShardComm:
     reduced in place on the device; with any other backend (gloo) they are
     staged through host memory."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, peer_exchange: bool = True):
+        """``peer_exchange``: sum the level histograms with the library's own
+        NVLink kernel (yabt_grow_xreduce) when every rank has its own GPU on
+        this node and the backend is NCCL; otherwise with all-reduces."""
         import torch.distributed as dist
         if not dist.is_initialized():
             raise RuntimeError("ShardComm needs an initialised torch.distributed process group")
@@ -50,6 +53,12 @@ class ShardComm:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.on_device = dist.get_backend(group) == "nccl"
+        self.peer_exchange = bool(peer_exchange) and self.on_device and 1 < self.world <= 8
+        if self.peer_exchange:
+            import hashlib
+            uuid = str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+            key = int.from_bytes(hashlib.sha1(uuid.encode()).digest()[:7], "little")
+            self.peer_exchange = len(set(self.int_values(key))) == self.world
 
     # in-place reductions -------------------------------------------------
     def _reduce(self, t: torch.Tensor, op) -> torch.Tensor:
@@ -185,11 +194,67 @@ def column_stats(Xfm: torch.Tensor, n_local: int, comm: ShardComm) -> tuple[torc
     return mean, std
 
 
+class PeerExchange:
+    """Every rank's level-histogram exchange buffer, mapped into this process
+    (CUDA IPC over NVLink, plain peer loads and stores), bound to a grower as
+    its small-child histogram buffer. ``reduce(level)`` launches
+    yabt_grow_xreduce: no host synchronisation and exactly the level's bytes.
+    ``close()`` must be called on every rank (it synchronises the ranks)."""
+
+    def __init__(self, grower, comm: ShardComm):
+        self.lib = lib = grower.lib
+        self.grower, self.comm = grower, comm
+        h = grower.h
+        nbytes = int(lib.yabt_grow_small_count(h, 62)) * 8          # the largest level
+        handle = (ctypes.c_char * 64)()
+        own = ctypes.c_void_p()
+        _lib.check(lib.yabt_xchg_alloc(nbytes, ctypes.byref(own), handle), "yabt_xchg_alloc")
+        self.own = own.value
+        hdr = int(lib.yabt_xchg_header_bytes())
+        dev = torch.device("cuda", torch.cuda.current_device())
+        mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(dev)
+        parts = [torch.empty_like(mine) for _ in range(comm.world)]
+        comm.dist.all_gather(parts, mine, group=comm.group)
+        self.opened = []
+        ptrs = []
+        for q, t in enumerate(parts):
+            if q == comm.rank:
+                ptrs.append(self.own)
+                continue
+            hq = (ctypes.c_char * 64).from_buffer_copy(bytes(t.cpu().numpy()))
+            pq = ctypes.c_void_p()
+            _lib.check(lib.yabt_xchg_open(hq, ctypes.byref(pq)), "yabt_xchg_open")
+            self.opened.append(pq.value)
+            ptrs.append(pq.value)
+        self.bufs = (ctypes.c_void_p * comm.world)(*ptrs)
+        _lib.check(lib.yabt_grower_set_small(h, self.own + hdr, nbytes), "yabt_grower_set_small")
+        self.epoch = 0
+        comm.dist.barrier(group=comm.group)
+
+    def reduce(self, level: int) -> None:
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        _lib.check(self.lib.yabt_grow_xreduce(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
+                                              self.epoch, _lib.stream_ptr()), "yabt_grow_xreduce")
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.comm.dist.barrier(group=self.comm.group)     # no rank still reads or writes a peer buffer
+        for p in self.opened:
+            self.lib.yabt_xchg_close(p)
+        self.opened = []
+        self.comm.dist.barrier(group=self.comm.group)
+        if self.own:
+            self.lib.yabt_xchg_free(self.own)
+            self.own = None
+
+
 def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     """One tree over the rows of every rank: the grower's step API with the
     quantisation words and each level's smaller-child histograms summed
-    between the steps. The level state (pairs, active) of the previous split
-    is copied to host memory while the next level's histogram kernels run, so
+    between the steps. With the peer exchange the sums are one kernel per
+    level that reads the level's size from the device. Otherwise they are
+    all-reduces: the level state (pairs, active) of the previous split is
+    copied to host memory while the next level's histogram kernels run, so
     each all-reduce covers exactly that level's histograms and the loop stops
     with the tree; the state is identical on every rank, so every rank makes
     the same collective calls."""
@@ -202,12 +267,23 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
         grower._level_event = torch.cuda.Event()
     info, ev = grower._level_host, grower._level_event
     state = _view(grower.ws, lib.yabt_grow_level_ptr(h), 4, torch.int32)
-    per_job = int(lib.yabt_grow_small_count(h, 0))
-    small = _view(grower.ws, lib.yabt_grow_small_ptr(h), int(lib.yabt_grow_small_count(h, grower.levels - 1)),
-                  torch.int64)
     _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
     comm.max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
     _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
+    xchg = getattr(grower, "_exchange", None)
+    if xchg is None and comm.peer_exchange:
+        xchg = grower._exchange = PeerExchange(grower, comm)
+    if xchg is not None:
+        # the NVLink exchange sizes itself from the device state: no host waits
+        for d in range(grower.levels):
+            _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
+            xchg.reduce(d)
+            _lib.check(lib.yabt_grow_split(h, ref, d, s), "yabt_grow_split")
+        _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
+        return
+    per_job = int(lib.yabt_grow_small_count(h, 0))
+    small = _view(grower.ws, lib.yabt_grow_small_ptr(h), int(lib.yabt_grow_small_count(h, grower.levels - 1)),
+                  torch.int64)
     jobs = 1
     for d in range(grower.levels):
         _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
