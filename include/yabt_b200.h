@@ -124,6 +124,11 @@ typedef struct {
   float* gate_scale;
   int32_t* leaf_of_row;           /* [n] final leaf (node id) of every row */
   int32_t* meta;                  /* [4] n_nodes, depth, device error bits, levels run */
+  /* optional input (device): the feature-major (F, n) bin matrix
+   * (yabt_bin_transform fm_out), or NULL; when given, the row partition reads
+   * each row's split bin from it (one byte per row instead of a sector of
+   * the tiled matrix)                                                      */
+  const uint8_t* bins_fm;
 } yabt_tree_args;
 
 /* Grow one tree (single device): all levels, no host synchronisation. */
@@ -234,10 +239,12 @@ int yabt_bin_fit_static(const float* Xfm, long long n, int F, const int32_t* sam
                         int max_bins, float* medians, float* edges, int32_t* edge_cnt, float* scales,
                         void* stream);
 /* NaN -> median in Xfm (in place), bins = #{edges < x} into the tiled layout
- * (and, if plain_out != NULL, the plain (n, F) matrix).
+ * (and, if plain_out != NULL, the plain (n, F) matrix; if fm_out != NULL, a
+ * feature-major (F, n) copy, which the grower's row partition reads).
  * Replaces Binner.transform / impute (yabt/binning.py:97-124).           */
 int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, const float* edges,
-                       const int32_t* edge_cnt, uint8_t* tiled, uint8_t* plain_out, void* stream);
+                       const int32_t* edge_cnt, uint8_t* tiled, uint8_t* plain_out, uint8_t* fm_out,
+                       void* stream);
 
 /* ------------------------------------------------------------------ neural leaves
  * Ridge-linear leaf models of one grown tree (fit_leaf_networks with

@@ -31,7 +31,7 @@ class TreeArgs(ctypes.Structure):
         ("reg_lambda", c_float), ("gamma", c_float), ("min_child_weight", c_float),
         ("learning_rate", c_float), ("interaction_boost", c_float), ("min_samples_leaf", ctypes.c_int32),
         ("feature", c_vp), ("threshold", c_vp), ("left", c_vp), ("right", c_vp), ("value", c_vp),
-        ("gate_scale", c_vp), ("leaf_of_row", c_vp), ("meta", c_vp),
+        ("gate_scale", c_vp), ("leaf_of_row", c_vp), ("meta", c_vp), ("bins_fm", c_vp),
     ]
 
 
@@ -109,7 +109,7 @@ SIGNATURES = [
     ("yabt_bin_median_final", c_int, [c_int, c_vp, c_ll, c_vp, c_vp]),
     ("yabt_bin_median_bufs", c_int, [c_int, c_vp, ctypes.POINTER(c_vp), ctypes.POINTER(c_ll), ctypes.POINTER(c_vp)]),
     ("yabt_bin_fit_edges", c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp]),
-    ("yabt_bin_transform", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    ("yabt_bin_transform", c_int, [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_leafnet_workspace_bytes", c_ll, [c_ll, c_int, c_int]),
     ("yabt_leafnet_fit", c_int, [ctypes.POINTER(LeafNetArgs), c_vp, c_ll, c_vp]),
     ("yabt_leafnet_stage", c_int, [ctypes.POINTER(LeafNetArgs), c_int, c_vp, c_ll, c_vp]),

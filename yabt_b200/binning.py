@@ -106,19 +106,24 @@ class Binner:
         return self.fit_device(Xfm, n)
 
     # ------------------------------------------------------------------ transform
-    def transform_device(self, Xfm: torch.Tensor, n: int, plain: bool = False):
+    def transform_device(self, Xfm: torch.Tensor, n: int, plain: bool = False, feature_major: bool = False):
         """Bins of a feature-major (F, n) device matrix. Imputes NaN in place.
-        Returns (tiled bin matrix, plain (n, F) uint8 or None)."""
+        Returns (tiled bin matrix, plain (n, F) uint8 or None), plus the
+        feature-major (F, n) uint8 bins when ``feature_major``."""
         assert self._dev is not None, "Binner not fitted"
         lib = _lib.load()
         F = Xfm.shape[0]
         med, edges, ecnt, _ = self._dev
         tiled = torch.empty(int(lib.yabt_bin_matrix_bytes(n, F)), dtype=torch.uint8, device=Xfm.device)
         pl = torch.empty(n, F, dtype=torch.uint8, device=Xfm.device) if plain else None
+        fm = torch.empty(F, n, dtype=torch.uint8, device=Xfm.device) if feature_major else None
         _lib.check(lib.yabt_bin_transform(Xfm.data_ptr(), n, F, med.data_ptr(), edges.data_ptr(),
                                           ecnt.data_ptr(), tiled.data_ptr(),
-                                          pl.data_ptr() if pl is not None else None, _lib.stream_ptr()),
+                                          pl.data_ptr() if pl is not None else None,
+                                          fm.data_ptr() if fm is not None else None, _lib.stream_ptr()),
                    "yabt_bin_transform")
+        if feature_major:
+            return tiled, pl, fm
         return tiled, pl
 
     def transform(self, X, device: str = "cuda") -> torch.Tensor:

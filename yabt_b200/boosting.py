@@ -182,7 +182,8 @@ class DeviceData:
             self.binner = Binner(max_bins).fit_device(self.Xfm, n)
         else:
             self.binner = Binner(max_bins).fit_device_sharded(self.Xfm, n, comm)
-        self.bins, _ = self.binner.transform_device(self.Xfm, n)   # imputes Xfm in place
+        # imputes Xfm in place; the feature-major copy feeds the row partition
+        self.bins, _, self.bins_fm = self.binner.transform_device(self.Xfm, n, feature_major=True)
         if comm is None:
             self.col_mean = torch.empty(F, dtype=torch.float32, device=device)
             self.col_std = torch.empty(F, dtype=torch.float32, device=device)
@@ -326,7 +327,8 @@ class Booster:
             out = dict(feature=forest.feature[t], threshold=forest.threshold[t], left=forest.left[t],
                        right=forest.right[t], value=forest.value[t], gate_scale=forest.gate[t],
                        leaf_of_row=leaf_of_row, meta=forest.meta[t])
-            a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost)
+            a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost,
+                            bins_fm=data.bins_fm)
             if comm is None:
                 grower.grow(a)
             else:

@@ -340,6 +340,7 @@ static int fill_io(yabt_grower* g, const yabt_tree_args* a, TreeIO* io) {
   io->feature = (long long*)a->feature; io->threshold = a->threshold;
   io->left = (long long*)a->left; io->right = (long long*)a->right;
   io->value = a->value; io->gate = a->gate_scale; io->leaf_of_row = a->leaf_of_row;
+  io->bins_fm = a->bins_fm;
   return YABT_OK;
 }
 

@@ -346,7 +346,7 @@ k_quantiles(const unsigned* __restrict__ keys, long long P, int max_bins, float*
 __global__ void __launch_bounds__(256)
 k_transform(float* __restrict__ Xfm, long long n, int F, const float* __restrict__ medians,
             const float* __restrict__ edges, const int* __restrict__ ecnt, uint8_t* __restrict__ tiled,
-            uint8_t* __restrict__ plain_out) {
+            uint8_t* __restrict__ plain_out, uint8_t* __restrict__ fm_out) {
   __shared__ float se[32][256];
   __shared__ int sc[32];
   __shared__ uint8_t sb[64][36];
@@ -369,6 +369,7 @@ k_transform(float* __restrict__ Xfm, long long n, int F, const float* __restrict
     int lo = 0, hi = sc[ff];
     while (lo < hi) { const int mid = (lo + hi) >> 1; if (se[ff][mid] < x) lo = mid + 1; else hi = mid; }
     sb[lane][ff] = (uint8_t)lo;
+    if (fm_out) fm_out[(long long)(f0 + ff) * n + r] = (uint8_t)lo;   // feature-major copy
   }
   __syncthreads();
   // write: thread -> (row, feature) pairs, byte addresses from the tiled layout
@@ -601,7 +602,8 @@ int yabt_bin_fit_edges(const float* Xs, long long nq, int F, int max_bins, void*
 }
 
 int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, const float* edges,
-                       const int32_t* edge_cnt, uint8_t* tiled, uint8_t* plain_out, void* stream) {
+                       const int32_t* edge_cnt, uint8_t* tiled, uint8_t* plain_out, uint8_t* fm_out,
+                       void* stream) {
   if (!Xfm || n < 0 || F <= 0 || !medians || !edges || !edge_cnt || !tiled) {
     set_error("yabt_bin_transform: bad arguments");
     return YABT_ERR_ARG;
@@ -615,7 +617,7 @@ int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, con
   }
   BCUDA(cudaMemsetAsync(tiled, 0, (size_t)bytes, s));
   dim3 grid((unsigned)((n + 63) / 64), (unsigned)((F + 31) / 32));
-  k_transform<<<grid, 256, 0, s>>>(Xfm, n, F, medians, edges, edge_cnt, tiled, plain_out);
+  k_transform<<<grid, 256, 0, s>>>(Xfm, n, F, medians, edges, edge_cnt, tiled, plain_out, fm_out);
   count_launches(1);
   BCUDA(cudaGetLastError());
   return YABT_OK;

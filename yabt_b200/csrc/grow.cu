@@ -494,13 +494,16 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     }
     const int f = b.split_f[m];
     const unsigned thr = (unsigned)b.split_b[m];
+    // the row's bin of the split feature: one byte of the feature-major copy,
+    // else a byte of the row's slab in the tiled matrix
     const FeatAddr fa = b.faddr[f];
-    const uint8_t* col = io.bins + fa.off + fa.pos;
+    const uint8_t* col = io.bins_fm ? io.bins_fm + (size_t)f * p.n : io.bins + fa.off + fa.pos;
+    const size_t stride = io.bins_fm ? 1 : (size_t)fa.width;
     bool lf[8];
     unsigned bal[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      lf[i] = ok[i] && (unsigned)__ldg(col + (size_t)row[i] * fa.width) <= thr;
+      lf[i] = ok[i] && (unsigned)__ldg(col + (size_t)row[i] * stride) <= thr;
       bal[i] = __ballot_sync(0xffffffffu, lf[i]);
       if (lane == 0) s_wc[i][warp] = __popc(bal[i]);
     }

@@ -171,6 +171,7 @@ struct TreeIO {
   float* value;
   float* gate;
   int* leaf_of_row;          // [n]
+  const uint8_t* bins_fm;    // feature-major (F, n) bins, or nullptr (partition reads the tiled matrix)
 };
 
 // the device state of a bound grower (C ABI handle), or nullptr

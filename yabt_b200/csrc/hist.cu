@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(RED_THREADS)
 k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_first,
          const int* __restrict__ job_nitems, const HistItem* __restrict__ items,
          const UnitDesc* __restrict__ units, GrowState* st, long long* __restrict__ out,
-         int F, int U, int level_gate) {
+         int F, int U, int level_gate, int igroups) {
   using Cfg = HistCfg<S, LIMBS>;
   constexpr int C = (LIMBS == 5) ? 3 : 2;
   constexpr int BPP = YABT_NB / RED_PARTS;     // bins per part (16)
@@ -274,6 +274,7 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   if (st->level != level_gate || !st->active) return;
   const int njobs = (level_gate == 0) ? 1 : st->P;
   int b = blockIdx.x;
+  const int grp = b % igroups; b /= igroups;
   const int part = b % RED_PARTS; b /= RED_PARTS;
   const int sub = b % S; b /= S;
   const int unit = b % U;
@@ -281,8 +282,13 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   if (job >= njobs) return;
   const UnitDesc& ud = units[unit];
   if (sub >= ud.nsub) return;
-  const int first = job_first[job * U + unit];
-  const int nit = job_nitems[job * U + unit];
+  // item group grp of igroups (levels with few jobs split their items so that
+  // enough blocks run; the groups' sums meet in int64 atomics)
+  const int nall = job_nitems[job * U + unit];
+  const int per = (nall + igroups - 1) / igroups;
+  const int first = job_first[job * U + unit] + grp * per;
+  const int nit = max(0, min(nall - grp * per, per));
+  if (nit == 0 && igroups > 1) return;   // nothing to add
   const int w = threadIdx.x;                               // (bin-in-part, lane)
   const size_t woff = (size_t)sub * YABT_NB * 32 + (size_t)part * BPP * 32 + w;
   long long ag = 0, ah = 0;
@@ -333,32 +339,46 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
     const int bl = e % BPP, j = (e / BPP) & 31, c = e / (BPP * 32);
     const int f = ud.feat[sub][j];
     if (f < 0) continue;
+    long long* dst;
+    long long v;
     if (c < C - 1) {
-      out[job_base + ((long long)c * F + f) * YABT_NB + part * BPP + bl] = tsm[c][j][bl];
-    } else if ((bl & 1) == 0) {   // counts: bins 2k, 2k+1 in one word
+      dst = out + job_base + ((long long)c * F + f) * YABT_NB + part * BPP + bl;
+      v = tsm[c][j][bl];
+    } else if ((bl & 1) == 0) {   // counts: bins 2k, 2k+1 in one word (no carry between the halves)
       const unsigned long long lo = (unsigned long long)tsm[c][j][bl] & 0xffffffffULL;
       const unsigned long long hi = (unsigned long long)tsm[c][j][bl + 1] << 32;
-      out[job_base + (long long)(C - 1) * F * YABT_NB + (long long)f * (YABT_NB / 2) + (part * BPP + bl) / 2] =
-          (long long)(lo | hi);
+      dst = out + job_base + (long long)(C - 1) * F * YABT_NB + (long long)f * (YABT_NB / 2) + (part * BPP + bl) / 2;
+      v = (long long)(lo | hi);
+    } else {
+      continue;
     }
+    if (igroups == 1) *dst = v;
+    else atomicAdd(reinterpret_cast<unsigned long long*>(dst), (unsigned long long)v);
   }
 }
 
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
                                 int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist) {
   const int* rows = d == 0 ? nullptr : b.rows[d & 1];
+  // levels with at most a few jobs split each job's items over several reduce
+  // blocks, which add into a zeroed histogram
+  const int igroups = std::max(1, 8 / jobs);
+  if (igroups > 1) {
+    const cudaError_t e = cudaMemsetAsync(b.small, 0, (size_t)jobs * small_job_words(p.C, p.F) * 8, s);
+    if (e != cudaSuccess) return e;
+  }
   if (!p.general) {
     k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
     if (after_hist) cudaEventRecord(after_hist, s);
-    k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS, RED_THREADS, 0, s>>>(b.partials, b.job_first, b.job_nitems,
-                                                              b.items, b.units, b.st, b.small, p.F, p.U, d);
+    k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
   } else {
     k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
     if (after_hist) cudaEventRecord(after_hist, s);
-    k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS, RED_THREADS, 0, s>>>(b.partials, b.job_first, b.job_nitems,
-                                                              b.items, b.units, b.st, b.small, p.F, p.U, d);
+    k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
   }
   count_launches(2);
   return cudaGetLastError();

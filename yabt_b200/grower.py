@@ -84,9 +84,13 @@ class Grower:
     def args(self, bins: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor | None,
              edges: EdgePack, params: TreeParams, out: dict,
              feature_mask: torch.Tensor | None = None,
-             interaction: torch.Tensor | None = None, interaction_boost: float = 0.5) -> _lib.TreeArgs:
+             interaction: torch.Tensor | None = None, interaction_boost: float = 0.5,
+             bins_fm: torch.Tensor | None = None) -> _lib.TreeArgs:
+        """``bins_fm``: optional feature-major (F, n) copy of the bins, read by
+        the row partition."""
         a = _lib.TreeArgs()
         a.bins = bins.data_ptr()
+        a.bins_fm = bins_fm.data_ptr() if bins_fm is not None else None
         a.grad = grad.data_ptr()
         a.hess = hess.data_ptr() if (hess is not None and self.general) else None
         a.edges, a.edge_off, a.edge_cnt = edges.values.data_ptr(), edges.off.data_ptr(), edges.cnt.data_ptr()
