@@ -253,14 +253,19 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
 }
 
 // One block (8 warps) per chunk of a leaf's rows. Each warp stages 32-row
-// batches through shared memory (lane k gathers row k's record; the next
-// batch is prefetched into registers while the current one is consumed),
-// normalises x, tracks the raw-x envelope, and lane e accumulates Gram /
-// rhs entries e and e+32 in fp64 over the rows in order. Warps are reduced in
-// order, so the chunk partial is deterministic.
-__global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
+// batches through shared memory as float64 rows (lane k gathers row k's record
+// and writes x1 = (x_norm[K], 1), h and -g; the next batch is prefetched into
+// registers while the current one is consumed) and tracks the raw-x envelope.
+// Lane e accumulates entries e and e+32 of the normal equations as
+// w_a * (w_b * w_c) over staged slots (a, b, c): M_ab = x1_a (x1_b h) and
+// b_a = x1_a (1 * -g) -- the reference's operation order -- with no branches;
+// even and odd rows go to separate accumulators (two independent chains) that
+// are added at the end. Warps are reduced in order: the chunk partial is
+// deterministic.
+constexpr int SROW = KMAX + 4;            // staged doubles per row: x1[KMAX + 1], h, -g, pad
+__global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
   __shared__ double sp[8][NE];
-  __shared__ float stage[8][32][REC];
+  __shared__ double stage[8][32][SROW];
   __shared__ float smin[8][KMAX], smax[8][KMAX];
   const int c = blockIdx.x;
   if (c >= a.flags[2]) return;
@@ -278,22 +283,24 @@ __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
     mu[k] = k < K ? a.col_mean[f] : 0.f;
     sd[k] = k < K ? fmaxf(a.col_std[f], 1e-6f) : 1.f;
   }
-  int ea[2], eb[2];
+  // staged slots: x1_k at k (k < K), 1 at K, h at KMAX + 1, -g at KMAX + 2
+  constexpr int S_H = KMAX + 1, S_NG = KMAX + 2;
+  int ia[2], ib[2], ic[2];
   bool ev[2];
   const int ntri = D * (D + 1) / 2;
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
     const int e = lane + 32 * q;
     ev[q] = e < ntri + D;
-    int ia = 0, ib = 0;
-    if (e < ntri) {
+    if (e < ntri) {                      // M[row][row + rem]
       int rem = e, row = 0;
       while (rem >= D - row) { rem -= D - row; ++row; }
-      ia = row; ib = row + rem;
-    } else { ia = e - ntri; ib = -1; }
-    ea[q] = ia; eb[q] = ib;
+      ia[q] = row; ib[q] = row + rem; ic[q] = S_H;
+    } else {                             // rhs entry e - ntri
+      ia[q] = ev[q] ? e - ntri : 0; ib[q] = K; ic[q] = S_NG;
+    }
   }
-  double acc[2] = {0.0, 0.0};
+  double acc0[2] = {0.0, 0.0}, acc1[2] = {0.0, 0.0};
   float mn[KMAX], mx[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) { mn[k] = INFINITY; mx[k] = -INFINITY; }
@@ -312,37 +319,37 @@ __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
   for (int p0 = w0; p0 < w1; p0 += 32) {
     const int nb = min(32, w1 - p0);
     {
-      // stage this lane's row: normalised x, g, h; envelope of raw x
-      float xr[KMAX] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-      float* st = stage[warp][lane];
+      const float xr[KMAX] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+      double* st = stage[warp][lane];
       if (lane < nb) {
 #pragma unroll
         for (int k = 0; k < KMAX; ++k) {
           if (k < K) { mn[k] = fminf(mn[k], xr[k]); mx[k] = fmaxf(mx[k], xr[k]); }
-          st[k] = __fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]);
+          st[k] = (double)__fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]);
         }
-        st[KMAX] = n2.x; st[KMAX + 1] = n2.y;
+        st[K] = 1.0;                     // bias input (K <= KMAX; slots K+1.. of x1 unused)
+        st[S_H] = (double)n2.y;
+        st[S_NG] = -(double)n2.x;
       }
     }
     __syncwarp();
     fetch(p0 + 32);   // next batch in flight while this one is consumed
     if (elig) {
-      for (int r = 0; r < nb; ++r) {
-        const float* st = stage[warp][r];
-        const double hh = (double)st[KMAX + 1], gg = (double)st[KMAX];
+      int r = 0;
+      for (; r + 1 < nb; r += 2) {
+        const double* s0 = stage[warp][r];
+        const double* s1 = stage[warp][r + 1];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          if (!ev[q]) continue;
-          const double xa = ea[q] < K ? (double)st[ea[q]] : 1.0;
-          if (eb[q] >= 0) {
-            const double xb = eb[q] < K ? (double)st[eb[q]] : 1.0;
-            // M_ab += x1_a * (x1_b * h)   (yabt/neural_leaves.py:71,82)
-            acc[q] = __dadd_rn(acc[q], __dmul_rn(xa, __dmul_rn(xb, hh)));
-          } else {
-            // b_a += -(x1_a * g)          (yabt/neural_leaves.py:72,83)
-            acc[q] = __dadd_rn(acc[q], -__dmul_rn(xa, gg));
-          }
+          acc0[q] = __dadd_rn(acc0[q], __dmul_rn(s0[ia[q]], __dmul_rn(s0[ib[q]], s0[ic[q]])));
+          acc1[q] = __dadd_rn(acc1[q], __dmul_rn(s1[ia[q]], __dmul_rn(s1[ib[q]], s1[ic[q]])));
         }
+      }
+      if (r < nb) {
+        const double* s0 = stage[warp][r];
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          acc0[q] = __dadd_rn(acc0[q], __dmul_rn(s0[ia[q]], __dmul_rn(s0[ib[q]], s0[ic[q]])));
       }
     }
     __syncwarp();
@@ -359,7 +366,7 @@ __global__ void __launch_bounds__(256) k_ln_gram(LeafNetArgs a) {
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
     const int e = lane + 32 * q;
-    if (e < NE) sp[warp][e] = ev[q] ? acc[q] : 0.0;
+    if (e < NE) sp[warp][e] = ev[q] ? __dadd_rn(acc0[q], acc1[q]) : 0.0;
   }
   __syncthreads();
   if (threadIdx.x < NE) {
