@@ -163,7 +163,7 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
     if (t.wide && p.S == 1) {
       for (int k0 = 0; k0 < 2; ++k0) {
         UnitDesc u; memset(&u, 0, sizeof(u));
-        u.off = t.off; u.width = t.width; u.wide = 1; u.k0 = k0; u.nsub = 1;
+        u.off = t.off; u.width = t.width; u.wide = 1; u.k0 = k0; u.nsub = 1; u.rep = 1; u.lw = 32;
         for (int j = 0; j < 32; ++j) { u.feat[0][j] = t.f0 + 32 * k0 + j; u.feat[1][j] = -1; }
         g->units.push_back(u);
       }
@@ -171,8 +171,14 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
       UnitDesc u; memset(&u, 0, sizeof(u));
       u.off = t.off; u.width = t.width; u.wide = t.wide; u.k0 = 0;
       u.nsub = t.wide ? 2 : 1;
+      u.rep = 1; u.lw = 32;
+      if (t.width == 16) {            // 16-wide tail tile: several rows per reduction
+        u.rep = t.nfeat <= 8 ? 4 : 2;
+        u.lw = 32 / u.rep;
+      }
       for (int j = 0; j < 32; ++j) {
-        u.feat[0][j] = j < std::min(t.nfeat, 32) ? t.f0 + j : -1;
+        const int jj = j % u.lw;        // lanes of one row hold features 0 .. lw-1
+        u.feat[0][j] = jj < std::min(t.nfeat, 32) ? t.f0 + jj : -1;
         u.feat[1][j] = (t.wide && 32 + j < t.nfeat) ? t.f0 + 32 + j : -1;
       }
       g->units.push_back(u);

@@ -33,6 +33,8 @@ struct UnitDesc {
   int wide;       // 64-wide interleaved tile
   int k0;         // byte (0/1) of a wide tile handled by this unit when S == 1
   int nsub;       // subs actually present (1 or 2)
+  int rep;        // narrow 16-wide tiles: rows per shared-memory reduction (1, 2 or 4);
+  int lw;         //   lanes per row (32 / rep); lane l handles feature l % lw of row l / lw
   int feat[2][32];
 };
 

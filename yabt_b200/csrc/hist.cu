@@ -174,6 +174,68 @@ __device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, const uint
   cp_wait<0>();
 }
 
+// A 16-wide tail tile with at most 16 real features: lane l takes feature
+// l % LW of row l / LW, so one shared-memory reduction covers REP = 32 / LW
+// rows of the stage (the tile's histogram is kept REP times, one copy per
+// lane group, and k_reduce adds the copies). Same staging as hist_warp.
+template <int S, int LIMBS, int REP>
+__device__ __forceinline__ void hist_warp_narrow(unsigned lb, unsigned ring, const uint8_t* __restrict__ tb,
+                                                 const int* __restrict__ lst, int base, int nrow,
+                                                 const float* __restrict__ g, const float* __restrict__ h,
+                                                 float gs, float hs, bool okf, int lane) {
+  using Pipe = HistPipe<S, LIMBS>;
+  constexpr int TW = 16, SB = Pipe::STAGE_BYTES, RPS = Pipe::RPS, STG = Pipe::STG;
+  constexpr int LW = 32 / REP;
+  static_assert(RPS % REP == 0, "stage rows");
+  const bool copier = lane < RPS;
+  const int nst = (nrow + RPS - 1) / RPS;
+  auto rid_of = [&](int s) -> int {
+    const int k = s * RPS + lane;
+    if (!copier || k >= nrow) return -1;
+    return lst ? __ldg(lst + base + k) : base + k;
+  };
+  auto copy = [&](int s, int r) {
+    if (r >= 0) cp_async16s(ring + (s % STG) * SB + lane * 64, tb + (size_t)r * TW);
+  };
+  float gq[STG], hq[STG];
+#pragma unroll
+  for (int s = 0; s < STG - 1; ++s) {
+    const int r = rid_of(s);
+    gq[s] = r >= 0 ? __ldg(g + r) : 0.f;
+    hq[s] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    if (s < nst) copy(s, r);
+    cp_commit();
+  }
+  int rnext = rid_of(STG - 1);
+  const int rsub = lane / LW, byte = lane % LW;
+  for (int s = 0; s < nst; ++s) {
+    const int r = rnext;
+    rnext = rid_of(s + STG);
+    gq[STG - 1] = r >= 0 ? __ldg(g + r) : 0.f;
+    hq[STG - 1] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    if (s + STG - 1 < nst) copy(s + STG - 1, r);
+    cp_commit();
+    cp_wait<STG - 1>();
+    __syncwarp();
+    const int vgl = __float2int_rn(gq[0] * gs);
+    const int vhl = (LIMBS == 5) ? __float2int_rn(hq[0] * hs) : 0;
+    const unsigned stg = ring + (s % STG) * SB;
+    const int nr = min(RPS, nrow - s * RPS);
+#pragma unroll
+    for (int it = 0; it < RPS / REP; ++it) {
+      const int q = it * REP + rsub;                   // stage row of this lane
+      const int vg = __shfl_sync(0xffffffffu, vgl, q);
+      const int vh = (LIMBS == 5) ? __shfl_sync(0xffffffffu, vhl, q) : 0;
+      const unsigned b = lds_u8(stg + q * 64 + byte);
+      acc_row<S, LIMBS, false>(lb, b, 0u, okf && q < nr, false, vg, vh);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int t = 0; t < STG - 1; ++t) { gq[t] = gq[t + 1]; hq[t] = hq[t + 1]; }
+  }
+  cp_wait<0>();
+}
+
 // rows: the active row list (nullptr = identity, row = begin + i)
 // Persistent: one block per SM claims runs of consecutive work items from a
 // device counter; the warps stream contiguous shares of each item's rows into
@@ -247,6 +309,10 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
         hist_warp<S, LIMBS, 64, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
       else if (ud.width == 32)
         hist_warp<S, LIMBS, 32, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+      else if (ud.rep == 4)
+        hist_warp_narrow<S, LIMBS, 4>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.feat[0][lane] >= 0, lane);
+      else if (ud.rep == 2)
+        hist_warp_narrow<S, LIMBS, 2>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.feat[0][lane] >= 0, lane);
       else
         hist_warp<S, LIMBS, 16, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
     }
@@ -338,15 +404,20 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   for (int e = threadIdx.x; e < C * 32 * BPP; e += blockDim.x) {
     const int bl = e % BPP, j = (e / BPP) & 31, c = e / (BPP * 32);
     const int f = ud.feat[sub][j];
-    if (f < 0) continue;
+    if (f < 0 || j >= ud.lw) continue;   // narrow tiles: lanes j, j+lw, ... are copies of one feature
     long long* dst;
     long long v;
+    auto val = [&](int bb) {          // sum of the lane copies of feature f
+      long long t = 0;
+      for (int k = j; k < 32; k += ud.lw) t += tsm[c][k][bb];
+      return t;
+    };
     if (c < C - 1) {
       dst = out + job_base + ((long long)c * F + f) * YABT_NB + part * BPP + bl;
-      v = tsm[c][j][bl];
+      v = val(bl);
     } else if ((bl & 1) == 0) {   // counts: bins 2k, 2k+1 in one word (no carry between the halves)
-      const unsigned long long lo = (unsigned long long)tsm[c][j][bl] & 0xffffffffULL;
-      const unsigned long long hi = (unsigned long long)tsm[c][j][bl + 1] << 32;
+      const unsigned long long lo = (unsigned long long)val(bl) & 0xffffffffULL;
+      const unsigned long long hi = (unsigned long long)val(bl + 1) << 32;
       dst = out + job_base + (long long)(C - 1) * F * YABT_NB + (long long)f * (YABT_NB / 2) + (part * BPP + bl) / 2;
       v = (long long)(lo | hi);
     } else {
