@@ -1,0 +1,113 @@
+"""The NVLink level exchange (yabt_grow_xreduce) on one GPU, without faulting
+or hanging it.
+
+1. A two-rank exchange whose second rank never arrives: the first rank's
+   kernel polls the peer's "histograms written" flag, gives up after its
+   bounded wait (about a second), sets the exchange-timeout bit in the tree's
+   error word and returns; the host reads the bit and the context stays
+   usable.
+2. A one-rank exchange (the kernel's own flags only) leaves the level's
+   histograms unchanged, so a tree grown with it equals a tree grown without.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+XCHG_TIMEOUT_BIT = 1 << 7
+
+
+def _setup(n=5000, F=12, seed=0):
+    from yabt_b200.grower import EdgePack, Grower, pack_bins
+    from yabt_b200.tree import TreeParams
+    rng = np.random.default_rng(seed)
+    binned = torch.from_numpy(rng.integers(0, 40, size=(n, F)).astype(np.uint8)).cuda()
+    grad = torch.from_numpy(rng.normal(size=n).astype(np.float32)).cuda()
+    hess = torch.ones(n, device="cuda")
+
+    class _B:   # edges: bin b <-> threshold b
+        edges_ = [torch.arange(39, dtype=torch.float32) for _ in range(F)]
+        scales_ = torch.ones(F)
+    gr = Grower(n, F, 15, 5, False, "cuda")
+    ep = EdgePack(list(_B.edges_), _B.scales_, "cuda")
+    out = gr.new_outputs()
+    a = gr.args(pack_bins(binned), grad, hess, ep, TreeParams(max_leaves=15, max_depth=5), out)
+    return gr, a, out
+
+
+def _xchg_buffers(gr, count):
+    from yabt_b200 import _lib
+    lib = gr.lib
+    nbytes = int(lib.yabt_grow_small_count(gr.h, 62)) * 8
+    bufs = []
+    for _ in range(count):
+        p, hnd = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        _lib.check(lib.yabt_xchg_alloc(nbytes, ctypes.byref(p), hnd), "yabt_xchg_alloc")
+        bufs.append(p.value)
+    return bufs, nbytes
+
+
+def test_exchange_wait_times_out_and_reports():
+    from yabt_b200 import _lib
+    gr, a, out = _setup()
+    lib = gr.lib
+    s = _lib.stream_ptr()
+    (b0, b1), nbytes = _xchg_buffers(gr, 2)
+    hdr = int(lib.yabt_xchg_header_bytes())
+    try:
+        _lib.check(lib.yabt_grower_set_small(gr.h, b0 + hdr, nbytes), "set_small")
+        ref = ctypes.byref(a)
+        _lib.check(lib.yabt_grow_begin(gr.h, ref, s), "begin")
+        _lib.check(lib.yabt_grow_init(gr.h, ref, s), "init")
+        _lib.check(lib.yabt_grow_hist(gr.h, ref, 0, s), "hist")
+        bufs = (ctypes.c_void_p * 2)(b0, b1)
+        # rank 0 of 2; rank 1 (buffer b1) never runs, so its flag is never set
+        _lib.check(lib.yabt_grow_xreduce(gr.h, bufs, 0, 2, 0, 1, s), "xreduce")
+        _lib.check(lib.yabt_grow_end(gr.h, ref, s), "end")
+        torch.cuda.synchronize()
+        assert int(out["meta"][2].item()) & XCHG_TIMEOUT_BIT
+        # the context is still usable: an ordinary tree grows cleanly afterwards
+        gr2, a2, out2 = _setup(seed=1)
+        gr2.grow(a2)
+        torch.cuda.synchronize()
+        assert int(out2["meta"][2].item()) == 0
+    finally:
+        torch.cuda.synchronize()
+        lib.yabt_xchg_free(b0)
+        lib.yabt_xchg_free(b1)
+
+
+def test_single_rank_exchange_is_identity():
+    from yabt_b200 import _lib
+    gr_ref, a_ref, out_ref = _setup(seed=2)
+    gr_ref.grow(a_ref)
+    gr, a, out = _setup(seed=2)
+    lib = gr.lib
+    s = _lib.stream_ptr()
+    (b0,), nbytes = _xchg_buffers(gr, 1)
+    hdr = int(lib.yabt_xchg_header_bytes())
+    try:
+        _lib.check(lib.yabt_grower_set_small(gr.h, b0 + hdr, nbytes), "set_small")
+        ref = ctypes.byref(a)
+        bufs = (ctypes.c_void_p * 1)(b0)
+        _lib.check(lib.yabt_grow_begin(gr.h, ref, s), "begin")
+        _lib.check(lib.yabt_grow_init(gr.h, ref, s), "init")
+        for d in range(gr.levels):
+            _lib.check(lib.yabt_grow_hist(gr.h, ref, d, s), "hist")
+            _lib.check(lib.yabt_grow_xreduce(gr.h, bufs, 0, 1, d, d + 1, s), "xreduce")
+            _lib.check(lib.yabt_grow_split(gr.h, ref, d, s), "split")
+        _lib.check(lib.yabt_grow_end(gr.h, ref, s), "end")
+        torch.cuda.synchronize()
+        assert int(out["meta"][2].item()) == 0
+        nn = int(out_ref["meta"][0].item())
+        assert int(out["meta"][0].item()) == nn > 1
+        for k in ("feature", "threshold", "left", "right", "value"):      # the tree's nodes
+            np.testing.assert_array_equal(out[k][:nn].cpu().numpy(), out_ref[k][:nn].cpu().numpy(), err_msg=k)
+        np.testing.assert_array_equal(out["leaf_of_row"].cpu().numpy(), out_ref["leaf_of_row"].cpu().numpy())
+    finally:
+        torch.cuda.synchronize()
+        lib.yabt_xchg_free(b0)
