@@ -131,7 +131,13 @@ typedef struct {
   const uint8_t* bins_fm;
 } yabt_tree_args;
 
-/* Grow one tree (single device): all levels, no host synchronisation. */
+/* Grow one tree (single device). The host stops queuing levels once the tree
+ * is complete: after each level's split the level state is copied to pinned
+ * host memory and read three levels later, so the GPU keeps three levels
+ * queued while the host waits. yabt_grower_set_level_wait(g, 0) queues every
+ * level without waiting instead (for callers that interleave several growers
+ * on several streams from one host thread).                              */
+int yabt_grower_set_level_wait(yabt_grower* g, int wait);
 int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream);
 
 /* Step-wise driving for row-sharded multi-GPU growth: the caller reduces

@@ -87,6 +87,7 @@ SIGNATURES = [
     ("yabt_grow_amax_ptr", c_vp, [c_vp]),
     ("yabt_grow_small_ptr", c_vp, [c_vp]),
     ("yabt_grow_level_ptr", c_vp, [c_vp]),
+    ("yabt_grower_set_level_wait", c_int, [c_vp, c_int]),
     ("yabt_xchg_header_bytes", c_ll, []),
     ("yabt_xchg_alloc", c_int, [c_ll, ctypes.POINTER(c_vp), c_vp]),
     ("yabt_xchg_open", c_int, [c_vp, ctypes.POINTER(c_vp)]),

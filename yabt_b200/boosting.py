@@ -244,6 +244,15 @@ class Booster:
         ``comm`` (a ``distributed.ShardComm``): X and y hold this rank's rows of
         a row-sharded training set; every rank must call ``fit`` with the same
         parameters and ends with the same model."""
+        for _ in self.fit_steps(X, y, eval_set, data, tree_callback, comm):
+            pass
+        return self
+
+    def fit_steps(self, X, y, eval_set=None, data: DeviceData | None = None, tree_callback=None, comm=None):
+        """``fit`` as a generator: yields the tree index after queuing each
+        tree's launches on the current CUDA stream (callers can interleave
+        several boosters on several streams); the model is complete when the
+        generator is exhausted."""
         p = self.p
         _check_supported(p)
         if comm is not None and (eval_set is not None or p.min_split_gain_rel > 0.0):
@@ -283,6 +292,7 @@ class Booster:
                         gamma=p.gamma, min_child_weight=p.min_child_weight,
                         min_samples_leaf=p.min_samples_leaf, learning_rate=p.learning_rate)
         grower = Grower(n, F, p.max_leaves, p.max_depth, general, dev)
+        grower.set_level_wait(getattr(self, "_level_wait", True))
         self.grower_ = grower
         K = min(p.leaf_net_features, F) if p.neural_leaves else 0
         if p.neural_leaves and not 1 <= K <= 8:
@@ -384,6 +394,7 @@ class Booster:
                     print(f"[{t}] train={float(self.loss.loss(margin, yt)):.5f} val={vl:.5f}")
                 if p.early_stopping_rounds and rounds_since_best >= p.early_stopping_rounds:
                     break
+            yield t
         if comm is not None and getattr(grower, "_exchange", None) is not None:
             grower._exchange.close()
             grower._exchange = None
@@ -408,7 +419,6 @@ class Booster:
                 tr.leaf_net_hi = forest.hi[t, :k, :K]
             self.trees.append(tr)
         self._packed = None
-        return self
 
     # ------------------------------------------------------------------ predict
     def _predict_trees(self, forest: Forest, t0: int, t1: int, X: torch.Tensor, base: float, n_nodes):

@@ -130,7 +130,16 @@ struct yabt_grower {
   // carve offsets
   struct Off { const char* name; long long bytes; long long off; };
   std::vector<Off> offs;
+  // yabt_grow_tree stops launching levels once a level reports the tree
+  // complete: the level state is copied to pinned host memory after each
+  // split and read LEVEL_LOOKAHEAD levels later (the GPU keeps that many
+  // levels queued, so the read rarely waits on work it could be doing)
+  int* host_state = nullptr;               // [LEVEL_SLOTS][4] pinned
+  cudaEvent_t lvl_ev[8] = {};
+  int level_wait = 1;                      // 0: queue every level without waiting
 };
+
+static constexpr int LEVEL_SLOTS = 8, LEVEL_LOOKAHEAD = 3;
 
 static long long al(long long x) { return (x + 255) & ~255LL; }
 
@@ -279,7 +288,11 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
 }
 
 int yabt_grower_destroy(yabt_grower* g) {
-  if (g) for (auto e : g->ev) cudaEventDestroy(e);
+  if (g) {
+    for (auto e : g->ev) cudaEventDestroy(e);
+    for (auto e : g->lvl_ev) if (e) cudaEventDestroy(e);
+    if (g->host_state) cudaFreeHost(g->host_state);
+  }
   delete g;
   return YABT_OK;
 }
@@ -402,9 +415,23 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   int rc;
   if ((rc = yabt_grow_begin(g, a, stream))) return rc;
   if ((rc = yabt_grow_init(g, a, stream))) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!g->host_state) {
+    CUDA_TRY(cudaHostAlloc((void**)&g->host_state, sizeof(int) * 4 * LEVEL_SLOTS, cudaHostAllocDefault));
+    for (auto& e : g->lvl_ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
   for (int d = 0; d < g->p.levels_max; ++d) {
     if ((rc = yabt_grow_hist(g, a, d, stream))) return rc;
     if ((rc = yabt_grow_split(g, a, d, stream))) return rc;
+    if (!g->level_wait) continue;
+    const int slot = d % LEVEL_SLOTS;
+    CUDA_TRY(cudaMemcpyAsync(g->host_state + 4 * slot, &g->b.st->level, 4 * sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaEventRecord(g->lvl_ev[slot], s));
+    if (d >= LEVEL_LOOKAHEAD) {
+      const int old = (d - LEVEL_LOOKAHEAD) % LEVEL_SLOTS;
+      CUDA_TRY(cudaEventSynchronize(g->lvl_ev[old]));
+      if (!g->host_state[4 * old + 1]) break;     // active == 0: later levels would be no-ops
+    }
   }
   return yabt_grow_end(g, a, stream);
 }
@@ -412,6 +439,12 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
 void* yabt_grow_amax_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->amax_g : nullptr; }
 void* yabt_grow_small_ptr(yabt_grower* g) { return g && g->bound ? (void*)g->b.small : nullptr; }
 void* yabt_grow_level_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->level : nullptr; }
+
+int yabt_grower_set_level_wait(yabt_grower* g, int wait) {
+  if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
+  g->level_wait = wait ? 1 : 0;
+  return YABT_OK;
+}
 
 int yabt_grower_set_small(yabt_grower* g, void* ptr, long long bytes) {
   if (!g || !g->bound || !ptr || ((uintptr_t)ptr & 255)) {

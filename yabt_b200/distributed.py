@@ -34,6 +34,7 @@ import torch
 from . import _lib
 
 QUANTILE_SAMPLE = 200_000
+LOOKAHEAD = 3         # levels the GPU keeps queued while the host checks for a complete tree
 
 
 class ShardComm:
@@ -274,11 +275,25 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     if xchg is None and comm.peer_exchange:
         xchg = grower._exchange = PeerExchange(grower, comm)
     if xchg is not None:
-        # the NVLink exchange sizes itself from the device state: no host waits
+        # the NVLink exchange sizes itself from the device state; the host reads
+        # each level's state LOOKAHEAD levels later (the GPU keeps that many
+        # levels queued) and stops launching once the tree is complete
+        if not hasattr(grower, "_level_ring"):
+            grower._level_ring = [(torch.cuda.Event(), torch.zeros(4, dtype=torch.int32).pin_memory())
+                                  for _ in range(8)]
+        ring = grower._level_ring
         for d in range(grower.levels):
             _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
             xchg.reduce(d)
             _lib.check(lib.yabt_grow_split(h, ref, d, s), "yabt_grow_split")
+            ev_d, host_d = ring[d % 8]
+            host_d.copy_(state, non_blocking=True)
+            ev_d.record()
+            if d >= LOOKAHEAD:
+                ev_o, host_o = ring[(d - LOOKAHEAD) % 8]
+                ev_o.synchronize()
+                if not int(host_o[1]):           # identical on every rank
+                    break
         _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
         return
     per_job = int(lib.yabt_grow_small_count(h, 0))

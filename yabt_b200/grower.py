@@ -111,6 +111,11 @@ class Grower:
         _lib.check(self.lib.yabt_grow_tree(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
                    "yabt_grow_tree")
 
+    def set_level_wait(self, wait: bool) -> None:
+        """Whether growing a tree may wait on the device to stop queuing levels
+        once the tree is complete (off: every level is queued, no host waits)."""
+        _lib.check(self.lib.yabt_grower_set_level_wait(self.h, 1 if wait else 0), "yabt_grower_set_level_wait")
+
     def set_timing(self, max_launches: int) -> None:
         """Record CUDA events around up to max_launches histogram launches."""
         _lib.check(self.lib.yabt_grower_set_timing(self.h, int(max_launches)), "yabt_grower_set_timing")

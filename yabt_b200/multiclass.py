@@ -19,19 +19,44 @@ class MulticlassBooster:
         self.boosters_: list[Booster] = []
         self.classes_: np.ndarray | None = None
 
-    def fit(self, X, y, eval_set=None) -> "MulticlassBooster":
+    def fit(self, X, y, eval_set=None, round_callback=None) -> "MulticlassBooster":
+        """One boosting round = one tree per class. The class boosters run on
+        their own CUDA streams, interleaved tree by tree, so one class's small
+        per-level kernels overlap another's histograms. ``round_callback(r)``,
+        if given, is called after round r's launches are queued."""
         self.classes_ = np.unique(y)
         dev = torch.device(self.params.resolve_device())
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         data = DeviceData(X, self.params.max_bins, dev)
-        self.boosters_ = []
+        main = torch.cuda.current_stream(dev)
+        self.boosters_, steps, streams = [], [], []
         for c in self.classes_:
             yb = (np.asarray(y) == c).astype(np.float32)
             ev = None
             if eval_set is not None:
                 ev = (eval_set[0], (np.asarray(eval_set[1]) == c).astype(np.float32))
             b = Booster(self.params, LogLoss())
-            b.fit(X, yb, eval_set=ev, data=data)
+            b._level_wait = False                 # one host thread feeds every stream: never block on one
+            st = torch.cuda.Stream(dev)
+            st.wait_stream(main)                  # the shared device data is ready
             self.boosters_.append(b)
+            steps.append(b.fit_steps(X, yb, eval_set=ev, data=data))
+            streams.append(st)
+        live = list(range(len(steps)))
+        r = 0
+        while live:
+            for i in list(live):
+                with torch.cuda.stream(streams[i]):
+                    try:
+                        next(steps[i])
+                    except StopIteration:
+                        live.remove(i)
+            if round_callback is not None and live:
+                round_callback(r, streams)
+            r += 1
+        for st in streams:
+            main.wait_stream(st)
         return self
 
     def predict_margin(self, X) -> np.ndarray:
