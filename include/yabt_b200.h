@@ -199,6 +199,10 @@ int yabt_grow_leaf_rows(yabt_grower* g, void** src, void** begin, void** count,
 
 /* X (n, F) row-major float32 -> Xfm (F, n) feature-major. */
 int yabt_transpose(const float* X, long long n, int F, float* Xfm, void* stream);
+/* A block of m rows into a larger feature-major matrix: Xfm[f * ld + r] =
+ * X[r * F + f] for r < m (pass Xfm + first row; used to transpose host data
+ * chunk by chunk while the next chunk is being copied in).                 */
+int yabt_transpose_block(const float* X, long long m, int F, float* Xfm, long long ld, void* stream);
 long long yabt_bin_fit_workspace_bytes(long long n, int F, long long nq);
 /* Medians over all rows; edges / scales from the sample rows sample_idx[nq]
  * (NULL: rows 0..nq-1). edges is [F][255] (first edge_cnt[f] valid).

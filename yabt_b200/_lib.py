@@ -98,6 +98,7 @@ SIGNATURES = [
     ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
     ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
     ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),
+    ("yabt_transpose_block", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_vp]),
     ("yabt_hist_build_workspace_bytes", c_ll, [c_ll, c_int, c_int]),
     ("yabt_hist_build", c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_int, c_int, c_int, c_vp, c_vp, c_vp,
                                 c_ll, c_vp]),

@@ -40,6 +40,48 @@ def to_device_f32(X, device) -> torch.Tensor:
     return t.to(device, non_blocking=True)
 
 
+def to_feature_major(X, device, chunk_bytes: int = 64 << 20) -> torch.Tensor:
+    """(F, n) float32 device matrix of a row-major (n, F) input. Host input is
+    copied in chunks through two device staging buffers on a copy stream, each
+    chunk transposed while the next one is in flight, so no (n, F) device
+    copy of the whole matrix is made."""
+    lib = _lib.load()
+    dev = _device(device)
+    if isinstance(X, torch.Tensor) and X.device.type == "cuda":
+        Xd = X.to(device=dev, dtype=torch.float32).contiguous()
+        n, F = Xd.shape
+        Xfm = torch.empty(F, n, dtype=torch.float32, device=dev)
+        _lib.check(lib.yabt_transpose(Xd.data_ptr(), n, F, Xfm.data_ptr(), _lib.stream_ptr()), "yabt_transpose")
+        return Xfm
+    Xh = X if isinstance(X, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(np.asarray(X, dtype=np.float32)))
+    Xh = Xh.to(torch.float32).contiguous()
+    n, F = Xh.shape
+    Xfm = torch.empty(F, n, dtype=torch.float32, device=dev)
+    if n == 0:
+        return Xfm
+    rows = max(1, min(n, chunk_bytes // (4 * F)))
+    main = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    stage = [torch.empty(rows, F, dtype=torch.float32, device=dev) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    for i, r0 in enumerate(range(0, n, rows)):
+        m = min(rows, n - r0)
+        k = i & 1
+        with torch.cuda.stream(copy):
+            if i >= 2:
+                copy.wait_event(freed[k])        # the transpose of chunk i-2 is done with this buffer
+            stage[k][:m].copy_(Xh[r0:r0 + m], non_blocking=True)
+            copied[k].record(copy)
+        main.wait_event(copied[k])
+        _lib.check(lib.yabt_transpose_block(stage[k].data_ptr(), m, F, Xfm.data_ptr() + 4 * r0, n,
+                                            _lib.stream_ptr()), "yabt_transpose_block")
+        freed[k].record(main)
+    for t in stage:
+        t.record_stream(copy)
+    return Xfm
+
+
 class Binner:
     """Quantile-bins float features into uint8 codes; same semantics as the
     reference: bin(x) = #{e_j < x}, so bin(x) <= b  <=>  x <= edges[b]."""

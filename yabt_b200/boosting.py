@@ -24,7 +24,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .binning import Binner, to_device_f32
+from .binning import Binner, to_device_f32, to_feature_major
 from .grower import Grower
 from .tree import Tree, TreeParams
 
@@ -170,13 +170,9 @@ class DeviceData:
         """``comm`` (a ``distributed.ShardComm``): X holds this rank's rows of a
         row-sharded training set; binning and column moments cover every rank."""
         lib = _lib.load()
-        Xd = to_device_f32(X, device)
-        self.n, self.F = int(Xd.shape[0]), int(Xd.shape[1])
+        self.Xfm = to_feature_major(X, device)
+        self.F, self.n = int(self.Xfm.shape[0]), int(self.Xfm.shape[1])
         n, F = self.n, self.F
-        self.Xfm = torch.empty(F, n, dtype=torch.float32, device=device)
-        _lib.check(lib.yabt_transpose(Xd.data_ptr(), n, F, self.Xfm.data_ptr(), _lib.stream_ptr()),
-                   "yabt_transpose")
-        del Xd
         self.comm = comm
         if comm is None:
             self.binner = Binner(max_bins).fit_device(self.Xfm, n)

@@ -29,7 +29,8 @@ __device__ __forceinline__ unsigned fkey(float x) { return isnan(x) ? KEY_NAN : 
 
 // ---------------------------------------------------------------- transpose
 // X (n, F) row-major -> Xfm (F, n)
-__global__ void k_transpose(const float* __restrict__ X, long long n, int F, float* __restrict__ Xfm) {
+// rows [0, n) of X (n, F) row-major -> Xfm[f * ld + r]
+__global__ void k_transpose(const float* __restrict__ X, long long n, int F, float* __restrict__ Xfm, long long ld) {
   __shared__ float t[32][33];
   const long long r0 = (long long)blockIdx.x * 32;
   const int f0 = blockIdx.y * 32;
@@ -43,7 +44,7 @@ __global__ void k_transpose(const float* __restrict__ X, long long n, int F, flo
   for (int i = ty; i < 32; i += 8) {
     const int f = f0 + i;
     const long long r = r0 + tx;
-    if (f < F && r < n) Xfm[(long long)f * n + r] = t[tx][i];
+    if (f < F && r < n) Xfm[(long long)f * ld + r] = t[tx][i];
   }
 }
 
@@ -421,7 +422,17 @@ int yabt_transpose(const float* X, long long n, int F, float* Xfm, void* stream)
   if (!X || !Xfm || n < 0 || F <= 0) { set_error("yabt_transpose: bad arguments"); return YABT_ERR_ARG; }
   if (n == 0) return YABT_OK;
   dim3 grid((unsigned)((n + 31) / 32), (unsigned)((F + 31) / 32));
-  k_transpose<<<grid, 256, 0, (cudaStream_t)stream>>>(X, n, F, Xfm);
+  k_transpose<<<grid, 256, 0, (cudaStream_t)stream>>>(X, n, F, Xfm, n);
+  count_launches(1);
+  BCUDA(cudaGetLastError());
+  return YABT_OK;
+}
+
+int yabt_transpose_block(const float* X, long long m, int F, float* Xfm, long long ld, void* stream) {
+  if (!X || !Xfm || m < 0 || F <= 0 || ld < m) { set_error("yabt_transpose_block: bad arguments"); return YABT_ERR_ARG; }
+  if (m == 0) return YABT_OK;
+  dim3 grid((unsigned)((m + 31) / 32), (unsigned)((F + 31) / 32));
+  k_transpose<<<grid, 256, 0, (cudaStream_t)stream>>>(X, m, F, Xfm, ld);
   count_launches(1);
   BCUDA(cudaGetLastError());
   return YABT_OK;
