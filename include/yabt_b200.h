@@ -129,6 +129,12 @@ typedef struct {
    * each row's split bin from it (one byte per row instead of a sector of
    * the tiled matrix)                                                      */
   const uint8_t* bins_fm;
+  /* optional input (device): grow the tree on these rows only (row
+   * subsampling, yabt/boosting.py:374-376), n_root of them, or NULL (all n
+   * rows; n_root is then ignored). leaf_of_row is written for these rows;
+   * yabt_grow_apply_all routes every row.                                  */
+  const int32_t* root_rows;
+  long long n_root;
 } yabt_tree_args;
 
 /* Grow one tree (single device). The host stops queuing levels once the tree
@@ -138,6 +144,18 @@ typedef struct {
  * level without waiting instead (for callers that interleave several growers
  * on several streams from one host thread).                              */
 int yabt_grower_set_level_wait(yabt_grower* g, int wait);
+/* After yabt_grow_tree: leaf_of_row for every row 0..n-1 (not only the root
+ * rows), routed by the split bins through the feature-major bins (required);
+ * Tree.apply of yabt/tree.py:82-116 on the training rows.                 */
+int yabt_grow_apply_all(yabt_grower* g, const yabt_tree_args* a, void* stream);
+/* Stable grouping of rows by leaf (node id < num_leaves <= 4096): rows[begin[l]
+ * .. begin[l] + count[l]) = the rows i with leaf_of_row[i] == l, increasing;
+ * the leaf-model ranges over every row after growth on a row sample
+ * (yabt/boosting.py:486-497 fits leaf models on all rows). Rows with an
+ * out-of-range leaf are skipped.                                           */
+long long yabt_group_rows_workspace_bytes(long long n, int num_leaves);
+int yabt_group_rows(const int32_t* leaf_of_row, long long n, int num_leaves, void* workspace, long long ws_bytes,
+                    int32_t* begin, int32_t* count, int32_t* rows, void* stream);
 int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream);
 
 /* Step-wise driving for row-sharded multi-GPU growth: the caller reduces

@@ -90,6 +90,8 @@ class BoostParams:
     leaf_net_features: int = 8
     leaf_net_l2: float = 1.0
     leaf_net_min_samples: int = 50
+    subsample: float = 1.0
+    seed: int = 0
 
 
 class Booster:
@@ -117,12 +119,24 @@ class Booster:
         tp = TreeParams(p.max_leaves, p.max_depth, p.reg_lambda, p.gamma,
                         p.min_child_weight, p.min_samples_leaf, p.learning_rate)
         col_mean, col_std = column_stats(Xraw)
+        # the reference's CPU generator (yabt/boosting.py:286) drives row subsampling
+        import torch
+        gen = torch.Generator(device="cpu").manual_seed(p.seed)
         self.records = []
         for t in range(p.n_estimators if n_trees is None else n_trees):
             g, h = self.loss.grad_hess(margin, y)
             imat = det.normalized() if det is not None else None
-            tree, leaf, _ = grow_levelwise(binned, g, h, self.binner.edges_, self.binner.scales_,
-                                           tp, None, imat, p.interaction_boost)
+            if p.subsample < 1.0:
+                # yabt/boosting.py:374-376, 392-393: grow on rows[:m] of a permutation,
+                # then route every row through the tree (:486)
+                m = int(n * p.subsample)
+                rows = torch.randperm(n, generator=gen)[:m].numpy()
+                tree, _, _ = grow_levelwise(binned[rows], g[rows], h[rows], self.binner.edges_,
+                                            self.binner.scales_, tp, None, imat, p.interaction_boost)
+                leaf = tree.apply(Xraw)
+            else:
+                tree, leaf, _ = grow_levelwise(binned, g, h, self.binner.edges_, self.binner.scales_,
+                                               tp, None, imat, p.interaction_boost)
             if p.neural_leaves:
                 tree = fit_leaf_networks(tree, Xraw, y, margin, self.loss, p, leaf,
                                          col_mean, col_std)

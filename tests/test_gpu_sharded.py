@@ -35,10 +35,10 @@ def _data():
     return X, y
 
 
-def _params(neural: bool):
+def _params(neural: bool, subsample: float = 1.0):
     from yabt_b200.boosting import BoostParams
     return BoostParams(n_estimators=4, max_leaves=15, max_depth=5, learning_rate=0.3, neural_leaves=neural,
-                       leaf_net_min_samples=50, min_samples_leaf=20)
+                       leaf_net_min_samples=50, min_samples_leaf=20, subsample=subsample)
 
 
 def _summary(b, Xt):
@@ -50,7 +50,7 @@ def _summary(b, Xt):
                 scales=scales.cpu().numpy(), trees=trees, pred=b.predict_margin(Xt))
 
 
-def _worker(rank, world, port, backend, neural, q):
+def _worker(rank, world, port, backend, neural, q, subsample=1.0):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -64,7 +64,7 @@ def _worker(rank, world, port, backend, neural, q):
         X, y = _data()
         off = sum(SPLIT[:rank])
         sl = slice(off, off + SPLIT[rank])
-        b = Booster(_params(neural), MSELoss())
+        b = Booster(_params(neural, subsample), MSELoss())
         b.fit(X[sl], y[sl], comm=ShardComm())
         torch.cuda.synchronize()
         q.put((rank, _summary(b, X[:1500])))
@@ -75,13 +75,13 @@ def _worker(rank, world, port, backend, neural, q):
         dist.destroy_process_group()
 
 
-def _run_sharded(backend, neural):
+def _run_sharded(backend, neural, subsample=1.0):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q, subsample)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in range(2))
@@ -92,10 +92,10 @@ def _run_sharded(backend, neural):
     return res
 
 
-def _single(neural):
+def _single(neural, subsample=1.0):
     from yabt_b200.boosting import Booster, MSELoss
     X, y = _data()
-    b = Booster(_params(neural), MSELoss())
+    b = Booster(_params(neural, subsample), MSELoss())
     b.fit(X, y)
     return _summary(b, X[:1500])
 
@@ -130,6 +130,11 @@ def _compare(res, ref, neural):
 @pytest.mark.parametrize("neural", [False, True])
 def test_two_ranks_one_gpu_gloo(neural):
     _compare(_run_sharded("gloo", neural), _single(neural), neural)
+
+
+def test_two_ranks_subsample_gloo():
+    """Row subsampling draws over the global rows: each rank grows on its share."""
+    _compare(_run_sharded("gloo", False, 0.6), _single(False, 0.6), False)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")

@@ -32,6 +32,7 @@ class TreeArgs(ctypes.Structure):
         ("learning_rate", c_float), ("interaction_boost", c_float), ("min_samples_leaf", ctypes.c_int32),
         ("feature", c_vp), ("threshold", c_vp), ("left", c_vp), ("right", c_vp), ("value", c_vp),
         ("gate_scale", c_vp), ("leaf_of_row", c_vp), ("meta", c_vp), ("bins_fm", c_vp),
+        ("root_rows", c_vp), ("n_root", c_ll),
     ]
 
 
@@ -88,6 +89,9 @@ SIGNATURES = [
     ("yabt_grow_small_ptr", c_vp, [c_vp]),
     ("yabt_grow_level_ptr", c_vp, [c_vp]),
     ("yabt_grower_set_level_wait", c_int, [c_vp, c_int]),
+    ("yabt_grow_apply_all", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_group_rows_workspace_bytes", c_ll, [c_ll, c_int]),
+    ("yabt_group_rows", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp]),
     ("yabt_xchg_header_bytes", c_ll, []),
     ("yabt_xchg_alloc", c_int, [c_ll, ctypes.POINTER(c_vp), c_vp]),
     ("yabt_xchg_open", c_int, [c_vp, ctypes.POINTER(c_vp)]),

@@ -149,7 +149,7 @@ def _check_supported(p: BoostParams) -> None:
                      ("refit_every", p.refit_every == 0), ("adaptive_features", not p.adaptive_features),
                      ("goss_enabled", not p.goss_enabled), ("product_features", not p.product_features),
                      ("auto_tune", not p.auto_tune), ("stochastic_routing", not p.stochastic_routing),
-                     ("leaf_net_hidden", p.leaf_net_hidden == 0), ("subsample", p.subsample >= 1.0),
+                     ("leaf_net_hidden", p.leaf_net_hidden == 0), ("subsample", 0.0 < p.subsample <= 1.0),
                      ("levelwise", p.levelwise is not False)):
         if not ok:
             bad.append(name)
@@ -302,6 +302,20 @@ class Booster:
             ln_ws = torch.empty(int(lib.yabt_leafnet_workspace_bytes(n, F, grower.max_nodes)),
                                 dtype=torch.uint8, device=dev)
         rows = grower.leaf_rows()
+        sub = p.subsample < 1.0
+        if sub:
+            # row subsampling: trees grow on a sample, leaf models and the margin
+            # update route every row (ranges from a stable grouping by leaf)
+            offset = 0
+            if comm is not None:
+                from .distributed import shard_layout
+                offset, _ = shard_layout(comm, n)
+            mn = grower.max_nodes
+            grp_ws = torch.empty(int(lib.yabt_group_rows_workspace_bytes(n, mn)), dtype=torch.uint8, device=dev)
+            grp_begin = torch.empty(mn, dtype=torch.int32, device=dev)
+            grp_count = torch.empty(mn, dtype=torch.int32, device=dev)
+            grp_rows = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+            grp_src = torch.zeros(mn, dtype=torch.int32, device=dev)     # every leaf range is in grp_rows
 
         margin_v = yv = Xv = None
         if eval_set is not None:
@@ -316,6 +330,15 @@ class Booster:
 
         n_built = 0
         for t in range(T):
+            root = None
+            if sub:
+                # yabt/boosting.py:374-376: rows[:m] of a permutation drawn from the
+                # CPU generator before the feature mask (the same draw order)
+                m = int(n_total * p.subsample)
+                perm = torch.randperm(n_total, generator=gen)[:m]
+                if comm is not None:
+                    perm = perm[(perm >= offset) & (perm < offset + n)] - offset
+                root = torch.sort(perm).values.to(torch.int32).to(dev)   # row order only affects locality
             if use_ia:
                 _lib.check(lib.yabt_interaction_normalize(scores.data_ptr(), F, imat.data_ptr(), s),
                            "yabt_interaction_normalize")
@@ -334,18 +357,28 @@ class Booster:
                        right=forest.right[t], value=forest.value[t], gate_scale=forest.gate[t],
                        leaf_of_row=leaf_of_row, meta=forest.meta[t])
             a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost,
-                            bins_fm=data.bins_fm)
+                            bins_fm=data.bins_fm, root_rows=root)
             if comm is None:
                 grower.grow(a)
             else:
                 from .distributed import grow_tree
                 grow_tree(grower, a, comm)
+            if sub:
+                # every row's leaf (the tree saw only the sample), grouped by leaf
+                _lib.check(lib.yabt_grow_apply_all(grower.h, ctypes.byref(a), s), "yabt_grow_apply_all")
+                _lib.check(lib.yabt_group_rows(leaf_of_row.data_ptr(), n, grower.max_nodes, grp_ws.data_ptr(),
+                                               grp_ws.numel(), grp_begin.data_ptr(), grp_count.data_ptr(),
+                                               grp_rows.data_ptr(), s), "yabt_group_rows")
             if p.neural_leaves:
                 la = _lib.LeafNetArgs()
                 la.feature = forest.feature[t].data_ptr(); la.value = forest.value[t].data_ptr()
                 la.max_nodes = grower.max_nodes; la.meta = forest.meta[t].data_ptr()
                 la.leaf_src, la.leaf_begin, la.leaf_count = rows["src"], rows["begin"], rows["count"]
                 la.fin, la.list0, la.list1 = rows["fin"], rows["list0"], rows["list1"]
+                if sub:
+                    la.leaf_src, la.leaf_begin, la.leaf_count = (grp_src.data_ptr(), grp_begin.data_ptr(),
+                                                                 grp_count.data_ptr())
+                    la.fin = grp_rows.data_ptr()
                 la.leaf_of_row = leaf_of_row.data_ptr(); la.Xfm = data.Xfm.data_ptr()
                 la.col_mean = data.col_mean.data_ptr(); la.col_std = data.col_std.data_ptr()
                 la.margin = margin.data_ptr(); la.y = yt.data_ptr(); la.n = n; la.F = F; la.K = K

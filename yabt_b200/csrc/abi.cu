@@ -28,7 +28,8 @@ cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&,
 cudaError_t launch_level_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
-cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, int*, int*, int, cudaStream_t);
+cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, const TreeIO&, int*, int*, int, cudaStream_t);
+cudaError_t launch_apply_all(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
 
 // ---------------------------------------------------------------- pack kernel
@@ -360,6 +361,9 @@ static int fill_io(yabt_grower* g, const yabt_tree_args* a, TreeIO* io) {
   io->left = (long long*)a->left; io->right = (long long*)a->right;
   io->value = a->value; io->gate = a->gate_scale; io->leaf_of_row = a->leaf_of_row;
   io->bins_fm = a->bins_fm;
+  io->root_rows = a->root_rows;
+  io->n_root = a->root_rows ? a->n_root : p.n;
+  if (io->n_root < 0 || io->n_root > p.n) { set_error("yabt_tree_args: n_root out of range"); return YABT_ERR_ARG; }
   return YABT_OK;
 }
 
@@ -407,7 +411,7 @@ int yabt_grow_end(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   TreeIO io;
   int rc = fill_io(g, a, &io);
   if (rc) return rc;
-  CUDA_TRY(launch_tree_finish(g->p, g->b, a->meta, a->leaf_of_row, g->nsm, (cudaStream_t)stream));
+  CUDA_TRY(launch_tree_finish(g->p, g->b, io, a->meta, a->leaf_of_row, g->nsm, (cudaStream_t)stream));
   return YABT_OK;
 }
 
@@ -439,6 +443,15 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
 void* yabt_grow_amax_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->amax_g : nullptr; }
 void* yabt_grow_small_ptr(yabt_grower* g) { return g && g->bound ? (void*)g->b.small : nullptr; }
 void* yabt_grow_level_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->level : nullptr; }
+
+int yabt_grow_apply_all(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (!io.bins_fm) { set_error("yabt_grow_apply_all: needs the feature-major bins (bins_fm)"); return YABT_ERR_ARG; }
+  CUDA_TRY(launch_apply_all(g->p, g->b, io, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
 
 int yabt_grower_set_level_wait(yabt_grower* g, int wait) {
   if (!g) { set_error("null grower"); return YABT_ERR_ARG; }

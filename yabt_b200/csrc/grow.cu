@@ -42,14 +42,15 @@ __device__ int warp_excl_scan(const int* in, int* out, int n) {
 
 // ------------------------------------------------------------------ per-tree setup
 __global__ void k_absmax(const float* __restrict__ g, const float* __restrict__ h, long long n,
-                         GrowState* st) {
+                         const int* __restrict__ root, GrowState* st) {
   unsigned mg = 0, mh = 0;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
+    const long long r = root ? root[i] : i;
     // bit patterns of non-negative floats order like the values, as signed and
     // as unsigned 32-bit integers (so ranks can combine them with an int max)
-    mg = max(mg, __float_as_uint(fabsf(g[i])));
-    if (h) mh = max(mh, __float_as_uint(fabsf(h[i])));
+    mg = max(mg, __float_as_uint(fabsf(g[r])));
+    if (h) mh = max(mh, __float_as_uint(fabsf(h[r])));
   }
   for (int o = 16; o; o >>= 1) {
     mg = max(mg, __shfl_xor_sync(0xffffffffu, mg, o));
@@ -88,12 +89,12 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
     quant_scale(st->amax_g, &st->qe_g, &st->gscale, &st->ginv);
     if (p.general) quant_scale(st->amax_h, &st->qe_h, &st->hscale, &st->hinv);
     else { st->qe_h = 0; st->hscale = 1.f; st->hinv = 1.f; }
-    b.act_gid[0][0] = 0; b.seg_begin[0][0] = 0; b.seg_count[0][0] = (int)p.n;
+    b.act_gid[0][0] = 0; b.seg_begin[0][0] = 0; b.seg_count[0][0] = (int)io.n_root;
     io.feature[0] = -1; io.threshold[0] = 0.f; io.left[0] = -1; io.right[0] = -1;
     io.value[0] = 0.f; io.gate[0] = 1.f; b.node_depth[0] = 0; b.node_bin[0] = -1;
-    // root histogram items: all rows, identity list
-    const int chunk = item_chunk(p.n, p.U);
-    const int nch = (int)((p.n + chunk - 1) / chunk);
+    // root histogram items: the root rows (positions into io.root_rows, or rows)
+    const int chunk = item_chunk(io.n_root, p.U);
+    const int nch = (int)((io.n_root + chunk - 1) / chunk);
     int slot = 0;
     for (int u = 0; u < p.U; ++u) {
       b.job_first[u] = slot;
@@ -103,19 +104,19 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
     if (slot > p.max_items) { atomicOr(&st->err, DERR_ITEM_OVERFLOW); slot = 0; }
     st->n_items = slot; st->item_counter = 0;
     for (int l = 0; l < 64; ++l) st->hist_rows[l] = 0;
-    st->hist_rows[0] = p.n;
-    st->acc_root_rows += p.n;
+    st->hist_rows[0] = io.n_root;
+    st->acc_root_rows += io.n_root;
     st->acc_launches += 1;
   }
   __syncthreads();
-  const int chunk = item_chunk(p.n, p.U);
-  const int nch = (int)((p.n + chunk - 1) / chunk);
+  const int chunk = item_chunk(io.n_root, p.U);
+  const int nch = (int)((io.n_root + chunk - 1) / chunk);
   if (nch * p.U <= p.max_items) {
     for (int i = threadIdx.x; i < nch * p.U; i += blockDim.x) {
       const int u = i / nch, c = i % nch;
       HistItem it;
       it.begin = c * chunk;
-      it.count = (int)min((long long)chunk, p.n - (long long)c * chunk);
+      it.count = (int)min((long long)chunk, io.n_root - (long long)c * chunk);
       it.unit = u; it.job = 0; it.slot = i;
       it.used = 0; it.pad[0] = it.pad[1] = 0;
       b.items[i] = it;
@@ -458,7 +459,7 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
   const int ntiles = st->n_tiles;
   const unsigned epoch = st->epoch;
-  const int* src = d == 0 ? nullptr : b.rows[cur];
+  const int* src = d == 0 ? io.root_rows : b.rows[cur];   // nullptr: identity
   int* dst = b.rows[nxt];
   __shared__ int s_tile, s_excl;
   __shared__ int s_wc[8][PART_THREADS / 32];
@@ -667,7 +668,7 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
 // and are disjoint) tile [0, n), so k_leaf_assign can map every position to
 // its leaf with a binary search.
 __global__ void __launch_bounds__(1024)
-k_finish(GrowParams p, GrowBufs b, int* meta) {
+k_finish(GrowParams p, GrowBufs b, int* meta, long long n_root) {
   GrowState* st = b.st;
   const int nn = st->n_nodes;
   __shared__ int s_nl;
@@ -677,7 +678,7 @@ k_finish(GrowParams p, GrowBufs b, int* meta) {
     meta[2] = (int)st->err;
     meta[3] = st->level;
     if (nn == 1) {   // single-leaf tree: the root owns every row
-      b.leaf_src[0] = SRC_IDENTITY; b.leaf_begin[0] = 0; b.leaf_count[0] = (int)p.n;
+      b.leaf_src[0] = SRC_IDENTITY; b.leaf_begin[0] = 0; b.leaf_count[0] = (int)n_root;
     }
     s_nl = 0;
   }
@@ -701,8 +702,10 @@ k_finish(GrowParams p, GrowBufs b, int* meta) {
   if (threadIdx.x == 0) st->n_leaves = s_nl;
 }
 
-// Writes leaf_of_row[row] = leaf for every position of the final leaf ranges.
-__global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_of_row) {
+// Writes leaf_of_row[row] = leaf for every position of the final leaf ranges
+// (SRC_IDENTITY positions are root positions: root[i], or i without a root list).
+__global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_of_row, const int* __restrict__ root,
+                              long long n_root) {
   GrowState* st = b.st;
   const int nl = st->n_leaves;
   extern __shared__ int sm_leaf[];          // [nl] begins, [nl] gids, [nl] srcs
@@ -714,7 +717,7 @@ __global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_o
     sb[i] = b.leaf_begin[g]; sg[i] = g; ss[i] = b.leaf_src[g];
   }
   __syncthreads();
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_root;
        i += (long long)gridDim.x * blockDim.x) {
     int lo = 0, hi = nl - 1;
     while (lo < hi) {
@@ -723,11 +726,34 @@ __global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_o
     }
     const int src = ss[lo];
     int row;
-    if (src == SRC_IDENTITY) row = (int)i;
+    if (src == SRC_IDENTITY) row = root ? root[i] : (int)i;
     else if (src == SRC_FIN) row = b.fin[i];
     else row = b.rows[src == SRC_LIST0 ? 0 : 1][i];
     leaf_of_row[row] = sg[lo];
   }
+}
+
+// Leaf of every row 0..n-1 of the grown tree, by its split bins: bin <= split
+// bin goes left (the same routing as the partition and as Tree.apply on the
+// imputed features, yabt/tree.py:82-116, since bin(x) <= b <=> x <= edges[b]).
+__global__ void k_apply_all(GrowParams p, GrowBufs b, TreeIO io) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long node = 0;
+    for (int depth = 0; depth <= p.levels_max && io.feature[node] >= 0; ++depth) {
+      const long long f = io.feature[node];
+      const unsigned bin = io.bins_fm[f * p.n + i];
+      node = bin <= (unsigned)b.node_bin[node] ? io.left[node] : io.right[node];
+    }
+    io.leaf_of_row[i] = (int)node;
+  }
+}
+
+cudaError_t launch_apply_all(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm, cudaStream_t s) {
+  const int grid = (int)std::min<long long>((p.n + 255) / 256, 8LL * nsm);
+  k_apply_all<<<std::max(grid, 1), 256, 0, s>>>(p, b, io);
+  count_launches(1);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ host side
@@ -766,8 +792,8 @@ cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const Tree
   cudaError_t e = cudaMemsetAsync(&b.st->amax_g, 0, 2 * sizeof(unsigned), s);
   if (e != cudaSuccess) return e;
 
-  const int grid = (int)std::min<long long>((p.n + 255) / 256, 8LL * nsm);
-  k_absmax<<<std::max(grid, 1), 256, 0, s>>>(io.g, p.general ? io.h : nullptr, p.n, b.st);
+  const int grid = (int)std::min<long long>((io.n_root + 255) / 256, 8LL * nsm);
+  k_absmax<<<std::max(grid, 1), 256, 0, s>>>(io.g, p.general ? io.h : nullptr, io.n_root, io.root_rows, b.st);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -778,11 +804,12 @@ cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeI
   return cudaGetLastError();
 }
 
-cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, int* meta, int* leaf_of_row,
-                               int nsm, cudaStream_t s) {
-  k_finish<<<1, 1024, 0, s>>>(p, b, meta);
-  const int grid = (int)std::min<long long>((p.n + 511) / 512, 4LL * nsm);
-  k_leaf_assign<<<std::max(grid, 1), 512, 3 * (p.max_leaves + 1) * sizeof(int), s>>>(p, b, leaf_of_row);
+cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int* meta,
+                               int* leaf_of_row, int nsm, cudaStream_t s) {
+  k_finish<<<1, 1024, 0, s>>>(p, b, meta, io.n_root);
+  const int grid = (int)std::min<long long>((io.n_root + 511) / 512, 4LL * nsm);
+  k_leaf_assign<<<std::max(grid, 1), 512, 3 * (p.max_leaves + 1) * sizeof(int), s>>>(p, b, leaf_of_row,
+                                                                                     io.root_rows, io.n_root);
   count_launches(2);
   return cudaGetLastError();
 }

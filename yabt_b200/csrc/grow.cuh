@@ -174,6 +174,8 @@ struct TreeIO {
   float* gate;
   int* leaf_of_row;          // [n]
   const uint8_t* bins_fm;    // feature-major (F, n) bins, or nullptr (partition reads the tiled matrix)
+  const int* root_rows;      // rows the tree is grown on (row subsampling), or nullptr: all n rows
+  long long n_root;          // number of root rows (n when root_rows is nullptr)
 };
 
 // the device state of a bound grower (C ABI handle), or nullptr

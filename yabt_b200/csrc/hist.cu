@@ -430,7 +430,7 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
 
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
                                 int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist) {
-  const int* rows = d == 0 ? nullptr : b.rows[d & 1];
+  const int* rows = d == 0 ? io.root_rows : b.rows[d & 1];   // nullptr: identity
   // levels with at most a few jobs split each job's items over several reduce
   // blocks, which add into a zeroed histogram
   const int igroups = std::max(1, 8 / jobs);

@@ -85,12 +85,17 @@ class Grower:
              edges: EdgePack, params: TreeParams, out: dict,
              feature_mask: torch.Tensor | None = None,
              interaction: torch.Tensor | None = None, interaction_boost: float = 0.5,
-             bins_fm: torch.Tensor | None = None) -> _lib.TreeArgs:
+             bins_fm: torch.Tensor | None = None, root_rows: torch.Tensor | None = None) -> _lib.TreeArgs:
         """``bins_fm``: optional feature-major (F, n) copy of the bins, read by
-        the row partition."""
+        the row partition. ``root_rows``: optional int32 device tensor of the
+        rows to grow the tree on (row subsampling)."""
         a = _lib.TreeArgs()
         a.bins = bins.data_ptr()
         a.bins_fm = bins_fm.data_ptr() if bins_fm is not None else None
+        a.root_rows = root_rows.data_ptr() if (root_rows is not None and root_rows.numel()) else None
+        a.n_root = int(root_rows.numel()) if root_rows is not None else 0
+        if root_rows is not None and root_rows.numel() == 0:
+            a.root_rows = self._empty_root().data_ptr()
         a.grad = grad.data_ptr()
         a.hess = hess.data_ptr() if (hess is not None and self.general) else None
         a.edges, a.edge_off, a.edge_cnt = edges.values.data_ptr(), edges.off.data_ptr(), edges.cnt.data_ptr()
@@ -110,6 +115,11 @@ class Grower:
     def grow(self, a: _lib.TreeArgs, stream=None) -> None:
         _lib.check(self.lib.yabt_grow_tree(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
                    "yabt_grow_tree")
+
+    def _empty_root(self) -> torch.Tensor:
+        if getattr(self, "_empty", None) is None:
+            self._empty = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self._empty
 
     def set_level_wait(self, wait: bool) -> None:
         """Whether growing a tree may wait on the device to stop queuing levels
