@@ -52,7 +52,8 @@ def workload_config(cfg: str, world: int) -> dict:
                         f"max_depth {depth}, {loss}, neural leaves, interaction steering",
             "global_rows": n, "rows_per_gpu": n // world,
             "l2": "inputs larger than L2 (bin matrix of C4: 2.08 GB)" if n * F > 10 ** 9 else "see workload",
-            "parallelism": f"row shards x{world}, NCCL all-reduce of level histograms"}
+            "parallelism": (f"row shards x{world}, level histograms summed by the NVLink exchange kernel"
+                            if world > 1 else "one GPU")}
 
 
 def make_data(cfg: str, n: int, F: int, device, seed: int = 0):
