@@ -76,6 +76,18 @@ class OTree:
             node = np.where(is_leaf[node], node, nxt)
         return node
 
+    def apply_bins(self, binned: np.ndarray) -> np.ndarray:
+        """Leaf index per row of the bin matrix: bin <= split bin goes left."""
+        n = binned.shape[0]
+        node = np.zeros(n, dtype=np.int64)
+        is_leaf = self.feature == LEAF
+        for _ in range(self.depth):
+            f = np.maximum(self.feature[node], 0)
+            go_left = binned[np.arange(n), f].astype(np.int64) <= self.split_bin[node]
+            nxt = np.where(go_left, self.left[node], self.right[node])
+            node = np.where(is_leaf[node], node, nxt)
+        return node
+
     def net_contribution(self, X: np.ndarray, node: np.ndarray) -> np.ndarray:
         """yabt/tree.py:118-128 (linear leaves)."""
         if self.leaf_net_feats is None:
@@ -296,3 +308,85 @@ def grow_levelwise(binned: np.ndarray, grad: np.ndarray, hess: np.ndarray,
         value=np.array(value, np.float32), depth=max(node_depth) + 1,
         gate_scale=np.array(gate, np.float32), split_bin=np.array(sbin, np.int64))
     return tree, node_of_row, trace
+
+
+def grow_bestfirst(binned: np.ndarray, grad: np.ndarray, hess: np.ndarray,
+                   edges: list[np.ndarray], scales: np.ndarray, params: TreeParams,
+                   feature_mask: np.ndarray | None = None,
+                   interaction_matrix: np.ndarray | None = None,
+                   interaction_boost: float = 0.5):
+    """Restates the best-first (heap) grower, yabt/tree.py:206-360, for axis
+    splits: a heap of candidate leaves keyed by (-gain, push order); pop the
+    best, partition its rows (stable), histogram the smaller child, subtract
+    for the sibling, push both children. Returns (OTree, node_of_row)."""
+    import heapq
+    import itertools
+    n, F = binned.shape
+    lam, gamma = params.reg_lambda, params.gamma
+    mcw, msl, lr = params.min_child_weight, params.min_samples_leaf, params.learning_rate
+    scales_c = np.maximum(scales.astype(np.float32), f32(1e-12))
+    imat = None if interaction_matrix is None else interaction_matrix.astype(np.float32)
+    feature, threshold, left, right, value, node_depth, gate, sbin = [], [], [], [], [], [], [], []
+
+    def tot(x):   # float32 sum of a float32 vector (summed in float64 and rounded)
+        return float(np.sum(x.astype(np.float64)).astype(np.float32))
+
+    def new_node(g_sum: float, h_sum: float, depth: int) -> int:   # yabt/tree.py:233-243
+        feature.append(LEAF); threshold.append(0.0); left.append(-1); right.append(-1)
+        value.append(-lr * g_sum / (h_sum + lam)); node_depth.append(depth); gate.append(1.0)
+        sbin.append(-1)
+        return len(feature) - 1
+
+    def hist_of(rows):
+        return scatter_hist(binned[rows], np.zeros(rows.size, np.int64), grad[rows], hess[rows], None, 1)[:, 0]
+
+    all_rows = np.arange(n)
+    root_hist = hist_of(all_rows)
+    root = new_node(tot(grad), tot(hess), 0)
+    tiebreak = itertools.count()
+    heap: list = []
+
+    def push_candidate(nid, rows, hist, path=()):                   # yabt/tree.py:252-290
+        if node_depth[nid] >= params.max_depth:
+            return
+        boost = None
+        if imat is not None and path:
+            pf = np.array(sorted(set(path)), np.int64)
+            boost = (f32(1.0) + f32(interaction_boost) * imat[pf].max(axis=0)).astype(np.float32)[None, :]
+        idx, gain, _ = split_scan(hist[:, None], lam, gamma, mcw, msl, feature_mask, boost)
+        g = float(gain[0])
+        if g > 0:
+            heapq.heappush(heap, (-g, next(tiebreak), nid, rows, hist, int(idx[0]) // B, int(idx[0]) % B, path))
+
+    push_candidate(root, all_rows, root_hist)
+    n_leaves = 1
+    while heap and n_leaves < params.max_leaves:                     # yabt/tree.py:295-348
+        _, _, nid, rows, hist, f, b, path = heapq.heappop(heap)
+        go_left = binned[rows, f] <= b
+        rows_l, rows_r = rows[go_left], rows[~go_left]
+        if rows_l.size <= rows_r.size:
+            hist_l = hist_of(rows_l)
+            hist_r = hist - hist_l
+        else:
+            hist_r = hist_of(rows_r)
+            hist_l = hist - hist_r
+        d = node_depth[nid] + 1
+        nl = new_node(tot(hist_l[0, 0]), tot(hist_l[1, 0]), d)
+        nr = new_node(tot(hist_r[0, 0]), tot(hist_r[1, 0]), d)
+        feature[nid] = f
+        e = edges[f]
+        threshold[nid] = float(e[min(b, len(e) - 1)])
+        gate[nid] = float(scales_c[f])
+        sbin[nid] = b
+        left[nid], right[nid] = nl, nr
+        value[nid] = 0.0
+        n_leaves += 1
+        push_candidate(nl, rows_l, hist_l, path + (f,))
+        push_candidate(nr, rows_r, hist_r, path + (f,))
+
+    tree = OTree(
+        feature=np.array(feature, np.int64), threshold=np.array(threshold, np.float32),
+        left=np.array(left, np.int64), right=np.array(right, np.int64),
+        value=np.array(value, np.float32), depth=max(node_depth) + 1,
+        gate_scale=np.array(gate, np.float32), split_bin=np.array(sbin, np.int64))
+    return tree, tree.apply_bins(binned)

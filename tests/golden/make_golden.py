@@ -19,6 +19,8 @@ tree-growth path:
                    (yabt/boosting.py:271-561) and their predict_margin, for
                    MSE and LogLoss, plus YABTClassifier multiclass
                    predict_proba (yabt/multiclass.py:40-44);
+* ``bestfirst.npz`` the best-first (heap) grower grow_tree (yabt/tree.py:206-360,
+                   axis splits), written by ``make_golden.py --bestfirst``;
 * ``hist.npz``     the torch scatter histogram the reference CUDA kernel is
                    tested against (tests/test_cuda_hist.py:13-22 of the reference).
 
@@ -198,5 +200,60 @@ def main(ref_root: str) -> None:
     print("golden fixtures written to", HERE)
 
 
+def bestfirst(ref_root: str) -> None:
+    """``bestfirst.npz``: the reference's best-first (heap) grower
+    (yabt/tree.py:206-360, axis splits) on seeded cases, run on a CPU-only host."""
+    sys.path.insert(0, ref_root)
+    import torch
+    from yabt.adaptive_features import FeatureInteractionDetector
+    from yabt.binning import Binner
+    from yabt.tree import TreeParams, grow_tree
+
+    assert not torch.cuda.is_available(), "run on a CPU-only host (numpy binner path)"
+    out = {}
+    bcases = [
+        dict(seed=30, n=3000, F=8, leaves=15, depth=64, msl=20, imat=False, fmask=False),
+        dict(seed=31, n=4000, F=12, leaves=31, depth=4, msl=5, imat=True, fmask=False),
+        dict(seed=32, n=2500, F=6, leaves=7, depth=64, msl=20, imat=True, fmask=True),
+        dict(seed=33, n=1500, F=10, leaves=63, depth=10, msl=1, imat=False, fmask=False),
+    ]
+    for i, c in enumerate(bcases):
+        X, _ = _data(c["seed"], c["n"], c["F"], 0.02)
+        binner = Binner(256).fit(X)
+        binned = binner.transform(X)
+        Xraw = torch.from_numpy(binner.impute(X))
+        rng = np.random.default_rng(c["seed"] + 100)
+        g = torch.from_numpy(rng.normal(size=c["n"]).astype(np.float32))
+        h = torch.from_numpy(rng.uniform(0.05, 0.25, size=c["n"]).astype(np.float32))
+        imat = None
+        if c["imat"]:
+            det = FeatureInteractionDetector(c["F"], device="cpu")
+            pairs = [(int(a), int(b)) for a, b in rng.integers(0, c["F"], size=(40, 2))]
+            pairs += [(0, 1)] * 6
+            det.update_from_path_pairs(pairs)
+            imat = det.normalized_matrix()
+        fm = None
+        if c["fmask"]:
+            fm = torch.from_numpy(rng.random(c["F"]) < 0.7)
+        tp = TreeParams(max_leaves=c["leaves"], max_depth=c["depth"], min_samples_leaf=c["msl"],
+                        learning_rate=0.1)
+        tree = grow_tree(binned, g, h, binner, tp, fm, interaction_matrix=imat, interaction_boost=0.5)
+        out[f"b{i}_X"] = X
+        out[f"b{i}_g"] = g.numpy(); out[f"b{i}_h"] = h.numpy()
+        out[f"b{i}_params"] = np.array([c["leaves"], c["depth"], c["msl"]], np.int64)
+        out[f"b{i}_imat"] = imat.numpy() if imat is not None else np.zeros((0, 0), np.float32)
+        out[f"b{i}_fmask"] = fm.numpy() if fm is not None else np.zeros(0, bool)
+        for k in ("feature", "threshold", "left", "right", "value", "gate_scale"):
+            out[f"b{i}_{k}"] = getattr(tree, k).numpy()
+        out[f"b{i}_leaf"] = tree.apply(Xraw).numpy()
+    out["ncases"] = np.array(len(bcases))
+    np.savez_compressed(os.path.join(HERE, "bestfirst.npz"), **out)
+    print("bestfirst fixtures written to", HERE)
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else "/root/reference"
+    if "--bestfirst" in sys.argv:
+        bestfirst(ref)
+    else:
+        main(ref)

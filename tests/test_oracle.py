@@ -92,6 +92,26 @@ def test_levelwise_grower_matches_reference(golden, case):
     np.testing.assert_array_equal(tree.apply(b.impute(X)), leaf)
 
 
+@pytest.mark.parametrize("case", range(4))
+def test_bestfirst_grower_matches_reference(golden, case):
+    """The best-first (heap) grower, yabt/tree.py:206-360, against the reference run."""
+    from oracle.grow import grow_bestfirst
+    z = golden("bestfirst")
+    X = z[f"b{case}_X"]
+    leaves, depth, msl = (int(v) for v in z[f"b{case}_params"])
+    b = Binner().fit(X)
+    imat = z[f"b{case}_imat"]
+    fm = z[f"b{case}_fmask"]
+    tree, leaf = grow_bestfirst(b.transform(X), z[f"b{case}_g"], z[f"b{case}_h"], b.edges_, b.scales_,
+                                TreeParams(max_leaves=leaves, max_depth=depth, min_samples_leaf=msl),
+                                fm if fm.size else None, imat if imat.size else None, 0.5)
+    for k in ("feature", "threshold", "left", "right", "gate_scale"):
+        np.testing.assert_array_equal(getattr(tree, k), z[f"b{case}_{k}"], err_msg=k)
+    np.testing.assert_allclose(tree.value, z[f"b{case}_value"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(leaf, z[f"b{case}_leaf"])
+    np.testing.assert_array_equal(tree.apply(b.impute(X)), leaf)
+
+
 def test_leaf_networks_match_reference(golden):
     z = golden("leafnet")
 
