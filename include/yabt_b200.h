@@ -158,6 +158,24 @@ int yabt_group_rows(const int32_t* leaf_of_row, long long n, int num_leaves, voi
                     int32_t* begin, int32_t* count, int32_t* rows, void* stream);
 int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream);
 
+/* Best-first (leaf-wise) growth, the heap grower of yabt/tree.py:206-360 that
+ * Booster uses when levelwise is False, or "auto" with max_leaves < 16
+ * (yabt/boosting.py:415-421): one split per step, the candidate leaf with the
+ * largest gain first (ties: lower node id = earlier push), children become
+ * candidates when depth < max_depth and gain > 0, at most max_leaves leaves.
+ * Same arguments, outputs and node numbering as the reference (children get
+ * the next two ids in split order). yabt_grow_tree_bestfirst runs the whole
+ * tree (host stop as yabt_grow_tree); the step-wise form, for callers that
+ * reduce the small-child histogram (one job) across ranks between the two
+ * halves of a step like yabt_grow_hist / yabt_grow_split, is
+ *   begin, init, bf_root_hist, [reduce], bf_scan(0),
+ *   for step = 1 .. max(1, max_leaves - 1): bf_split(step), [reduce], bf_scan(step)
+ *   end.                                                                    */
+int yabt_grow_tree_bestfirst(yabt_grower* g, const yabt_tree_args* a, void* stream);
+int yabt_grow_bf_root_hist(yabt_grower* g, const yabt_tree_args* a, void* stream);
+int yabt_grow_bf_split(yabt_grower* g, const yabt_tree_args* a, int step, void* stream);
+int yabt_grow_bf_scan(yabt_grower* g, const yabt_tree_args* a, int step, void* stream);
+
 /* Step-wise driving for row-sharded multi-GPU growth: the caller reduces
  * (max, as int32) the two words at yabt_grow_amax_ptr() -- bit patterns of
  * max |g| and max |h| -- after yabt_grow_begin, and sums (int64) the

@@ -15,7 +15,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .binning import Binner
-from .grow import OTree, TreeParams, grow_levelwise
+from .grow import OTree, TreeParams, grow_bestfirst, grow_levelwise
 from .leafnet import column_stats, fit_leaf_networks
 
 f32 = np.float32
@@ -92,11 +92,14 @@ class BoostParams:
     leaf_net_min_samples: int = 50
     subsample: float = 1.0
     seed: int = 0
+    levelwise: bool | str = "auto"
 
 
 class Booster:
-    """Level-wise Newton boosting on CPU (yabt/boosting.py:271-561 with
-    ``levelwise=True``)."""
+    """Newton boosting on CPU (yabt/boosting.py:271-561) with the grower the
+    reference picks on a CUDA device (yabt/boosting.py:415-421): level-wise
+    for ``levelwise=True`` or ``"auto"`` with max_leaves >= 16, else the
+    best-first heap grower."""
 
     def __init__(self, params: BoostParams, loss):
         self.p = params
@@ -126,17 +129,25 @@ class Booster:
         for t in range(p.n_estimators if n_trees is None else n_trees):
             g, h = self.loss.grad_hess(margin, y)
             imat = det.normalized() if det is not None else None
+            lw = p.levelwise is True or (p.levelwise == "auto" and p.max_leaves >= 16)
+
+            def grow(b_, g_, h_):
+                if lw:
+                    tree_, leaf_, _ = grow_levelwise(b_, g_, h_, self.binner.edges_, self.binner.scales_,
+                                                     tp, None, imat, p.interaction_boost)
+                else:
+                    tree_, leaf_ = grow_bestfirst(b_, g_, h_, self.binner.edges_, self.binner.scales_,
+                                                  tp, None, imat, p.interaction_boost)
+                return tree_, leaf_
             if p.subsample < 1.0:
                 # yabt/boosting.py:374-376, 392-393: grow on rows[:m] of a permutation,
                 # then route every row through the tree (:486)
                 m = int(n * p.subsample)
                 rows = torch.randperm(n, generator=gen)[:m].numpy()
-                tree, _, _ = grow_levelwise(binned[rows], g[rows], h[rows], self.binner.edges_,
-                                            self.binner.scales_, tp, None, imat, p.interaction_boost)
+                tree, _ = grow(binned[rows], g[rows], h[rows])
                 leaf = tree.apply(Xraw)
             else:
-                tree, leaf, _ = grow_levelwise(binned, g, h, self.binner.edges_, self.binner.scales_,
-                                               tp, None, imat, p.interaction_boost)
+                tree, leaf = grow(binned, g, h)
             if p.neural_leaves:
                 tree = fit_leaf_networks(tree, Xraw, y, margin, self.loss, p, leaf,
                                          col_mean, col_std)

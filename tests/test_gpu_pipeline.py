@@ -98,18 +98,18 @@ def test_reference_golden_predictions(golden):
     """Booster fits on the reference's golden inputs reproduce its predictions."""
     from yabt_b200 import Booster, BoostParams, LogLoss, MSELoss
     z = golden("boost")
-    bm = Booster(BoostParams(n_estimators=12, max_leaves=15, learning_rate=0.1), MSELoss()).fit(z["mse_X"], z["mse_y"])
+    bm = Booster(BoostParams(n_estimators=12, max_leaves=15, learning_rate=0.1, levelwise=True), MSELoss()).fit(z["mse_X"], z["mse_y"])
     for t in range(3):
         np.testing.assert_array_equal(bm.trees[t].feature.cpu().numpy(), z[f"mse_t{t}_feature"])
     np.testing.assert_allclose(bm.predict_margin(z["mse_X"]), z["mse_pred"], rtol=1e-4, atol=1e-4)
-    bl = Booster(BoostParams(n_estimators=10, max_leaves=15, learning_rate=0.2), LogLoss()).fit(z["log_X"], z["log_y"])
+    bl = Booster(BoostParams(n_estimators=10, max_leaves=15, learning_rate=0.2, levelwise=True), LogLoss()).fit(z["log_X"], z["log_y"])
     np.testing.assert_allclose(bl.predict_margin(z["log_X"]), z["log_pred"], rtol=1e-4, atol=1e-4)
 
 
 def test_sklearn_estimators_golden(golden):
     from yabt_b200 import YABTClassifier, YABTRegressor
     z = golden("boost")
-    clf = YABTClassifier(n_estimators=6, max_leaves=15, seed=0).fit(z["mc_X"], z["mc_y"])
+    clf = YABTClassifier(n_estimators=6, max_leaves=15, levelwise=True, seed=0).fit(z["mc_X"], z["mc_y"])
     np.testing.assert_allclose(clf.predict_proba(z["mc_X"]), z["mc_proba"], rtol=1e-4, atol=1e-5)
     reg = YABTRegressor(n_estimators=20).fit(z["mse_X"], z["mse_y"])
     r = z["mse_y"] - reg.predict(z["mse_X"])

@@ -133,12 +133,12 @@ def test_leaf_networks_match_reference(golden):
 
 def test_boosting_matches_reference(golden):
     z = golden("boost")
-    bm = Booster(BoostParams(n_estimators=12, max_leaves=15, learning_rate=0.1), MSELoss())
+    bm = Booster(BoostParams(n_estimators=12, max_leaves=15, learning_rate=0.1, levelwise=True), MSELoss())
     bm.fit(z["mse_X"], z["mse_y"])
     for t in range(3):
         np.testing.assert_array_equal(bm.trees[t].feature, z[f"mse_t{t}_feature"])
     np.testing.assert_allclose(bm.predict_margin(z["mse_X"]), z["mse_pred"], rtol=1e-4, atol=1e-5)
-    bl = Booster(BoostParams(n_estimators=10, max_leaves=15, learning_rate=0.2), LogLoss())
+    bl = Booster(BoostParams(n_estimators=10, max_leaves=15, learning_rate=0.2, levelwise=True), LogLoss())
     bl.fit(z["log_X"], z["log_y"])
     np.testing.assert_allclose(bl.predict_margin(z["log_X"]), z["log_pred"], rtol=1e-4, atol=1e-5)
 

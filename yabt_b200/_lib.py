@@ -80,6 +80,10 @@ SIGNATURES = [
     ("yabt_grower_max_nodes", c_int, [c_vp]),
     ("yabt_grower_levels", c_int, [c_vp]),
     ("yabt_grow_tree", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_tree_bestfirst", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_bf_root_hist", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
+    ("yabt_grow_bf_split", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_int, c_vp]),
+    ("yabt_grow_bf_scan", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_int, c_vp]),
     ("yabt_grow_begin", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
     ("yabt_grow_init", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
     ("yabt_grow_hist", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_int, c_vp]),

@@ -143,6 +143,14 @@ class BoostParams:
         return self.device
 
 
+def use_bestfirst(p: BoostParams) -> bool:
+    """The grower the reference picks on a CUDA device, yabt/boosting.py:415-421:
+    level-wise for ``levelwise=True``, or ``"auto"`` with max_leaves >= 16;
+    otherwise the best-first heap grower (kernel splits, which also force the
+    heap there, are not part of this path)."""
+    return not (p.levelwise is True or (p.levelwise == "auto" and p.max_leaves >= 16))
+
+
 def _check_supported(p: BoostParams) -> None:
     bad = []
     for name, ok in (("kernel_splits", not p.kernel_splits), ("refine_steps", p.refine_steps == 0),
@@ -150,11 +158,11 @@ def _check_supported(p: BoostParams) -> None:
                      ("goss_enabled", not p.goss_enabled), ("product_features", not p.product_features),
                      ("auto_tune", not p.auto_tune), ("stochastic_routing", not p.stochastic_routing),
                      ("leaf_net_hidden", p.leaf_net_hidden == 0), ("subsample", 0.0 < p.subsample <= 1.0),
-                     ("levelwise", p.levelwise is not False)):
+                     ("levelwise", p.levelwise in (True, False, "auto"))):
         if not ok:
             bad.append(name)
     if bad:
-        raise NotImplementedError(f"yabt_b200 implements the level-wise GPU growth path; unsupported "
+        raise NotImplementedError(f"yabt_b200 implements the GPU tree-growth path; unsupported "
                                   f"options: {', '.join(bad)}")
     dev = p.resolve_device()
     if not str(dev).startswith("cuda"):
@@ -284,6 +292,7 @@ class Booster:
         _lib.check(lib.yabt_grad_init(margin.data_ptr(), yt.data_ptr(), n, self.loss.kind, grad.data_ptr(),
                                       hess.data_ptr() if hess is not None else None, s), "yabt_grad_init")
 
+        bestfirst = use_bestfirst(p)
         tp = TreeParams(max_leaves=p.max_leaves, max_depth=p.max_depth, reg_lambda=p.reg_lambda,
                         gamma=p.gamma, min_child_weight=p.min_child_weight,
                         min_samples_leaf=p.min_samples_leaf, learning_rate=p.learning_rate)
@@ -359,7 +368,10 @@ class Booster:
             a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost,
                             bins_fm=data.bins_fm, root_rows=root)
             if comm is None:
-                grower.grow(a)
+                grower.grow(a, bestfirst=bestfirst)
+            elif bestfirst:
+                from .distributed import grow_tree_bestfirst
+                grow_tree_bestfirst(grower, a, comm)
             else:
                 from .distributed import grow_tree
                 grow_tree(grower, a, comm)

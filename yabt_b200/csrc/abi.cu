@@ -30,6 +30,11 @@ cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&,
 cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
 cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, const TreeIO&, int*, int*, int, cudaStream_t);
 cudaError_t launch_apply_all(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
+cudaError_t launch_hist_kernels(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, int, cudaStream_t,
+                                cudaEvent_t);
+cudaError_t launch_bf_root_scan(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
+cudaError_t launch_bf_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_bf_scan(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
 
 // ---------------------------------------------------------------- pack kernel
@@ -205,15 +210,18 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
   auto add = [&](const char* nm, long long bytes) { g->offs.push_back({nm, bytes, 0}); };
   add("st", sizeof(GrowState));
   add("rows0", n * 4); add("rows1", n * 4); add("fin", n * 4);
-  add("segb0", p.maxa * 4); add("segb1", p.maxa * 4);
-  add("segc0", p.maxa * 4); add("segc1", p.maxa * 4);
+  add("segb0", std::max(p.maxa, 2) * 4); add("segb1", std::max(p.maxa, 2) * 4);
+  add("segc0", std::max(p.maxa, 2) * 4); add("segc1", std::max(p.maxa, 2) * 4);
   add("gid0", p.maxa * 4); add("gid1", p.maxa * 4);
   add("hist0", p.maxa * HN); add("hist1", p.maxa * HN);
   add("small", (long long)p.max_pairs * small_job_words(p.C, F) * 8);
   add("pm0", (long long)p.maxa * F * 4); add("pm1", (long long)p.maxa * F * 4);
   add("best", (long long)p.maxa * F * sizeof(NodeBest));
   add("nbest", (long long)p.maxa * sizeof(NodeBest));
-  add("nkey", (long long)p.maxa * 8);
+  add("nkey", (long long)std::max(p.maxa, 2) * 8);   // best-first folds two children
+  add("bffeat", 2LL * F * sizeof(BfCand));
+  add("bfcand", (long long)p.maxn * sizeof(BfCand));
+  add("nslot", (long long)p.maxn * 4);
   add("tot", (long long)p.maxa * sizeof(NodeTot));
   add("pair_pos", p.max_pairs * 4); add("pair_sil", p.max_pairs * 4);
   add("split_pair", p.maxa * 4); add("split_f", p.maxa * 4); add("split_b", p.maxa * 4);
@@ -265,6 +273,7 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
   b.hist[0] = (long long*)P("hist0"); b.hist[1] = (long long*)P("hist1");
   b.small = (long long*)P("small");
   b.node_key = (unsigned long long*)P("nkey");
+  b.bf_feat = (BfCand*)P("bffeat"); b.bf_cand = (BfCand*)P("bfcand"); b.node_slot = (int*)P("nslot");
   b.pathmax[0] = (float*)P("pm0"); b.pathmax[1] = (float*)P("pm1");
   b.best = (NodeBest*)P("best"); b.nbest = (NodeBest*)P("nbest"); b.tot = (NodeTot*)P("tot");
   b.pair_pos = (int*)P("pair_pos"); b.pair_sil = (int*)P("pair_sil");
@@ -435,6 +444,61 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
       const int old = (d - LEVEL_LOOKAHEAD) % LEVEL_SLOTS;
       CUDA_TRY(cudaEventSynchronize(g->lvl_ev[old]));
       if (!g->host_state[4 * old + 1]) break;     // active == 0: later levels would be no-ops
+    }
+  }
+  return yabt_grow_end(g, a, stream);
+}
+
+int yabt_grow_bf_root_hist(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  CUDA_TRY(launch_hist_kernels(g->p, g->b, io, 0, 1, g->nsm, (cudaStream_t)stream, nullptr));
+  return YABT_OK;
+}
+
+int yabt_grow_bf_split(yabt_grower* g, const yabt_tree_args* a, int step, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (step < 1 || step > std::max(1, g->p.max_leaves - 1)) { set_error("step out of range"); return YABT_ERR_ARG; }
+  CUDA_TRY(launch_bf_split(g->p, g->b, io, step, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_bf_scan(yabt_grower* g, const yabt_tree_args* a, int step, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (step < 0 || step > std::max(1, g->p.max_leaves - 1)) { set_error("step out of range"); return YABT_ERR_ARG; }
+  if (step == 0) CUDA_TRY(launch_bf_root_scan(g->p, g->b, io, (cudaStream_t)stream));
+  else CUDA_TRY(launch_bf_scan(g->p, g->b, io, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_tree_bestfirst(yabt_grower* g, const yabt_tree_args* a, void* stream) {
+  int rc;
+  if ((rc = yabt_grow_begin(g, a, stream))) return rc;
+  if ((rc = yabt_grow_init(g, a, stream))) return rc;
+  if ((rc = yabt_grow_bf_root_hist(g, a, stream))) return rc;
+  if ((rc = yabt_grow_bf_scan(g, a, 0, stream))) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (g->level_wait && !g->host_state) {
+    CUDA_TRY(cudaHostAlloc((void**)&g->host_state, sizeof(int) * 4 * LEVEL_SLOTS, cudaHostAllocDefault));
+    for (auto& e : g->lvl_ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  const int steps = std::max(1, g->p.max_leaves - 1);
+  for (int k = 1; k <= steps; ++k) {
+    if ((rc = yabt_grow_bf_split(g, a, k, stream))) return rc;
+    if ((rc = yabt_grow_bf_scan(g, a, k, stream))) return rc;
+    if (!g->level_wait) continue;
+    const int slot = k % LEVEL_SLOTS;
+    CUDA_TRY(cudaMemcpyAsync(g->host_state + 4 * slot, &g->b.st->level, 4 * sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaEventRecord(g->lvl_ev[slot], s));
+    if (k > LEVEL_LOOKAHEAD) {
+      const int old = (k - LEVEL_LOOKAHEAD) % LEVEL_SLOTS;
+      CUDA_TRY(cudaEventSynchronize(g->lvl_ev[old]));
+      if (!g->host_state[4 * old + 1]) break;     // active == 0: later steps would be no-ops
     }
   }
   return yabt_grow_end(g, a, stream);

@@ -756,6 +756,362 @@ cudaError_t launch_apply_all(const GrowParams& p, const GrowBufs& b, const TreeI
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ best-first growth
+// Restates the heap grower, yabt/tree.py:206-360: candidate leaves ordered by
+// (-gain, push order); the best one is split, its rows partitioned stably, the
+// smaller child histogrammed and the sibling obtained by subtraction, and both
+// children become candidates when depth < max_depth and their gain > 0. Push
+// order equals node-id order (a node is pushed right after it is created), so
+// ties go to the lower node id. One split per step, with the level-wise
+// kernels doing the partition (one node), the item plan and the histogram:
+//     k_bf_pick -> k_partition -> k_plan -> k_hist -> k_reduce -> k_bf_scan
+// Every live leaf keeps its rows in rows[0] at a disjoint range and its full
+// histogram in hist[0] at its slot (the left child inherits the parent's slot,
+// the right child takes a new one: at most max_leaves slots). Leaves that are
+// never split again may keep their rows in rows[1] (SRC_LIST1).
+
+// Per (child, feature): best bin of one feature of a candidate node, with the
+// exact left sums of the winning bin. v: the lane's 8 bins (exclusive of
+// nothing: raw bin sums), per channel. Lane 0 writes the record and folds the
+// feature into node_key[c].
+template <int C>
+__device__ __forceinline__ void bf_scan_feature(const GrowParams& p, const GrowBufs& b, const TreeIO& io,
+                                                long long (&v)[C][8], int c, int f, float pm, float ginv,
+                                                float hinv) {
+  const int lane = threadIdx.x & 31;
+  const float lam = p.lam, gam = p.gamma, mcw = p.mcw, fmsl = (float)p.msl;
+  const bool fok = !(p.use_fmask && io.fmask && !io.fmask[f]);
+  long long lt[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+#pragma unroll
+    for (int i = 1; i < 8; ++i) v[k][i] += v[k][i - 1];
+    long long x = v[k][7];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    lt[k] = __shfl_sync(0xffffffffu, x, 31);
+    const long long excl = x - v[k][7];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[k][i] += excl;
+  }
+  const float G = __fmul_rn(__ll2float_rn(lt[0]), ginv);
+  const float H = (C == 3) ? __fmul_rn(__ll2float_rn(lt[1]), hinv) : __ll2float_rn(lt[C - 1]);
+  const float Cn = __ll2float_rn(lt[C - 1]);
+  const float t3 = __fdiv_rn(__fmul_rn(G, G), __fadd_rn(H, lam));
+  const float boost = p.use_imat ? __fadd_rn(1.f, __fmul_rn(p.ib, pm)) : 1.f;
+  float bsel = -INFINITY, bgain = -INFINITY;
+  int bbin = 0;
+  long long bgl = 0, bhl = 0, bcl = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int bin = lane * 8 + i;
+    const float GL = __fmul_rn(__ll2float_rn(v[0][i]), ginv);
+    const float CL = __ll2float_rn(v[C - 1][i]);
+    const float HL = (C == 3) ? __fmul_rn(__ll2float_rn(v[1][i]), hinv) : CL;
+    const float GR = __fsub_rn(G, GL), HR = __fsub_rn(H, HL), CR = __fsub_rn(Cn, CL);
+    const float t1 = __fdiv_rn(__fmul_rn(GL, GL), __fadd_rn(HL, lam));
+    const float t2 = __fdiv_rn(__fmul_rn(GR, GR), __fadd_rn(HR, lam));
+    float gain = __fsub_rn(__fmul_rn(0.5f, __fsub_rn(__fadd_rn(t1, t2), t3)), gam);
+    const bool valid = fok && bin != YABT_NB - 1 && CL >= fmsl && CR >= fmsl && HL >= mcw && HR >= mcw;
+    if (!valid) gain = -INFINITY;
+    const float sel = p.use_imat ? __fmul_rn(gain, boost) : gain;
+    if (i == 0 || sel > bsel) {
+      bsel = sel; bgain = gain; bbin = bin;
+      bgl = v[0][i]; bhl = v[C - 2][i]; bcl = v[C - 1][i];
+    }
+  }
+  // warp argmax: larger sel wins, ties -> lower bin
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, bsel, o);
+    const int ob = __shfl_xor_sync(0xffffffffu, bbin, o);
+    const float og = __shfl_xor_sync(0xffffffffu, bgain, o);
+    const long long ogl = __shfl_xor_sync(0xffffffffu, bgl, o);
+    const long long ohl = __shfl_xor_sync(0xffffffffu, bhl, o);
+    const long long ocl = __shfl_xor_sync(0xffffffffu, bcl, o);
+    if (os > bsel || (os == bsel && ob < bbin)) {
+      bsel = os; bbin = ob; bgain = og; bgl = ogl; bhl = ohl; bcl = ocl;
+    }
+  }
+  if (lane == 0) {
+    BfCand r;
+    r.gain = bgain; r.f = f; r.bin = bbin; r.flag = 0;
+    r.gl = bgl; r.cl = bcl; r.hl = (C == 3) ? bhl : bcl;
+    r.g = lt[0]; r.c = lt[C - 1]; r.h = (C == 3) ? lt[1] : lt[C - 1];
+    b.bf_feat[(size_t)c * p.F + f] = r;
+    atomicMax(&b.node_key[c], ((unsigned long long)f2ord(bsel) << 32) | (0xffffffffu - (unsigned)f));
+  }
+}
+
+// Scan of the root (root != 0: the level-0 histogram in `small`) or of the two
+// children of the node the last k_bf_pick split. Blocks [0, fblocks): one warp
+// per feature handles both children (the left child's slot is the parent's,
+// so the parent's bins are read before either child is written). Blocks
+// beyond: the children's row ranges (copied back from rows[1] to rows[0] when
+// the children stay candidates).
+template <int C>
+__global__ void __launch_bounds__(SCAN_WARPS * 32)
+k_bf_scan(GrowParams p, GrowBufs b, TreeIO io, int root) {
+  GrowState* st = b.st;
+  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t FB = (size_t)p.F * YABT_NB;
+  const size_t HN = (size_t)C * FB;
+  if (root) {
+    if (!st->active) return;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      b.leaf_src[0] = SRC_IDENTITY; b.leaf_begin[0] = 0; b.leaf_count[0] = (int)io.n_root;
+      b.node_slot[0] = 0;
+      st->bf_next_slot = 1; st->bf_split = -2; st->bf_scan = 1;
+    }
+  } else {
+    if (st->bf_split < 0) return;
+    if (blockIdx.x >= fblocks) {
+      // children row ranges; while they stay candidates their rows go back to rows[0]
+      const int nl = st->n_nodes - 2, nr = nl + 1;
+      const int B = b.seg_begin[0][0], cnt = b.seg_count[0][0];
+      const int keep = st->bf_scan;
+      if (blockIdx.x == fblocks && threadIdx.x == 0) {
+        const int src = keep ? SRC_LIST0 : SRC_LIST1;
+        b.leaf_src[nl] = src; b.leaf_begin[nl] = b.seg_begin[1][0]; b.leaf_count[nl] = b.seg_count[1][0];
+        b.leaf_src[nr] = src; b.leaf_begin[nr] = b.seg_begin[1][1]; b.leaf_count[nr] = b.seg_count[1][1];
+      }
+      if (keep) {
+        const int nb = gridDim.x - fblocks;
+        for (int i = (blockIdx.x - fblocks) * blockDim.x + threadIdx.x; i < cnt; i += nb * blockDim.x)
+          b.rows[0][B + i] = b.rows[1][B + i];
+      }
+      return;
+    }
+    if (!st->bf_scan) return;
+  }
+  const int f = blockIdx.x * SCAN_WARPS + warp;
+  if (blockIdx.x >= fblocks || f >= p.F) return;
+  const float ginv = st->ginv, hinv = st->hinv;
+  const long long* sm = b.small + (size_t)f * YABT_NB + lane * 8;
+  const long long* scnt = b.small + (size_t)(C - 1) * FB + (size_t)f * (YABT_NB / 2) + lane * 4;
+  long long vs[C][8];
+#pragma unroll
+  for (int c = 0; c < C - 1; ++c) {
+    const longlong2* q = reinterpret_cast<const longlong2*>(sm + c * FB);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const longlong2 t = q[i]; vs[c][2 * i] = t.x; vs[c][2 * i + 1] = t.y; }
+  }
+  {
+    const longlong2* q = reinterpret_cast<const longlong2*>(scnt);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const longlong2 t = q[i];
+      vs[C - 1][4 * i + 0] = (long long)((unsigned long long)t.x & 0xffffffffULL);
+      vs[C - 1][4 * i + 1] = (long long)((unsigned long long)t.x >> 32);
+      vs[C - 1][4 * i + 2] = (long long)((unsigned long long)t.y & 0xffffffffULL);
+      vs[C - 1][4 * i + 3] = (long long)((unsigned long long)t.y >> 32);
+    }
+  }
+  if (root) {
+    if (p.max_depth > 0) {
+      long long* dst = b.hist[0] + (size_t)f * YABT_NB + lane * 8;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        longlong2* q = reinterpret_cast<longlong2*>(dst + c * FB);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = make_longlong2(vs[c][2 * i], vs[c][2 * i + 1]);
+      }
+    }
+    bf_scan_feature<C>(p, b, io, vs, 0, f, b.pathmax[0][f], ginv, hinv);
+    return;
+  }
+  // children of node m: the small one from `small`, the other = parent - small
+  const int m = st->bf_split;
+  const int nl = st->n_nodes - 2, nr = nl + 1;
+  const int ps = b.node_slot[nl], rs = b.node_slot[nr];
+  const bool sil = b.pair_sil[0] != 0;
+  long long vo[C][8];
+  {
+    const long long* par = b.hist[0] + (size_t)ps * HN + (size_t)f * YABT_NB + lane * 8;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const longlong2* q = reinterpret_cast<const longlong2*>(par + c * FB);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const longlong2 t = q[i];
+        vo[c][2 * i] = t.x - vs[c][2 * i];
+        vo[c][2 * i + 1] = t.y - vs[c][2 * i + 1];
+      }
+    }
+  }
+  float pm = 0.f;
+  if (p.use_imat) {
+    pm = fmaxf(b.pathmax[0][(size_t)ps * p.F + f], io.imat[(size_t)io.feature[m] * p.F + f]);
+    __syncwarp();
+    if (lane == 0) {
+      b.pathmax[0][(size_t)ps * p.F + f] = pm;
+      b.pathmax[0][(size_t)rs * p.F + f] = pm;
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    long long v[C][8];
+    const bool from_small = (ch == 0) == sil;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] = from_small ? vs[c][i] : vo[c][i];
+    long long* dst = b.hist[0] + (size_t)(ch == 0 ? ps : rs) * HN + (size_t)f * YABT_NB + lane * 8;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      longlong2* q = reinterpret_cast<longlong2*>(dst + c * FB);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[i] = make_longlong2(v[c][2 * i], v[c][2 * i + 1]);
+    }
+    bf_scan_feature<C>(p, b, io, v, ch, f, pm, ginv, hinv);
+  }
+}
+
+__device__ __forceinline__ float bf_value(const GrowParams& p, const GrowState* st, long long g, long long h) {
+  // leaf value -lr * G / (H + lambda) in double on the float32 sums, yabt/tree.py:233-243
+  const float G = __fmul_rn(__ll2float_rn(g), st->ginv);
+  const float H = p.general ? __fmul_rn(__ll2float_rn(h), st->hinv) : __ll2float_rn(h);
+  return (float)(-(double)p.lr * (double)G / ((double)H + (double)p.lam));
+}
+
+// One block. Commits the candidates the last k_bf_scan produced, pops the best
+// candidate (largest gain, ties -> lower node id) and sets up its split: the
+// tree arrays of the node and its two children, and the partition of its row
+// range (one active position, `part_gate` selects the source list).
+__global__ void __launch_bounds__(1024)
+k_bf_pick(GrowParams p, GrowBufs b, TreeIO io, int part_gate) {
+  GrowState* st = b.st;
+  if (!st->active) return;
+  __shared__ unsigned long long s_key;
+  __shared__ int s_m;
+  const int split = st->bf_split;
+  const int n0 = st->n_nodes;
+  // A: commit the scanned nodes (the root, or the two newest nodes)
+  const int ncommit = !st->bf_scan ? 0 : split == -2 ? 1 : split >= 0 ? 2 : 0;
+  if (threadIdx.x < ncommit) {
+    const int c = threadIdx.x;
+    const int gid = split == -2 ? 0 : n0 - 2 + c;
+    const unsigned long long key = b.node_key[c];
+    const int f = (int)(0xffffffffu - (unsigned)(key & 0xffffffffULL));
+    BfCand r = b.bf_feat[(size_t)c * p.F + ((unsigned)f < (unsigned)p.F ? f : 0)];
+    r.flag = (b.node_depth[gid] < p.max_depth && r.gain > 0.f) ? 1 : 0;
+    b.bf_cand[gid] = r;
+    if (split == -2) io.value[0] = bf_value(p, st, r.g, r.h);
+  }
+  if (threadIdx.x < 2) b.node_key[threadIdx.x] = 0ULL;
+  if (threadIdx.x == 0) s_key = 0ULL;
+  __syncthreads();
+  // B: pop the best candidate
+  const int leaves = (n0 + 1) / 2;
+  if (leaves < p.max_leaves) {
+    for (int g = threadIdx.x; g < n0; g += blockDim.x) {
+      const BfCand& r = b.bf_cand[g];
+      if (r.flag) atomicMax(&s_key, ((unsigned long long)f2ord(r.gain) << 32) | (0xffffffffu - (unsigned)g));
+    }
+  }
+  __syncthreads();
+  const unsigned long long key = s_key;
+  if (key == 0ULL || n0 + 2 > p.maxn) {
+    if (threadIdx.x == 0) {
+      if (key != 0ULL) atomicOr(&st->err, DERR_NODE_OVERFLOW);
+      st->active = 0; st->bf_split = -1; st->bf_scan = 0;
+      st->level = -1; st->part_level = -1; st->plan_level = -1;
+    }
+    return;
+  }
+  const int m = (int)(0xffffffffu - (unsigned)(key & 0xffffffffULL));
+  const BfCand r = b.bf_cand[m];
+  const int B = b.leaf_begin[m], cnt = b.leaf_count[m];
+  const int nt = (cnt + PART_TILE - 1) / PART_TILE;
+  if (threadIdx.x == 0) {
+    const int f = r.f, bin = r.bin, ne = io.edge_cnt[f];
+    const int nl = n0, nr = n0 + 1, d = b.node_depth[m] + 1;
+    b.bf_cand[m].flag = 0;
+    io.feature[m] = f;
+    io.threshold[m] = io.edges[io.edge_off[f] + min(bin, ne - 1)];
+    io.gate[m] = fmaxf(io.scales[f], 1e-12f);
+    io.value[m] = 0.f;
+    io.left[m] = nl; io.right[m] = nr;
+    b.node_bin[m] = bin;
+    const float vL = bf_value(p, st, r.gl, r.hl);
+    const float vR = bf_value(p, st, r.g - r.gl, r.h - r.hl);
+    for (int k = 0; k < 2; ++k) {
+      const int q = n0 + k;
+      io.feature[q] = -1; io.threshold[q] = 0.f; io.left[q] = -1; io.right[q] = -1;
+      io.value[q] = k == 0 ? vL : vR; io.gate[q] = 1.f;
+      b.node_depth[q] = d; b.node_bin[q] = -1;
+      b.bf_cand[q].flag = 0;
+    }
+    b.node_slot[nl] = b.node_slot[m];
+    b.node_slot[nr] = st->bf_next_slot;
+    st->bf_next_slot = st->bf_next_slot + 1;
+    // the partition of one active position (pair 0); smaller child by row count
+    b.seg_begin[0][0] = B; b.seg_count[0][0] = cnt;
+    // children inherit the region; the partition's last tile fills in the split
+    // point (a rank with no rows of the node has no tile)
+    b.seg_begin[1][0] = B; b.seg_count[1][0] = 0;
+    b.seg_begin[1][1] = B; b.seg_count[1][1] = cnt;
+    b.split_pair[0] = 0; b.split_f[0] = f; b.split_b[0] = bin;
+    b.pair_pos[0] = 0; b.pair_sil[0] = r.cl <= r.c - r.cl;
+    const int leaves_after = leaves + 1;
+    const int scan = d < p.max_depth && leaves_after < p.max_leaves;
+    st->n_nodes = n0 + 2;
+    st->depth_max = max(st->depth_max, d);
+    st->bf_split = m; st->bf_scan = scan;
+    st->P = 1; st->M = 1;
+    st->n_tiles = nt; st->tile_counter = 0;
+    st->epoch = st->epoch + 1;
+    st->part_level = part_gate;
+    st->plan_level = scan ? part_gate : -1;
+    st->level = scan ? 1 : -1;           // the histogram kernels run at level 1 (rows[1])
+    st->active = leaves_after < p.max_leaves ? 1 : 0;
+  }
+  for (int e = threadIdx.x; e < nt; e += blockDim.x) {
+    PartTile t;
+    t.pos = 0; t.begin = B + e * PART_TILE; t.end = min(B + cnt, t.begin + PART_TILE);
+    t.last = e == nt - 1; t.t_in_node = e;
+    t.pad[0] = t.pad[1] = t.pad[2] = 0;
+    b.tiles[e] = t;
+  }
+}
+
+cudaError_t launch_bf_root_scan(const GrowParams& p, const GrowBufs& b, const TreeIO& io, cudaStream_t s) {
+  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  if (!p.general) k_bf_scan<2><<<fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, 1);
+  else k_bf_scan<3><<<fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, 1);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+// One best-first step, first half: pop the best candidate, partition its rows
+// and histogram the smaller child into `small`. Step 1 splits the root, whose
+// rows are root positions (partition gate 0); later steps read rows[0] (gate 2).
+cudaError_t launch_bf_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int step, int nsm,
+                            cudaStream_t s) {
+  const int gate = step == 1 ? 0 : 2;
+  k_bf_pick<<<1, 1024, 0, s>>>(p, b, io, gate);
+  const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
+  k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, gate);
+  k_plan<<<1, 1024, 0, s>>>(p, b, gate);
+  count_launches(3);
+  return launch_hist_kernels(p, b, io, 1, 1, nsm, s, nullptr);
+}
+
+// Second half: the children's histograms, scans and row ranges.
+cudaError_t launch_bf_scan(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm, cudaStream_t s) {
+  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  const int grid = fblocks + std::max(1, std::min<int>(nsm, (int)((p.n + 2047) / 2048)));
+  if (!p.general) k_bf_scan<2><<<grid, SCAN_WARPS * 32, 0, s>>>(p, b, io, 0);
+  else k_bf_scan<3><<<grid, SCAN_WARPS * 32, 0, s>>>(p, b, io, 0);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ host side
 struct HostStep {
   int S, LIMBS, C;

@@ -65,6 +65,14 @@ struct NodeBest {       // best split of one (node, feature)
   long long cl;         // exact left row count (global)
 };
 
+struct BfCand {         // best-first: a node's chosen split with exact sums
+  float gain;           // true gain (-inf: no valid split)
+  int f, bin;
+  int flag;             // 1: a candidate (gain > 0, depth < max_depth, still a leaf)
+  long long gl, hl, cl; // exact left sums at the split (hl = cl on the unit-hessian path)
+  long long g, h, c;    // exact node totals
+};
+
 struct NodeTot {        // node totals
   float G, H, C;
   int pad;
@@ -92,7 +100,9 @@ struct GrowState {
   int depth_max;        // deepest node depth so far
   unsigned amax_g, amax_h;  // bit patterns of max |g| and max |h|
   int n_leaves;
-  int pad[2];
+  int bf_split;         // best-first: node split by the current step (-2: root scanned, -1: none)
+  int bf_next_slot;     // best-first: next free histogram slot
+  int bf_scan;          // best-first: 1 if the children of bf_split are histogrammed and scanned
   long long hist_rows[64];   // rows histogrammed at each level (algorithmic-traffic accounting)
   long long acc_root_rows;   // accumulated since the last yabt_grower_acc_reset: root-level rows,
   long long acc_child_rows;  // smaller-child rows of deeper levels,
@@ -153,6 +163,10 @@ struct GrowBufs {
   int* leaf_count;       // [maxn]
   int* node_depth;       // [maxn]
   int* node_bin;         // [maxn] split bin of internal nodes, -1 at leaves
+  // best-first growth
+  BfCand* bf_feat;       // [2][F] per child position and feature: best split of the feature
+  BfCand* bf_cand;       // [maxn] per node: its best split
+  int* node_slot;        // [maxn] histogram / path-max slot of a leaf (slots < maxa)
 };
 
 // Caller-owned inputs / outputs of one tree.

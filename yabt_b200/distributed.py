@@ -314,6 +314,55 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
 
 
+def grow_tree_bestfirst(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
+    """Best-first growth (yabt/tree.py:206-360) over the rows of every rank:
+    the step-wise best-first API with the quantisation words, the root
+    histogram and each step's smaller-child histogram (one job) summed between
+    the halves of a step. The candidate choice reads only summed histograms,
+    so every rank splits the same nodes and makes the same collective calls;
+    the host stops LOOKAHEAD steps after the device reports the tree complete."""
+    lib = grower.lib
+    h = grower.h
+    s = _lib.stream_ptr()
+    ref = ctypes.byref(a)
+    if not hasattr(grower, "_level_ring"):
+        grower._level_ring = [(torch.cuda.Event(), torch.zeros(4, dtype=torch.int32).pin_memory())
+                              for _ in range(8)]
+    ring = grower._level_ring
+    state = _view(grower.ws, lib.yabt_grow_level_ptr(h), 4, torch.int32)
+    _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
+    comm.max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
+    _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
+    xchg = getattr(grower, "_exchange", None)
+    if xchg is None and comm.peer_exchange:
+        xchg = grower._exchange = PeerExchange(grower, comm)
+    per_job = int(lib.yabt_grow_small_count(h, 0))
+    small = _view(grower.ws, lib.yabt_grow_small_ptr(h), per_job, torch.int64)
+
+    def reduce(level):
+        if xchg is not None:
+            xchg.reduce(level)           # sizes itself from the device state (a no-op step skips)
+        else:
+            comm.sum_(small)
+
+    _lib.check(lib.yabt_grow_bf_root_hist(h, ref, s), "yabt_grow_bf_root_hist")
+    reduce(0)
+    _lib.check(lib.yabt_grow_bf_scan(h, ref, 0, s), "yabt_grow_bf_scan")
+    for k in range(1, max(1, grower.max_leaves - 1) + 1):
+        _lib.check(lib.yabt_grow_bf_split(h, ref, k, s), "yabt_grow_bf_split")
+        reduce(1)                            # the best-first histogram runs at level 1
+        _lib.check(lib.yabt_grow_bf_scan(h, ref, k, s), "yabt_grow_bf_scan")
+        ev_k, host_k = ring[k % 8]
+        host_k.copy_(state, non_blocking=True)
+        ev_k.record()
+        if k > LOOKAHEAD:
+            ev_o, host_o = ring[(k - LOOKAHEAD) % 8]
+            ev_o.synchronize()
+            if not int(host_o[1]):           # identical on every rank
+                break
+    _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
+
+
 def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, comm: ShardComm) -> None:
     """Leaf models of one tree over the rows of every rank: the three stages
     of yabt_leafnet_stage with the statistics reduced in between."""

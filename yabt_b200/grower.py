@@ -112,9 +112,15 @@ class Grower:
             setattr(a, k, out[k].data_ptr())
         return a
 
-    def grow(self, a: _lib.TreeArgs, stream=None) -> None:
-        _lib.check(self.lib.yabt_grow_tree(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
-                   "yabt_grow_tree")
+    def grow(self, a: _lib.TreeArgs, stream=None, bestfirst: bool = False) -> None:
+        """One tree: level-wise (yabt/tree.py:362-625), or best-first, the heap
+        grower of yabt/tree.py:206-360."""
+        if bestfirst:
+            _lib.check(self.lib.yabt_grow_tree_bestfirst(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
+                       "yabt_grow_tree_bestfirst")
+        else:
+            _lib.check(self.lib.yabt_grow_tree(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
+                       "yabt_grow_tree")
 
     def _empty_root(self) -> torch.Tensor:
         if getattr(self, "_empty", None) is None:
@@ -180,19 +186,10 @@ def trim_tree(out: dict, n_nodes: int, depth: int) -> Tree:
 _GROWERS: dict = {}
 
 
-def grow_tree_levelwise(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor, binner,
-                        params: TreeParams, feature_mask: torch.Tensor | None = None,
-                        interaction_matrix: torch.Tensor | None = None,
-                        interaction_boost: float = 0.5, *, return_leaf: bool = False):
-    """Drop-in for yabt/tree.py:362-625 on a CUDA device.
-
-    ``binned`` is the plain (n, F) uint8 bin matrix (it is packed into the
-    tiled layout on the device). The hessian channel is dropped when every
-    hessian equals 1 (squared loss), which the reference's float32 sums of
-    ones reproduce exactly. Returns the ``Tree`` (and the leaf of every row
-    when ``return_leaf``)."""
+def _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matrix, interaction_boost,
+              return_leaf, bestfirst, name):
     if binned.device.type != "cuda":
-        raise ValueError("grow_tree_levelwise (yabt_b200) needs CUDA tensors")
+        raise ValueError(f"{name} (yabt_b200) needs CUDA tensors")
     n, F = binned.shape
     dev = binned.device
     general = not bool(torch.all(hess == 1.0))
@@ -208,7 +205,7 @@ def grow_tree_levelwise(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Te
     g = grad.to(torch.float32).contiguous()
     h = hess.to(torch.float32).contiguous()
     a = gr.args(tiled, g, h, ep, params, out, fm, im, interaction_boost)
-    gr.grow(a)
+    gr.grow(a, bestfirst=bestfirst)
     meta = out["meta"].tolist()
     if meta[2] != 0:
         raise _lib.YabtError(f"device error bits 0x{meta[2]:x} while growing a tree")
@@ -216,3 +213,31 @@ def grow_tree_levelwise(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Te
     if return_leaf:
         return tree, out["leaf_of_row"].to(torch.int64)
     return tree
+
+
+def grow_tree_levelwise(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor, binner,
+                        params: TreeParams, feature_mask: torch.Tensor | None = None,
+                        interaction_matrix: torch.Tensor | None = None,
+                        interaction_boost: float = 0.5, *, return_leaf: bool = False):
+    """Drop-in for yabt/tree.py:362-625 on a CUDA device.
+
+    ``binned`` is the plain (n, F) uint8 bin matrix (it is packed into the
+    tiled layout on the device). The hessian channel is dropped when every
+    hessian equals 1 (squared loss), which the reference's float32 sums of
+    ones reproduce exactly. Returns the ``Tree`` (and the leaf of every row
+    when ``return_leaf``)."""
+    return _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matrix, interaction_boost,
+                     return_leaf, False, "grow_tree_levelwise")
+
+
+def grow_tree(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor, binner,
+              params: TreeParams, feature_mask: torch.Tensor | None = None,
+              interaction_matrix: torch.Tensor | None = None,
+              interaction_boost: float = 0.5, *, return_leaf: bool = False):
+    """Drop-in for the best-first (heap) grower yabt/tree.py:206-360 on a CUDA
+    device, axis splits (kernel splits are not part of this path): the leaf
+    with the largest split gain is split first (ties: the earlier-pushed,
+    i.e. lower node id), up to ``max_leaves`` leaves and ``max_depth``.
+    Arguments and results as :func:`grow_tree_levelwise`."""
+    return _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matrix, interaction_boost,
+                     return_leaf, True, "grow_tree")
