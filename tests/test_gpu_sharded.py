@@ -35,10 +35,11 @@ def _data():
     return X, y
 
 
-def _params(neural: bool, subsample: float = 1.0):
+def _params(neural: bool, subsample: float = 1.0, levelwise="auto"):
+    """max_leaves=15: "auto" grows best-first (yabt/boosting.py:420), True level-wise."""
     from yabt_b200.boosting import BoostParams
     return BoostParams(n_estimators=4, max_leaves=15, max_depth=5, learning_rate=0.3, neural_leaves=neural,
-                       leaf_net_min_samples=50, min_samples_leaf=20, subsample=subsample)
+                       leaf_net_min_samples=50, min_samples_leaf=20, subsample=subsample, levelwise=levelwise)
 
 
 def _summary(b, Xt):
@@ -50,7 +51,7 @@ def _summary(b, Xt):
                 scales=scales.cpu().numpy(), trees=trees, pred=b.predict_margin(Xt))
 
 
-def _worker(rank, world, port, backend, neural, q, subsample=1.0):
+def _worker(rank, world, port, backend, neural, q, subsample=1.0, levelwise="auto"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -64,7 +65,7 @@ def _worker(rank, world, port, backend, neural, q, subsample=1.0):
         X, y = _data()
         off = sum(SPLIT[:rank])
         sl = slice(off, off + SPLIT[rank])
-        b = Booster(_params(neural, subsample), MSELoss())
+        b = Booster(_params(neural, subsample, levelwise), MSELoss())
         b.fit(X[sl], y[sl], comm=ShardComm())
         torch.cuda.synchronize()
         q.put((rank, _summary(b, X[:1500])))
@@ -75,13 +76,13 @@ def _worker(rank, world, port, backend, neural, q, subsample=1.0):
         dist.destroy_process_group()
 
 
-def _run_sharded(backend, neural, subsample=1.0):
+def _run_sharded(backend, neural, subsample=1.0, levelwise="auto"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q, subsample)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q, subsample, levelwise)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in range(2))
@@ -92,10 +93,10 @@ def _run_sharded(backend, neural, subsample=1.0):
     return res
 
 
-def _single(neural, subsample=1.0):
+def _single(neural, subsample=1.0, levelwise="auto"):
     from yabt_b200.boosting import Booster, MSELoss
     X, y = _data()
-    b = Booster(_params(neural, subsample), MSELoss())
+    b = Booster(_params(neural, subsample, levelwise), MSELoss())
     b.fit(X, y)
     return _summary(b, X[:1500])
 
@@ -127,9 +128,10 @@ def _compare(res, ref, neural):
     np.testing.assert_array_equal(res[0]["pred"], res[1]["pred"])
 
 
+@pytest.mark.parametrize("levelwise", [True, "auto"])
 @pytest.mark.parametrize("neural", [False, True])
-def test_two_ranks_one_gpu_gloo(neural):
-    _compare(_run_sharded("gloo", neural), _single(neural), neural)
+def test_two_ranks_one_gpu_gloo(neural, levelwise):
+    _compare(_run_sharded("gloo", neural, levelwise=levelwise), _single(neural, levelwise=levelwise), neural)
 
 
 def test_two_ranks_subsample_gloo():
@@ -138,5 +140,8 @@ def test_two_ranks_subsample_gloo():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_nccl():
-    _compare(_run_sharded("nccl", True), _single(True), True)
+@pytest.mark.parametrize("levelwise", [True, "auto"])
+def test_two_ranks_nccl(levelwise):
+    """One rank per GPU: the level (or best-first step) histograms are summed by
+    the NVLink exchange kernel."""
+    _compare(_run_sharded("nccl", True, levelwise=levelwise), _single(True, levelwise=levelwise), True)
