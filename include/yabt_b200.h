@@ -172,6 +172,13 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream);
  *   for step = 1 .. max(1, max_leaves - 1): bf_split(step), [reduce], bf_scan(step)
  *   end.                                                                    */
 int yabt_grow_tree_bestfirst(yabt_grower* g, const yabt_tree_args* a, void* stream);
+/* Arithmetic of best-first growth: 0 (default) that of the heap grower
+ * yabt/tree.py:206-360 (float32 split scan, ties to the earlier push); 1 that
+ * of the C / Numba grower cgrow (yabt/_cgrow/grow.c:243-427, wrapped by
+ * grow_tree_c, yabt/grow_c.py:336-456): float64 split scan over bins below
+ * min(edges + 1, 256), float64 leaf values, ties to the lower active-leaf
+ * slot.                                                                   */
+int yabt_grower_set_bestfirst_f64(yabt_grower* g, int on);
 int yabt_grow_bf_root_hist(yabt_grower* g, const yabt_tree_args* a, void* stream);
 int yabt_grow_bf_split(yabt_grower* g, const yabt_tree_args* a, int step, void* stream);
 int yabt_grow_bf_scan(yabt_grower* g, const yabt_tree_args* a, int step, void* stream);

@@ -48,7 +48,8 @@ def _p(a: np.ndarray):
 
 def grow(binned_fm: np.ndarray, grad: np.ndarray, hess: np.ndarray, nbins: np.ndarray,
          max_leaves: int, max_depth: int, lam=1.0, gamma=0.0, mcw=1e-3, msl=20, lr=0.1,
-         imat: np.ndarray | None = None, ib: float = 0.5, threads: int = 0):
+         imat: np.ndarray | None = None, ib: float = 0.5, threads: int = 0,
+         fmask: np.ndarray | None = None):
     """One leaf-wise tree with the reference C grower. binned_fm is (F, n) uint8.
     Returns (feature, thr_bin, left, right, value, depth) arrays."""
     lib = load()
@@ -56,7 +57,7 @@ def grow(binned_fm: np.ndarray, grad: np.ndarray, hess: np.ndarray, nbins: np.nd
     m = 2 * max_leaves + 1
     outs = [np.empty(m, np.int64) for _ in range(4)] + [np.empty(m, np.float32), np.empty(m, np.int64)]
     z64, z32 = np.zeros(1, np.int64), np.zeros(1, np.int32)
-    fmask = np.ones(F, np.uint8)
+    fmask = np.ones(F, np.uint8) if fmask is None else np.ascontiguousarray(fmask, np.uint8)
     im = np.ascontiguousarray(imat, np.float32) if imat is not None else np.zeros((1, 1), np.float32)
     k = lib.cgrow(_p(binned_fm), _p(grad), _p(hess), _p(fmask), _p(im), float(ib), int(imat is not None),
                   _p(z64), _p(z32), _p(z32), _p(z32), 0, _p(nbins), n, F, 256, float(lam), float(gamma),

@@ -1,6 +1,10 @@
-"""CUDA best-first (heap) grower, yabt/tree.py:206-360, vs the CPU oracle
-restatement (oracle.grow.grow_bestfirst, itself pinned to the reference's own
-runs in tests/golden/bestfirst.npz)."""
+"""CUDA best-first growth on the GPU.
+
+* The heap grower, yabt/tree.py:206-360, against the CPU oracle restatement
+  (oracle.grow.grow_bestfirst, itself pinned to the reference's own runs in
+  tests/golden/bestfirst.npz).
+* The C / Numba grower's arithmetic (grow_tree_c) against the reference's own
+  C grower, yabt/_cgrow/grow.c, compiled from its source into oracle/_ref."""
 import numpy as np
 import pytest
 import torch
@@ -112,3 +116,65 @@ def test_booster_auto_uses_bestfirst_below_16_leaves():
         np.testing.assert_array_equal(gb.trees[t].feature.cpu().numpy(), ob.trees[t].feature, err_msg=f"tree {t}")
         np.testing.assert_array_equal(gb.trees[t].left.cpu().numpy(), ob.trees[t].left, err_msg=f"tree {t}")
     np.testing.assert_allclose(gb.predict_margin(X), ob.predict_margin(X), rtol=1e-4, atol=1e-4)
+
+
+def _cgrow_pair(seed, n, F, leaves, depth, msl, imat=None, fmask=None, unit_h=False, gamma=0.0):
+    from oracle import cgrow
+    from yabt_b200.grower import grow_tree_c
+    from yabt_b200.tree import TreeParams
+    if not cgrow.available():
+        pytest.skip("oracle/_ref/libcgrow.so not built")
+    X, g, h = _dyadic(seed, n, F)
+    if unit_h:
+        h = np.ones(n, np.float32)
+    b = OBinner().fit(X)
+    binned = b.transform(X)
+    nbins = np.array([min(len(e) + 1, 256) for e in b.edges_], np.int32)
+    ref = cgrow.grow(np.ascontiguousarray(binned.T), g, h, nbins, leaves, depth, lam=1.0, gamma=gamma, mcw=1e-3,
+                     msl=msl, lr=0.1, imat=imat, ib=0.5, fmask=fmask)
+    tp = TreeParams(max_leaves=leaves, max_depth=depth, min_samples_leaf=msl, gamma=gamma)
+    gt, gl = grow_tree_c(torch.from_numpy(binned).cuda(), torch.from_numpy(g).cuda(), torch.from_numpy(h).cuda(),
+                         b, tp, torch.from_numpy(fmask.astype(bool)).cuda() if fmask is not None else None,
+                         torch.from_numpy(imat).cuda() if imat is not None else None, 0.5, return_leaf=True)
+    return b, binned, ref, gt, gl.cpu().numpy()
+
+
+def _check_cgrow(b, binned, ref, gt, gl):
+    feat, thr_bin, left, right, value, depth = ref
+    np.testing.assert_array_equal(gt.feature.cpu().numpy(), feat, err_msg="feature")
+    np.testing.assert_array_equal(gt.left.cpu().numpy(), left, err_msg="left")
+    np.testing.assert_array_equal(gt.right.cpu().numpy(), right, err_msg="right")
+    np.testing.assert_array_equal(gt.value.cpu().numpy(), value, err_msg="value")   # float64 math on exact sums
+    thr = np.array([b.edges_[f][min(int(t), len(b.edges_[f]) - 1)] if f >= 0 else 0.0
+                    for f, t in zip(feat, thr_bin)], np.float32)
+    np.testing.assert_array_equal(gt.threshold.cpu().numpy(), thr, err_msg="threshold")
+    assert gt.depth == int(depth.max()) + 1
+    # the leaf of every row: the C grower's tree routed on the bins
+    node = np.zeros(binned.shape[0], np.int64)
+    for _ in range(int(depth.max()) + 1):
+        f = feat[node]
+        inner = f >= 0
+        go_left = binned[np.arange(len(node)), np.where(inner, f, 0)] <= thr_bin[node]
+        node = np.where(inner, np.where(go_left, left[node], right[node]), node)
+    np.testing.assert_array_equal(gl, node)
+
+
+@pytest.mark.parametrize("seed,n,F,leaves,depth", [(20, 3000, 8, 15, 64), (21, 20000, 20, 31, 64),
+                                                   (22, 5000, 70, 12, 3), (23, 1500, 10, 63, 10),
+                                                   (24, 257, 3, 15, 64), (25, 9000, 33, 2, 64)])
+def test_c_grower_math_matches_reference_cgrow(seed, n, F, leaves, depth):
+    """grow_tree_c on the GPU equals the reference's own C grower bit for bit
+    (dyadic gradients: the C grower's float32 histogram bins are exact)."""
+    _check_cgrow(*_cgrow_pair(seed, n, F, leaves, depth, 5 if n < 2000 else 20))
+
+
+def test_c_grower_math_unit_hessian_and_gamma():
+    _check_cgrow(*_cgrow_pair(26, 30000, 65, 31, 64, 20, unit_h=True, gamma=0.25))
+
+
+def test_c_grower_math_interaction_and_mask():
+    rng = np.random.default_rng(27)
+    imat = rng.random(size=(12, 12)).astype(np.float32)
+    fmask = (rng.random(12) < 0.7).astype(np.uint8)
+    fmask[0] = 1
+    _check_cgrow(*_cgrow_pair(27, 6000, 12, 14, 6, 20, imat, fmask))

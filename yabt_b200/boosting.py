@@ -151,6 +151,14 @@ def use_bestfirst(p: BoostParams) -> bool:
     return not (p.levelwise is True or (p.levelwise == "auto" and p.max_leaves >= 16))
 
 
+def use_c_grower_math(p: BoostParams) -> bool:
+    """Best-first trees in the C / Numba grower's arithmetic: the reference runs
+    that grower on a CUDA device when ``numba_grower=True`` and the level-wise
+    grower is off (yabt/boosting.py:424-426; ``c_grower`` only picks between
+    the C and Numba builds, which grow identical trees)."""
+    return use_bestfirst(p) and p.numba_grower is True
+
+
 def _check_supported(p: BoostParams) -> None:
     bad = []
     for name, ok in (("kernel_splits", not p.kernel_splits), ("refine_steps", p.refine_steps == 0),
@@ -297,6 +305,8 @@ class Booster:
                         gamma=p.gamma, min_child_weight=p.min_child_weight,
                         min_samples_leaf=p.min_samples_leaf, learning_rate=p.learning_rate)
         grower = Grower(n, F, p.max_leaves, p.max_depth, general, dev)
+        _lib.check(lib.yabt_grower_set_bestfirst_f64(grower.h, 1 if use_c_grower_math(p) else 0),
+                   "yabt_grower_set_bestfirst_f64")
         grower.set_level_wait(getattr(self, "_level_wait", True))
         self.grower_ = grower
         K = min(p.leaf_net_features, F) if p.neural_leaves else 0
@@ -368,7 +378,7 @@ class Booster:
             a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost,
                             bins_fm=data.bins_fm, root_rows=root)
             if comm is None:
-                grower.grow(a, bestfirst=bestfirst)
+                grower.grow(a, bestfirst=bestfirst, f64=use_c_grower_math(p))
             elif bestfirst:
                 from .distributed import grow_tree_bestfirst
                 grow_tree_bestfirst(grower, a, comm)

@@ -517,6 +517,12 @@ int yabt_grow_apply_all(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   return YABT_OK;
 }
 
+int yabt_grower_set_bestfirst_f64(yabt_grower* g, int on) {
+  if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
+  g->p.bf_f64 = on ? 1 : 0;
+  return YABT_OK;
+}
+
 int yabt_grower_set_level_wait(yabt_grower* g, int wait) {
   if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
   g->level_wait = wait ? 1 : 0;

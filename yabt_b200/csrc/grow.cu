@@ -838,12 +838,97 @@ __device__ __forceinline__ void bf_scan_feature(const GrowParams& p, const GrowB
   }
   if (lane == 0) {
     BfCand r;
-    r.gain = bgain; r.f = f; r.bin = bbin; r.flag = 0;
+    r.sel = bsel; r.gain = bgain; r.f = f; r.bin = bbin; r.flag = 0;
     r.gl = bgl; r.cl = bcl; r.hl = (C == 3) ? bhl : bcl;
     r.g = lt[0]; r.c = lt[C - 1]; r.h = (C == 3) ? lt[1] : lt[C - 1];
     b.bf_feat[(size_t)c * p.F + f] = r;
     atomicMax(&b.node_key[c], ((unsigned long long)f2ord(bsel) << 32) | (0xffffffffu - (unsigned)f));
   }
+}
+
+// The same in the arithmetic of the reference's C / Numba grower
+// (yabt/_cgrow/grow.c:124-199 best_split): float64 sums of the bins (here the
+// exact sums, converted), float64 gain in the same operand order without
+// contraction, candidate bins b < nbins - 1 with nbins = min(edges + 1, 256),
+// first maximum of gain * boost with a strict '>', and bin -1 when the
+// feature has no valid split. The node's feature is chosen in k_bf_pick.
+template <int C>
+__device__ __forceinline__ void bf_scan_feature_f64(const GrowParams& p, const GrowBufs& b, const TreeIO& io,
+                                                    long long (&v)[C][8], int c, int f, float pm, double ginv,
+                                                    double hinv) {
+  const int lane = threadIdx.x & 31;
+  const double lam = (double)p.lam, gam = (double)p.gamma, mcw = (double)p.mcw, msl = (double)p.msl;
+  const bool fok = !(p.use_fmask && io.fmask && !io.fmask[f]);
+  const int nb = min(io.edge_cnt[f] + 1, YABT_NB);
+  long long lt[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+#pragma unroll
+    for (int i = 1; i < 8; ++i) v[k][i] += v[k][i - 1];
+    long long x = v[k][7];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    lt[k] = __shfl_sync(0xffffffffu, x, 31);
+    const long long excl = x - v[k][7];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[k][i] += excl;
+  }
+  const double G = __dmul_rn((double)lt[0], ginv);
+  const double H = (C == 3) ? __dmul_rn((double)lt[1], hinv) : (double)lt[C - 1];
+  const double Cn = (double)lt[C - 1];
+  const double parent = __ddiv_rn(__dmul_rn(G, G), __dadd_rn(H, lam));
+  const double bo = p.use_imat ? (double)__fadd_rn(1.f, __fmul_rn(p.ib, pm)) : 1.0;
+  double bsel = -INFINITY, bgain = -INFINITY;
+  int bbin = -1;
+  long long bgl = 0, bhl = 0, bcl = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int bin = lane * 8 + i;
+    const double GL = __dmul_rn((double)v[0][i], ginv);
+    const double CL = (double)v[C - 1][i];
+    const double HL = (C == 3) ? __dmul_rn((double)v[1][i], hinv) : CL;
+    const double GR = __dsub_rn(G, GL), HR = __dsub_rn(H, HL), CR = __dsub_rn(Cn, CL);
+    if (!(fok && bin < nb - 1 && CL >= msl && CR >= msl && HL >= mcw && HR >= mcw)) continue;
+    const double t1 = __ddiv_rn(__dmul_rn(GL, GL), __dadd_rn(HL, lam));
+    const double t2 = __ddiv_rn(__dmul_rn(GR, GR), __dadd_rn(HR, lam));
+    const double gain = __dsub_rn(__dmul_rn(0.5, __dsub_rn(__dadd_rn(t1, t2), parent)), gam);
+    const double sel = __dmul_rn(gain, bo);
+    if (sel > bsel) {
+      bsel = sel; bgain = gain; bbin = bin;
+      bgl = v[0][i]; bhl = v[C - 2][i]; bcl = v[C - 1][i];
+    }
+  }
+  // warp: the first maximum in bin order (larger sel, ties -> lower bin; no valid bin = -1 last)
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const double os = __shfl_xor_sync(0xffffffffu, bsel, o);
+    const int ob = __shfl_xor_sync(0xffffffffu, bbin, o);
+    const double og = __shfl_xor_sync(0xffffffffu, bgain, o);
+    const long long ogl = __shfl_xor_sync(0xffffffffu, bgl, o);
+    const long long ohl = __shfl_xor_sync(0xffffffffu, bhl, o);
+    const long long ocl = __shfl_xor_sync(0xffffffffu, bcl, o);
+    const bool take = ob >= 0 && (bbin < 0 || os > bsel || (os == bsel && ob < bbin));
+    if (take) {
+      bsel = os; bbin = ob; bgain = og; bgl = ogl; bhl = ohl; bcl = ocl;
+    }
+  }
+  if (lane == 0) {
+    BfCand r;
+    r.sel = bsel; r.gain = (float)bgain; r.f = f; r.bin = bbin; r.flag = 0;
+    r.gl = bgl; r.cl = bcl; r.hl = (C == 3) ? bhl : bcl;
+    r.g = lt[0]; r.c = lt[C - 1]; r.h = (C == 3) ? lt[1] : lt[C - 1];
+    b.bf_feat[(size_t)c * p.F + f] = r;
+  }
+}
+
+template <int C>
+__device__ __forceinline__ void bf_scan_any(const GrowParams& p, const GrowBufs& b, const TreeIO& io,
+                                            long long (&v)[C][8], int c, int f, float pm, const GrowState* st) {
+  if (p.bf_f64) bf_scan_feature_f64<C>(p, b, io, v, c, f, pm, (double)st->ginv, (double)st->hinv);
+  else bf_scan_feature<C>(p, b, io, v, c, f, pm, st->ginv, st->hinv);
 }
 
 // Scan of the root (root != 0: the level-0 histogram in `small`) or of the two
@@ -890,7 +975,6 @@ k_bf_scan(GrowParams p, GrowBufs b, TreeIO io, int root) {
   }
   const int f = blockIdx.x * SCAN_WARPS + warp;
   if (blockIdx.x >= fblocks || f >= p.F) return;
-  const float ginv = st->ginv, hinv = st->hinv;
   const long long* sm = b.small + (size_t)f * YABT_NB + lane * 8;
   const long long* scnt = b.small + (size_t)(C - 1) * FB + (size_t)f * (YABT_NB / 2) + lane * 4;
   long long vs[C][8];
@@ -921,7 +1005,7 @@ k_bf_scan(GrowParams p, GrowBufs b, TreeIO io, int root) {
         for (int i = 0; i < 4; ++i) q[i] = make_longlong2(vs[c][2 * i], vs[c][2 * i + 1]);
       }
     }
-    bf_scan_feature<C>(p, b, io, vs, 0, f, b.pathmax[0][f], ginv, hinv);
+    bf_scan_any<C>(p, b, io, vs, 0, f, b.pathmax[0][f], st);
     return;
   }
   // children of node m: the small one from `small`, the other = parent - small
@@ -968,15 +1052,60 @@ k_bf_scan(GrowParams p, GrowBufs b, TreeIO io, int root) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) q[i] = make_longlong2(v[c][2 * i], v[c][2 * i + 1]);
     }
-    bf_scan_feature<C>(p, b, io, v, ch, f, pm, ginv, hinv);
+    bf_scan_any<C>(p, b, io, v, ch, f, pm, st);
   }
 }
 
 __device__ __forceinline__ float bf_value(const GrowParams& p, const GrowState* st, long long g, long long h) {
+  if (p.bf_f64) {
+    // -lr * G / (H + lambda) on the float64 sums, yabt/_cgrow/grow.c:318-323,355-363
+    const double G = __dmul_rn((double)g, (double)st->ginv);
+    const double H = p.general ? __dmul_rn((double)h, (double)st->hinv) : (double)h;
+    return (float)__ddiv_rn(__dmul_rn(-(double)p.lr, G), __dadd_rn(H, (double)p.lam));
+  }
   // leaf value -lr * G / (H + lambda) in double on the float32 sums, yabt/tree.py:233-243
   const float G = __fmul_rn(__ll2float_rn(g), st->ginv);
   const float H = p.general ? __fmul_rn(__ll2float_rn(h), st->hinv) : __ll2float_rn(h);
   return (float)(-(double)p.lr * (double)G / ((double)H + (double)p.lam));
+}
+
+// float64 mode: the child's feature is the first maximum of sel over features
+// with a valid split (yabt/_cgrow/grow.c:189-199); the whole block reduces.
+// Returns F when no feature has one.
+__device__ int bf_best_feature_f64(const GrowParams& p, const BfCand* __restrict__ rec) {
+  __shared__ double s_sel[32];
+  __shared__ int s_f[32];
+  __shared__ int s_best;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double bs = -INFINITY;
+  int bf = p.F;
+  for (int f = threadIdx.x; f < p.F; f += blockDim.x) {
+    const BfCand& r = rec[f];
+    if (r.bin >= 0 && (bf == p.F || r.sel > bs)) { bs = r.sel; bf = f; }
+  }
+  auto better = [&](double os, int of) { return of < p.F && (bf == p.F || os > bs || (os == bs && of < bf)); };
+  for (int o = 16; o; o >>= 1) {
+    const double os = __shfl_xor_sync(0xffffffffu, bs, o);
+    const int of = __shfl_xor_sync(0xffffffffu, bf, o);
+    if (better(os, of)) { bs = os; bf = of; }
+  }
+  if (lane == 0) { s_sel[warp] = bs; s_f[warp] = bf; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    bs = lane < nw ? s_sel[lane] : -INFINITY;
+    bf = lane < nw ? s_f[lane] : p.F;
+    for (int o = 16; o; o >>= 1) {
+      const double os = __shfl_xor_sync(0xffffffffu, bs, o);
+      const int of = __shfl_xor_sync(0xffffffffu, bf, o);
+      if (better(os, of)) { bs = os; bf = of; }
+    }
+    if (lane == 0) s_best = bf;
+  }
+  __syncthreads();
+  const int res = s_best;
+  __syncthreads();
+  return res;
 }
 
 // One block. Commits the candidates the last k_bf_scan produced, pops the best
@@ -988,21 +1117,28 @@ k_bf_pick(GrowParams p, GrowBufs b, TreeIO io, int part_gate) {
   GrowState* st = b.st;
   if (!st->active) return;
   __shared__ unsigned long long s_key;
-  __shared__ int s_m;
   const int split = st->bf_split;
   const int n0 = st->n_nodes;
   // A: commit the scanned nodes (the root, or the two newest nodes)
   const int ncommit = !st->bf_scan ? 0 : split == -2 ? 1 : split >= 0 ? 2 : 0;
-  if (threadIdx.x < ncommit) {
-    const int c = threadIdx.x;
-    const int gid = split == -2 ? 0 : n0 - 2 + c;
-    const unsigned long long key = b.node_key[c];
-    const int f = (int)(0xffffffffu - (unsigned)(key & 0xffffffffULL));
-    BfCand r = b.bf_feat[(size_t)c * p.F + ((unsigned)f < (unsigned)p.F ? f : 0)];
-    r.flag = (b.node_depth[gid] < p.max_depth && r.gain > 0.f) ? 1 : 0;
-    b.bf_cand[gid] = r;
-    if (split == -2) io.value[0] = bf_value(p, st, r.g, r.h);
+  for (int c = 0; c < ncommit; ++c) {
+    int f;
+    if (p.bf_f64) {
+      f = bf_best_feature_f64(p, b.bf_feat + (size_t)c * p.F);
+    } else {
+      const unsigned long long key = b.node_key[c];
+      f = (int)(0xffffffffu - (unsigned)(key & 0xffffffffULL));
+    }
+    if (threadIdx.x == 0) {
+      const int gid = split == -2 ? 0 : n0 - 2 + c;
+      BfCand r = b.bf_feat[(size_t)c * p.F + ((unsigned)f < (unsigned)p.F ? f : 0)];
+      if ((unsigned)f >= (unsigned)p.F) r.gain = -INFINITY;     // no valid split at all
+      r.flag = (b.node_depth[gid] < p.max_depth && r.gain > 0.f) ? 1 : 0;
+      b.bf_cand[gid] = r;
+      if (split == -2) io.value[0] = bf_value(p, st, r.g, r.h);
+    }
   }
+  __syncthreads();
   if (threadIdx.x < 2) b.node_key[threadIdx.x] = 0ULL;
   if (threadIdx.x == 0) s_key = 0ULL;
   __syncthreads();
@@ -1011,7 +1147,10 @@ k_bf_pick(GrowParams p, GrowBufs b, TreeIO io, int part_gate) {
   if (leaves < p.max_leaves) {
     for (int g = threadIdx.x; g < n0; g += blockDim.x) {
       const BfCand& r = b.bf_cand[g];
-      if (r.flag) atomicMax(&s_key, ((unsigned long long)f2ord(r.gain) << 32) | (0xffffffffu - (unsigned)g));
+      // ties: the earlier push (lower node id) for the heap grower; the lower
+      // active-leaf slot for the C / Numba grower (grow.c:299-306)
+      const unsigned tie = p.bf_f64 ? (unsigned)b.node_slot[g] : (unsigned)g;
+      if (r.flag) atomicMax(&s_key, ((unsigned long long)f2ord(r.gain) << 32) | (0xffffffffu - tie));
     }
   }
   __syncthreads();
@@ -1024,7 +1163,17 @@ k_bf_pick(GrowParams p, GrowBufs b, TreeIO io, int part_gate) {
     }
     return;
   }
-  const int m = (int)(0xffffffffu - (unsigned)(key & 0xffffffffULL));
+  __shared__ int s_pick;
+  if (threadIdx.x == 0) {
+    const unsigned tie = 0xffffffffu - (unsigned)(key & 0xffffffffULL);
+    int m = (int)tie;
+    if (p.bf_f64)            // the slot names the node: the leaf that holds it
+      for (int g = 0; g < n0; ++g)
+        if (b.bf_cand[g].flag && (unsigned)b.node_slot[g] == tie) { m = g; break; }
+    s_pick = m;
+  }
+  __syncthreads();
+  const int m = s_pick;
   const BfCand r = b.bf_cand[m];
   const int B = b.leaf_begin[m], cnt = b.leaf_count[m];
   const int nt = (cnt + PART_TILE - 1) / PART_TILE;

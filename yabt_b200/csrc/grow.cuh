@@ -66,8 +66,9 @@ struct NodeBest {       // best split of one (node, feature)
 };
 
 struct BfCand {         // best-first: a node's chosen split with exact sums
+  double sel;           // selection score (gain * boost); float64 mode: of the float64 gain
   float gain;           // true gain (-inf: no valid split)
-  int f, bin;
+  int f, bin;           // bin -1: the feature has no valid split (float64 mode)
   int flag;             // 1: a candidate (gain > 0, depth < max_depth, still a leaf)
   long long gl, hl, cl; // exact left sums at the split (hl = cl on the unit-hessian path)
   long long g, h, c;    // exact node totals
@@ -125,6 +126,7 @@ struct GrowParams {
   int msl;
   int use_imat;
   int use_fmask;
+  int bf_f64;           // best-first in the C / Numba grower's arithmetic (float64 scan, slot tie order)
 };
 
 // Device pointers of one grower workspace.

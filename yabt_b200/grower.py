@@ -112,10 +112,13 @@ class Grower:
             setattr(a, k, out[k].data_ptr())
         return a
 
-    def grow(self, a: _lib.TreeArgs, stream=None, bestfirst: bool = False) -> None:
-        """One tree: level-wise (yabt/tree.py:362-625), or best-first, the heap
-        grower of yabt/tree.py:206-360."""
+    def grow(self, a: _lib.TreeArgs, stream=None, bestfirst: bool = False, f64: bool = False) -> None:
+        """One tree: level-wise (yabt/tree.py:362-625), or best-first: the heap
+        grower of yabt/tree.py:206-360, or with ``f64`` the C / Numba grower's
+        arithmetic (yabt/_cgrow/grow.c:243-427)."""
         if bestfirst:
+            _lib.check(self.lib.yabt_grower_set_bestfirst_f64(self.h, 1 if f64 else 0),
+                       "yabt_grower_set_bestfirst_f64")
             _lib.check(self.lib.yabt_grow_tree_bestfirst(self.h, ctypes.byref(a), _lib.stream_ptr(stream)),
                        "yabt_grow_tree_bestfirst")
         else:
@@ -187,7 +190,7 @@ _GROWERS: dict = {}
 
 
 def _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matrix, interaction_boost,
-              return_leaf, bestfirst, name):
+              return_leaf, bestfirst, name, f64=False):
     if binned.device.type != "cuda":
         raise ValueError(f"{name} (yabt_b200) needs CUDA tensors")
     n, F = binned.shape
@@ -205,7 +208,7 @@ def _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matr
     g = grad.to(torch.float32).contiguous()
     h = hess.to(torch.float32).contiguous()
     a = gr.args(tiled, g, h, ep, params, out, fm, im, interaction_boost)
-    gr.grow(a, bestfirst=bestfirst)
+    gr.grow(a, bestfirst=bestfirst, f64=f64)
     meta = out["meta"].tolist()
     if meta[2] != 0:
         raise _lib.YabtError(f"device error bits 0x{meta[2]:x} while growing a tree")
@@ -241,3 +244,17 @@ def grow_tree(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor, binn
     Arguments and results as :func:`grow_tree_levelwise`."""
     return _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matrix, interaction_boost,
                      return_leaf, True, "grow_tree")
+
+
+def grow_tree_c(binned: torch.Tensor, grad: torch.Tensor, hess: torch.Tensor, binner,
+                params: TreeParams, feature_mask: torch.Tensor | None = None,
+                interaction_matrix: torch.Tensor | None = None,
+                interaction_boost: float = 0.5, *, return_leaf: bool = False):
+    """Drop-in for the reference's OpenMP C grower ``grow_tree_c``
+    (yabt/grow_c.py:336-456, kernel yabt/_cgrow/grow.c:243-427; the Numba
+    grower computes the same trees) on a CUDA device: best-first growth with
+    the C grower's float64 split scan and leaf values and its tie order.
+    Histograms are exact sums, so trees equal the C grower's wherever its
+    float32 histogram bins are exact (and agree to rounding elsewhere)."""
+    return _grow_one(binned, grad, hess, binner, params, feature_mask, interaction_matrix, interaction_boost,
+                     return_leaf, True, "grow_tree_c", f64=True)
