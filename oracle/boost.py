@@ -93,6 +93,31 @@ class BoostParams:
     subsample: float = 1.0
     seed: int = 0
     levelwise: bool | str = "auto"
+    goss_enabled: bool = False
+    goss_ratio: float = 0.9
+    goss_device: str = "cpu"      # the device of the sampler's generator (the reference's is the fit device)
+
+
+def _goss_rows(g: np.ndarray, ratio: float, gen, device: str):
+    """The GOSS draw, yabt/adaptive_features.py:75-110: the ceil-free budget
+    keep = max(1, round(n ratio)), top = max(1, min(keep, round(n (1 - ratio)))),
+    the top rows by |g| from a descending argsort, then randperm(rest)[:keep - top]
+    from the sampler's own generator, weighted (n - top) / drawn. The sort and the
+    generator are torch's on ``device`` (the reference draws on the fit device).
+    Returns (rows, weights or None) as numpy arrays."""
+    import torch
+    n = g.shape[0]
+    ratio = min(max(ratio, 0.0), 1.0)
+    keep_n = max(1, round(n * ratio))
+    top_n = max(1, min(keep_n, round(n * (1.0 - ratio))))
+    order = torch.argsort(torch.from_numpy(g).to(device).abs(), descending=True)
+    if keep_n - top_n <= 0 or order.numel() == top_n:
+        return order[:top_n].cpu().numpy(), None
+    rest = order[top_n:]
+    drawn = rest[torch.randperm(rest.numel(), generator=gen, device=device)[:keep_n - top_n]]
+    w = np.ones(top_n + drawn.numel(), np.float32)
+    w[top_n:] = np.float32((n - top_n) / drawn.numel())
+    return torch.cat([order[:top_n], drawn]).cpu().numpy(), w
 
 
 class Booster:
@@ -125,6 +150,7 @@ class Booster:
         # the reference's CPU generator (yabt/boosting.py:286) drives row subsampling
         import torch
         gen = torch.Generator(device="cpu").manual_seed(p.seed)
+        goss_gen = torch.Generator(device=p.goss_device).manual_seed(p.seed) if p.goss_enabled else None
         self.records = []
         for t in range(p.n_estimators if n_trees is None else n_trees):
             g, h = self.loss.grad_hess(margin, y)
@@ -139,7 +165,15 @@ class Booster:
                     tree_, leaf_ = grow_bestfirst(b_, g_, h_, self.binner.edges_, self.binner.scales_,
                                                   tp, None, imat, p.interaction_boost)
                 return tree_, leaf_
-            if p.subsample < 1.0:
+            if p.goss_enabled:
+                # yabt/boosting.py:371-374,393-396; sampler yabt/adaptive_features.py:75-110
+                rows, w = _goss_rows(g, p.goss_ratio, goss_gen, p.goss_device)
+                gs, hs = g[rows], h[rows]
+                if w is not None:
+                    gs, hs = (gs * w).astype(np.float32), (hs * w).astype(np.float32)
+                tree, _ = grow(binned[rows], gs, hs)
+                leaf = tree.apply(Xraw)
+            elif p.subsample < 1.0:
                 # yabt/boosting.py:374-376, 392-393: grow on rows[:m] of a permutation,
                 # then route every row through the tree (:486)
                 m = int(n * p.subsample)

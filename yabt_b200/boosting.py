@@ -163,7 +163,7 @@ def _check_supported(p: BoostParams) -> None:
     bad = []
     for name, ok in (("kernel_splits", not p.kernel_splits), ("refine_steps", p.refine_steps == 0),
                      ("refit_every", p.refit_every == 0), ("adaptive_features", not p.adaptive_features),
-                     ("goss_enabled", not p.goss_enabled), ("product_features", not p.product_features),
+                     ("product_features", not p.product_features),
                      ("auto_tune", not p.auto_tune), ("stochastic_routing", not p.stochastic_routing),
                      ("leaf_net_hidden", p.leaf_net_hidden == 0), ("subsample", 0.0 < p.subsample <= 1.0),
                      ("levelwise", p.levelwise in (True, False, "auto"))):
@@ -267,8 +267,8 @@ class Booster:
         generator is exhausted."""
         p = self.p
         _check_supported(p)
-        if comm is not None and (eval_set is not None or p.min_split_gain_rel > 0.0):
-            raise NotImplementedError("row-sharded fits support neither eval_set nor min_split_gain_rel")
+        if comm is not None and (eval_set is not None or p.min_split_gain_rel > 0.0 or p.goss_enabled):
+            raise NotImplementedError("row-sharded fits support neither eval_set, min_split_gain_rel nor GOSS")
         dev = torch.device(p.resolve_device())
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
@@ -304,7 +304,9 @@ class Booster:
         tp = TreeParams(max_leaves=p.max_leaves, max_depth=p.max_depth, reg_lambda=p.reg_lambda,
                         gamma=p.gamma, min_child_weight=p.min_child_weight,
                         min_samples_leaf=p.min_samples_leaf, learning_rate=p.learning_rate)
-        grower = Grower(n, F, p.max_leaves, p.max_depth, general, dev)
+        goss = p.goss_enabled
+        # GOSS reweights the sampled rows' hessians, so the tree needs the hessian channel
+        grower = Grower(n, F, p.max_leaves, p.max_depth, general or goss, dev)
         _lib.check(lib.yabt_grower_set_bestfirst_f64(grower.h, 1 if use_c_grower_math(p) else 0),
                    "yabt_grower_set_bestfirst_f64")
         grower.set_level_wait(getattr(self, "_level_wait", True))
@@ -321,7 +323,12 @@ class Booster:
             ln_ws = torch.empty(int(lib.yabt_leafnet_workspace_bytes(n, F, grower.max_nodes)),
                                 dtype=torch.uint8, device=dev)
         rows = grower.leaf_rows()
-        sub = p.subsample < 1.0
+        sub = p.subsample < 1.0 or goss
+        if goss:
+            # yabt/boosting.py:337-338: the sampler's device generator, seeded once per fit
+            goss_gen = torch.Generator(device=dev).manual_seed(p.seed)
+            g_goss = torch.zeros(n, dtype=torch.float32, device=dev)
+            h_goss = torch.zeros(n, dtype=torch.float32, device=dev)
         if sub:
             # row subsampling: trees grow on a sample, leaf models and the margin
             # update route every row (ranges from a stable grouping by leaf)
@@ -350,7 +357,18 @@ class Booster:
         n_built = 0
         for t in range(T):
             root = None
-            if sub:
+            g_tree, h_tree = grad, hess
+            if goss:
+                # yabt/boosting.py:371-374,393-396 (GOSS takes precedence over subsample):
+                # the tree grows on the sampled rows with grad, hess times the row weights
+                from .sampling import goss_sample
+                sel, w = goss_sample(grad, p.goss_ratio, goss_gen)
+                g_goss.index_copy_(0, sel, grad[sel] * w if w is not None else grad[sel])
+                hs = hess[sel] if hess is not None else torch.ones(sel.numel(), device=dev)
+                h_goss.index_copy_(0, sel, hs * w if w is not None else hs)
+                g_tree, h_tree = g_goss, h_goss
+                root = torch.sort(sel).values.to(torch.int32)   # row order only affects locality
+            elif sub:
                 # yabt/boosting.py:374-376: rows[:m] of a permutation drawn from the
                 # CPU generator before the feature mask (the same draw order)
                 m = int(n_total * p.subsample)
@@ -375,7 +393,7 @@ class Booster:
             out = dict(feature=forest.feature[t], threshold=forest.threshold[t], left=forest.left[t],
                        right=forest.right[t], value=forest.value[t], gate_scale=forest.gate[t],
                        leaf_of_row=leaf_of_row, meta=forest.meta[t])
-            a = grower.args(data.bins, grad, hess, _Edges, tp_t, out, fmask, imat, p.interaction_boost,
+            a = grower.args(data.bins, g_tree, h_tree, _Edges, tp_t, out, fmask, imat, p.interaction_boost,
                             bins_fm=data.bins_fm, root_rows=root)
             if comm is None:
                 grower.grow(a, bestfirst=bestfirst, f64=use_c_grower_math(p))
