@@ -21,6 +21,7 @@ impl=reference  the reference's own CPU implementation of the path (its OpenMP
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -30,6 +31,8 @@ import tempfile
 import time
 
 import numpy as np
+
+HIST_TRAFFIC_PER_ALG_BYTE = 3073.8 / 1609.9   # k_hist DRAM bytes per algorithmic byte (C4 shape, ncu)
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
@@ -364,6 +367,12 @@ def run_ours(args):
     hist_total_ms = sum(hist_ms)
     achieved = alg_bytes / (hist_total_ms / 1000.0) / 1e9 if hist_total_ms > 0 else float("nan")
     alg_per_launch = alg_bytes / max(hist_launches, 1)
+    # DRAM traffic of k_hist per launch: one ncu capture (dram__bytes_read.sum +
+    # dram__bytes_write.sum over the k_hist launches of one 2M-row C4 tree) gave
+    # 3073.8 MB against 1609.9 MB of algorithmic bytes; scaled by the same
+    # algorithmic bytes here (levels below the root read nearly the whole bin
+    # matrix, so traffic grows with the rows as the algorithmic bytes do)
+    traffic_per_launch = HIST_TRAFFIC_PER_ALG_BYTE * alg_per_launch if cfg == "c4" else None
     avg_hist_ms = hist_total_ms / max(hist_launches, 1)
     peaks = {}
     try:
@@ -371,6 +380,17 @@ def run_ours(args):
     except Exception:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
+    # the shared-memory reduction ceiling of k_hist on this GPU (the kernel issues
+    # 3 u32 reductions per (row, feature) on the unit-hessian path, 5 otherwise)
+    limbs = 3 if loss_name == "mse" else 5
+    sink = torch.zeros(1, dtype=torch.int64, device=dev)
+    pms, pupd = ctypes.c_float(), ctypes.c_longlong()
+    red_peak = 0.0
+    for _ in range(3):
+        _lib.check(lib.yabt_probe_shared_red(limbs, 400, sink.data_ptr(), _lib.stream_ptr(), ctypes.byref(pms),
+                                             ctypes.byref(pupd)), "yabt_probe_shared_red")
+        red_peak = max(red_peak, pupd.value / (pms.value / 1000.0) / 1e9)
+    red_achieved = (root_rows + child_rows) * F / (hist_total_ms / 1000.0) / 1e9 if hist_total_ms > 0 else 0.0
     rows_hist = torch.tensor([float(root_rows + child_rows)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(rows_hist)
@@ -424,11 +444,20 @@ def run_ours(args):
             "bin_reads_per_sec": bin_reads_per_s,
             "gpu_launches": marks.get("launches1", 0) - marks.get("launches0", 0),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": traffic_per_launch,
+                         "traffic_source": "ncu capture of one 2M-row C4 tree, scaled by algorithmic bytes"
+                         if traffic_per_launch else None,
                          "kernel": "k_hist", "alg_bytes_per_launch": alg_per_launch,
                          "avg_launch_ms": avg_hist_ms, "launches_timed": hist_launches,
                          "hist_share_of_step": hist_total_ms / ms,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
+            # k_hist is bound by shared-memory reductions, not HBM: its (row, feature)
+            # update rate against the same reductions issued alone (yabt_probe_shared_red)
+            "atomic_roofline": {"bound": "shared_atomic", "kernel": "k_hist", "achieved": red_achieved,
+                                "peak": red_peak, "unit": "G (row, feature) updates/s",
+                                "frac": red_achieved / red_peak if red_peak > 0 else None,
+                                "u32_reductions_per_update": limbs,
+                                "peak_source": "yabt_probe_shared_red, measured in this run"},
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,

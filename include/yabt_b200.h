@@ -36,6 +36,14 @@ int yabt_last_error(char* buf, int len);
 /* Number of kernels the library has launched so far in this process. */
 long long yabt_launch_count(void);
 
+/* Measurement only (no reference counterpart): the shared-memory reduction
+ * ceiling of the histogram kernel. Issues k_hist's u32 reductions (limbs = 3:
+ * unit-hessian path, two 32-feature subs per lane; 5: general path) with its
+ * layout and grid and pseudo-random bins, twice (warm-up, then timed);
+ * *ms = the timed launch, *updates = its (row, feature) updates. sink: 8 bytes
+ * of device memory the result is folded into. Synchronises the stream.     */
+int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates);
+
 /* ------------------------------------------------------------------ bin matrix
  * The tiled bin-matrix layout: features in column tiles (64-wide tiles, then
  * a 32-wide tile if >= 32 features remain, then a 16- or 32-wide padded

@@ -1,0 +1,90 @@
+// Measurement only: the shared-memory reduction throughput that bounds k_hist.
+//
+// k_hist adds every (row, feature) into exact u32 limbs of a shared histogram
+// laid out [limb][sub][bin][lane] (lane = feature, so the 32 lanes of one
+// reduction hit 32 different banks): 3 reductions per (row, feature) on the
+// unit-hessian path (g low, g high, count; two 32-feature subs per lane),
+// 5 on the general path (g, h low / high, count; one sub). This kernel issues
+// the same reductions with the same layout, grid (one 1024-thread block per
+// SM) and pseudo-random bins, and nothing else, so its rate of (row, feature)
+// updates is the ceiling k_hist's own rate is compared with. Every address
+// stays inside the block's histogram; there are no waits.
+#include "../../include/yabt_b200.h"
+#include "common.cuh"
+
+namespace yabt {
+namespace {
+
+constexpr int PROBE_THREADS = 1024;
+
+template <int LIMBS, int S>
+__global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsigned long long* sink) {
+  extern __shared__ __align__(16) unsigned psh[];
+  constexpr int WORDS = LIMBS * S * YABT_NB * 32;
+  constexpr int LS = S * YABT_NB * 32 * 4;       // bytes between limbs
+  for (int i = threadIdx.x; i < WORDS; i += blockDim.x) psh[i] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const unsigned lb = (unsigned)__cvta_generic_to_shared(psh) + lane * 4;
+  unsigned seed = blockIdx.x * 977u + threadIdx.x * 131u + 1u;
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll 4
+    for (int r = 0; r < 64; ++r) {
+      seed = seed * 1664525u + 1013904223u;                 // LCG: bins of this lane's features
+      const unsigned v = seed >> 8;
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        const unsigned bin = (seed >> (24 - 8 * s)) & 0xFFu;
+        const unsigned a = lb + (bin << 7) + s * YABT_NB * 32 * 4;
+#pragma unroll
+        for (int l = 0; l < LIMBS; ++l)
+          asm volatile("red.shared.add.u32 [%0], %1;\n" ::"r"(a + l * LS), "r"(l == LIMBS - 1 ? 1u : v & 0xFFFFu)
+                       : "memory");
+      }
+    }
+  }
+  __syncthreads();
+  unsigned long long acc = 0;
+  for (int i = threadIdx.x; i < WORDS; i += blockDim.x) acc += psh[i];
+  atomicAdd(sink, acc);      // keeps the reductions observable
+}
+
+template <int LIMBS, int S>
+int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, long long* updates) {
+  constexpr int SMEM = LIMBS * S * YABT_NB * 32 * 4;
+  int dev = 0, nsm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_probe_red<LIMBS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (e == cudaSuccess) e = cudaEventCreate(&a);
+  if (e == cudaSuccess) e = cudaEventCreate(&b);
+  if (e == cudaSuccess) {
+    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink);        // warm-up
+    cudaEventRecord(a, s);
+    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink);
+    cudaEventRecord(b, s);
+    e = cudaEventSynchronize(b);
+  }
+  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, a, b);
+  if (a) cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  if (e != cudaSuccess) { set_error("yabt_probe_shared_red: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  *updates = (long long)nsm * PROBE_THREADS * iters * 64 * S;
+  return YABT_OK;
+}
+
+}  // namespace
+}  // namespace yabt
+
+using namespace yabt;
+
+extern "C" int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates) {
+  if ((limbs != 3 && limbs != 5) || iters <= 0 || !sink || !ms || !updates) {
+    set_error("yabt_probe_shared_red: limbs must be 3 or 5, iters > 0, non-null outputs");
+    return YABT_ERR_ARG;
+  }
+  auto* k = static_cast<unsigned long long*>(sink);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return limbs == 3 ? run_probe<3, 2>(iters, k, s, ms, updates) : run_probe<5, 1>(iters, k, s, ms, updates);
+}
