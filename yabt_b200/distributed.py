@@ -336,8 +336,9 @@ def grow_tree_bestfirst(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     xchg = getattr(grower, "_exchange", None)
     if xchg is None and comm.peer_exchange:
         xchg = grower._exchange = PeerExchange(grower, comm)
-    per_job = int(lib.yabt_grow_small_count(h, 0))
-    small = _view(grower.ws, lib.yabt_grow_small_ptr(h), per_job, torch.int64)
+    small = None
+    if xchg is None:   # with the exchange the histograms live in its buffer, outside the workspace
+        small = _view(grower.ws, lib.yabt_grow_small_ptr(h), int(lib.yabt_grow_small_count(h, 0)), torch.int64)
 
     def reduce(level):
         if xchg is not None:
