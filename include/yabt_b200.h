@@ -187,6 +187,23 @@ int yabt_grow_tree_bestfirst(yabt_grower* g, const yabt_tree_args* a, void* stre
  * min(edges + 1, 256), float64 leaf values, ties to the lower active-leaf
  * slot.                                                                   */
 int yabt_grower_set_bestfirst_f64(yabt_grower* g, int on);
+
+/* Multi-task trees: grow_multitask_tree (yabt/multitask.py:60-150) with
+ * find_best_split_multi (yabt/histogram.py:143-188) for squared-loss tasks
+ * (YABTMultiTaskRegressor): one best-first structure for `tasks` targets
+ * (1..8), split on the sum of the per-task gains, validity from the shared
+ * counts; values[node * tasks + t] = -lr * G_t / (count + lambda). The grower
+ * must be created with general = 1; grads are task-major [tasks][n] (rows of
+ * a->root_rows when given); a->grad / a->hess must be non-null (not read) and
+ * a->value is scratch (scalar values are not meaningful here). The tree
+ * arrays, leaf_of_row and meta are written as by yabt_grow_tree.
+ * yabt_mt_update: margin[t][i] += values[leaf[i]][t] (values may be null),
+ * then grad[t][i] = margin[t][i] - y[t][i] (grad may be null).            */
+long long yabt_mt_workspace_bytes(const yabt_grower* g, int tasks);
+int yabt_grow_tree_multitask(yabt_grower* g, const yabt_tree_args* a, int tasks, const float* grads, void* ws,
+                             long long ws_bytes, float* values, void* stream);
+int yabt_mt_update(const int32_t* leaf_of_row, const float* values, int tasks, long long n, float* margin,
+                   const float* y, float* grad, void* stream);
 int yabt_grow_bf_root_hist(yabt_grower* g, const yabt_tree_args* a, void* stream);
 int yabt_grow_bf_split(yabt_grower* g, const yabt_tree_args* a, int step, void* stream);
 int yabt_grow_bf_scan(yabt_grower* g, const yabt_tree_args* a, int step, void* stream);

@@ -251,9 +251,65 @@ def bestfirst(ref_root: str) -> None:
     print("bestfirst fixtures written to", HERE)
 
 
+def multitask(ref_root: str) -> None:
+    """``multitask.npz``: the reference's multi-task grower
+    (yabt/multitask.py:60-150) on seeded cases with squared-loss gradients, and
+    a YABTMultiTaskRegressor fit (yabt/sklearn_api.py:366-402), on a CPU-only
+    host."""
+    sys.path.insert(0, ref_root)
+    import torch
+    from yabt.binning import Binner
+    from yabt.boosting import BoostParams
+    from yabt.multitask import grow_multitask_tree
+    from yabt.sklearn_api import YABTMultiTaskRegressor
+
+    assert not torch.cuda.is_available(), "run on a CPU-only host (numpy binner path)"
+    out = {}
+    mcases = [
+        dict(seed=40, n=3000, F=8, T=2, leaves=15, depth=64, msl=20, fmask=False),
+        dict(seed=41, n=4000, F=12, T=3, leaves=31, depth=5, msl=5, fmask=False),
+        dict(seed=42, n=2500, F=6, T=1, leaves=9, depth=64, msl=20, fmask=True),
+        dict(seed=43, n=2000, F=10, T=5, leaves=24, depth=8, msl=10, fmask=False),
+    ]
+    for i, c in enumerate(mcases):
+        X, _ = _data(c["seed"], c["n"], c["F"], 0.02)
+        binner = Binner(256).fit(X)
+        binned = binner.transform(X)
+        Xraw = torch.from_numpy(binner.impute(X))
+        rng = np.random.default_rng(c["seed"] + 100)
+        g = torch.from_numpy(rng.normal(size=(c["n"], c["T"])).astype(np.float32))
+        h = torch.ones_like(g)
+        fm = torch.from_numpy(rng.random(c["F"]) < 0.7) if c["fmask"] else None
+        p = BoostParams(max_leaves=c["leaves"], max_depth=c["depth"], min_samples_leaf=c["msl"],
+                        learning_rate=0.1, device="cpu")
+        tree = grow_multitask_tree(binned, g, h, binner, p, fm)
+        out[f"m{i}_X"] = X
+        out[f"m{i}_g"] = g.numpy()
+        out[f"m{i}_params"] = np.array([c["leaves"], c["depth"], c["msl"]], np.int64)
+        out[f"m{i}_fmask"] = fm.numpy() if fm is not None else np.zeros(0, bool)
+        for k in ("feature", "threshold", "left", "right", "value"):
+            out[f"m{i}_{k}"] = getattr(tree, k).numpy()
+        out[f"m{i}_leaf"] = tree.apply(Xraw).numpy()
+    out["ncases"] = np.array(len(mcases))
+    # an estimator fit: three correlated targets
+    X, _ = _data(44, 3000, 8, 0.02)
+    z = np.nan_to_num(X)
+    rng = np.random.default_rng(45)
+    Y = np.stack([np.sin(z[:, 0]) + z[:, 1], z[:, 1] * z[:, 2], 0.5 * z[:, 0] - z[:, 3]], axis=1)
+    Y = (Y + 0.1 * rng.normal(size=Y.shape)).astype(np.float32)
+    est = YABTMultiTaskRegressor(n_estimators=8, max_leaves=15, learning_rate=0.2, device="cpu").fit(X, Y)
+    out["est_X"], out["est_Y"] = X, Y
+    out["est_pred"] = est.predict(X).astype(np.float32)
+    out["est_feature0"] = est.booster_.trees[0].feature.numpy()
+    np.savez_compressed(os.path.join(HERE, "multitask.npz"), **out)
+    print("multitask fixtures written to", HERE)
+
+
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else "/root/reference"
     if "--bestfirst" in sys.argv:
         bestfirst(ref)
+    elif "--multitask" in sys.argv:
+        multitask(ref)
     else:
         main(ref)

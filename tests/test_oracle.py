@@ -184,3 +184,23 @@ def test_interaction_detector_normalisation():
     d2 = InteractionDetector(6)
     d2.update([(0, 1), (2, 3), (4, 5)])
     assert d2.normalized().max() == 0.0
+
+
+@pytest.mark.parametrize("case", range(4))
+def test_multitask_grower_matches_reference(golden, case):
+    """The multi-task grower, yabt/multitask.py:60-150, against the reference run."""
+    from oracle.multitask import grow_multitask
+    z = golden("multitask")
+    X, g = z[f"m{case}_X"], z[f"m{case}_g"]
+    leaves, depth, msl = (int(v) for v in z[f"m{case}_params"])
+    fm = z[f"m{case}_fmask"]
+    b = Binner().fit(X)
+    feat, thr, left, right, value, _, leaf = grow_multitask(
+        b.transform(X), g, np.ones_like(g), b.edges_,
+        TreeParams(max_leaves=leaves, max_depth=depth, min_samples_leaf=msl), fm if fm.size else None)
+    np.testing.assert_array_equal(feat, z[f"m{case}_feature"])
+    np.testing.assert_array_equal(left, z[f"m{case}_left"])
+    np.testing.assert_array_equal(right, z[f"m{case}_right"])
+    np.testing.assert_array_equal(thr, z[f"m{case}_threshold"])
+    np.testing.assert_allclose(value, z[f"m{case}_value"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_array_equal(leaf, z[f"m{case}_leaf"])

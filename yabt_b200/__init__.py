@@ -12,10 +12,11 @@ from .binning import Binner  # noqa: F401
 from .boosting import Booster, BoostParams, LogLoss, MSELoss  # noqa: F401
 from .grower import grow_tree, grow_tree_c, grow_tree_levelwise  # noqa: F401
 from .multiclass import MulticlassBooster  # noqa: F401
-from .sklearn_api import YABTClassifier, YABTRegressor  # noqa: F401
+from .multitask import MultiTaskBooster  # noqa: F401
+from .sklearn_api import YABTClassifier, YABTMultiTaskRegressor, YABTRegressor  # noqa: F401
 from .tree import LEAF, Tree, TreeParams  # noqa: F401
 
 __all__ = [
     "Binner", "Booster", "BoostParams", "LogLoss", "MSELoss", "MulticlassBooster",
-    "YABTClassifier", "YABTRegressor", "Tree", "TreeParams", "LEAF", "grow_tree", "grow_tree_c", "grow_tree_levelwise",
+    "YABTClassifier", "YABTRegressor", "YABTMultiTaskRegressor", "MultiTaskBooster", "Tree", "TreeParams", "LEAF", "grow_tree", "grow_tree_c", "grow_tree_levelwise",
 ]

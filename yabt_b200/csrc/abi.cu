@@ -35,6 +35,12 @@ cudaError_t launch_hist_kernels(const GrowParams&, const GrowBufs&, const TreeIO
 cudaError_t launch_bf_root_scan(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
 cudaError_t launch_bf_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_bf_scan(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
+cudaError_t launch_bf_pick_partition(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_absmax_shared(const float* const*, int, long long, const int*, GrowState*, int, cudaStream_t);
+cudaError_t launch_mt_scan(const GrowParams&, const GrowBufs&, const MtBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_mt_commit(const GrowParams&, const GrowBufs&, const MtBufs&, cudaStream_t);
+cudaError_t launch_mt_values(const GrowParams&, const GrowBufs&, const MtBufs&, cudaStream_t);
+cudaError_t launch_mt_update(const int*, const float*, int, long long, float*, const float*, float*, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
 
 // ---------------------------------------------------------------- pack kernel
@@ -502,6 +508,117 @@ int yabt_grow_tree_bestfirst(yabt_grower* g, const yabt_tree_args* a, void* stre
     }
   }
   return yabt_grow_end(g, a, stream);
+}
+
+}  // extern "C"
+
+// multi-task workspace: small-child channels, per-slot histograms, records, zeros
+static long long mt_carve(const yabt_grower* g, int T, char* base, MtBufs* mb) {
+  const GrowParams& p = g->p;
+  const int P = (T + 1) / 2;
+  const long long FB = (long long)p.F * YABT_NB;
+  long long o = 0;
+  auto take = [&](long long bytes) { const long long at = o; o += al(bytes); return base ? base + at : nullptr; };
+  char* small = take((2LL * P * FB + (long long)p.F * (YABT_NB / 2)) * 8);
+  char* hist = take((long long)p.maxa * (T + 1) * FB * 8);
+  char* feat = take(2LL * p.F * sizeof(MtRec));
+  char* cand = take((long long)p.maxn * sizeof(MtRec));
+  char* zeros = take(p.n * 4);
+  if (mb) {
+    mb->T = T; mb->P = P;
+    mb->small = (long long*)small; mb->hist = (long long*)hist;
+    mb->feat = (MtRec*)feat; mb->cand = (MtRec*)cand; mb->zeros = (const float*)zeros;
+  }
+  return o;
+}
+
+// the histogram of this level's smaller child for every task: ceil(T/2) passes
+// of the two-channel kernel into the channel pairs of mb.small
+static cudaError_t mt_hist_passes(yabt_grower* g, const TreeIO& io, const MtBufs& mb, int level, cudaStream_t s) {
+  const long long FB = (long long)g->p.F * YABT_NB;
+  for (int i = 0; i < mb.P; ++i) {
+    if (i > 0) {
+      const cudaError_t e = cudaMemsetAsync(&g->b.st->item_counter, 0, sizeof(int), s);
+      if (e != cudaSuccess) return e;
+    }
+    GrowBufs b = g->b;
+    b.small = mb.small + 2LL * i * FB;
+    TreeIO io2 = io;
+    io2.g = mb.grads + 2LL * i * g->p.n;
+    io2.h = 2 * i + 1 < mb.T ? mb.grads + (2LL * i + 1) * g->p.n : mb.zeros;
+    const cudaError_t e = launch_hist_kernels(g->p, b, io2, level, 1, g->nsm, s, nullptr);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+extern "C" {
+
+long long yabt_mt_workspace_bytes(const yabt_grower* g, int tasks) {
+  if (!g || tasks < 1 || tasks > MT_MAX) return -1;
+  return mt_carve(g, tasks, nullptr, nullptr);
+}
+
+int yabt_grow_tree_multitask(yabt_grower* g, const yabt_tree_args* a, int tasks, const float* grads, void* ws,
+                             long long ws_bytes, float* values, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (!g->p.general || tasks < 1 || tasks > MT_MAX || !grads || !ws || !values || ((uintptr_t)ws & 255)) {
+    set_error("yabt_grow_tree_multitask: needs a grower created with general=1, 1 <= tasks <= %d, "
+              "gradients, values and a 256-byte aligned workspace", MT_MAX);
+    return YABT_ERR_ARG;
+  }
+  if (ws_bytes < yabt_mt_workspace_bytes(g, tasks)) { set_error("yabt_grow_tree_multitask: workspace too small"); return YABT_ERR_WORKSPACE; }
+  if (g->p.bf_f64) { set_error("yabt_grow_tree_multitask: the float64 best-first mode does not apply"); return YABT_ERR_ARG; }
+  MtBufs mb;
+  mt_carve(g, tasks, static_cast<char*>(ws), &mb);
+  mb.grads = grads; mb.values = values; mb.scratch_value = nullptr;
+  cudaStream_t s = (cudaStream_t)stream;
+  const GrowParams& p = g->p;
+  if (tasks % 2) CUDA_TRY(cudaMemsetAsync((void*)mb.zeros, 0, p.n * 4, s));
+  std::vector<const float*> arrays(tasks);
+  for (int t = 0; t < tasks; ++t) arrays[t] = grads + (long long)t * p.n;
+  CUDA_TRY(launch_absmax_shared(arrays.data(), tasks, io.n_root, io.root_rows, g->b.st, g->nsm, s));
+  CUDA_TRY(launch_tree_init(p, g->b, io, s));
+  CUDA_TRY(mt_hist_passes(g, io, mb, 0, s));
+  CUDA_TRY(launch_mt_scan(p, g->b, mb, io, 1, g->nsm, s));
+  if (g->level_wait && !g->host_state) {
+    CUDA_TRY(cudaHostAlloc((void**)&g->host_state, sizeof(int) * 4 * LEVEL_SLOTS, cudaHostAllocDefault));
+    for (auto& e : g->lvl_ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  const int steps = std::max(1, p.max_leaves - 1);
+  for (int k = 1; k <= steps; ++k) {
+    CUDA_TRY(launch_mt_commit(p, g->b, mb, s));
+    CUDA_TRY(launch_bf_pick_partition(p, g->b, io, k, g->nsm, s));
+    CUDA_TRY(launch_mt_values(p, g->b, mb, s));
+    CUDA_TRY(mt_hist_passes(g, io, mb, 1, s));
+    CUDA_TRY(launch_mt_scan(p, g->b, mb, io, 0, g->nsm, s));
+    if (!g->level_wait) continue;
+    const int slot = k % LEVEL_SLOTS;
+    CUDA_TRY(cudaMemcpyAsync(g->host_state + 4 * slot, &g->b.st->level, 4 * sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaEventRecord(g->lvl_ev[slot], s));
+    if (k > LEVEL_LOOKAHEAD) {
+      const int old = (k - LEVEL_LOOKAHEAD) % LEVEL_SLOTS;
+      CUDA_TRY(cudaEventSynchronize(g->lvl_ev[old]));
+      if (!g->host_state[4 * old + 1]) break;
+    }
+  }
+  CUDA_TRY(launch_tree_finish(p, g->b, io, a->meta, a->leaf_of_row, g->nsm, s));
+  return YABT_OK;
+}
+
+int yabt_mt_update(const int32_t* leaf_of_row, const float* values, int tasks, long long n, float* margin,
+                   const float* y, float* grad, void* stream) {
+  if (tasks < 1 || n < 0 || !margin || (values && !leaf_of_row) || (grad && !y)) {
+    set_error("yabt_mt_update: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  int dev = 0, nsm = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  CUDA_TRY(launch_mt_update(leaf_of_row, values, tasks, n, margin, y, grad, nsm, (cudaStream_t)stream));
+  return YABT_OK;
 }
 
 void* yabt_grow_amax_ptr(yabt_grower* g) { return g && g->bound ? (void*)&g->b.st->amax_g : nullptr; }

@@ -1240,15 +1240,36 @@ cudaError_t launch_bf_root_scan(const GrowParams& p, const GrowBufs& b, const Tr
 // One best-first step, first half: pop the best candidate, partition its rows
 // and histogram the smaller child into `small`. Step 1 splits the root, whose
 // rows are root positions (partition gate 0); later steps read rows[0] (gate 2).
-cudaError_t launch_bf_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int step, int nsm,
-                            cudaStream_t s) {
+cudaError_t launch_bf_pick_partition(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int step, int nsm,
+                                     cudaStream_t s) {
   const int gate = step == 1 ? 0 : 2;
   k_bf_pick<<<1, 1024, 0, s>>>(p, b, io, gate);
   const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
   k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, gate);
   k_plan<<<1, 1024, 0, s>>>(p, b, gate);
   count_launches(3);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bf_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int step, int nsm,
+                            cudaStream_t s) {
+  const cudaError_t e = launch_bf_pick_partition(p, b, io, step, nsm, s);
+  if (e != cudaSuccess) return e;
   return launch_hist_kernels(p, b, io, 1, 1, nsm, s, nullptr);
+}
+
+// max |g| over several gradient arrays into the hessian word too (one
+// quantisation scale shared by both histogram channels)
+cudaError_t launch_absmax_shared(const float* const* arrays, int count, long long n_root, const int* root,
+                                 GrowState* st, int nsm, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(&st->amax_g, 0, 2 * sizeof(unsigned), s);
+  if (e != cudaSuccess) return e;
+  const int grid = (int)std::min<long long>((n_root + 255) / 256, 8LL * nsm);
+  for (int i = 0; i < count; ++i) k_absmax<<<std::max(grid, 1), 256, 0, s>>>(arrays[i], nullptr, n_root, root, st);
+  count_launches(count);
+  e = cudaMemcpyAsync(&st->amax_h, &st->amax_g, sizeof(unsigned), cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
 }
 
 // Second half: the children's histograms, scans and row ranges.

@@ -194,6 +194,24 @@ struct TreeIO {
   long long n_root;          // number of root rows (n when root_rows is nullptr)
 };
 
+// Multi-task growth (shared structure, one leaf value per task).
+constexpr int MT_MAX = 8;            // tasks per tree
+struct MtRec {                       // per-task exact sums of a node's chosen split
+  long long gl[MT_MAX];              // left gradient sums at the split bin
+  long long g[MT_MAX];               // node gradient totals
+};
+struct MtBufs {
+  int T, P;                 // tasks, task pairs (histogram passes)
+  const float* grads;       // [T][n] task-major gradients
+  const float* zeros;       // [n] zeros: the second channel of the last pass when T is odd
+  long long* small;         // [2P][F][256] value channels, then counts [F][128] (two bins per word)
+  long long* hist;          // [slot][T + 1][F][256]: per-task channels, then counts
+  MtRec* feat;              // [2][F] per child position and feature
+  MtRec* cand;              // [maxn] per node
+  float* values;            // [maxn][T] leaf values (output)
+  float* scratch_value;     // [maxn] scalar values the shared best-first kernels write (unused)
+};
+
 // the device state of a bound grower (C ABI handle), or nullptr
 GrowState* grower_state(struct yabt_grower* g);
 

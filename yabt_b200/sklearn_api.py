@@ -128,3 +128,36 @@ class YABTRegressor(_YABTBase, RegressorMixin):
 
     def predict(self, X) -> np.ndarray:
         return self._margin(X) * self._y_std + self._y_mean
+
+
+class YABTMultiTaskRegressor(_YABTBase, RegressorMixin):
+    """Multi-output regression with one shared tree structure across the
+    targets and a leaf value per target (yabt/sklearn_api.py:366-402): every
+    target is standardised, splits are chosen on the summed per-target gain.
+    Only the core split and sampling parameters apply, as in the reference."""
+
+    def fit(self, X, Y, eval_set=None):
+        from .multitask import MultiTaskBooster
+        Y = np.asarray(Y, dtype=np.float32)
+        self._y_1d = Y.ndim == 1
+        if self._y_1d:
+            Y = Y[:, None]
+        self.n_tasks_ = Y.shape[1]
+        self._y_mean = Y.mean(axis=0)
+        std = Y.std(axis=0)
+        self._y_std = np.where(std == 0, 1.0, std).astype(np.float32)
+        Yt = (Y - self._y_mean) / self._y_std
+        ev = None
+        if eval_set is not None:
+            Yv = np.asarray(eval_set[1], dtype=np.float32)
+            if Yv.ndim == 1:
+                Yv = Yv[:, None]
+            ev = (np.asarray(eval_set[0], dtype=np.float32), (Yv - self._y_mean) / self._y_std)
+        self.booster_ = MultiTaskBooster(self._boost_params(), MSELoss())
+        self.booster_.fit(np.asarray(X, dtype=np.float32), Yt, eval_set=ev)
+        return self
+
+    def predict(self, X) -> np.ndarray:
+        m = self.booster_.predict_margin(np.asarray(X, dtype=np.float32))
+        out = m * self._y_std + self._y_mean
+        return out[:, 0] if self._y_1d else out
