@@ -83,13 +83,16 @@ template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 // Block geometry and shared-memory budget of k_hist: the histogram plus a
-// per-warp ring of STG stages of RPS row slots (64 bytes each).
+// per-warp ring of STG stages of RPS row slots (64 bytes each). Eight rows per
+// stage let every lane of a 64-wide tile copy 16 bytes and halve the per-row
+// share of the stage bookkeeping (row ids, gradients, copy issue, waits); two
+// stages (one in flight while one is consumed) keep the ring at 32 KB.
 template <int S, int LIMBS>
 struct HistPipe {
   static constexpr int WARPS = 32;
   static constexpr int THREADS = WARPS * 32;
-  static constexpr int STG = 4;
-  static constexpr int RPS = 4;                         // rows per stage
+  static constexpr int STG = 2;
+  static constexpr int RPS = 8;                         // rows per stage
   static constexpr int STAGE_BYTES = RPS * 64;
   static constexpr int SMEM = HistCfg<S, LIMBS>::SMEM + WARPS * STG * STAGE_BYTES;
 };
