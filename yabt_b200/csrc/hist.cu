@@ -78,6 +78,12 @@ __device__ __forceinline__ unsigned lds_u8(unsigned a) {
   asm volatile("ld.shared.u8 %0, [%1];\n" : "=h"(v) : "r"(a));
   return v;
 }
+__device__ __forceinline__ void sts_u32(unsigned a, int v) {
+  asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void lds_v4(unsigned a, int& x, int& y, int& z, int& w) {
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n" : "=r"(x), "=r"(y), "=r"(z), "=r"(w) : "r"(a) : "memory");
+}
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
@@ -94,7 +100,9 @@ struct HistPipe {
   static constexpr int STG = 2;
   static constexpr int RPS = 8;                         // rows per stage
   static constexpr int STAGE_BYTES = RPS * 64;
-  static constexpr int SMEM = HistCfg<S, LIMBS>::SMEM + WARPS * STG * STAGE_BYTES;
+  static constexpr int VSLOT = 64;                      // per warp: a stage's quantised g (and h) values
+  static constexpr int SMEM = HistCfg<S, LIMBS>::SMEM + WARPS * STG * STAGE_BYTES + WARPS * VSLOT;
+  static_assert(RPS == 8, "a stage's values are read back as two 16-byte loads");
 };
 
 // One work item of one warp: rows [0, nrow) of its share (positions in the row
@@ -105,7 +113,7 @@ struct HistPipe {
 // The loads and shuffles of a stage's rows are issued before their shared-
 // memory reductions, and full stages need no per-row bounds checks.
 template <int S, int LIMBS, int TW, bool FULL>
-__device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, const uint8_t* __restrict__ tb,
+__device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, unsigned vslot, const uint8_t* __restrict__ tb,
                                           const int* __restrict__ lst, int base, int nrow,
                                           const float* __restrict__ g, const float* __restrict__ h,
                                           float gs, float hs, int k0, bool ok0, bool ok1, int lane) {
@@ -146,18 +154,29 @@ __device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, const uint
     hq[STG - 1] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
     if (s + STG - 1 < nst) copy(s + STG - 1, r);
     cp_commit();
+    // the first lane of each stage row publishes the row's quantised values;
+    // every lane reads all of them back with 16-byte loads (no per-row shuffle)
+    if (lane % LPR == 0 && rr < RPS) {
+      sts_u32(vslot + rr * 4, __float2int_rn(gq[0] * gs));
+      if (LIMBS == 5) sts_u32(vslot + 32 + rr * 4, __float2int_rn(hq[0] * hs));
+    }
     cp_wait<STG - 1>();
     __syncwarp();
-    const int vgl = __float2int_rn(gq[0] * gs);
-    const int vhl = (LIMBS == 5) ? __float2int_rn(hq[0] * hs) : 0;
     const unsigned stg = ring + (s % STG) * SB;   // row q at stg + 64 q
     const int nr = min(RPS, nrow - s * RPS);
     unsigned wv[RPS];
     int vg[RPS], vh[RPS];
+    lds_v4(vslot, vg[0], vg[1], vg[2], vg[3]);
+    lds_v4(vslot + 16, vg[4], vg[5], vg[6], vg[7]);
+    if (LIMBS == 5) {
+      lds_v4(vslot + 32, vh[0], vh[1], vh[2], vh[3]);
+      lds_v4(vslot + 48, vh[4], vh[5], vh[6], vh[7]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < RPS; ++q) vh[q] = 0;
+    }
 #pragma unroll
     for (int q = 0; q < RPS; ++q) {
-      vg[q] = __shfl_sync(0xffffffffu, vgl, q * LPR);
-      vh[q] = (LIMBS == 5) ? __shfl_sync(0xffffffffu, vhl, q * LPR) : 0;
       if constexpr (TW == 64 && S == 2) wv[q] = lds_u16(stg + q * 64 + boff);
       else wv[q] = lds_u8(stg + q * 64 + boff);
     }
@@ -260,6 +279,7 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
   const unsigned sh_s = (unsigned)__cvta_generic_to_shared(sh);
   const unsigned lb = sh_s + lane * 4;                       // word (bin 0, lane) of limb 0
   const unsigned ring = sh_s + Cfg::WORDS * 4 + warp * Pipe::STG * Pipe::STAGE_BYTES;
+  const unsigned vslot = sh_s + Cfg::WORDS * 4 + Pipe::WARPS * Pipe::STG * Pipe::STAGE_BYTES + warp * Pipe::VSLOT;
   auto flush = [&](int seg_item) {
     __syncthreads();
     unsigned* dst = partials + (size_t)items[seg_item].slot * Cfg::WORDS;
@@ -307,17 +327,17 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
       const int base = rows ? w0 : item.begin + w0;
       const bool full = ud.width == 64 && (S == 1 || ud.nsub == 2);
       if (full)
-        hist_warp<S, LIMBS, 64, true>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+        hist_warp<S, LIMBS, 64, true>(lb, ring, vslot, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
       else if (ud.width == 64)
-        hist_warp<S, LIMBS, 64, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
+        hist_warp<S, LIMBS, 64, false>(lb, ring, vslot, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
       else if (ud.width == 32)
-        hist_warp<S, LIMBS, 32, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+        hist_warp<S, LIMBS, 32, false>(lb, ring, vslot, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
       else if (ud.rep == 4)
         hist_warp_narrow<S, LIMBS, 4>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.feat[0][lane] >= 0, lane);
       else if (ud.rep == 2)
         hist_warp_narrow<S, LIMBS, 2>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, ud.feat[0][lane] >= 0, lane);
       else
-        hist_warp<S, LIMBS, 16, false>(lb, ring, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
+        hist_warp<S, LIMBS, 16, false>(lb, ring, vslot, tb, lst, base, w1 - w0, g, h, gs, hs, 0, ok0, false, lane);
     }
     flush(seg);
   }
