@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
 // even and odd rows go to separate accumulators (two independent chains) that
 // are added at the end. Warps are reduced in order: the chunk partial is
 // deterministic.
-constexpr int SROW = KMAX + 4;            // staged doubles per row: x1[KMAX + 1], h, -g, pad
+constexpr int SROW = 2 * (KMAX + 1) + 2;  // staged doubles per row: x1[KMAX + 1], h x1[KMAX + 1], -g, pad
 __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
   __shared__ double sp[8][NE];
   __shared__ double stage[8][32][SROW];
@@ -283,9 +283,11 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
     mu[k] = k < K ? a.col_mean[f] : 0.f;
     sd[k] = k < K ? fmaxf(a.col_std[f], 1e-6f) : 1.f;
   }
-  // staged slots: x1_k at k (k < K), 1 at K, h at KMAX + 1, -g at KMAX + 2
-  constexpr int S_H = KMAX + 1, S_NG = KMAX + 2;
-  int ia[2], ib[2], ic[2];
+  // staged slots: x1_k at k (k < K), 1 at K; h x1_k at S_HX + k; -g at S_NG.
+  // Every accumulator is one fused product of two staged values:
+  // M[a][b] += (h x1_a) x1_b, rhs[a] += (-g) x1_a.
+  constexpr int S_HX = KMAX + 1, S_NG = 2 * (KMAX + 1);
+  int ia[2], ib[2];
   bool ev[2];
   const int ntri = D * (D + 1) / 2;
 #pragma unroll
@@ -295,9 +297,9 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
     if (e < ntri) {                      // M[row][row + rem]
       int rem = e, row = 0;
       while (rem >= D - row) { rem -= D - row; ++row; }
-      ia[q] = row; ib[q] = row + rem; ic[q] = S_H;
+      ia[q] = S_HX + row; ib[q] = row + rem;
     } else {                             // rhs entry e - ntri
-      ia[q] = ev[q] ? e - ntri : 0; ib[q] = K; ic[q] = S_NG;
+      ia[q] = S_NG; ib[q] = ev[q] ? e - ntri : 0;
     }
   }
   double acc0[2] = {0.0, 0.0}, acc1[2] = {0.0, 0.0};
@@ -322,13 +324,16 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
       const float xr[KMAX] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
       double* st = stage[warp][lane];
       if (lane < nb) {
+        const double hh = (double)n2.y;
 #pragma unroll
         for (int k = 0; k < KMAX; ++k) {
           if (k < K) { mn[k] = fminf(mn[k], xr[k]); mx[k] = fmaxf(mx[k], xr[k]); }
-          st[k] = (double)__fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]);
+          const double x1 = (double)__fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]);
+          st[k] = x1;
+          st[S_HX + k] = __dmul_rn(hh, x1);
         }
         st[K] = 1.0;                     // bias input (K <= KMAX; slots K+1.. of x1 unused)
-        st[S_H] = (double)n2.y;
+        st[S_HX + K] = hh;
         st[S_NG] = -(double)n2.x;
       }
     }
@@ -341,15 +346,14 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
         const double* s1 = stage[warp][r + 1];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          acc0[q] = __dadd_rn(acc0[q], __dmul_rn(s0[ia[q]], __dmul_rn(s0[ib[q]], s0[ic[q]])));
-          acc1[q] = __dadd_rn(acc1[q], __dmul_rn(s1[ia[q]], __dmul_rn(s1[ib[q]], s1[ic[q]])));
+          acc0[q] = __fma_rn(s0[ia[q]], s0[ib[q]], acc0[q]);
+          acc1[q] = __fma_rn(s1[ia[q]], s1[ib[q]], acc1[q]);
         }
       }
       if (r < nb) {
         const double* s0 = stage[warp][r];
 #pragma unroll
-        for (int q = 0; q < 2; ++q)
-          acc0[q] = __dadd_rn(acc0[q], __dmul_rn(s0[ia[q]], __dmul_rn(s0[ib[q]], s0[ic[q]])));
+        for (int q = 0; q < 2; ++q) acc0[q] = __fma_rn(s0[ia[q]], s0[ib[q]], acc0[q]);
       }
     }
     __syncwarp();
