@@ -457,6 +457,9 @@ def run_ours(args):
                                 "peak": red_peak, "unit": "G (row, feature) updates/s",
                                 "frac": red_achieved / red_peak if red_peak > 0 else None,
                                 "u32_reductions_per_update": limbs,
+                                # the root level of every tree after the first reuses the fit's
+                                # per-bin row counts and issues one reduction fewer per update
+                                "root_reductions_per_update_cached_counts": limbs - 1,
                                 "peak_source": "yabt_probe_shared_red, measured in this run"},
             "clocks": clocks,
             "e2e": e2e,

@@ -152,6 +152,13 @@ typedef struct {
  * level without waiting instead (for callers that interleave several growers
  * on several streams from one host thread).                              */
 int yabt_grower_set_level_wait(yabt_grower* g, int wait);
+/* Root-level row counts cached across the trees of a fit: with on = 1, the
+ * next root histogram over all rows (no root_rows) keeps its per-bin row
+ * counts, and later root histograms over all rows skip the count channel and
+ * copy them in (the same rows and bins give the same counts). The caller
+ * turns it on only while the bin matrix stays the same (Booster.fit);
+ * on = 0 turns it off and forgets the counts. Off by default.             */
+int yabt_grower_set_root_count_cache(yabt_grower* g, int on);
 /* After yabt_grow_tree: leaf_of_row for every row 0..n-1 (not only the root
  * rows), routed by the split bins through the feature-major bins (required);
  * Tree.apply of yabt/tree.py:82-116 on the training rows.                 */

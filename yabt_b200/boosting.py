@@ -309,6 +309,9 @@ class Booster:
         grower = Grower(n, F, p.max_leaves, p.max_depth, general or goss, dev)
         _lib.check(lib.yabt_grower_set_bestfirst_f64(grower.h, 1 if use_c_grower_math(p) else 0),
                    "yabt_grower_set_bestfirst_f64")
+        # the bin matrix is fixed for the fit: root histograms over all rows reuse
+        # the first tree's per-bin row counts (trees grown on a row sample do not)
+        _lib.check(lib.yabt_grower_set_root_count_cache(grower.h, 1), "yabt_grower_set_root_count_cache")
         grower.set_level_wait(getattr(self, "_level_wait", True))
         self.grower_ = grower
         K = min(p.leaf_net_features, F) if p.neural_leaves else 0

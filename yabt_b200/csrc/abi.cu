@@ -24,14 +24,14 @@ void set_error(const char* fmt, ...) {
 }
 
 cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t,
-                              cudaEvent_t after_hist);
+                              cudaEvent_t after_hist, int root_counts);
 cudaError_t launch_level_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
 cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, const TreeIO&, int*, int*, int, cudaStream_t);
 cudaError_t launch_apply_all(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t launch_hist_kernels(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, int, cudaStream_t,
-                                cudaEvent_t);
+                                cudaEvent_t, int);
 cudaError_t launch_bf_root_scan(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
 cudaError_t launch_bf_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_bf_scan(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
@@ -149,6 +149,9 @@ struct yabt_grower {
   int* host_state = nullptr;               // [LEVEL_SLOTS][4] pinned
   cudaEvent_t lvl_ev[8] = {};
   int level_wait = 1;                      // 0: queue every level without waiting
+  // cached root-level counts (yabt_grower_set_root_count_cache): 0 off; 1 on,
+  // recorded by the next root histogram over all rows and reused after that
+  int rc_mode = 0, rc_valid = 0;
 };
 
 static constexpr int LEVEL_SLOTS = 8, LEVEL_LOOKAHEAD = 3;
@@ -225,6 +228,7 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
   add("best", (long long)p.maxa * F * sizeof(NodeBest));
   add("nbest", (long long)p.maxa * sizeof(NodeBest));
   add("nkey", (long long)std::max(p.maxa, 2) * 8);   // best-first folds two children
+  add("rootcnt", (long long)F * (YABT_NB / 2) * 8);
   add("bffeat", 2LL * F * sizeof(BfCand));
   add("bfcand", (long long)p.maxn * sizeof(BfCand));
   add("nslot", (long long)p.maxn * 4);
@@ -279,6 +283,7 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
   b.hist[0] = (long long*)P("hist0"); b.hist[1] = (long long*)P("hist1");
   b.small = (long long*)P("small");
   b.node_key = (unsigned long long*)P("nkey");
+  b.root_cnt = (long long*)P("rootcnt");
   b.bf_feat = (BfCand*)P("bffeat"); b.bf_cand = (BfCand*)P("bfcand"); b.node_slot = (int*)P("nslot");
   b.pathmax[0] = (float*)P("pm0"); b.pathmax[1] = (float*)P("pm1");
   b.best = (NodeBest*)P("best"); b.nbest = (NodeBest*)P("nbest"); b.tot = (NodeTot*)P("tot");
@@ -357,6 +362,14 @@ int yabt_grower_hist_times(yabt_grower* g, float* ms, int cap, int* count) {
 
 }  // extern "C"
 
+// the root-count mode of this tree's root histogram (see launch_hist_kernels)
+static int root_count_mode(yabt_grower* g, const TreeIO& io) {
+  if (!g->rc_mode || io.root_rows) return 0;
+  if (g->rc_valid) return 2;
+  g->rc_valid = 1;          // this launch records them
+  return 1;
+}
+
 static int fill_io(yabt_grower* g, const yabt_tree_args* a, TreeIO* io) {
   if (!g || !a || !g->bound) { set_error("grower not created/bound"); return YABT_ERR_ARG; }
   if (!a->bins || !a->grad || (g->p.general && !a->hess) || !a->edges || !a->edge_off || !a->edge_cnt ||
@@ -408,7 +421,8 @@ int yabt_grow_hist(yabt_grower* g, const yabt_tree_args* a, int level, void* str
   cudaStream_t s = (cudaStream_t)stream;
   const bool tm = g->timing && g->ev_used + 2 <= (int)g->ev.size();
   if (tm) CUDA_TRY(cudaEventRecord(g->ev[g->ev_used], s));
-  CUDA_TRY(launch_level_hist(g->p, g->b, io, level, g->nsm, s, tm ? g->ev[g->ev_used + 1] : nullptr));
+  CUDA_TRY(launch_level_hist(g->p, g->b, io, level, g->nsm, s, tm ? g->ev[g->ev_used + 1] : nullptr,
+                             level == 0 ? root_count_mode(g, io) : 0));
   if (tm) g->ev_used += 2;
   return YABT_OK;
 }
@@ -459,7 +473,7 @@ int yabt_grow_bf_root_hist(yabt_grower* g, const yabt_tree_args* a, void* stream
   TreeIO io;
   int rc = fill_io(g, a, &io);
   if (rc) return rc;
-  CUDA_TRY(launch_hist_kernels(g->p, g->b, io, 0, 1, g->nsm, (cudaStream_t)stream, nullptr));
+  CUDA_TRY(launch_hist_kernels(g->p, g->b, io, 0, 1, g->nsm, (cudaStream_t)stream, nullptr, root_count_mode(g, io)));
   return YABT_OK;
 }
 
@@ -546,7 +560,7 @@ static cudaError_t mt_hist_passes(yabt_grower* g, const TreeIO& io, const MtBufs
     TreeIO io2 = io;
     io2.g = mb.grads + 2LL * i * g->p.n;
     io2.h = 2 * i + 1 < mb.T ? mb.grads + (2LL * i + 1) * g->p.n : mb.zeros;
-    const cudaError_t e = launch_hist_kernels(g->p, b, io2, level, 1, g->nsm, s, nullptr);
+    const cudaError_t e = launch_hist_kernels(g->p, b, io2, level, 1, g->nsm, s, nullptr, 0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -631,6 +645,13 @@ int yabt_grow_apply_all(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   if (rc) return rc;
   if (!io.bins_fm) { set_error("yabt_grow_apply_all: needs the feature-major bins (bins_fm)"); return YABT_ERR_ARG; }
   CUDA_TRY(launch_apply_all(g->p, g->b, io, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grower_set_root_count_cache(yabt_grower* g, int on) {
+  if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
+  g->rc_mode = on ? 1 : 0;
+  g->rc_valid = 0;
   return YABT_OK;
 }
 

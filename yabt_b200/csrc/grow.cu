@@ -17,7 +17,7 @@
 namespace yabt {
 
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                                int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist);
+                                int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist, int root_counts);
 
 __device__ __forceinline__ int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
@@ -1255,7 +1255,7 @@ cudaError_t launch_bf_split(const GrowParams& p, const GrowBufs& b, const TreeIO
                             cudaStream_t s) {
   const cudaError_t e = launch_bf_pick_partition(p, b, io, step, nsm, s);
   if (e != cudaSuccess) return e;
-  return launch_hist_kernels(p, b, io, 1, 1, nsm, s, nullptr);
+  return launch_hist_kernels(p, b, io, 1, 1, nsm, s, nullptr, 0);
 }
 
 // max |g| over several gradient arrays into the hessian word too (one
@@ -1295,8 +1295,8 @@ static inline int jobs_bound(int d, int max_pairs) {
 
 // Launches of one level. Returns a CUDA error code (0 on success).
 cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                              int nsm, cudaStream_t s, cudaEvent_t after_hist) {
-  return launch_hist_kernels(p, b, io, d, jobs_bound(d, p.max_pairs), nsm, s, after_hist);
+                              int nsm, cudaStream_t s, cudaEvent_t after_hist, int root_counts) {
+  return launch_hist_kernels(p, b, io, d, jobs_bound(d, p.max_pairs), nsm, s, after_hist, root_counts);
 }
 
 cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,

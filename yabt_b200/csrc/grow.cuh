@@ -138,6 +138,7 @@ struct GrowBufs {
   int* seg_count[2];
   int* act_gid[2];
   long long* hist[2];    // [maxa][C][F][256] int64 full histograms per level parity
+  long long* root_cnt;   // [F][128] packed per-bin row counts of all rows (cached root level)
   long long* small;      // [max_pairs][small_job_words(C, F)] small-child (or root) histograms:
                          // value channels [C-1][F][256], then counts [F][128] with bins
                          // 2k, 2k+1 packed in the low / high 32 bits of one int64

@@ -21,9 +21,16 @@
 
 namespace yabt {
 
+// LIMBS: 3 (g low, g high, count; two subs per lane) or 5 (g, h low / high,
+// count; one sub); 2 and 4 are the same without the count limb, for a root
+// level whose per-bin row counts are cached (the counts of all rows do not
+// change between the trees of a fit).
 template <int S, int LIMBS>
 struct HistCfg {
-  static_assert((S == 2 && LIMBS == 3) || (S == 1 && LIMBS == 5), "supported (S, LIMBS) pairs");
+  static_assert((S == 2 && (LIMBS == 3 || LIMBS == 2)) || (S == 1 && (LIMBS == 5 || LIMBS == 4)),
+                "supported (S, LIMBS) pairs");
+  static constexpr bool HAS_H = LIMBS >= 4;                 // hessian limbs present
+  static constexpr bool HAS_CNT = (LIMBS & 1) != 0;         // count limb present (the last one)
   static constexpr int WORDS = LIMBS * S * YABT_NB * 32;   // u32 words per histogram
   static constexpr int LIMB_STRIDE = S * YABT_NB * 32;      // words between limbs
   static constexpr int SMEM = WORDS * 4;
@@ -48,18 +55,18 @@ __device__ __forceinline__ void acc_row(unsigned lb, unsigned b0, unsigned b1, b
     const unsigned a0 = lb + (b0 << 7);
     red_s<0>(a0, glo);
     red_s<LS>(a0, ghi);
-    if constexpr (LIMBS == 5) {
+    if constexpr (HistCfg<S, LIMBS>::HAS_H) {
       red_s<2 * LS>(a0, (unsigned)vh & 0xFFFFu);
       red_s<3 * LS>(a0, (unsigned)(vh >> 16));
     }
-    red_s<(LIMBS - 1) * LS>(a0, 1u);
+    if constexpr (HistCfg<S, LIMBS>::HAS_CNT) red_s<(LIMBS - 1) * LS>(a0, 1u);
   }
   if constexpr (S == 2) {
     if (FULL || ok1) {
       const unsigned a1 = lb + (b1 << 7) + YABT_NB * 32 * 4;
       red_s<0>(a1, glo);
       red_s<LS>(a1, ghi);
-      red_s<(LIMBS - 1) * LS>(a1, 1u);
+      if constexpr (HistCfg<S, LIMBS>::HAS_CNT) red_s<(LIMBS - 1) * LS>(a1, 1u);
     }
   }
 }
@@ -140,7 +147,7 @@ __device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, unsigned v
   for (int s = 0; s < STG - 1; ++s) {
     const int r = rid_of(s);
     gq[s] = r >= 0 ? __ldg(g + r) : 0.f;
-    hq[s] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    hq[s] = (HistCfg<S, LIMBS>::HAS_H && r >= 0) ? __ldg(h + r) : 0.f;
     if (s < nst) copy(s, r);
     cp_commit();
   }
@@ -151,14 +158,14 @@ __device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, unsigned v
     const int r = rnext;
     rnext = rid_of(s + STG);
     gq[STG - 1] = r >= 0 ? __ldg(g + r) : 0.f;
-    hq[STG - 1] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    hq[STG - 1] = (HistCfg<S, LIMBS>::HAS_H && r >= 0) ? __ldg(h + r) : 0.f;
     if (s + STG - 1 < nst) copy(s + STG - 1, r);
     cp_commit();
     // the first lane of each stage row publishes the row's quantised values;
     // every lane reads all of them back with 16-byte loads (no per-row shuffle)
     if (lane % LPR == 0 && rr < RPS) {
       sts_u32(vslot + rr * 4, __float2int_rn(gq[0] * gs));
-      if (LIMBS == 5) sts_u32(vslot + 32 + rr * 4, __float2int_rn(hq[0] * hs));
+      if (HistCfg<S, LIMBS>::HAS_H) sts_u32(vslot + 32 + rr * 4, __float2int_rn(hq[0] * hs));
     }
     cp_wait<STG - 1>();
     __syncwarp();
@@ -168,7 +175,7 @@ __device__ __forceinline__ void hist_warp(unsigned lb, unsigned ring, unsigned v
     int vg[RPS], vh[RPS];
     lds_v4(vslot, vg[0], vg[1], vg[2], vg[3]);
     lds_v4(vslot + 16, vg[4], vg[5], vg[6], vg[7]);
-    if (LIMBS == 5) {
+    if (HistCfg<S, LIMBS>::HAS_H) {
       lds_v4(vslot + 32, vh[0], vh[1], vh[2], vh[3]);
       lds_v4(vslot + 48, vh[4], vh[5], vh[6], vh[7]);
     } else {
@@ -224,7 +231,7 @@ __device__ __forceinline__ void hist_warp_narrow(unsigned lb, unsigned ring, con
   for (int s = 0; s < STG - 1; ++s) {
     const int r = rid_of(s);
     gq[s] = r >= 0 ? __ldg(g + r) : 0.f;
-    hq[s] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    hq[s] = (HistCfg<S, LIMBS>::HAS_H && r >= 0) ? __ldg(h + r) : 0.f;
     if (s < nst) copy(s, r);
     cp_commit();
   }
@@ -234,20 +241,20 @@ __device__ __forceinline__ void hist_warp_narrow(unsigned lb, unsigned ring, con
     const int r = rnext;
     rnext = rid_of(s + STG);
     gq[STG - 1] = r >= 0 ? __ldg(g + r) : 0.f;
-    hq[STG - 1] = (LIMBS == 5 && r >= 0) ? __ldg(h + r) : 0.f;
+    hq[STG - 1] = (HistCfg<S, LIMBS>::HAS_H && r >= 0) ? __ldg(h + r) : 0.f;
     if (s + STG - 1 < nst) copy(s + STG - 1, r);
     cp_commit();
     cp_wait<STG - 1>();
     __syncwarp();
     const int vgl = __float2int_rn(gq[0] * gs);
-    const int vhl = (LIMBS == 5) ? __float2int_rn(hq[0] * hs) : 0;
+    const int vhl = HistCfg<S, LIMBS>::HAS_H ? __float2int_rn(hq[0] * hs) : 0;
     const unsigned stg = ring + (s % STG) * SB;
     const int nr = min(RPS, nrow - s * RPS);
 #pragma unroll
     for (int it = 0; it < RPS / REP; ++it) {
       const int q = it * REP + rsub;                   // stage row of this lane
       const int vg = __shfl_sync(0xffffffffu, vgl, q);
-      const int vh = (LIMBS == 5) ? __shfl_sync(0xffffffffu, vhl, q) : 0;
+      const int vh = HistCfg<S, LIMBS>::HAS_H ? __shfl_sync(0xffffffffu, vhl, q) : 0;
       const unsigned b = lds_u8(stg + q * 64 + byte);
       acc_row<S, LIMBS, false>(lb, b, 0u, okf && q < nr, false, vg, vh);
     }
@@ -357,7 +364,8 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
          const UnitDesc* __restrict__ units, GrowState* st, long long* __restrict__ out,
          int F, int U, int level_gate, int igroups) {
   using Cfg = HistCfg<S, LIMBS>;
-  constexpr int C = (LIMBS == 5) ? 3 : 2;
+  constexpr int C = Cfg::HAS_H ? 3 : 2;       // output channels (counts last)
+  constexpr int CW = Cfg::HAS_CNT ? C : C - 1; // channels written here (cached counts are copied in)
   constexpr int BPP = YABT_NB / RED_PARTS;     // bins per part (16)
   __shared__ long long tsm[C][32][BPP + 1];
   if (st->level != level_gate || !st->active) return;
@@ -394,16 +402,16 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
       const unsigned* p = partials + (size_t)__ldg(&ip->slot) * Cfg::WORDS + woff;
       lo[u] = used ? __ldg(p) : 0u;
       hi[u] = used ? __ldg(p + Cfg::LIMB_STRIDE) : 0u;
-      if constexpr (LIMBS == 5) {
+      if constexpr (Cfg::HAS_H) {
         hlo[u] = used ? __ldg(p + 2 * Cfg::LIMB_STRIDE) : 0u;
         hhi[u] = used ? __ldg(p + 3 * Cfg::LIMB_STRIDE) : 0u;
       }
-      cn[u] = used ? __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE) : 0u;
+      cn[u] = (Cfg::HAS_CNT && used) ? __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE) : 0u;
     }
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
       ag += (long long)(int)hi[u] * 65536LL + (long long)lo[u];
-      if constexpr (LIMBS == 5) ah += (long long)(int)hhi[u] * 65536LL + (long long)hlo[u];
+      if constexpr (Cfg::HAS_H) ah += (long long)(int)hhi[u] * 65536LL + (long long)hlo[u];
       ac += cn[u];
     }
   }
@@ -412,9 +420,9 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
     if (__ldg(&ip->used) == 0) continue;
     const unsigned* p = partials + (size_t)__ldg(&ip->slot) * Cfg::WORDS + woff;
     ag += (long long)(int)__ldg(p + Cfg::LIMB_STRIDE) * 65536LL + (long long)__ldg(p);
-    if constexpr (LIMBS == 5)
+    if constexpr (Cfg::HAS_H)
       ah += (long long)(int)__ldg(p + 3 * Cfg::LIMB_STRIDE) * 65536LL + (long long)__ldg(p + 2 * Cfg::LIMB_STRIDE);
-    ac += __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE);
+    if constexpr (Cfg::HAS_CNT) ac += __ldg(p + (LIMBS - 1) * Cfg::LIMB_STRIDE);
   }
   {
     const int bl = w >> 5, j = w & 31;
@@ -424,7 +432,7 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   }
   __syncthreads();
   const long long job_base = (long long)job * small_job_words(C, F);
-  for (int e = threadIdx.x; e < C * 32 * BPP; e += blockDim.x) {
+  for (int e = threadIdx.x; e < CW * 32 * BPP; e += blockDim.x) {
     const int bl = e % BPP, j = (e / BPP) & 31, c = e / (BPP * 32);
     const int f = ud.feat[sub][j];
     if (f < 0 || j >= ud.lw) continue;   // narrow tiles: lanes j, j+lw, ... are copies of one feature
@@ -451,9 +459,15 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   }
 }
 
+// root_counts (level 0 over all rows only): 0 as usual; 1 as usual and keep a
+// copy of the per-bin row counts in b.root_cnt; 2 the kernels without the
+// count limb, the counts copied in from b.root_cnt.
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                                int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist) {
+                                int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist, int root_counts) {
   const int* rows = d == 0 ? io.root_rows : b.rows[d & 1];   // nullptr: identity
+  if (d != 0 || io.root_rows) root_counts = 0;
+  const size_t cnt_off = (size_t)(p.C - 1) * p.F * YABT_NB;      // count words of job 0 in `small`
+  const size_t cnt_bytes = (size_t)p.F * (YABT_NB / 2) * 8;
   // levels with at most a few jobs split each job's items over several reduce
   // blocks, which add into a zeroed histogram
   const int igroups = std::max(1, 8 / jobs);
@@ -461,26 +475,47 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
     const cudaError_t e = cudaMemsetAsync(b.small, 0, (size_t)jobs * small_job_words(p.C, p.F) * 8, s);
     if (e != cudaSuccess) return e;
   }
-  if (!p.general) {
+  if (!p.general && root_counts != 2) {
     k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
     if (after_hist) cudaEventRecord(after_hist, s);
     k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
         b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
-  } else {
+  } else if (!p.general) {
+    k_hist<2, 2><<<nsm, HistPipe<2, 2>::THREADS, HistPipe<2, 2>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+                                                      b.st, b.partials, d);
+    if (after_hist) cudaEventRecord(after_hist, s);
+    k_reduce<2, 2><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
+  } else if (root_counts != 2) {
     k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d);
     if (after_hist) cudaEventRecord(after_hist, s);
     k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
         b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
+  } else {
+    k_hist<1, 4><<<nsm, HistPipe<1, 4>::THREADS, HistPipe<1, 4>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+                                                      b.st, b.partials, d);
+    if (after_hist) cudaEventRecord(after_hist, s);
+    k_reduce<1, 4><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
   }
   count_launches(2);
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && root_counts == 1)
+    e = cudaMemcpyAsync(b.root_cnt, b.small + cnt_off, cnt_bytes, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess && root_counts == 2)
+    e = cudaMemcpyAsync(b.small + cnt_off, b.root_cnt, cnt_bytes, cudaMemcpyDeviceToDevice, s);
+  return e;
 }
 
 cudaError_t set_hist_smem_attrs() {
   cudaError_t e = cudaFuncSetAttribute(k_hist<2, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        HistPipe<2, 3>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_hist<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, HistPipe<2, 2>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_hist<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, HistPipe<1, 4>::SMEM);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(k_hist<1, 5>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               HistPipe<1, 5>::SMEM);
