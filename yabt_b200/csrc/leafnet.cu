@@ -522,15 +522,25 @@ struct UpdateArgs {
 // Per-leaf tables (value, linear, lo, hi) are staged in shared memory; rows
 // stream in natural order.
 __global__ void __launch_bounds__(256) k_update(UpdateArgs u, int nn) {
-  extern __shared__ float tb[];            // value[nn], linear/lo/hi[nn][K]
+  // per-leaf tables in shared memory: linear / lo / hi as [nn][KMAX] (padded,
+  // so a row reads each table with two 16-byte loads), then value[nn]
+  extern __shared__ __align__(16) float tb[];
   const bool nets = u.linear && u.has_nets && u.has_nets[0];
   const int K = nets ? u.K : 0;
-  float* sval = tb;
-  float* slin = tb + nn;
-  float* slo = slin + nn * K;
-  float* shi = slo + nn * K;
+  float* slin = tb;
+  float* slo = slin + (size_t)nn * KMAX;
+  float* shi = slo + (size_t)nn * KMAX;
+  float* sval = nets ? shi + (size_t)nn * KMAX : tb;   // without leaf models only the values
   for (int i = threadIdx.x; i < nn; i += blockDim.x) sval[i] = u.value[i];
-  for (int i = threadIdx.x; i < nn * K; i += blockDim.x) { slin[i] = u.linear[i]; slo[i] = u.lo[i]; shi[i] = u.hi[i]; }
+  if (nets) {
+    for (int i = threadIdx.x; i < nn * KMAX; i += blockDim.x) {
+      const int l = i / KMAX, k = i % KMAX;
+      const bool in = k < K;
+      slin[i] = in ? u.linear[l * K + k] : 0.f;
+      slo[i] = in ? u.lo[l * K + k] : 0.f;
+      shi[i] = in ? u.hi[l * K + k] : 0.f;
+    }
+  }
   __syncthreads();
   int fk[KMAX];
 #pragma unroll
@@ -540,14 +550,24 @@ __global__ void __launch_bounds__(256) k_update(UpdateArgs u, int nn) {
     const int l = u.leaf_of_row[i];
     float c = sval[l];
     if (nets) {
+      float lin[KMAX], lo[KMAX], hi[KMAX];
+      const float4* p4 = reinterpret_cast<const float4*>(slin + (size_t)l * KMAX);
+      const float4* q4 = reinterpret_cast<const float4*>(slo + (size_t)l * KMAX);
+      const float4* r4 = reinterpret_cast<const float4*>(shi + (size_t)l * KMAX);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float4 a = p4[h], b = q4[h], d = r4[h];
+        lin[4 * h] = a.x; lin[4 * h + 1] = a.y; lin[4 * h + 2] = a.z; lin[4 * h + 3] = a.w;
+        lo[4 * h] = b.x; lo[4 * h + 1] = b.y; lo[4 * h + 2] = b.z; lo[4 * h + 3] = b.w;
+        hi[4 * h] = d.x; hi[4 * h + 1] = d.y; hi[4 * h + 2] = d.z; hi[4 * h + 3] = d.w;
+      }
       float s = 0.f;
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
         if (k < K) {
-          const int o = l * K + k;
           const float x = u.Xfm[(long long)fk[k] * u.n + i];
-          const float xc = fminf(fmaxf(x, slo[o]), shi[o]);
-          s = __fadd_rn(s, __fmul_rn(slin[o], xc));
+          const float xc = fminf(fmaxf(x, lo[k]), hi[k]);
+          s = __fadd_rn(s, __fmul_rn(lin[k], xc));
         }
       }
       c = __fadd_rn(c, s);
@@ -852,8 +872,7 @@ int yabt_update_margin(const yabt_update_args* p, void* stream) {
   if (p->n == 0) return YABT_OK;
   if (p->max_nodes <= 0) { set_error("yabt_update_margin: max_nodes must be > 0"); return YABT_ERR_ARG; }
   const int grid = (int)std::min<long long>((p->n + 255) / 256, 148LL * 8);
-  const int K = p->linear ? p->K : 0;
-  const size_t smem = (size_t)p->max_nodes * (1 + 3 * K) * sizeof(float);
+  const size_t smem = (size_t)p->max_nodes * (p->linear ? 1 + 3 * KMAX : 1) * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) { set_error("k_update smem: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
