@@ -78,3 +78,40 @@ def test_grow_matches_golden_inputs(golden, case):
                              imat if imat.size else None, fm if fm.size else None)
     _check(ot, oleaf, gt, gl)
     np.testing.assert_array_equal(gt.feature.cpu().numpy(), z[f"g{case}_feature"])
+
+
+@pytest.mark.parametrize("general", [False, True])
+def test_root_count_cache_reproduces_uncached_trees(general):
+    """yabt_grower_set_root_count_cache: after the first tree records the root's
+    per-bin row counts, later root histograms skip the count channel and copy
+    them in; the trees must equal those of a grower without the cache."""
+    from yabt_b200 import _lib
+    from yabt_b200.grower import EdgePack, Grower, pack_bins
+    from yabt_b200.tree import TreeParams
+    rng = np.random.default_rng(21)
+    n, F = 30000, 70
+    X = rng.normal(size=(n, F)).astype(np.float32)
+    b = OBinner().fit(X)
+    bins = pack_bins(torch.from_numpy(b.transform(X)).cuda())
+    ep = EdgePack(list(b.edges_), b.scales_, "cuda")
+    tp = TreeParams(max_leaves=63, max_depth=8, min_samples_leaf=20)
+    outs = []
+    for cached in (True, False):
+        gr = Grower(n, F, 63, 8, general, "cuda")
+        _lib.check(gr.lib.yabt_grower_set_root_count_cache(gr.h, 1 if cached else 0), "cache")
+        trees = []
+        for t in range(3):
+            r = np.random.default_rng(100 + t)
+            g = torch.from_numpy((r.integers(-512, 512, size=n) / 256.0).astype(np.float32)).cuda()
+            h = (torch.from_numpy((r.integers(1, 64, size=n) / 256.0).astype(np.float32)).cuda() if general
+                 else torch.ones(n, device="cuda"))
+            out = gr.new_outputs()
+            gr.grow(gr.args(bins, g, h, ep, tp, out))
+            torch.cuda.synchronize()
+            k = int(out["meta"][0].item())
+            trees.append({key: out[key][:k].cpu().numpy() for key in ("feature", "threshold", "left", "value")}
+                         | {"leaf": out["leaf_of_row"].cpu().numpy()})
+        outs.append(trees)
+    for t in range(3):
+        for key in ("feature", "threshold", "left", "value", "leaf"):
+            np.testing.assert_array_equal(outs[0][t][key], outs[1][t][key], err_msg=f"tree {t} {key}")
