@@ -286,6 +286,8 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
             _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
             xchg.reduce(d)
             _lib.check(lib.yabt_grow_split(h, ref, d, s), "yabt_grow_split")
+            if not getattr(grower, "level_wait", True):
+                continue                         # every level queued (finished levels are no-ops on every rank)
             ev_d, host_d = ring[d % 8]
             host_d.copy_(state, non_blocking=True)
             ev_d.record()

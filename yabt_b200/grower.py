@@ -134,6 +134,7 @@ class Grower:
         """Whether growing a tree may wait on the device to stop queuing levels
         once the tree is complete (off: every level is queued, no host waits)."""
         _lib.check(self.lib.yabt_grower_set_level_wait(self.h, 1 if wait else 0), "yabt_grower_set_level_wait")
+        self.level_wait = bool(wait)
 
     def set_timing(self, max_launches: int) -> None:
         """Record CUDA events around up to max_launches histogram launches."""
