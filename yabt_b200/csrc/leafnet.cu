@@ -15,8 +15,9 @@
 //   k_ln_rows     natural row order: per-row record (x_norm[K], g, h), per-leaf
 //                 min/max envelope of the raw inputs
 //   k_ln_gram     per leaf segment chunk: fp64 normal-equation partial sums
-//                 M = sum h x1 x1^T (upper triangle), b = -sum g x1, one lane
-//                 per entry, fixed order (deterministic)
+//                 M = sum h x1 x1^T (upper triangle), b = -sum g x1, every
+//                 accumulator in registers of the lane that owns the row,
+//                 fixed order (deterministic)
 //   k_ln_solve    per leaf: reduce chunk partials in order, add the ridge,
 //                 Cholesky solve, fold normalisation + learning rate
 //   k_update      margin += value[leaf] + sum_k linear * clamp(x, lo, hi);
@@ -252,20 +253,17 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
   }
 }
 
-// One block (8 warps) per chunk of a leaf's rows. Each warp stages 32-row
-// batches through shared memory as float64 rows (lane k gathers row k's record
-// and writes x1 = (x_norm[K], 1), h and -g; the next batch is prefetched into
-// registers while the current one is consumed) and tracks the raw-x envelope.
-// Lane e accumulates entries e and e+32 of the normal equations as
-// w_a * (w_b * w_c) over staged slots (a, b, c): M_ab = x1_a (x1_b h) and
-// b_a = x1_a (1 * -g) -- the reference's operation order -- with no branches;
-// even and odd rows go to separate accumulators (two independent chains) that
-// are added at the end. Warps are reduced in order: the chunk partial is
-// deterministic.
-constexpr int SROW = 2 * (KMAX + 1) + 2;  // staged doubles per row: x1[KMAX + 1], h x1[KMAX + 1], -g, pad
-__global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
+// One block (8 warps) per chunk of a leaf's rows; each lane owns rows (the
+// lane's share of its warp's rows) and keeps every normal-equation
+// accumulator in registers: with x1 = (x_norm[K], 1) padded with zeros to
+// KMAX + 1 entries, M_ij += (h x1_i) x1_j for i <= j (45 fused products) and
+// b_i += (-g) x1_i (9). The next row's record is loaded while the current one
+// is used, and the raw-x envelope is tracked on the way. At the end of the
+// chunk each warp adds its lanes' sums (butterfly), the warps are added in
+// order, and the chunk partial is written in the packed layout of the D = K + 1
+// system: the chunk partial is deterministic.
+__global__ void __launch_bounds__(256, 1) k_ln_gram(LeafNetArgs a) {
   __shared__ double sp[8][NE];
-  __shared__ double stage[8][32][SROW];
   __shared__ float smin[8][KMAX], smax[8][KMAX];
   const int c = blockIdx.x;
   if (c >= a.flags[2]) return;
@@ -276,6 +274,8 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
   const int b0 = a.chunk_begin[c], b1 = a.chunk_end[c];
   const int K = a.K, D = K + 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int DM = KMAX + 1;                 // padded system size
+  constexpr int NT = DM * (DM + 1) / 2;        // upper-triangle entries of the padded system
   float mu[KMAX], sd[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) {
@@ -283,80 +283,69 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
     mu[k] = k < K ? a.col_mean[f] : 0.f;
     sd[k] = k < K ? fmaxf(a.col_std[f], 1e-6f) : 1.f;
   }
-  // staged slots: x1_k at k (k < K), 1 at K; h x1_k at S_HX + k; -g at S_NG.
-  // Every accumulator is one fused product of two staged values:
-  // M[a][b] += (h x1_a) x1_b, rhs[a] += (-g) x1_a.
-  constexpr int S_HX = KMAX + 1, S_NG = 2 * (KMAX + 1);
-  int ia[2], ib[2];
-  bool ev[2];
-  const int ntri = D * (D + 1) / 2;
+  double acc[NT], accb[DM];
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int e = lane + 32 * q;
-    ev[q] = e < ntri + D;
-    if (e < ntri) {                      // M[row][row + rem]
-      int rem = e, row = 0;
-      while (rem >= D - row) { rem -= D - row; ++row; }
-      ia[q] = S_HX + row; ib[q] = row + rem;
-    } else {                             // rhs entry e - ntri
-      ia[q] = S_NG; ib[q] = ev[q] ? e - ntri : 0;
-    }
-  }
-  double acc0[2] = {0.0, 0.0}, acc1[2] = {0.0, 0.0};
+  for (int e = 0; e < NT; ++e) acc[e] = 0.0;
+#pragma unroll
+  for (int i = 0; i < DM; ++i) accb[i] = 0.0;
   float mn[KMAX], mx[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) { mn[k] = INFINITY; mx[k] = -INFINITY; }
   const int per = (b1 - b0 + 7) / 8;
   const int w0 = b0 + warp * per, w1 = min(b1, w0 + per);
-  float4 n0, n1, n2;   // prefetched record of this lane's row in the next batch
-  auto fetch = [&](int p0) {
-    const int p = p0 + lane;
-    if (p < w1) {
-      const int row = lst ? lst[p] : p;
-      const float4* r4 = reinterpret_cast<const float4*>(a.rec + (long long)row * REC);
-      n0 = __ldg(r4); n1 = __ldg(r4 + 1); n2 = __ldg(r4 + 2);
-    }
+  auto fetch = [&](int p, float4& r0, float4& r1, float4& r2) {
+    const int row = lst ? lst[p] : p;
+    const float4* r4 = reinterpret_cast<const float4*>(a.rec + (long long)row * REC);
+    r0 = __ldg(r4); r1 = __ldg(r4 + 1); r2 = __ldg(r4 + 2);
   };
-  fetch(w0);
-  for (int p0 = w0; p0 < w1; p0 += 32) {
-    const int nb = min(32, w1 - p0);
-    {
-      const float xr[KMAX] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-      double* st = stage[warp][lane];
-      if (lane < nb) {
-        const double hh = (double)n2.y;
+  float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0, c2 = c0;
+  int p = w0 + lane;
+  if (p < w1) fetch(p, c0, c1, c2);
+  for (; p < w1; p += 32) {
+    float4 n0 = c0, n1 = c1, n2 = c2;
+    if (p + 32 < w1) fetch(p + 32, n0, n1, n2);   // next row in flight
+    const float xr[KMAX] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    double x[DM];
 #pragma unroll
-        for (int k = 0; k < KMAX; ++k) {
-          if (k < K) { mn[k] = fminf(mn[k], xr[k]); mx[k] = fmaxf(mx[k], xr[k]); }
-          const double x1 = (double)__fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]);
-          st[k] = x1;
-          st[S_HX + k] = __dmul_rn(hh, x1);
-        }
-        st[K] = 1.0;                     // bias input (K <= KMAX; slots K+1.. of x1 unused)
-        st[S_HX + K] = hh;
-        st[S_NG] = -(double)n2.x;
-      }
+    for (int k = 0; k < KMAX; ++k) {
+      if (k < K) { mn[k] = fminf(mn[k], xr[k]); mx[k] = fmaxf(mx[k], xr[k]); }
+      x[k] = k < K ? (double)__fdiv_rn(__fsub_rn(xr[k], mu[k]), sd[k]) : (k == K ? 1.0 : 0.0);
     }
-    __syncwarp();
-    fetch(p0 + 32);   // next batch in flight while this one is consumed
+    x[KMAX] = K == KMAX ? 1.0 : 0.0;            // the bias input sits at index K
     if (elig) {
-      int r = 0;
-      for (; r + 1 < nb; r += 2) {
-        const double* s0 = stage[warp][r];
-        const double* s1 = stage[warp][r + 1];
+      const double hh = (double)c2.y, ng = -(double)c2.x;
+      int e = 0;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          acc0[q] = __fma_rn(s0[ia[q]], s0[ib[q]], acc0[q]);
-          acc1[q] = __fma_rn(s1[ia[q]], s1[ib[q]], acc1[q]);
-        }
-      }
-      if (r < nb) {
-        const double* s0 = stage[warp][r];
+      for (int i = 0; i < DM; ++i) {
+        const double hx = __dmul_rn(hh, x[i]);
 #pragma unroll
-        for (int q = 0; q < 2; ++q) acc0[q] = __fma_rn(s0[ia[q]], s0[ib[q]], acc0[q]);
+        for (int j = i; j < DM; ++j, ++e) acc[e] = __fma_rn(hx, x[j], acc[e]);
+        accb[i] = __fma_rn(ng, x[i], accb[i]);
       }
     }
-    __syncwarp();
+    c0 = n0; c1 = n1; c2 = n2;
+  }
+  // warp sums (every lane ends with them), then lane 0 writes the packed entries
+#pragma unroll
+  for (int e = 0; e < NT; ++e)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc[e] = __dadd_rn(acc[e], __shfl_xor_sync(0xffffffffu, acc[e], o));
+#pragma unroll
+  for (int i = 0; i < DM; ++i)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) accb[i] = __dadd_rn(accb[i], __shfl_xor_sync(0xffffffffu, accb[i], o));
+  const int ntri = D * (D + 1) / 2;
+  for (int e = lane; e < NE; e += 32) sp[warp][e] = 0.0;
+  __syncwarp();
+  if (lane == 0) {
+    int e = 0;
+#pragma unroll
+    for (int i = 0; i < DM; ++i) {
+#pragma unroll
+      for (int j = i; j < DM; ++j, ++e)
+        if (j < D) sp[warp][i * D - i * (i - 1) / 2 + (j - i)] = acc[e];
+      if (i < D) sp[warp][ntri + i] = accb[i];
+    }
   }
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) {
@@ -366,11 +355,6 @@ __global__ void __launch_bounds__(256, 4) k_ln_gram(LeafNetArgs a) {
       a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, o));
     }
     if (lane == 0) { smin[warp][k] = a0; smax[warp][k] = a1; }
-  }
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int e = lane + 32 * q;
-    if (e < NE) sp[warp][e] = ev[q] ? __dadd_rn(acc0[q], acc1[q]) : 0.0;
   }
   __syncthreads();
   if (threadIdx.x < NE) {
