@@ -56,10 +56,12 @@ def _fit_pair(X, y, loss, n_trees, **kw):
     return ob, gb
 
 
-@pytest.mark.parametrize("loss", ["mse", "logloss"])
-def test_first_tree_with_leaf_nets_matches_oracle(loss):
-    """One full boosting iteration (grad -> tree -> leaf nets -> margin) vs the oracle."""
-    X, y = _data(40, 6000, 10, 0.02)
+@pytest.mark.parametrize("loss,n", [("mse", 6000), ("logloss", 6000), ("mse", 1_300_000)])
+def test_first_tree_with_leaf_nets_matches_oracle(loss, n):
+    """One full boosting iteration (grad -> tree -> leaf nets -> margin) vs the
+    oracle; at 1.3M rows each fp64 Gram partial holds 4,096 rows (8,192 rows per
+    leaf and more span several partials)."""
+    X, y = _data(40, n, 10, 0.02)
     if loss == "logloss":
         y = (y > np.median(y)).astype(np.float32)
     ob, gb = _fit_pair(X, y, loss, 1, max_leaves=31)

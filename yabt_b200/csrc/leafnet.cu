@@ -32,7 +32,18 @@ namespace yabt {
 
 constexpr int KMAX = 8;                 // leaf-model inputs (leaf_net_features <= 8)
 constexpr int NE = (KMAX + 1) * (KMAX + 2) / 2 + (KMAX + 1);   // 45 + 9 = 54 accumulators
-constexpr int GRAM_CHUNK = 2048;        // rows per Gram partial (small: enough blocks at small n)
+constexpr int GRAM_CHUNK = 2048;        // smallest rows per Gram partial (enough blocks at small n)
+constexpr long long GRAM_SPLIT = 296;   // large fits: about 2 x 148 partials of full size (see gram_rows)
+
+// Rows per Gram partial: 2,048 x m, m = n / (2,048 x 296) clamped to [1, 8].
+// Each partial pays fixed costs (its start-up loads, the warp sums of 54
+// accumulators); large fits give each lane more rows to spread them over.
+// A function of n alone, so a fit's partials, and hence its sums, do not
+// depend on the device.
+inline int gram_rows(long long n) {
+  const long long m = n / (GRAM_CHUNK * GRAM_SPLIT);
+  return GRAM_CHUNK * (int)(m < 1 ? 1 : (m > 8 ? 8 : m));
+}
 
 struct LeafNetArgs {
   // tree (device)
@@ -86,6 +97,7 @@ struct LeafNetArgs {
   double* partial;            // [max_chunks][NE]
   double* totals;             // [maxn][NE] per-node sums of the chunk partials
   int max_chunks;
+  int chunk_rows;             // rows per Gram partial (gram_rows(n))
 };
 
 constexpr int REC = 12;   // floats per row record: raw x[8], g, h, pad[2] (48 bytes)
@@ -219,7 +231,7 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
     const bool leaf = a.feature[g] < 0;
     const int c = leaf ? a.leaf_count[g] : 0;
     a.counts[g] = c;
-    a.leaf_nch[g] = (c + GRAM_CHUNK - 1) / GRAM_CHUNK;
+    a.leaf_nch[g] = (c + a.chunk_rows - 1) / a.chunk_rows;
     if (leaf && c >= a.min_samples) atomicAdd(&s_ne, 1);
   }
   __syncthreads();
@@ -247,8 +259,8 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
       const int idx = f0 + q;
       if (idx >= a.max_chunks) break;
       a.chunk_leaf[idx] = g;
-      a.chunk_begin[idx] = a.leaf_begin[g] + q * GRAM_CHUNK;
-      a.chunk_end[idx] = a.leaf_begin[g] + min(c, (q + 1) * GRAM_CHUNK);
+      a.chunk_begin[idx] = a.leaf_begin[g] + q * a.chunk_rows;
+      a.chunk_end[idx] = a.leaf_begin[g] + min(c, (q + 1) * a.chunk_rows);
     }
   }
 }
@@ -257,8 +269,9 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
 // lane's share of its warp's rows) and keeps every normal-equation
 // accumulator in registers: with x1 = (x_norm[K], 1) padded with zeros to
 // KMAX + 1 entries, M_ij += (h x1_i) x1_j for i <= j (45 fused products) and
-// b_i += (-g) x1_i (9). The next row's record is loaded while the current one
-// is used, and the raw-x envelope is tracked on the way. At the end of the
+// b_i += (-g) x1_i (9). The records of the next two rows and the list index
+// of the one after are in flight while the current row is used (the index
+// load never stalls a record load), and the raw-x envelope is tracked on the way. At the end of the
 // chunk each warp adds its lanes' sums (butterfly), the warps are added in
 // order, and the chunk partial is written in the packed layout of the D = K + 1
 // system: the chunk partial is deterministic.
@@ -293,17 +306,24 @@ __global__ void __launch_bounds__(256, 1) k_ln_gram(LeafNetArgs a) {
   for (int k = 0; k < KMAX; ++k) { mn[k] = INFINITY; mx[k] = -INFINITY; }
   const int per = (b1 - b0 + 7) / 8;
   const int w0 = b0 + warp * per, w1 = min(b1, w0 + per);
-  auto fetch = [&](int p, float4& r0, float4& r1, float4& r2) {
-    const int row = lst ? lst[p] : p;
-    const float4* r4 = reinterpret_cast<const float4*>(a.rec + (long long)row * REC);
-    r0 = __ldg(r4); r1 = __ldg(r4 + 1); r2 = __ldg(r4 + 2);
+  auto row_of = [&](int q) { return lst ? __ldg(lst + q) : q; };
+  auto fetch = [&](int row, float4& r0, float4& r1, float2& r2) {   // raw x[8]; g, h
+    const float* r = a.rec + (long long)row * REC;
+    r0 = __ldg(reinterpret_cast<const float4*>(r));
+    r1 = __ldg(reinterpret_cast<const float4*>(r) + 1);
+    r2 = __ldg(reinterpret_cast<const float2*>(r + KMAX));
   };
-  float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0, c2 = c0;
-  int p = w0 + lane;
-  if (p < w1) fetch(p, c0, c1, c2);
+  float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0, n0 = c0, n1 = c0;
+  float2 c2 = make_float2(0.f, 0.f), n2 = c2;
+  int p = w0 + lane, i2 = 0;
+  if (p < w1) fetch(row_of(p), c0, c1, c2);
+  if (p + 32 < w1) fetch(row_of(p + 32), n0, n1, n2);
+  if (p + 64 < w1) i2 = row_of(p + 64);
   for (; p < w1; p += 32) {
-    float4 n0 = c0, n1 = c1, n2 = c2;
-    if (p + 32 < w1) fetch(p + 32, n0, n1, n2);   // next row in flight
+    float4 m0 = n0, m1 = n1;
+    float2 m2 = n2;
+    if (p + 64 < w1) fetch(i2, m0, m1, m2);       // record two rows ahead
+    if (p + 96 < w1) i2 = row_of(p + 96);          // list index three rows ahead
     const float xr[KMAX] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     double x[DM];
 #pragma unroll
@@ -324,6 +344,7 @@ __global__ void __launch_bounds__(256, 1) k_ln_gram(LeafNetArgs a) {
       }
     }
     c0 = n0; c1 = n1; c2 = n2;
+    n0 = m0; n1 = m1; n2 = m2;
   }
   // warp sums (every lane ends with them), then lane 0 writes the packed entries
 #pragma unroll
@@ -766,6 +787,7 @@ static int leafnet_carve(const yabt_leafnet_args* p, void* workspace, long long 
   a.totals = (double*)w; w += al((long long)p->max_nodes * NE * 8);
   a.env = (float*)w;
   a.max_chunks = (int)max_chunks;
+  a.chunk_rows = gram_rows(p->n);
   *out = a;
   return YABT_OK;
 }
@@ -794,7 +816,8 @@ static cudaError_t leafnet_launch(const LeafNetArgs& a, int stage, cudaStream_t 
       }
       k_ln_plan<<<1, 1024, 0, s>>>(a);
       k_ln_elig<<<1, 1024, 0, s>>>(a);
-      k_ln_gram<<<(unsigned)a.max_chunks, 256, 0, s>>>(a);
+      k_ln_gram<<<(unsigned)std::min<long long>(a.max_chunks, a.n / a.chunk_rows + a.n_nodes_cap + 1), 256, 0,
+                  s>>>(a);
       k_ln_total<<<nblk, 128, 0, s>>>(a);
       count_launches(5);
       break;
