@@ -199,24 +199,40 @@ __global__ void __launch_bounds__(1024) k_ln_pad(LeafNetArgs a) {
 
 // ------------------------------------------------------------------ per-row records
 // Natural row order, streaming: record = (raw x[K], g, h) at margin + value[leaf].
+// A thread takes two rows per step (i and i + grid stride) and issues every
+// load of both before it stores either record.
 __global__ void __launch_bounds__(256) k_ln_rows(LeafNetArgs a) {
   const int K = a.K;
   int fk[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) fk[k] = k < K ? (int)a.feats[k] : 0;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < a.n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int l = a.leaf_of_row[i];
-    float g, h;
-    loss_gh(a.loss, __fadd_rn(a.margin[i], a.value[l]), a.y[i], &g, &h);
-    float r[REC];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < a.n; i0 += 2 * stride) {
+    int l[2];
+    float m[2], y[2], v[2], x[2][KMAX];
 #pragma unroll
-    for (int k = 0; k < KMAX; ++k) r[k] = k < K ? a.Xfm[(long long)fk[k] * a.n + i] : 0.f;
-    r[KMAX] = g; r[KMAX + 1] = h; r[KMAX + 2] = 0.f; r[KMAX + 3] = 0.f;
-    float4* dst = reinterpret_cast<float4*>(a.rec + i * REC);
-    dst[0] = make_float4(r[0], r[1], r[2], r[3]);
-    dst[1] = make_float4(r[4], r[5], r[6], r[7]);
-    dst[2] = make_float4(r[8], r[9], r[10], r[11]);
+    for (int r = 0; r < 2; ++r) {
+      const long long i = i0 + r * stride;
+      const bool ok = i < a.n;
+      l[r] = ok ? a.leaf_of_row[i] : 0;
+      m[r] = ok ? a.margin[i] : 0.f;
+      y[r] = ok ? a.y[i] : 0.f;
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) x[r][k] = (ok && k < K) ? a.Xfm[(long long)fk[k] * a.n + i] : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) v[r] = i0 + r * stride < a.n ? a.value[l[r]] : 0.f;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const long long i = i0 + r * stride;
+      if (i >= a.n) break;
+      float g, h;
+      loss_gh(a.loss, __fadd_rn(m[r], v[r]), y[r], &g, &h);
+      float4* dst = reinterpret_cast<float4*>(a.rec + i * REC);
+      dst[0] = make_float4(x[r][0], x[r][1], x[r][2], x[r][3]);
+      dst[1] = make_float4(x[r][4], x[r][5], x[r][6], x[r][7]);
+      dst[2] = make_float4(g, h, 0.f, 0.f);
+    }
   }
 }
 
@@ -525,7 +541,8 @@ struct UpdateArgs {
 };
 
 // Per-leaf tables (value, linear, lo, hi) are staged in shared memory; rows
-// stream in natural order.
+// stream in natural order, two a thread per step (i and i + grid stride) with
+// every load of both issued before either row's margin and gradient are stored.
 __global__ void __launch_bounds__(256) k_update(UpdateArgs u, int nn) {
   // per-leaf tables in shared memory: linear / lo / hi as [nn][KMAX] (padded,
   // so a row reads each table with two 16-byte loads), then value[nn]
@@ -550,40 +567,56 @@ __global__ void __launch_bounds__(256) k_update(UpdateArgs u, int nn) {
   int fk[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) fk[k] = (k < K) ? (int)u.feats[k] : 0;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < u.n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int l = u.leaf_of_row[i];
-    float c = sval[l];
-    if (nets) {
-      float lin[KMAX], lo[KMAX], hi[KMAX];
-      const float4* p4 = reinterpret_cast<const float4*>(slin + (size_t)l * KMAX);
-      const float4* q4 = reinterpret_cast<const float4*>(slo + (size_t)l * KMAX);
-      const float4* r4 = reinterpret_cast<const float4*>(shi + (size_t)l * KMAX);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < u.n; i0 += 2 * stride) {
+    int lr[2];
+    float mr[2], yr[2], xr[2][KMAX];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float4 a = p4[h], b = q4[h], d = r4[h];
-        lin[4 * h] = a.x; lin[4 * h + 1] = a.y; lin[4 * h + 2] = a.z; lin[4 * h + 3] = a.w;
-        lo[4 * h] = b.x; lo[4 * h + 1] = b.y; lo[4 * h + 2] = b.z; lo[4 * h + 3] = b.w;
-        hi[4 * h] = d.x; hi[4 * h + 1] = d.y; hi[4 * h + 2] = d.z; hi[4 * h + 3] = d.w;
-      }
-      float s = 0.f;
+    for (int r = 0; r < 2; ++r) {
+      const long long i = i0 + r * stride;
+      const bool ok = i < u.n;
+      lr[r] = ok ? u.leaf_of_row[i] : 0;
+      mr[r] = ok ? u.margin[i] : 0.f;
+      yr[r] = (ok && u.grad) ? u.y[i] : 0.f;
 #pragma unroll
-      for (int k = 0; k < KMAX; ++k) {
-        if (k < K) {
-          const float x = u.Xfm[(long long)fk[k] * u.n + i];
-          const float xc = fminf(fmaxf(x, lo[k]), hi[k]);
-          s = __fadd_rn(s, __fmul_rn(lin[k], xc));
-        }
-      }
-      c = __fadd_rn(c, s);
+      for (int k = 0; k < KMAX; ++k) xr[r][k] = (ok && k < K) ? u.Xfm[(long long)fk[k] * u.n + i] : 0.f;
     }
-    const float m = __fadd_rn(u.margin[i], c);
-    u.margin[i] = m;
-    if (u.grad) {
-      float g, h;
-      loss_gh(u.loss, m, u.y[i], &g, &h);
-      u.grad[i] = g;
-      if (u.hess) u.hess[i] = h;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const long long i = i0 + r * stride;
+      if (i >= u.n) break;
+      const int l = lr[r];
+      float c = sval[l];
+      if (nets) {
+        float lin[KMAX], lo[KMAX], hi[KMAX];
+        const float4* p4 = reinterpret_cast<const float4*>(slin + (size_t)l * KMAX);
+        const float4* q4 = reinterpret_cast<const float4*>(slo + (size_t)l * KMAX);
+        const float4* r4 = reinterpret_cast<const float4*>(shi + (size_t)l * KMAX);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float4 a = p4[h], b = q4[h], d = r4[h];
+          lin[4 * h] = a.x; lin[4 * h + 1] = a.y; lin[4 * h + 2] = a.z; lin[4 * h + 3] = a.w;
+          lo[4 * h] = b.x; lo[4 * h + 1] = b.y; lo[4 * h + 2] = b.z; lo[4 * h + 3] = b.w;
+          hi[4 * h] = d.x; hi[4 * h + 1] = d.y; hi[4 * h + 2] = d.z; hi[4 * h + 3] = d.w;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+          if (k < K) {
+            const float xc = fminf(fmaxf(xr[r][k], lo[k]), hi[k]);
+            s = __fadd_rn(s, __fmul_rn(lin[k], xc));
+          }
+        }
+        c = __fadd_rn(c, s);
+      }
+      const float m = __fadd_rn(mr[r], c);
+      u.margin[i] = m;
+      if (u.grad) {
+        float g, h;
+        loss_gh(u.loss, m, yr[r], &g, &h);
+        u.grad[i] = g;
+        if (u.hess) u.hess[i] = h;
+      }
     }
   }
 }
@@ -878,12 +911,15 @@ int yabt_update_margin(const yabt_update_args* p, void* stream) {
   u.margin = p->margin; u.y = p->y; u.grad = p->grad; u.hess = p->hess; u.loss = p->loss;
   if (p->n == 0) return YABT_OK;
   if (p->max_nodes <= 0) { set_error("yabt_update_margin: max_nodes must be > 0"); return YABT_ERR_ARG; }
-  const int grid = (int)std::min<long long>((p->n + 255) / 256, 148LL * 8);
   const size_t smem = (size_t)p->max_nodes * (p->linear ? 1 + 3 * KMAX : 1) * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) { set_error("k_update smem: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
   }
+  // one wave of resident blocks (the tables are staged once per block)
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_update, 256, smem) != cudaSuccess || occ < 1) occ = 1;
+  const int grid = (int)std::min<long long>((p->n + 511) / 512, 148LL * occ);
   k_update<<<grid, 256, smem, (cudaStream_t)stream>>>(u, p->max_nodes);
   count_launches(1);
   LCUDA(cudaGetLastError());
