@@ -116,7 +116,7 @@ int yabt_pack_bins(const uint8_t* plain, long long n, int F, uint8_t* tiled, voi
   host_tiles(F, n, &bytes);
   CUDA_TRY(cudaMemsetAsync(tiled, 0, (size_t)bytes, s));
   const long long total = n * F;
-  const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 32);
+  const int grid = (int)std::min<long long>((total + 255) / 256, (long long)YABT_SMS_HINT * 32);
   k_pack_bins<<<grid, 256, 0, s>>>(plain, n, F, tiled);
   count_launches(1);
   CUDA_TRY(cudaGetLastError());

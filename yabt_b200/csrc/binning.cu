@@ -498,7 +498,7 @@ static cudaError_t fit_edges(const float* Xfm, long long n, int F, const int32_t
   unsigned* keys = w.keys;
   {
     const long long total = (long long)F * P;
-    const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    const int grid = (int)std::min<long long>((total + 255) / 256, (long long)YABT_SMS_HINT * 16);
     k_sample_keys<<<grid, 256, 0, s>>>(Xfm, n, F, idx, nq, P, keys);
     count_launches(2);   // sample keys + first bitonic pass
   }
@@ -509,7 +509,7 @@ static cudaError_t fit_edges(const float* Xfm, long long n, int F, const int32_t
     for (long long k = 2 * BL; k <= P; k <<= 1) {
       for (long long j = k >> 1; j >= BL; j >>= 1) {
         const long long half = (long long)F * P / 2;
-        const int grid = (int)std::min<long long>((half + 255) / 256, 148LL * 16);
+        const int grid = (int)std::min<long long>((half + 255) / 256, (long long)YABT_SMS_HINT * 16);
         k_bitonic_global<<<grid, 256, 0, s>>>(keys, P, F, k, j);
         count_launches(1);
       }

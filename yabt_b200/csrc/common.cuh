@@ -23,7 +23,7 @@
 
 #define YABT_NB 256                 // bins per feature (uint8 codes)
 #define YABT_TILE 64                // features per full tile
-#define YABT_SMS_HINT 148
+#define YABT_SMS_HINT 148           // SMs of a B200: sizes grid-stride grids and per-level work targets
 
 namespace yabt {
 

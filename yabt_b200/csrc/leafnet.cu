@@ -827,7 +827,7 @@ static int leafnet_carve(const yabt_leafnet_args* p, void* workspace, long long 
 
 // Stage s of the leaf-model fit (see yabt_leafnet_stage in the header).
 static cudaError_t leafnet_launch(const LeafNetArgs& a, int stage, cudaStream_t s) {
-  const int nsm = 148;
+  const int nsm = YABT_SMS_HINT;
   const int nblk = (a.n_nodes_cap + 3) / 4;
   switch (stage) {
     case 0: {
@@ -919,7 +919,7 @@ int yabt_update_margin(const yabt_update_args* p, void* stream) {
   // one wave of resident blocks (the tables are staged once per block)
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_update, 256, smem) != cudaSuccess || occ < 1) occ = 1;
-  const int grid = (int)std::min<long long>((p->n + 511) / 512, 148LL * occ);
+  const int grid = (int)std::min<long long>((p->n + 511) / 512, (long long)YABT_SMS_HINT * occ);
   k_update<<<grid, 256, smem, (cudaStream_t)stream>>>(u, p->max_nodes);
   count_launches(1);
   LCUDA(cudaGetLastError());
@@ -929,7 +929,7 @@ int yabt_update_margin(const yabt_update_args* p, void* stream) {
 int yabt_grad_init(const float* margin, const float* y, long long n, int loss, float* grad, float* hess, void* stream) {
   if (!margin || !y || !grad || n < 0) { set_error("yabt_grad_init: bad arguments"); return YABT_ERR_ARG; }
   if (n == 0) return YABT_OK;
-  const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 8);
+  const int grid = (int)std::min<long long>((n + 255) / 256, (long long)YABT_SMS_HINT * 8);
   k_grad_init<<<grid, 256, 0, (cudaStream_t)stream>>>(margin, y, n, loss, grad, hess);
   count_launches(1);
   LCUDA(cudaGetLastError());

@@ -121,7 +121,7 @@ int yabt_apply_tree(const float* X, long long n, int F, const int64_t* feature, 
 int yabt_impute_rows(float* X, long long n, int F, const float* medians, void* stream) {
   if (!X || n < 0 || F <= 0 || !medians) { set_error("yabt_impute_rows: bad arguments"); return YABT_ERR_ARG; }
   if (n == 0) return YABT_OK;
-  const int grid = (int)std::min<long long>((n * F + 255) / 256, 148LL * 16);
+  const int grid = (int)std::min<long long>((n * F + 255) / 256, (long long)YABT_SMS_HINT * 16);
   k_impute_rows<<<grid, 256, 0, (cudaStream_t)stream>>>(X, n, F, medians);
   count_launches(1);
   cudaError_t e = cudaGetLastError();
