@@ -107,3 +107,32 @@ def test_tiled_layout_addresses(lib, n, F):
     for f in range(F):
         assert lib.yabt_bin_address(n, F, f, ctypes.byref(off), ctypes.byref(width), ctypes.byref(pos)) == 0
         assert (off.value, width.value, pos.value) == addr[f], f
+
+
+def test_struct_layouts_match_header(tmp_path):
+    """Every argument struct of the header has the size and field offsets of
+    its ctypes mirror in ``yabt_b200/_lib.py`` (a C compiler lays out the
+    header's structs; a mismatch would make the library read the wrong bytes)."""
+    import shutil
+    import subprocess
+    from yabt_b200 import _lib
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    mirrors = {"yabt_tree_args": _lib.TreeArgs, "yabt_leafnet_args": _lib.LeafNetArgs,
+               "yabt_update_args": _lib.UpdateArgs}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", f'#include "{HEADER}"', "int main(void) {"]
+    for cname, mirror in mirrors.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for field, _ in mirror._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src, exe = tmp_path / "layout.c", tmp_path / "layout"
+    src.write_text("\n".join(lines) + "\n")
+    subprocess.run([cc, "-std=c11", "-o", str(exe), str(src)], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l.strip()}
+    for cname, mirror in mirrors.items():
+        assert got[(cname, "sizeof")] == ctypes.sizeof(mirror), cname
+        for field, _ in mirror._fields_:
+            assert got[(cname, field)] == getattr(mirror, field).offset, f"{cname}.{field}"
