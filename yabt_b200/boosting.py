@@ -8,11 +8,14 @@ device-resident forest arrays; ``Tree`` objects are views of those arrays,
 materialised once at the end of ``fit``.
 
 Supported ``BoostParams`` (the reference's defaults are the supported path):
-level-wise growth, interaction steering, ridge-linear neural leaves, feature
-subsampling (``colsample``), ``min_split_gain_rel``, eval-set early stopping.
-Options outside the GPU tree-growth path (kernel splits, refinement / refit,
-GOSS, adaptive features, product features, auto-tune, MLP leaves, stochastic
-routing, row subsampling, the best-first grower) raise NotImplementedError.
+level-wise growth, the best-first grower (the heap order of yabt/tree.py, or
+the C / Numba grower's arithmetic with ``numba_grower=True``), interaction
+steering, ridge-linear neural leaves, row subsampling (``subsample``), GOSS
+(``goss_enabled``), feature subsampling (``colsample``),
+``min_split_gain_rel``, eval-set early stopping. Options outside the GPU
+tree-growth path (kernel splits, refinement / refit, adaptive features,
+product features, auto-tune, MLP leaves, stochastic routing) raise
+NotImplementedError.
 """
 
 from __future__ import annotations
