@@ -115,3 +115,35 @@ def test_root_count_cache_reproduces_uncached_trees(general):
     for t in range(3):
         for key in ("feature", "threshold", "left", "value", "leaf"):
             np.testing.assert_array_equal(outs[0][t][key], outs[1][t][key], err_msg=f"tree {t} {key}")
+
+
+@pytest.mark.parametrize("case", ["constant_columns", "fewer_rows_than_two_leaves", "max_leaves_2",
+                                  "max_depth_1", "one_constant_column"])
+def test_grow_degenerate_trees(case):
+    """Trees that stop early: a root-only tree (constant columns, or fewer rows
+    than two leaves of min_samples_leaf), a single split (max_leaves = 2,
+    max_depth = 1) and a constant column among others (never chosen). Dyadic
+    gradients: the structure and leaf of every row equal the oracle's; values
+    within 1e-5."""
+    rng = np.random.default_rng(7)
+    n, F, leaves, depth, msl = 500, 5, 31, 64, 20
+    X = rng.normal(size=(n, F)).astype(np.float32)
+    g = (rng.integers(-512, 512, size=n) / 256.0).astype(np.float32)
+    h = (rng.integers(1, 64, size=n) / 256.0).astype(np.float32)
+    if case == "constant_columns":
+        X = np.full((n, 4), 3.0, np.float32)
+    elif case == "fewer_rows_than_two_leaves":
+        X, g, h = X[:30], g[:30], h[:30]
+    elif case == "max_leaves_2":
+        leaves = 2
+    elif case == "max_depth_1":
+        leaves, depth = 255, 1
+    else:
+        X[:, 2] = 1.0
+        msl = 5
+    ot, oleaf, gt, gl = _run(X, g, h, leaves, depth, msl)
+    _check(ot, oleaf, gt, gl)
+    if case in ("constant_columns", "fewer_rows_than_two_leaves"):
+        assert gt.feature.numel() == 1 and int(gt.feature[0]) == -1
+    if case == "one_constant_column":
+        assert not bool((gt.feature == 2).any())
