@@ -132,3 +132,22 @@ def test_apply_equals_training_leaf():
     ot = OTree(t.feature.cpu().numpy(), t.threshold.cpu().numpy(), t.left.cpu().numpy(), t.right.cpu().numpy(),
                t.value.cpu().numpy(), t.depth, t.gate_scale.cpu().numpy())
     np.testing.assert_array_equal(leaf.cpu().numpy(), ot.apply(ob.impute(X)))
+
+
+def test_predict_on_zero_rows():
+    """Every estimator predicts an empty matrix as an empty result (the
+    reference's numpy / torch prediction path does)."""
+    from yabt_b200 import YABTClassifier, YABTMultiTaskRegressor, YABTRegressor
+    X, y = _data(11, 2000, 6, 0.02)
+    X0 = X[:0]
+    reg = YABTRegressor(n_estimators=3, max_leaves=15).fit(X, y)
+    assert reg.predict(X0).shape == (0,)
+    clf = YABTClassifier(n_estimators=3, max_leaves=15).fit(X, (y > np.median(y)).astype(int))
+    assert clf.predict(X0).shape == (0,)
+    assert clf.predict_proba(X0).shape == (0, 2)
+    yc = np.digitize(y, np.quantile(y, [1 / 3, 2 / 3]))
+    mc = YABTClassifier(n_estimators=3, max_leaves=15).fit(X, yc)
+    assert mc.predict(X0).shape == (0,)
+    assert mc.predict_proba(X0).shape == (0, 3)
+    mt = YABTMultiTaskRegressor(n_estimators=3, max_leaves=15).fit(X, np.stack([y, -y], axis=1))
+    assert mt.predict(X0).shape == (0, 2)

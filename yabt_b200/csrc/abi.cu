@@ -624,6 +624,7 @@ int yabt_grow_tree_multitask(yabt_grower* g, const yabt_tree_args* a, int tasks,
 
 int yabt_mt_update(const int32_t* leaf_of_row, const float* values, int tasks, long long n, float* margin,
                    const float* y, float* grad, void* stream) {
+  if (n == 0 && tasks >= 1) return YABT_OK;   // no rows: nothing is read (buffers may be NULL)
   if (tasks < 1 || n < 0 || !margin || (values && !leaf_of_row) || (grad && !y)) {
     set_error("yabt_mt_update: bad arguments");
     return YABT_ERR_ARG;

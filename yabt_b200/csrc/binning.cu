@@ -419,6 +419,7 @@ long long yabt_bin_fit_workspace_bytes(long long n, int F, long long nq) {
 }
 
 int yabt_transpose(const float* X, long long n, int F, float* Xfm, void* stream) {
+  if (n == 0 && F > 0) return YABT_OK;   // no rows: nothing is read (buffers may be NULL)
   if (!X || !Xfm || n < 0 || F <= 0) { set_error("yabt_transpose: bad arguments"); return YABT_ERR_ARG; }
   if (n == 0) return YABT_OK;
   dim3 grid((unsigned)((n + 31) / 32), (unsigned)((F + 31) / 32));
@@ -615,6 +616,7 @@ int yabt_bin_fit_edges(const float* Xs, long long nq, int F, int max_bins, void*
 int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, const float* edges,
                        const int32_t* edge_cnt, uint8_t* tiled, uint8_t* plain_out, uint8_t* fm_out,
                        void* stream) {
+  if (n == 0 && F > 0) return YABT_OK;   // no rows: nothing is read (buffers may be NULL)
   if (!Xfm || n < 0 || F <= 0 || !medians || !edges || !edge_cnt || !tiled) {
     set_error("yabt_bin_transform: bad arguments");
     return YABT_ERR_ARG;

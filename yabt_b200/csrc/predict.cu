@@ -87,6 +87,7 @@ int yabt_predict_forest(const float* X, long long n, int F, int ntrees, const in
                         const int32_t* right, const float* value, const int32_t* has_nets,
                         const int64_t* feats, int K, const float* linear, const float* lo, const float* hi,
                         float base, float* out, void* stream) {
+  if (n == 0 && F > 0 && ntrees >= 0) return YABT_OK;   // no rows: nothing is read (buffers may be NULL)
   if (!X || n < 0 || F <= 0 || ntrees < 0 || !out || (ntrees > 0 && (!tree_off || !feature || !threshold ||
       !left || !right || !value))) {
     set_error("yabt_predict_forest: bad arguments");
@@ -104,6 +105,7 @@ int yabt_predict_forest(const float* X, long long n, int F, int ntrees, const in
 
 int yabt_apply_tree(const float* X, long long n, int F, const int64_t* feature, const float* threshold,
                     const int64_t* left, const int64_t* right, int64_t* out, void* stream) {
+  if (n == 0 && F > 0) return YABT_OK;   // no rows: nothing is read (buffers may be NULL)
   if (!X || n < 0 || F <= 0 || !feature || !threshold || !left || !right || !out) {
     set_error("yabt_apply_tree: bad arguments");
     return YABT_ERR_ARG;
@@ -119,6 +121,7 @@ int yabt_apply_tree(const float* X, long long n, int F, const int64_t* feature, 
 }
 
 int yabt_impute_rows(float* X, long long n, int F, const float* medians, void* stream) {
+  if (n == 0 && F > 0) return YABT_OK;   // no rows: nothing is read (buffers may be NULL)
   if (!X || n < 0 || F <= 0 || !medians) { set_error("yabt_impute_rows: bad arguments"); return YABT_ERR_ARG; }
   if (n == 0) return YABT_OK;
   const int grid = (int)std::min<long long>((n * F + 255) / 256, (long long)YABT_SMS_HINT * 16);
