@@ -151,3 +151,4 @@ def test_predict_on_zero_rows():
     assert mc.predict_proba(X0).shape == (0, 3)
     mt = YABTMultiTaskRegressor(n_estimators=3, max_leaves=15).fit(X, np.stack([y, -y], axis=1))
     assert mt.predict(X0).shape == (0, 2)
+    assert tuple(reg.booster_.binner.transform(X0).shape) == (0, 6)
