@@ -40,6 +40,8 @@ long long yabt_launch_count(void);
  * ceiling of the histogram kernel. Issues k_hist's u32 reductions (limbs = 3:
  * unit-hessian path, two 32-feature subs per lane; 5: general path) with its
  * layout and grid and pseudo-random bins, twice (warm-up, then timed);
+ * limbs = 1 or 2 issue the packed 64-bit form instead (one u64 reduction per
+ * (row, feature) carrying value and count, two subs; or two u64, one sub);
  * *ms = the timed launch, *updates = its (row, feature) updates. sink: 8 bytes
  * of device memory the result is folded into. Synchronises the stream.     */
 int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates);

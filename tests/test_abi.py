@@ -136,3 +136,14 @@ def test_struct_layouts_match_header(tmp_path):
         assert got[(cname, "sizeof")] == ctypes.sizeof(mirror), cname
         for field, _ in mirror._fields_:
             assert got[(cname, field)] == getattr(mirror, field).offset, f"{cname}.{field}"
+
+
+def test_probe_rejects_bad_arguments_before_any_device_call(lib):
+    """The measurement probe validates its arguments on the host: unsupported
+    limb counts and missing outputs return YABT_ERR_ARG (1) without a GPU."""
+    ms, upd = ctypes.c_float(), ctypes.c_longlong()
+    for limbs in (0, 4, 6, -1):
+        assert lib.yabt_probe_shared_red(limbs, 1, None, None, ctypes.byref(ms), ctypes.byref(upd)) == 1
+    for limbs in (1, 2, 3, 5):
+        assert lib.yabt_probe_shared_red(limbs, 0, None, None, ctypes.byref(ms), ctypes.byref(upd)) == 1
+        assert lib.yabt_probe_shared_red(limbs, 1, None, None, None, None) == 1
