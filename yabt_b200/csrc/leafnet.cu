@@ -287,10 +287,10 @@ __global__ void __launch_bounds__(1024) k_ln_plan(LeafNetArgs a) {
 // KMAX + 1 entries, M_ij += (h x1_i) x1_j for i <= j (45 fused products) and
 // b_i += (-g) x1_i (9). The records of the next two rows and the list index
 // of the one after are in flight while the current row is used (the index
-// load never stalls a record load), and the raw-x envelope is tracked on the way. At the end of the
-// chunk each warp adds its lanes' sums (butterfly), the warps are added in
-// order, and the chunk partial is written in the packed layout of the D = K + 1
-// system: the chunk partial is deterministic.
+// load never stalls a record load), and the raw-x envelope is tracked on the
+// way. At the end of the chunk each warp adds its lanes' sums (butterfly), the
+// warps are added in order, and the chunk partial is written in the packed
+// layout of the D = K + 1 system: the chunk partial is deterministic.
 __global__ void __launch_bounds__(256, 1) k_ln_gram(LeafNetArgs a) {
   __shared__ double sp[8][NE];
   __shared__ float smin[8][KMAX], smax[8][KMAX];
