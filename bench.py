@@ -5,9 +5,10 @@
 
 A step is one boosting iteration (gradients, level-wise tree growth, ridge-
 linear neural leaves, interaction-score update, margin update) on the
-configuration's synthetic data. The default workload is BASELINE config 4
-(10M x 200 correlated features, 255 leaves, max depth 10, squared loss,
-neural leaves and interaction steering on). Prints one JSON line.
+configuration's synthetic data. The default workload is a 10,000,000 x 200
+regression with correlated features (blocks of 10 columns, pairwise
+correlation 0.3), 255 leaves, max depth 10, squared loss, neural leaves and
+interaction steering on. Prints one JSON line.
 
 value   trees/s over all GPUs with the inputs resident in HBM (CUDA events,
         max over ranks).
@@ -135,9 +136,12 @@ class ClockSampler:
         rows = [r for r in rows if len(r) >= 10 and r[2].replace(".", "").isdigit()]
 
         def stamp(r):
+            """Wall-clock seconds of an nvidia-smi timestamp, with or without a
+            fractional part ("2026/12/02 06:23:01.123" or "... 06:23:01")."""
             try:
-                return time.mktime(time.strptime(r[0].split(".")[0], "%Y/%m/%d %H:%M:%S")) + \
-                    float("0." + r[0].split(".")[1]) if "." in r[0] else 0.0
+                whole, _, frac = r[0].partition(".")
+                secs = time.mktime(time.strptime(whole.strip(), "%Y/%m/%d %H:%M:%S"))
+                return secs + (float("0." + frac) if frac.strip().isdigit() else 0.0)
             except Exception:
                 return None
         inside = rows
@@ -283,6 +287,27 @@ def run_multiclass(args):
         "clocks": clocks, "e2e": None, "cpu_baseline": None}))
 
 
+def model_digest(booster, W: int, K: int, dist=None) -> dict:
+    """SHA-256 over the timed trees (feature, threshold, left of trees W..W+K-1)
+    and the root histogram's per-bin row counts summed over the ranks. Row
+    shards change no split, count or partition, so the digest is the same at
+    every GPU count."""
+    import hashlib
+    import torch
+    h = hashlib.sha256()
+    for t in booster.trees[W:W + K]:
+        for a in (t.feature, t.threshold, t.left):
+            h.update(a.detach().cpu().numpy().tobytes())
+    counts = booster.grower_.root_counts()
+    if dist is not None:
+        dist.all_reduce(counts)
+    h.update(counts.cpu().numpy().tobytes())
+    torch.cuda.synchronize()
+    return {"sha256": h.hexdigest(), "trees": K,
+            "covers": "feature, threshold and left child of every timed tree; root per-bin row counts "
+                      "summed over ranks"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -395,6 +420,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(rows_hist)
     bin_reads_per_s = float(rows_hist.item()) * F / (ms / 1000.0)
+    digest = model_digest(booster, W, K, dist if world > 1 else None)
 
     # e2e through the public estimator API from host memory (every rank fits
     # its host shard; the slowest rank's wall time counts)
@@ -464,6 +490,7 @@ def run_ours(args):
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "model_digest": digest,
         }
         print(json.dumps(line))
     if world > 1:

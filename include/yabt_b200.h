@@ -161,6 +161,12 @@ int yabt_grower_set_level_wait(yabt_grower* g, int wait);
  * turns it on only while the bin matrix stays the same (Booster.fit);
  * on = 0 turns it off and forgets the counts. Off by default.             */
 int yabt_grower_set_root_count_cache(yabt_grower* g, int on);
+/* The cached root counts, unpacked: out[f][b] (device, F x 256 int64) = the
+ * number of this grower's rows whose bin of feature f is b, as recorded by
+ * the last root histogram over all rows with the cache on; the count channel
+ * of the root histogram of yabt/tree.py:425-452 (scatter_hist over every
+ * row). YABT_ERR_ARG when nothing has been recorded yet.                  */
+int yabt_grower_root_counts(yabt_grower* g, int64_t* out, void* stream);
 /* After yabt_grow_tree: leaf_of_row for every row 0..n-1 (not only the root
  * rows), routed by the split bins through the feature-major bins (required);
  * Tree.apply of yabt/tree.py:82-116 on the training rows.                 */

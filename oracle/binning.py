@@ -52,12 +52,14 @@ def quantile_sorted(s: np.ndarray, q: np.ndarray) -> np.ndarray:
 def nanmedian_f32(col: np.ndarray) -> np.float32:
     """np.nanmedian of a float32 column: mean of the two middle order
     statistics computed as float32(a + b) / 2 (yabt/binning.py:32-33)."""
-    c = np.sort(col[~np.isnan(col)])
+    c = col[~np.isnan(col)]
     m = c.shape[0]
     if m == 0:
         return np.float32(np.nan)
+    # the middle order statistics (a partial sort places them as a full sort would)
     if m % 2 == 1:
-        return np.float32(c[m // 2])
+        return np.float32(np.partition(c, m // 2)[m // 2])
+    c = np.partition(c, [m // 2 - 1, m // 2])
     s = np.float32(c[m // 2 - 1]) + np.float32(c[m // 2])
     return np.float32(s / np.float32(2.0))
 
@@ -83,7 +85,7 @@ class Binner:
     def fit(self, X: np.ndarray) -> "Binner":
         X = np.asarray(X, dtype=np.float32)
         n, F = X.shape
-        med = np.array([nanmedian_f32(X[:, f]) for f in range(F)], dtype=np.float32)
+        med = np.array([nanmedian_f32(np.ascontiguousarray(X[:, f])) for f in range(F)], dtype=np.float32)
         self.medians_ = np.where(np.isnan(med), np.float32(0.0), med).astype(np.float32)
         idx = self.sample_rows(n)
         Xq = X if idx is None else X[idx]
@@ -108,15 +110,26 @@ class Binner:
 
     def impute(self, X: np.ndarray) -> np.ndarray:
         """yabt/binning.py:121-124."""
-        X = np.asarray(X, dtype=np.float32)
-        return np.where(np.isnan(X), self.medians_, X).astype(np.float32)
+        Xi = np.array(X, dtype=np.float32)          # one copy
+        np.copyto(Xi, self.medians_[None, :], where=np.isnan(Xi))
+        return Xi
 
     def transform(self, X: np.ndarray) -> np.ndarray:
         """bin(x) = #{edges < x} as uint8 (yabt/binning.py:97-112)."""
-        Xi = self.impute(X)
-        out = np.empty(Xi.shape, dtype=np.uint8)
-        for f in range(Xi.shape[1]):
-            out[:, f] = np.searchsorted(self.edges_[f], Xi[:, f], side="left").astype(np.uint8)
+        X = np.asarray(X, dtype=np.float32)
+        n, F = X.shape
+        out = np.empty((n, F), dtype=np.uint8)
+        from concurrent.futures import ThreadPoolExecutor
+        import os
+        with ThreadPoolExecutor(max(1, min(16, os.cpu_count() or 1))) as pool:
+            for r0 in range(0, n, 1 << 16):       # row blocks: contiguous columns within a block
+                XiT = np.ascontiguousarray(self.impute(X[r0:r0 + (1 << 16)]).T)
+                ob = np.empty(XiT.shape, np.uint8)
+
+                def one(f):                        # searchsorted releases the GIL
+                    ob[f] = np.searchsorted(self.edges_[f], XiT[f], side="left")
+                list(pool.map(one, range(F)))
+                out[r0:r0 + (1 << 16)] = ob.T
         return out
 
     def edge_value(self, f: int, b: int) -> float:

@@ -120,21 +120,62 @@ class OTree:
         return pairs
 
 
+def feature_major(a: np.ndarray) -> np.ndarray:
+    """(F, n) contiguous copy of an (n, F) matrix, transposed in row blocks
+    (a whole-matrix transpose copy is cache-unfriendly at millions of rows)."""
+    n, F = a.shape
+    out = np.empty((F, n), dtype=a.dtype)
+    for r0 in range(0, n, 1 << 15):
+        out[:, r0:r0 + (1 << 15)] = a[r0:r0 + (1 << 15)].T
+    return out
+
+
 def scatter_hist(binned: np.ndarray, slot: np.ndarray, g: np.ndarray, h: np.ndarray,
                  w: np.ndarray | None, K: int) -> np.ndarray:
-    """(3, K, F, 256) float32 histogram, sequential float32 adds in row-major
-    element order (yabt/tree.py:442-452; yabt/_cuda/hist.cu:27-49 computes the
-    same sums with atomics)."""
-    n, F = binned.shape
-    flat = (slot.astype(np.int64)[:, None] * (F * B)
-            + np.arange(F, dtype=np.int64)[None, :] * B
-            + binned.astype(np.int64)).reshape(-1)
-    out = np.zeros((3, K * F * B), dtype=np.float32)
-    np.add.at(out[0], flat, np.repeat(g.astype(np.float32), F))
-    np.add.at(out[1], flat, np.repeat(h.astype(np.float32), F))
-    ww = np.ones(n, np.float32) if w is None else w.astype(np.float32)
-    np.add.at(out[2], flat, np.repeat(ww, F))
-    return out.reshape(3, K, F, B)
+    """(3, K, F, 256) float32 histogram, sequential float32 adds in row order
+    (yabt/tree.py:442-452; yabt/_cuda/hist.cu:27-49 computes the same sums with
+    atomics)."""
+    return scatter_hist_fm(feature_major(binned), slot, g, h, w, K)
+
+
+def scatter_hist_fm(binned_fm: np.ndarray, slot: np.ndarray, g: np.ndarray, h: np.ndarray,
+                    w: np.ndarray | None, K: int) -> np.ndarray:
+    """``scatter_hist`` of a feature-major (F, n) bin matrix.
+
+    Every bin belongs to one feature, so adding feature by feature performs the
+    same sequence of float32 additions into each bin as one pass in row-major
+    element order (``np.add.at`` is sequential). Channels whose values are all
+    one (the row count, a unit hessian) are integer counts below 2^24, which a
+    sequential float32 sum represents exactly, so they are counted directly."""
+    F, n = binned_fm.shape
+    out = np.zeros((3, K, F, B), dtype=np.float32)
+    if n == 0:
+        return out
+    base = slot.astype(np.int64) * B
+    g32 = g.astype(np.float32)
+    h32 = h.astype(np.float32)
+    w32 = None if w is None else w.astype(np.float32)
+    unit_h = bool(np.all(h32 == 1.0))
+    unit_w = w32 is None or bool(np.all(w32 == 1.0))
+    for f in range(F):
+        idx = base + binned_fm[f]
+        cnt = np.bincount(idx, minlength=K * B).astype(np.float32).reshape(K, B)
+        acc = np.zeros(K * B, np.float32)
+        np.add.at(acc, idx, g32)
+        out[0, :, f] = acc.reshape(K, B)
+        if unit_h:
+            out[1, :, f] = cnt
+        else:
+            acc = np.zeros(K * B, np.float32)
+            np.add.at(acc, idx, h32)
+            out[1, :, f] = acc.reshape(K, B)
+        if unit_w:
+            out[2, :, f] = cnt
+        else:
+            acc = np.zeros(K * B, np.float32)
+            np.add.at(acc, idx, w32)
+            out[2, :, f] = acc.reshape(K, B)
+    return out
 
 
 def split_scan(hist: np.ndarray, lam: float, gamma: float, mcw: float, msl: int,
@@ -209,7 +250,8 @@ def grow_levelwise(binned: np.ndarray, grad: np.ndarray, hess: np.ndarray,
     add_leaf(-lr * gsum / (hsum + lam), 0)
     node_of_row = np.zeros(n, dtype=np.int64)
     active = [0]
-    hist = scatter_hist(binned, np.zeros(n, np.int64), grad, hess, None, 1)
+    binned_fm = feature_major(binned)
+    hist = scatter_hist_fm(binned_fm, np.zeros(n, np.int64), grad, hess, None, 1)
     pathmax = np.zeros((1, F), np.float32) if imat is not None else None
     remaining = params.max_leaves - 1
     depth = 0
@@ -287,7 +329,7 @@ def grow_levelwise(binned: np.ndarray, grad: np.ndarray, hess: np.ndarray,
             sil_row = sil[np.maximum(pair_row, 0)]
             small = part & (go_left == sil_row)
             rows = np.nonzero(small)[0]
-            hs = scatter_hist(binned[rows], pair_row[rows], grad[rows], hess[rows], None, P)
+            hs = scatter_hist_fm(binned_fm[:, rows], pair_row[rows], grad[rows], hess[rows], None, P)
             hp = hist[:, sp]
             ho = hp - hs
             s4 = sil.reshape(1, P, 1, 1)

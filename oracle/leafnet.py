@@ -26,10 +26,13 @@ f32 = np.float32
 
 def column_stats(X: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """Column mean and unbiased std (float64 accumulation, float32 result)."""
-    X64 = X.astype(np.float64)
-    mu = X64.mean(axis=0)
-    n = X.shape[0]
-    var = ((X64 - mu) ** 2).sum(axis=0) / max(n - 1, 1)
+    n, F = X.shape
+    mu = np.empty(F, np.float64)
+    var = np.empty(F, np.float64)
+    for f0 in range(0, F, 16):                # column blocks bound the float64 copies
+        X64 = X[:, f0:f0 + 16].astype(np.float64)
+        mu[f0:f0 + 16] = X64.mean(axis=0)
+        var[f0:f0 + 16] = ((X64 - mu[f0:f0 + 16]) ** 2).sum(axis=0) / max(n - 1, 1)
     return mu.astype(np.float32), np.sqrt(var).astype(np.float32)
 
 

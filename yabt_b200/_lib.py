@@ -85,6 +85,7 @@ SIGNATURES = [
     ("yabt_grow_tree_bestfirst", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
     ("yabt_grower_set_bestfirst_f64", c_int, [c_vp, c_int]),
     ("yabt_grower_set_root_count_cache", c_int, [c_vp, c_int]),
+    ("yabt_grower_root_counts", c_int, [c_vp, c_vp, c_vp]),
     ("yabt_mt_workspace_bytes", c_ll, [c_vp, c_int]),
     ("yabt_grow_tree_multitask", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_int, c_vp, c_vp, c_ll, c_vp, c_vp]),
     ("yabt_mt_update", c_int, [c_vp, c_vp, c_int, c_ll, c_vp, c_vp, c_vp, c_vp]),

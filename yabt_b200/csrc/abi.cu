@@ -42,6 +42,7 @@ cudaError_t launch_mt_commit(const GrowParams&, const GrowBufs&, const MtBufs&, 
 cudaError_t launch_mt_values(const GrowParams&, const GrowBufs&, const MtBufs&, cudaStream_t);
 cudaError_t launch_mt_update(const int*, const float*, int, long long, float*, const float*, float*, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
+cudaError_t launch_unpack_counts(const GrowParams&, const GrowBufs&, long long*, cudaStream_t);
 
 // ---------------------------------------------------------------- pack kernel
 __global__ void k_pack_bins(const uint8_t* __restrict__ plain, long long n, int F,
@@ -653,6 +654,16 @@ int yabt_grower_set_root_count_cache(yabt_grower* g, int on) {
   if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
   g->rc_mode = on ? 1 : 0;
   g->rc_valid = 0;
+  return YABT_OK;
+}
+
+int yabt_grower_root_counts(yabt_grower* g, int64_t* out, void* stream) {
+  if (!g || !g->bound || !out) { set_error("yabt_grower_root_counts: needs a bound grower and an output"); return YABT_ERR_ARG; }
+  if (!g->rc_mode || !g->rc_valid) {
+    set_error("yabt_grower_root_counts: no root counts recorded (cache off, or no root histogram over all rows yet)");
+    return YABT_ERR_ARG;
+  }
+  CUDA_TRY(launch_unpack_counts(g->p, g->b, reinterpret_cast<long long*>(out), (cudaStream_t)stream));
   return YABT_OK;
 }
 

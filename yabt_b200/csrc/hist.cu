@@ -509,6 +509,23 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
   return e;
 }
 
+// root_cnt [F][128] (bins 2k, 2k + 1 in the low, high 32 bits) -> out [F][256]
+__global__ void k_unpack_counts(const long long* __restrict__ packed, long long F, long long* __restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < F * (YABT_NB / 2);
+       i += (long long)gridDim.x * blockDim.x) {
+    const unsigned long long w = (unsigned long long)packed[i];
+    out[2 * i] = (long long)(w & 0xffffffffull);
+    out[2 * i + 1] = (long long)(w >> 32);
+  }
+}
+
+cudaError_t launch_unpack_counts(const GrowParams& p, const GrowBufs& b, long long* out, cudaStream_t s) {
+  const long long words = (long long)p.F * (YABT_NB / 2);
+  k_unpack_counts<<<(unsigned)std::min<long long>((words + 255) / 256, 4096), 256, 0, s>>>(b.root_cnt, p.F, out);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 cudaError_t set_hist_smem_attrs() {
   cudaError_t e = cudaFuncSetAttribute(k_hist<2, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        HistPipe<2, 3>::SMEM);

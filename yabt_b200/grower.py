@@ -154,6 +154,14 @@ class Grower:
         _lib.check(self.lib.yabt_grower_acc_read(self.h, buf), "yabt_grower_acc_read")
         return int(buf[0]), int(buf[1]), int(buf[2])
 
+    def root_counts(self) -> torch.Tensor:
+        """(F, 256) int64 per-bin row counts of this grower's rows, recorded by
+        the last root histogram over all rows (the root-count cache must be on)."""
+        out = torch.empty(self.F, 256, dtype=torch.int64, device=self.device)
+        _lib.check(self.lib.yabt_grower_root_counts(self.h, out.data_ptr(), _lib.stream_ptr()),
+                   "yabt_grower_root_counts")
+        return out
+
     def hist_rows(self) -> list[int]:
         buf = (ctypes.c_longlong * 64)()
         _lib.check(self.lib.yabt_grower_hist_rows(self.h, buf, 64), "yabt_grower_hist_rows")
