@@ -287,6 +287,26 @@ def run_multiclass(args):
         "clocks": clocks, "e2e": None, "cpu_baseline": None}))
 
 
+PHASE_TREES = 3      # trees grown after the timed ones with per-phase timing on
+
+
+def phase_summary(phases, trees: int, dist, dev) -> dict:
+    """Device time per tree of each phase of the library's launches, over the
+    phase pass (the trees after the timed region, grown with CUDA events around
+    every launch group; the max over ranks)."""
+    import torch
+    rec = phases.read()
+    phases.stop()
+    names = phases.names()
+    t = torch.tensor([rec.get(n, {}).get("ms", 0.0) for n in names], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    per = {n: round(float(v) / trees, 4) for n, v in zip(names, t.tolist()) if v > 0}
+    return {"ms_per_tree": per, "sum_ms_per_tree": round(sum(per.values()), 4), "trees": trees,
+            "how": "CUDA events around every launch group of the library in trees grown after the timed "
+                   "region (max over ranks); collective = host-issued NCCL all-reduces"}
+
+
 def model_digest(booster, W: int, K: int, dist=None) -> dict:
     """SHA-256 over the timed trees (feature, threshold, left of trees W..W+K-1)
     and the root histogram's per-bin row counts summed over the ranks. Row
@@ -344,7 +364,8 @@ def run_ours(args):
         torch.cuda.empty_cache()
     loss = MSELoss() if loss_name == "mse" else LogLoss()
     W, K = args.warmup, args.steps
-    params = BoostParams(n_estimators=W + K, max_leaves=leaves, max_depth=depth, learning_rate=lr)
+    P = PHASE_TREES
+    params = BoostParams(n_estimators=W + K + P, max_leaves=leaves, max_depth=depth, learning_rate=lr)
     data = DeviceData(X, params.max_bins, dev, comm=comm)
     y_host = y.cpu().numpy()
     del X
@@ -367,17 +388,22 @@ def run_ours(args):
             ev["stop"] = torch.cuda.Event(enable_timing=True)
             ev["stop"].record()
             marks["launches1"] = int(lib.yabt_launch_count())
+            marks["acc"] = grower.acc_read()          # rows histogrammed by the timed trees (waits for them)
+            if P:
+                phases.start()                        # the untimed phase pass: trees W+K .. W+K+P-1
 
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    from yabt_b200 import phases
     booster = Booster(params, loss)
     booster.fit(None, y_host, data=data, tree_callback=cb, comm=comm)
     torch.cuda.synchronize()
+    phase_split = phase_summary(phases, P, dist if world > 1 else None, dev) if P else None
     clocks = sampler.stop((marks["t0"], time.time())) if sampler else None
     ms = ev["start"].elapsed_time(ev["stop"])
     hist_ms = booster.grower_.hist_times()
-    root_rows, child_rows, hist_launches = booster.grower_.acc_read()
+    root_rows, child_rows, hist_launches = marks["acc"]
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -491,6 +517,7 @@ def run_ours(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "model_digest": digest,
+            "phases": phase_split,
         }
         print(json.dumps(line))
     if world > 1:

@@ -38,13 +38,30 @@ long long yabt_launch_count(void);
 
 /* Measurement only (no reference counterpart): the shared-memory reduction
  * ceiling of the histogram kernel. Issues k_hist's u32 reductions (limbs = 3:
- * unit-hessian path, two 32-feature subs per lane; 5: general path) with its
- * layout and grid and pseudo-random bins, twice (warm-up, then timed);
- * limbs = 1 or 2 issue the packed 64-bit form instead (one u64 reduction per
- * (row, feature) carrying value and count, two subs; or two u64, one sub);
- * *ms = the timed launch, *updates = its (row, feature) updates. sink: 8 bytes
- * of device memory the result is folded into. Synchronises the stream.     */
+ * unit-hessian path, two 32-feature subs per lane; 5: general path; 2 and 4:
+ * the same at a root whose counts come from the fit's cache) with its layout
+ * and grid and pseudo-random bins, twice (warm-up, then timed); *ms = the
+ * timed launch, *updates = its (row, feature) updates. sink: 8 bytes of
+ * device memory the result is folded into. Synchronises the stream.       */
 int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates);
+
+/* Per-phase device timing (no reference counterpart; the reference's loop only
+ * prints progress, yabt/boosting.py:329-342). Every launch group of the
+ * library sits in a named phase (yabt_phase_name: begin, hist, reduce,
+ * exchange, scan, finalize, partition, plan, finish, leafnet, interaction,
+ * update, binning, collective, other), which always opens an NVTX range.
+ * yabt_phase_timing(max) > 0 creates (or reuses) a pool of max event pairs
+ * on the current device, clears it and records every phase range launched on
+ * that device until the pool is full; 0 stops recording. yabt_phase_read
+ * sums the recorded ranges per phase (ms[p], counts[p]; nphases >=
+ * yabt_phase_count()), waiting for their events. yabt_phase_push/pop let
+ * host code time its own stream work (collectives) as a phase.            */
+int yabt_phase_count(void);
+int yabt_phase_name(int phase, char* buf, int len);
+int yabt_phase_timing(int max_ranges);
+int yabt_phase_read(double* ms, long long* counts, int nphases);
+int yabt_phase_push(int phase, void* stream);
+int yabt_phase_pop(void);
 
 /* ------------------------------------------------------------------ bin matrix
  * The tiled bin-matrix layout: features in column tiles (64-wide tiles, then

@@ -12,9 +12,10 @@ CUDA booster and the CPU oracle booster on the same matrix and requires:
 * every compared tree's features, thresholds and children bit-exact, and the
   leaf of every training row (``Tree.apply`` on the imputed matrix) equal to
   the oracle's;
-* leaf values within 1e-5 relative to the gradient magnitudes summed into
-  them (the north-star bound on histogram sums: the oracle adds float32 row by
-  row, the device sums exactly) and predictions within 1e-4 relative.
+* leaf values within 1e-5 relative to the gradient magnitudes summed along
+  their histograms' path from the root (the north-star bound on histogram
+  sums: the oracle adds float32 row by row and subtracts float32 histograms,
+  the device sums exactly) and predictions within 1e-4 relative.
 """
 
 import os
@@ -58,17 +59,33 @@ def _check_root_counts(bins, gb):
     np.testing.assert_array_equal(got, want)
 
 
-def _value_tolerance(rec, nodes, lr, lam=1.0):
-    """Per-node bound on a leaf value's difference: 1e-5 relative to the
-    magnitudes summed (sum |g| over the leaf's rows, the north-star bound on
-    gradient sums), through v = -lr G / (H + lambda), plus 1e-5 of the value.
-    The oracle adds gradients in float32 row by row, the device sums them
-    exactly; where a leaf's gradients cancel (log-loss: p - y of both signs)
-    the float32 sum's error is large against G itself but not against sum |g|."""
+def _value_tolerance(rec, tree, lr, lam=1.0):
+    """Per-node bound on a leaf value's difference from the oracle's.
+
+    The oracle restates the reference's arithmetic: float32 histograms added
+    row by row, and every larger child's histogram the float32 difference
+    parent - smaller child, so a node's bin sums carry the rounding of every
+    histogram on its path from the root. The device sums exactly and rounds
+    once. The bound is the north-star tolerance for histogram sums, 1e-5
+    relative to the magnitudes summed, taken along that path (sum over the
+    node's ancestors a and itself of sum_{rows in a} |g|), carried through
+    v = -lr G / (H + lambda)."""
+    nodes = tree.value.size
     leaf = rec["leaf"]
-    gabs = np.bincount(leaf, weights=np.abs(rec["g"].astype(np.float64)), minlength=nodes)
+    s = np.bincount(leaf, weights=np.abs(rec["g"].astype(np.float64)), minlength=nodes)
     hsum = np.bincount(leaf, weights=rec["h"].astype(np.float64), minlength=nodes)
-    return 1e-5 * lr * gabs / (hsum + lam) + 1e-6
+    parent = np.full(nodes, -1, np.int64)
+    inner = np.nonzero(tree.feature >= 0)[0]
+    parent[tree.left[inner]] = inner
+    parent[tree.right[inner]] = inner
+    for v in range(nodes - 1, 0, -1):          # children are created after their parent
+        if parent[v] >= 0:
+            s[parent[v]] += s[v]
+    path = s.copy()
+    for v in range(1, nodes):
+        if parent[v] >= 0:
+            path[v] += path[parent[v]]
+    return 1e-5 * lr * path / (hsum + lam) + 1e-6
 
 
 def _check_trees(X, ob, gb, trees):
@@ -80,7 +97,7 @@ def _check_trees(X, ob, gb, trees):
         for k in ("feature", "threshold", "left", "right"):
             np.testing.assert_array_equal(getattr(gt, k).cpu().numpy(), getattr(ot, k), err_msg=f"tree {t} {k}")
         gv = gt.value.cpu().numpy()
-        tol = _value_tolerance(ob.records[t], ot.value.size, lr) + 1e-5 * np.abs(ot.value)
+        tol = _value_tolerance(ob.records[t], ot, lr) + 1e-5 * np.abs(ot.value)
         bad = np.abs(gv.astype(np.float64) - ot.value) > tol
         assert not bad.any(), (f"tree {t} values: nodes {np.nonzero(bad)[0][:8]}, got {gv[bad][:8]}, "
                                f"want {ot.value[bad][:8]}, tolerance {tol[bad][:8]}")

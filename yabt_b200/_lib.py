@@ -66,6 +66,12 @@ SIGNATURES = [
     ("yabt_launch_count", c_ll, []),
     ("yabt_probe_shared_red", c_int, [c_int, c_int, c_vp, c_vp, ctypes.POINTER(ctypes.c_float),
                                       ctypes.POINTER(ctypes.c_longlong)]),
+    ("yabt_phase_count", c_int, []),
+    ("yabt_phase_name", c_int, [c_int, ctypes.c_char_p, c_int]),
+    ("yabt_phase_timing", c_int, [c_int]),
+    ("yabt_phase_read", c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_ll), c_int]),
+    ("yabt_phase_push", c_int, [c_int, c_vp]),
+    ("yabt_phase_pop", c_int, []),
     ("yabt_grower_set_timing", c_int, [c_vp, c_int]),
     ("yabt_grower_hist_times", c_int, [c_vp, ctypes.POINTER(c_float), c_int, ctypes.POINTER(c_int)]),
     ("yabt_grower_hist_rows", c_int, [c_vp, ctypes.POINTER(c_ll), c_int]),

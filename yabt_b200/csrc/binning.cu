@@ -539,6 +539,7 @@ int yabt_bin_fit(const float* Xfm, long long n, int F, const int32_t* sample_idx
   }
   if (ws_bytes < yabt_bin_fit_workspace_bytes(n, F, nq)) { set_error("yabt_bin_fit: workspace too small"); return YABT_ERR_WORKSPACE; }
   cudaStream_t s = (cudaStream_t)stream;
+  PhaseScope ph(PH_BINNING, s);
   const FitWs w = carve_fit(workspace, F);
   // medians: radix select over all rows
   for (int pass = 0; pass < 3; ++pass) {
@@ -623,6 +624,7 @@ int yabt_bin_transform(float* Xfm, long long n, int F, const float* medians, con
   }
   if (n == 0) return YABT_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  PhaseScope ph(PH_BINNING, s);
   long long bytes = 0;
   {
     std::vector<TileInfo> t(tile_count(F) + 1);

@@ -53,6 +53,40 @@ void set_error(const char* fmt, ...);
 // host-side count of kernel launches issued by the library (gpu_launches)
 void count_launches(int k);
 
+// ---------------------------------------------------------------- phases
+// Launch groups by phase (phase.cu): an NVTX range always, CUDA events on the
+// launching stream while phase timing is on (yabt_phase_timing).
+enum Phase : int {
+  PH_BEGIN = 0,    // per-tree set-up: gradient quantisation scale, tree init
+  PH_HIST,         // k_hist (and the build_hist drop-in)
+  PH_REDUCE,       // k_reduce
+  PH_XCHG,         // cross-GPU level-histogram exchange kernel
+  PH_SCAN,         // split-gain scan
+  PH_FINALIZE,     // per-level split choice / best-first pick
+  PH_PARTITION,    // row partition
+  PH_PLAN,         // next level's histogram work items
+  PH_FINISH,       // tree finish, leaf of every row
+  PH_LEAFNET,      // ridge-linear leaf models
+  PH_INTERACT,     // interaction detector
+  PH_UPDATE,       // margin update and next gradients
+  PH_BINNING,      // binning (once per fit)
+  PH_COLLECTIVE,   // host-issued collectives (yabt_phase_push from the host)
+  PH_OTHER,
+  PH_COUNT
+};
+
+class PhaseScope {
+ public:
+  PhaseScope(int phase, cudaStream_t s);
+  ~PhaseScope();
+  PhaseScope(const PhaseScope&) = delete;
+  PhaseScope& operator=(const PhaseScope&) = delete;
+
+ private:
+  int slot_;
+  cudaStream_t s_;
+};
+
 // ---------------------------------------------------------------- layout
 struct TileInfo {
   int f0;        // first feature

@@ -1230,6 +1230,7 @@ k_bf_pick(GrowParams p, GrowBufs b, TreeIO io, int part_gate) {
 }
 
 cudaError_t launch_bf_root_scan(const GrowParams& p, const GrowBufs& b, const TreeIO& io, cudaStream_t s) {
+  PhaseScope ph(PH_SCAN, s);
   const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
   if (!p.general) k_bf_scan<2><<<fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, 1);
   else k_bf_scan<3><<<fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, 1);
@@ -1243,10 +1244,19 @@ cudaError_t launch_bf_root_scan(const GrowParams& p, const GrowBufs& b, const Tr
 cudaError_t launch_bf_pick_partition(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int step, int nsm,
                                      cudaStream_t s) {
   const int gate = step == 1 ? 0 : 2;
-  k_bf_pick<<<1, 1024, 0, s>>>(p, b, io, gate);
+  {
+    PhaseScope ph(PH_FINALIZE, s);
+    k_bf_pick<<<1, 1024, 0, s>>>(p, b, io, gate);
+  }
   const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
-  k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, gate);
-  k_plan<<<1, 1024, 0, s>>>(p, b, gate);
+  {
+    PhaseScope ph(PH_PARTITION, s);
+    k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, gate);
+  }
+  {
+    PhaseScope ph(PH_PLAN, s);
+    k_plan<<<1, 1024, 0, s>>>(p, b, gate);
+  }
   count_launches(3);
   return cudaGetLastError();
 }
@@ -1262,6 +1272,7 @@ cudaError_t launch_bf_split(const GrowParams& p, const GrowBufs& b, const TreeIO
 // quantisation scale shared by both histogram channels)
 cudaError_t launch_absmax_shared(const float* const* arrays, int count, long long n_root, const int* root,
                                  GrowState* st, int nsm, cudaStream_t s) {
+  PhaseScope ph(PH_BEGIN, s);
   cudaError_t e = cudaMemsetAsync(&st->amax_g, 0, 2 * sizeof(unsigned), s);
   if (e != cudaSuccess) return e;
   const int grid = (int)std::min<long long>((n_root + 255) / 256, 8LL * nsm);
@@ -1274,6 +1285,7 @@ cudaError_t launch_absmax_shared(const float* const* arrays, int count, long lon
 
 // Second half: the children's histograms, scans and row ranges.
 cudaError_t launch_bf_scan(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm, cudaStream_t s) {
+  PhaseScope ph(PH_SCAN, s);
   const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
   const int grid = fblocks + std::max(1, std::min<int>(nsm, (int)((p.n + 2047) / 2048)));
   if (!p.general) k_bf_scan<2><<<grid, SCAN_WARPS * 32, 0, s>>>(p, b, io, 0);
@@ -1303,18 +1315,31 @@ cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const Tre
                                int nsm, cudaStream_t s) {
   const int jobs = jobs_bound(d, p.max_pairs);
   const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
-  if (!p.general) k_scan<2><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
-  else k_scan<3><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
-  k_finalize<<<1, 1024, 0, s>>>(p, b, io, d);
+  {
+    PhaseScope ph(PH_SCAN, s);
+    if (!p.general) k_scan<2><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
+    else k_scan<3><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
+  }
+  {
+    PhaseScope ph(PH_FINALIZE, s);
+    k_finalize<<<1, 1024, 0, s>>>(p, b, io, d);
+  }
   const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
-  k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, d);
-  k_plan<<<1, 1024, 0, s>>>(p, b, d);
+  {
+    PhaseScope ph(PH_PARTITION, s);
+    k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, d);
+  }
+  {
+    PhaseScope ph(PH_PLAN, s);
+    k_plan<<<1, 1024, 0, s>>>(p, b, d);
+  }
   count_launches(4);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm,
                               cudaStream_t s) {
+  PhaseScope ph(PH_BEGIN, s);
   cudaError_t e = cudaMemsetAsync(&b.st->amax_g, 0, 2 * sizeof(unsigned), s);
   if (e != cudaSuccess) return e;
 
@@ -1325,6 +1350,7 @@ cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const Tree
 }
 
 cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeIO& io, cudaStream_t s) {
+  PhaseScope ph(PH_BEGIN, s);
   k_tree_init<<<1, 1024, 0, s>>>(p, b, io);
   count_launches(1);
   return cudaGetLastError();
@@ -1332,6 +1358,7 @@ cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeI
 
 cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int* meta,
                                int* leaf_of_row, int nsm, cudaStream_t s) {
+  PhaseScope ph(PH_FINISH, s);
   k_finish<<<1, 1024, 0, s>>>(p, b, meta, io.n_root);
   const int grid = (int)std::min<long long>((io.n_root + 511) / 512, 4LL * nsm);
   k_leaf_assign<<<std::max(grid, 1), 512, 3 * (p.max_leaves + 1) * sizeof(int), s>>>(p, b, leaf_of_row,

@@ -476,29 +476,29 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
     if (e != cudaSuccess) return e;
   }
   if (!p.general && root_counts != 2) {
-    k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d);
+    { PhaseScope ph(PH_HIST, s); k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+                                                      b.st, b.partials, d); }
     if (after_hist) cudaEventRecord(after_hist, s);
-    k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
-        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
+    { PhaseScope ph(PH_REDUCE, s); k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
   } else if (!p.general) {
-    k_hist<2, 2><<<nsm, HistPipe<2, 2>::THREADS, HistPipe<2, 2>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d);
+    { PhaseScope ph(PH_HIST, s); k_hist<2, 2><<<nsm, HistPipe<2, 2>::THREADS, HistPipe<2, 2>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+                                                      b.st, b.partials, d); }
     if (after_hist) cudaEventRecord(after_hist, s);
-    k_reduce<2, 2><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
-        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
+    { PhaseScope ph(PH_REDUCE, s); k_reduce<2, 2><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
   } else if (root_counts != 2) {
-    k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d);
+    { PhaseScope ph(PH_HIST, s); k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+                                                      b.st, b.partials, d); }
     if (after_hist) cudaEventRecord(after_hist, s);
-    k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
-        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
+    { PhaseScope ph(PH_REDUCE, s); k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
   } else {
-    k_hist<1, 4><<<nsm, HistPipe<1, 4>::THREADS, HistPipe<1, 4>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d);
+    { PhaseScope ph(PH_HIST, s); k_hist<1, 4><<<nsm, HistPipe<1, 4>::THREADS, HistPipe<1, 4>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+                                                      b.st, b.partials, d); }
     if (after_hist) cudaEventRecord(after_hist, s);
-    k_reduce<1, 4><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
-        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups);
+    { PhaseScope ph(PH_REDUCE, s); k_reduce<1, 4><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+        b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
   }
   count_launches(2);
   cudaError_t e = cudaGetLastError();

@@ -342,6 +342,7 @@ int yabt_hist_build(const uint8_t* binned, const int64_t* slot, const float* g, 
     return YABT_ERR_WORKSPACE;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PhaseScope ph(PH_HIST, s);
   HpBufs b;
   hp_carve(n, K, F, static_cast<char*>(workspace), &b);
   cudaError_t e = cudaFuncSetAttribute(k_hp_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, HP_SMEM);

@@ -829,6 +829,7 @@ static int leafnet_carve(const yabt_leafnet_args* p, void* workspace, long long 
 static cudaError_t leafnet_launch(const LeafNetArgs& a, int stage, cudaStream_t s) {
   const int nsm = YABT_SMS_HINT;
   const int nblk = (a.n_nodes_cap + 3) / 4;
+  PhaseScope ph(PH_LEAFNET, s);
   switch (stage) {
     case 0: {
       k_ln_select<<<1, 1024, 0, s>>>(a);
@@ -920,6 +921,7 @@ int yabt_update_margin(const yabt_update_args* p, void* stream) {
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_update, 256, smem) != cudaSuccess || occ < 1) occ = 1;
   const int grid = (int)std::min<long long>((p->n + 511) / 512, (long long)YABT_SMS_HINT * occ);
+  PhaseScope ph(PH_UPDATE, (cudaStream_t)stream);
   k_update<<<grid, 256, smem, (cudaStream_t)stream>>>(u, p->max_nodes);
   count_launches(1);
   LCUDA(cudaGetLastError());
@@ -930,6 +932,7 @@ int yabt_grad_init(const float* margin, const float* y, long long n, int loss, f
   if (!margin || !y || !grad || n < 0) { set_error("yabt_grad_init: bad arguments"); return YABT_ERR_ARG; }
   if (n == 0) return YABT_OK;
   const int grid = (int)std::min<long long>((n + 255) / 256, (long long)YABT_SMS_HINT * 8);
+  PhaseScope ph(PH_UPDATE, (cudaStream_t)stream);
   k_grad_init<<<grid, 256, 0, (cudaStream_t)stream>>>(margin, y, n, loss, grad, hess);
   count_launches(1);
   LCUDA(cudaGetLastError());
@@ -970,6 +973,7 @@ int yabt_interaction_update(const int64_t* feature, const int64_t* left, const i
     return YABT_ERR_ARG;
   }
   (void)max_nodes;
+  PhaseScope ph(PH_INTERACT, (cudaStream_t)stream);
   k_ia_update<<<1, 512, 0, (cudaStream_t)stream>>>((const long long*)feature, (const long long*)left,
                                                    (const long long*)right, meta, F, scores, parent_scratch);
   count_launches(1);
@@ -979,6 +983,7 @@ int yabt_interaction_update(const int64_t* feature, const int64_t* left, const i
 
 int yabt_interaction_normalize(const float* scores, int F, float* imat, void* stream) {
   if (!scores || !imat || F <= 0) { set_error("yabt_interaction_normalize: bad arguments"); return YABT_ERR_ARG; }
+  PhaseScope ph(PH_INTERACT, (cudaStream_t)stream);
   k_ia_normalize<<<1, 1024, 0, (cudaStream_t)stream>>>(scores, F, imat);
   count_launches(1);
   LCUDA(cudaGetLastError());

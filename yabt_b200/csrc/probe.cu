@@ -8,12 +8,8 @@
 // the same reductions with the same layout, grid (one 1024-thread block per
 // SM) and pseudo-random bins, and nothing else, so its rate of (row, feature)
 // updates is the ceiling k_hist's own rate is compared with. Every address
-// stays inside the block's histogram; there are no waits.
-//
-// The 64-bit forms measure the packed-limb alternative: one red.shared.add.u64
-// per (row, feature) carrying a biased value and the row count in one word
-// (limbs 1, two subs per lane), or that word plus a second one for the hessian
-// (limbs 2, one sub). Layout [limb][sub][bin][lane] of u64 words.
+// stays inside the block's histogram; there are no waits. Limbs 2 and 4 are
+// the root levels whose counts come from the fit's cache (no count limb).
 #include "../../include/yabt_b200.h"
 #include "common.cuh"
 
@@ -55,38 +51,6 @@ __global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsig
 }
 
 template <int LIMBS, int S>
-__global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red64(int iters, unsigned long long* sink) {
-  extern __shared__ __align__(16) unsigned long long psh64[];
-  constexpr int WORDS = LIMBS * S * YABT_NB * 32;
-  constexpr int LS = S * YABT_NB * 32 * 8;       // bytes between limbs
-  for (int i = threadIdx.x; i < WORDS; i += blockDim.x) psh64[i] = 0ULL;
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const unsigned lb = (unsigned)__cvta_generic_to_shared(psh64) + lane * 8;
-  unsigned seed = blockIdx.x * 977u + threadIdx.x * 131u + 1u;
-  for (int it = 0; it < iters; ++it) {
-#pragma unroll 4
-    for (int r = 0; r < 64; ++r) {
-      seed = seed * 1664525u + 1013904223u;                 // LCG: bins of this lane's features
-      const unsigned long long v = seed >> 1;               // a biased value below 2^31
-#pragma unroll
-      for (int s = 0; s < S; ++s) {
-        const unsigned bin = (seed >> (24 - 8 * s)) & 0xFFu;
-        const unsigned a = lb + (bin << 8) + s * YABT_NB * 32 * 8;
-#pragma unroll
-        for (int l = 0; l < LIMBS; ++l)
-          asm volatile("red.shared.add.u64 [%0], %1;\n" ::"r"(a + l * LS), "l"(l == 0 ? (1ULL << 47) + v : v)
-                       : "memory");
-      }
-    }
-  }
-  __syncthreads();
-  unsigned long long acc = 0;
-  for (int i = threadIdx.x; i < WORDS; i += blockDim.x) acc += psh64[i];
-  atomicAdd(sink, acc);      // keeps the reductions observable
-}
-
-template <int LIMBS, int S>
 int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, long long* updates) {
   constexpr int SMEM = LIMBS * S * YABT_NB * 32 * 4;
   int dev = 0, nsm = 0;
@@ -111,40 +75,14 @@ int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, lo
   return YABT_OK;
 }
 
-template <int LIMBS, int S>
-int run_probe64(int iters, unsigned long long* sink, cudaStream_t s, float* ms, long long* updates) {
-  constexpr int SMEM = LIMBS * S * YABT_NB * 32 * 8;
-  int dev = 0, nsm = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_probe_red64<LIMBS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-  cudaEvent_t a = nullptr, b = nullptr;
-  if (e == cudaSuccess) e = cudaEventCreate(&a);
-  if (e == cudaSuccess) e = cudaEventCreate(&b);
-  if (e == cudaSuccess) {
-    k_probe_red64<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink);      // warm-up
-    cudaEventRecord(a, s);
-    k_probe_red64<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink);
-    cudaEventRecord(b, s);
-    e = cudaEventSynchronize(b);
-  }
-  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, a, b);
-  if (a) cudaEventDestroy(a);
-  if (b) cudaEventDestroy(b);
-  if (e != cudaSuccess) { set_error("yabt_probe_shared_red: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
-  *updates = (long long)nsm * PROBE_THREADS * iters * 64 * S;
-  return YABT_OK;
-}
-
 }  // namespace
 }  // namespace yabt
 
 using namespace yabt;
 
 extern "C" int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates) {
-  if ((limbs < 1 || limbs > 3) && limbs != 5) {
-    set_error("yabt_probe_shared_red: limbs must be 1, 2 (u64), 3 or 5 (u32)");
+  if (limbs < 2 || limbs > 5) {
+    set_error("yabt_probe_shared_red: limbs must be 2 or 3 (two 32-feature subs per lane), 4 or 5 (one sub)");
     return YABT_ERR_ARG;
   }
   if (iters <= 0 || !sink || !ms || !updates) {
@@ -154,9 +92,9 @@ extern "C" int yabt_probe_shared_red(int limbs, int iters, void* sink, void* str
   auto* k = static_cast<unsigned long long*>(sink);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (limbs) {
-    case 1: return run_probe64<1, 2>(iters, k, s, ms, updates);
-    case 2: return run_probe64<2, 1>(iters, k, s, ms, updates);
+    case 2: return run_probe<2, 2>(iters, k, s, ms, updates);
     case 3: return run_probe<3, 2>(iters, k, s, ms, updates);
+    case 4: return run_probe<4, 1>(iters, k, s, ms, updates);
     default: return run_probe<5, 1>(iters, k, s, ms, updates);
   }
 }

@@ -163,6 +163,7 @@ int yabt_group_rows(const int32_t* leaf_of_row, long long n, int num_leaves, voi
     return YABT_ERR_WORKSPACE;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PhaseScope ph(PH_PARTITION, s);
   int *cnt, *total, *err;
   grp_carve(n, num_leaves, static_cast<char*>(workspace), &cnt, &total, &err);
   const int nch = (int)((n + GRP_CHUNK - 1) / GRP_CHUNK);

@@ -179,7 +179,10 @@ int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, i
   int dev = 0, nsm = YABT_SMS_HINT;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   // one block per SM: every block waits on the flags, so all must be resident
-  k_xreduce<<<nsm, 512, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
+  {
+    PhaseScope ph(PH_XCHG, static_cast<cudaStream_t>(stream));
+    k_xreduce<<<nsm, 512, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
+  }
   count_launches(1);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) { set_error("yabt_grow_xreduce: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }

@@ -65,7 +65,12 @@ class ShardComm:
     def _reduce(self, t: torch.Tensor, op) -> torch.Tensor:
         if self.world == 1:
             return t
-        if self.on_device or t.device.type == "cpu":
+        if self.on_device:
+            from .phases import host_phase
+            with host_phase():
+                self.dist.all_reduce(t, op=op, group=self.group)
+            return t
+        if t.device.type == "cpu":
             self.dist.all_reduce(t, op=op, group=self.group)
             return t
         h = t.cpu()
