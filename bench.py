@@ -15,8 +15,9 @@ value   trees/s over all GPUs with the inputs resident in HBM (CUDA events,
 e2e     trees/s through the public estimator API (YABTRegressor.fit) from host
         memory: host->device copy of X and y, binning and K trees per fit.
 impl=reference  the reference's own CPU implementation of the path (its OpenMP
-        C grower yabt/_cgrow/grow.c, built under oracle/_ref, plus the oracle
-        restatement of its leaf models) on a row sample, scaled to the workload.
+        C grower yabt/_cgrow/grow.c and C apply, built under oracle/_ref, with
+        interaction steering, plus the oracle restatement of its leaf models)
+        on all host cores, on a 2,000,000-row sample, scaled to the workload.
 """
 
 from __future__ import annotations
@@ -160,11 +161,17 @@ class ClockSampler:
 
 
 def cpu_reference(cfg: str, steps: int, warmup: int, threads: int, sample_rows: int, X_src=None, y_src=None):
-    """The reference's CPU path (C grower + C apply + leaf models) on a row
-    sample of the workload; returns (trees/s scaled to the full workload,
-    seconds per sample step, sample description)."""
+    """The reference's CPU path on a row sample of the workload: per iteration,
+    gradients, interaction steering (the reference steers for n >= 2000,
+    yabt/boosting.py:339,410-412), its OpenMP C grower, its C apply, the leaf
+    models (numpy restatement of yabt/neural_leaves.py:131-184; the reference's
+    torch code cannot travel to the GPU box) and the margin update. ``warmup``
+    untimed iterations, then the median of ``steps`` timed ones (trees 2..k of
+    the fit when warmup is 1). Returns a dict: trees/s of the full workload
+    (per-row cost x rows), seconds per sample step, ns per row, description."""
     from oracle import cgrow
     from oracle.binning import Binner as OBinner
+    from oracle.boost import InteractionDetector
     n, F, leaves, depth, loss, lr = CONFIGS[cfg]
     if X_src is None:
         rng = np.random.default_rng(0)
@@ -176,14 +183,19 @@ def cpu_reference(cfg: str, steps: int, warmup: int, threads: int, sample_rows: 
     bins_fm = np.ascontiguousarray(b.transform(X).T)
     Xi = b.impute(X)
     margin = np.full(X.shape[0], float(y.mean()), np.float32)
+    det = InteractionDetector(F) if X.shape[0] >= 2000 else None
     times = []
     for s in range(warmup + steps):
-        dt, margin = cgrow.boosting_step_seconds(bins_fm, Xi, y, margin, b.edges_, leaves, depth, lr, threads)
+        dt, margin = cgrow.boosting_step_seconds(bins_fm, Xi, y, margin, b.edges_, leaves, depth, lr, threads,
+                                                 detector=det)
         if s >= warmup:
             times.append(dt)
     per = statistics.median(times)
-    scale = X.shape[0] / n
-    return scale / per, per, f"{X.shape[0]} of {n} rows x {F} features, {leaves} leaves; trees/s scaled by rows"
+    m = X.shape[0]
+    return {"trees_per_s": m / (n * per), "s_per_step": per, "ns_per_row": per / m * 1e9, "rows": m,
+            "threads": threads,
+            "desc": f"{m} of {n} rows x {F} features, {leaves} leaves, interaction steering, {threads} threads, "
+                    f"median of {steps} iterations after {warmup}; trees/s = rows / (n x s per step)"}
 
 
 def run_reference(args):
@@ -203,16 +215,43 @@ def run_reference(args):
     if torch.cuda.is_available():
         Xd, yd = make_data(cfg, sample, F, "cuda", seed=0)
         X, y = Xd.cpu().numpy(), yd.cpu().numpy()
-    tps, per, desc = cpu_reference(cfg, args.steps, args.warmup, threads, sample, X, y)
+    r = cpu_reference(cfg, args.steps, args.warmup, threads, sample, X, y)
+    tps = r["trees_per_s"]
     line = {"impl": "reference", "metric": "trees_per_sec", "value": tps, "unit": "trees/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(cfg, args.gpus),
+            "sample_ms_per_step": 1000.0 * r["s_per_step"], "ns_per_row": r["ns_per_row"],
             "cpu_baseline": {"value": tps, "unit": "trees/s", "cores": threads, "kind": "reference",
-                             "sample": desc},
+                             "sample": r["desc"]},
             "e2e": {"value": tps, "unit": "trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
+
+
+def cpu_baseline_leg(cfg: str, dev) -> dict | None:
+    """The reference's CPU path timed on this host for the JSON line's
+    ``cpu_baseline``: all host cores at two sample sizes (the per-row cost of
+    each shows whether scaling by rows holds), and the reference's default
+    thread cap of 8 (yabt/grow_c.py:283-302) at the smaller one. The value is
+    the larger sample at all cores."""
+    from oracle import cgrow
+    if not cgrow.available():
+        return None
+    n, F = CONFIGS[cfg][:2]
+    cores = os.cpu_count() or 1
+    runs = []
+    for rows, threads in ((500_000, cores), (2_000_000, cores), (500_000, min(8, cores))):
+        rows = min(rows, n)
+        Xs, ys = make_data(cfg, rows, F, dev, seed=0)
+        r = cpu_reference(cfg, 2, 1, threads, rows, Xs.cpu().numpy(), ys.cpu().numpy())
+        del Xs, ys
+        runs.append({k: r[k] for k in ("rows", "threads", "s_per_step", "ns_per_row", "trees_per_s")})
+    main = runs[1]
+    return {"value": main["trees_per_s"], "unit": "trees/s", "cores": main["threads"], "kind": "reference",
+            "sample": f"{main['rows']} of {n} rows, interaction steering, median of 2 iterations after 1; "
+                      "trees/s = rows / (n x s per step)",
+            "os_cpu_count": cores, "omp_num_threads": os.environ.get("OMP_NUM_THREADS"), "runs": runs}
 
 
 def run_multiclass(args):
@@ -470,22 +509,25 @@ def run_ours(args):
             t = torch.tensor([dt], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             dt = float(t.item())
+        stages = dict(getattr(est.booster_, "fit_timings_", {}))
+        if world > 1 and stages:
+            keys = sorted(stages)
+            t = torch.tensor([stages[k] for k in keys], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            stages = dict(zip(keys, t.tolist()))
         e2e = {"value": K / dt, "unit": "trees/s",
                "h2d_bytes_per_step": int(n * (F + 1) * 4 / K),   # X and y of every rank, once per fit
                # fit reads back each tree's meta row (4 int32) and leaf-model flag (int32)
-               "d2h_bytes_per_step": 4 * 4 + 4}
+               "d2h_bytes_per_step": 4 * 4 + 4,
+               "fit_s": dt,
+               # host wall seconds of the fit's stages (max over ranks): host->device copy
+               # with the transpose, bin fit, bin transform, column moments, then trees
+               "stages_s": {k: round(v, 4) for k, v in stages.items()}}
         del Xh, est
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        from oracle import cgrow
-        if cgrow.available():
-            sample = min(n, args.ref_rows)
-            Xs, ys = make_data(cfg, sample, F, dev, seed=0)
-            tps, per, desc = cpu_reference(cfg, 1, 1, os.cpu_count() or 1, sample, Xs.cpu().numpy(),
-                                           ys.cpu().numpy())
-            cpu = {"value": tps, "unit": "trees/s", "cores": os.cpu_count(), "kind": "reference",
-                   "sample": desc}
+        cpu = cpu_baseline_leg(cfg, dev)
 
     if rank == 0:
         line = {
@@ -532,7 +574,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
-    ap.add_argument("--ref-rows", type=int, default=500_000)
+    ap.add_argument("--ref-rows", type=int, default=2_000_000)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--rows", type=int, default=0,

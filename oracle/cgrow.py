@@ -77,12 +77,15 @@ def apply(X: np.ndarray, feature, threshold, left, right, threads: int = 0) -> n
 
 
 def boosting_step_seconds(binned_fm, X, y, margin, edges, max_leaves, max_depth, lr, threads,
-                          leaf_nets: bool = True):
+                          leaf_nets: bool = True, detector=None, col_stats=None):
     """Time one CPU boosting iteration of the reference path on the given rows:
-    squared-loss gradients, the C grower (yabt/grow_c.py:336), the C apply
-    (yabt/grow_c.py:303) and ridge-linear leaf models (oracle restatement of
-    yabt/neural_leaves.py:131-184), then the margin update. Returns
-    (seconds, new_margin)."""
+    squared-loss gradients, the interaction matrix (yabt/boosting.py:339,410-412:
+    steering is on for n >= 2000; ``detector`` is an oracle.boost.InteractionDetector
+    kept across iterations, or None to steer nothing), the C grower
+    (yabt/grow_c.py:336), the C apply (yabt/grow_c.py:303), ridge-linear leaf
+    models (oracle restatement of yabt/neural_leaves.py:131-184), the detector's
+    update with the tree's path pairs (yabt/boosting.py:508-509) and the margin
+    update. Returns (seconds, new_margin)."""
     from .grow import OTree
     from .leafnet import fit_leaf_networks
     from .boost import MSELoss
@@ -94,14 +97,18 @@ def boosting_step_seconds(binned_fm, X, y, margin, edges, max_leaves, max_depth,
     t0 = time.perf_counter()
     g = (margin - y).astype(np.float32)
     h = np.ones_like(g)
+    imat = detector.normalized() if detector is not None else None
     feat, tb, left, right, value, depth = grow(binned_fm, g, h, nbins, max_leaves, max_depth, lr=lr,
-                                               threads=threads)
+                                               threads=threads, imat=imat)
     thr = np.array([edges[f][min(b, len(edges[f]) - 1)] if f >= 0 else 0.0
                     for f, b in zip(feat, tb)], np.float32)
     leaf = apply(X, feat, thr, left, right, threads)
     tree = OTree(feat, thr, left, right, value, int(depth.max()) + 1, np.ones(len(feat), np.float32))
     if leaf_nets:
-        tree = fit_leaf_networks(tree, X, y, margin, MSELoss(), P(), leaf)
+        cm, cs = col_stats if col_stats is not None else (None, None)
+        tree = fit_leaf_networks(tree, X, y, margin, MSELoss(), P(), leaf, cm, cs)
+    if detector is not None:
+        detector.update(tree.path_feature_pairs())
     contrib = tree.value[leaf]
     if tree.leaf_net_feats is not None:
         contrib = contrib + tree.net_contribution(X, leaf)

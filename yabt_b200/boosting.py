@@ -21,6 +21,7 @@ NotImplementedError.
 from __future__ import annotations
 
 import ctypes
+import time
 from dataclasses import dataclass, fields
 
 import numpy as np
@@ -189,7 +190,15 @@ class DeviceData:
         """``comm`` (a ``distributed.ShardComm``): X holds this rank's rows of a
         row-sharded training set; binning and column moments cover every rank."""
         lib = _lib.load()
+        # host wall time of each preparation stage (the stream is drained at
+        # each boundary; these stages run once per fit)
+        stamps = [time.perf_counter()]
+
+        def stage_done():
+            torch.cuda.synchronize(device)
+            stamps.append(time.perf_counter())
         self.Xfm = to_feature_major(X, device)
+        stage_done()
         self.F, self.n = int(self.Xfm.shape[0]), int(self.Xfm.shape[1])
         n, F = self.n, self.F
         self.comm = comm
@@ -197,8 +206,10 @@ class DeviceData:
             self.binner = Binner(max_bins).fit_device(self.Xfm, n)
         else:
             self.binner = Binner(max_bins).fit_device_sharded(self.Xfm, n, comm)
+        stage_done()
         # imputes Xfm in place; the feature-major copy feeds the row partition
         self.bins, _, self.bins_fm = self.binner.transform_device(self.Xfm, n, feature_major=True)
+        stage_done()
         if comm is None:
             self.col_mean = torch.empty(F, dtype=torch.float32, device=device)
             self.col_std = torch.empty(F, dtype=torch.float32, device=device)
@@ -207,6 +218,9 @@ class DeviceData:
         else:
             from .distributed import column_stats
             self.col_mean, self.col_std = column_stats(self.Xfm, n, comm)
+        stage_done()
+        self.timings = {k: stamps[i + 1] - stamps[i] for i, k in
+                        enumerate(("to_device_s", "bin_fit_s", "bin_transform_s", "column_stats_s"))}
         med, edges, ecnt, scales = self.binner._dev
         self.edges = edges                      # [F][255]
         self.edge_off = (torch.arange(F, dtype=torch.int32, device=device) * 255).contiguous()
@@ -276,6 +290,8 @@ class Booster:
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
         self.device_ = str(dev)
+        t_fit = time.perf_counter()
+        own_data = data is None
         if data is None:
             data = DeviceData(X, p.max_bins, dev, comm=comm)
         elif comm is not None and data.comm is None:
@@ -482,6 +498,12 @@ class Booster:
         self._margin_train = margin
         self.interaction_scores_ = scores
         meta = forest.meta[:n_built].cpu()
+        # host wall time of the fit's stages: preparing the matrix (when fit built
+        # it) and everything after it (trees, leaf models, margins)
+        t_end = time.perf_counter()
+        prep = sum(data.timings.values()) if own_data else 0.0
+        self.fit_timings_ = dict(data.timings if own_data else {}, trees_s=t_end - t_fit - prep,
+                                 total_s=t_end - t_fit)
         err = int(meta[:, 2].abs().sum()) if n_built else 0
         if err:
             raise _lib.YabtError(f"device error bits set while growing trees (0x{err:x})")
