@@ -44,6 +44,13 @@ long long yabt_launch_count(void);
  * timed launch, *updates = its (row, feature) updates. sink: 8 bytes of
  * device memory the result is folded into. Synchronises the stream.       */
 int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates);
+/* The same with each lane's reductions of a (row, feature) predicated off
+ * with probability 1 - active/32 (0 <= active <= 32): what a sparse-bin
+ * histogram that skips each feature's default bin issues
+ * (yabt/grow_numba.py:42-87, yabt/_cgrow/grow.c:68-107). *updates still
+ * counts every (row, feature), issued or not.                             */
+int yabt_probe_shared_red_masked(int limbs, int iters, int active, void* sink, void* stream, float* ms,
+                                 long long* updates);
 
 /* Per-phase device timing (no reference counterpart; the reference's loop only
  * prints progress, yabt/boosting.py:329-342). Every launch group of the

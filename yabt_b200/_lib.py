@@ -66,6 +66,8 @@ SIGNATURES = [
     ("yabt_launch_count", c_ll, []),
     ("yabt_probe_shared_red", c_int, [c_int, c_int, c_vp, c_vp, ctypes.POINTER(ctypes.c_float),
                                       ctypes.POINTER(ctypes.c_longlong)]),
+    ("yabt_probe_shared_red_masked", c_int, [c_int, c_int, c_int, c_vp, c_vp, ctypes.POINTER(ctypes.c_float),
+                                             ctypes.POINTER(ctypes.c_longlong)]),
     ("yabt_phase_count", c_int, []),
     ("yabt_phase_name", c_int, [c_int, ctypes.c_char_p, c_int]),
     ("yabt_phase_timing", c_int, [c_int]),

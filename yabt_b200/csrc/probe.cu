@@ -18,8 +18,11 @@ namespace {
 
 constexpr int PROBE_THREADS = 1024;
 
+// active < 32: each lane issues a (row, feature)'s reductions only with
+// probability active/32 (a hash of the row and lane), the rest predicated off,
+// as a sparse-bin histogram skipping the default bin would issue them.
 template <int LIMBS, int S>
-__global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsigned long long* sink) {
+__global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsigned long long* sink, int active) {
   extern __shared__ __align__(16) unsigned psh[];
   constexpr int WORDS = LIMBS * S * YABT_NB * 32;
   constexpr int LS = S * YABT_NB * 32 * 4;       // bytes between limbs
@@ -37,6 +40,7 @@ __global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsig
       for (int s = 0; s < S; ++s) {
         const unsigned bin = (seed >> (24 - 8 * s)) & 0xFFu;
         const unsigned a = lb + (bin << 7) + s * YABT_NB * 32 * 4;
+        if (((seed >> (3 + 5 * s)) & 31u) >= (unsigned)active) continue;
 #pragma unroll
         for (int l = 0; l < LIMBS; ++l)
           asm volatile("red.shared.add.u32 [%0], %1;\n" ::"r"(a + l * LS), "r"(l == LIMBS - 1 ? 1u : v & 0xFFFFu)
@@ -51,7 +55,7 @@ __global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsig
 }
 
 template <int LIMBS, int S>
-int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, long long* updates) {
+int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, long long* updates, int active) {
   constexpr int SMEM = LIMBS * S * YABT_NB * 32 * 4;
   int dev = 0, nsm = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -61,9 +65,9 @@ int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, lo
   if (e == cudaSuccess) e = cudaEventCreate(&a);
   if (e == cudaSuccess) e = cudaEventCreate(&b);
   if (e == cudaSuccess) {
-    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink);        // warm-up
+    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink, active);        // warm-up
     cudaEventRecord(a, s);
-    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink);
+    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink, active);
     cudaEventRecord(b, s);
     e = cudaEventSynchronize(b);
   }
@@ -80,21 +84,30 @@ int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, lo
 
 using namespace yabt;
 
-extern "C" int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates) {
+static int probe(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates, int active) {
   if (limbs < 2 || limbs > 5) {
     set_error("yabt_probe_shared_red: limbs must be 2 or 3 (two 32-feature subs per lane), 4 or 5 (one sub)");
     return YABT_ERR_ARG;
   }
-  if (iters <= 0 || !sink || !ms || !updates) {
-    set_error("yabt_probe_shared_red: iters > 0 and non-null outputs required");
+  if (iters <= 0 || !sink || !ms || !updates || active < 0 || active > 32) {
+    set_error("yabt_probe_shared_red: iters > 0, 0 <= active <= 32 and non-null outputs required");
     return YABT_ERR_ARG;
   }
   auto* k = static_cast<unsigned long long*>(sink);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (limbs) {
-    case 2: return run_probe<2, 2>(iters, k, s, ms, updates);
-    case 3: return run_probe<3, 2>(iters, k, s, ms, updates);
-    case 4: return run_probe<4, 1>(iters, k, s, ms, updates);
-    default: return run_probe<5, 1>(iters, k, s, ms, updates);
+    case 2: return run_probe<2, 2>(iters, k, s, ms, updates, active);
+    case 3: return run_probe<3, 2>(iters, k, s, ms, updates, active);
+    case 4: return run_probe<4, 1>(iters, k, s, ms, updates, active);
+    default: return run_probe<5, 1>(iters, k, s, ms, updates, active);
   }
+}
+
+extern "C" int yabt_probe_shared_red(int limbs, int iters, void* sink, void* stream, float* ms, long long* updates) {
+  return probe(limbs, iters, sink, stream, ms, updates, 32);
+}
+
+extern "C" int yabt_probe_shared_red_masked(int limbs, int iters, int active, void* sink, void* stream, float* ms,
+                                            long long* updates) {
+  return probe(limbs, iters, sink, stream, ms, updates, active);
 }
