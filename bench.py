@@ -311,6 +311,19 @@ def run_multiclass(args):
     except Exception:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
+    # sparse-bin question (30% exact zeros per column): the shared-reduction
+    # ceiling with every lane issuing, and with 30% of the lanes predicated off
+    # as a histogram that skips each feature's default bin would issue them
+    sink = torch.zeros(1, dtype=torch.int64, device=dev)
+    probe = {}
+    for active in (32, 22):
+        rate = 0.0
+        for _ in range(3):
+            pms, pupd = ctypes.c_float(), ctypes.c_longlong()
+            _lib.check(lib.yabt_probe_shared_red_masked(5, 400, active, sink.data_ptr(), _lib.stream_ptr(),
+                                                        ctypes.byref(pms), ctypes.byref(pupd)), "probe")
+            rate = max(rate, pupd.value / (pms.value / 1000.0) / 1e9)
+        probe[f"active_{active}_of_32"] = rate
     print(json.dumps({
         "metric": "trees_per_sec", "value": nc * K / (ms / 1000.0), "unit": "trees/s", "n_gpus": 1,
         "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
@@ -323,7 +336,10 @@ def run_multiclass(args):
                      "traffic": None, "kernel": "k_hist", "launches_timed": launches,
                      "hist_share_of_step": hist_ms / ms,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
-        "clocks": clocks, "e2e": None, "cpu_baseline": None}))
+        "clocks": clocks, "e2e": None, "cpu_baseline": None,
+        "sparse_bin_probe": {"unit": "G (row, feature) updates/s", "limbs": 5, **probe,
+                             "how": "yabt_probe_shared_red_masked: k_hist's reductions alone, all lanes "
+                                    "vs 22 of 32 lanes issuing (30% default-bin entries skipped)"}}))
 
 
 PHASE_TREES = 3      # trees grown after the timed ones with per-phase timing on
