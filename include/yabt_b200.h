@@ -292,6 +292,20 @@ int yabt_xchg_free(void* ptr);
 int yabt_grower_set_small(yabt_grower* g, void* ptr, long long bytes);
 int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
                       void* stream);
+/* Element-wise all-reduce of a small device vector over the same mapped
+ * exchange buffers (the per-tree reductions of a row-sharded fit -- the
+ * quantisation words, the leaf-model sums and envelopes -- that the reference
+ * computes over all rows, yabt/tree.py:473, yabt/neural_leaves.py:147-184):
+ * dst = reduce over ranks of src, count elements of kind 0 int64 sum, 1
+ * float64 sum, 2 int32 max, 3 float32 max; summed in rank order, so every
+ * rank gets the same result. src and dst may alias; count * element size must
+ * fit buf_bytes (each exchange buffer's data bytes). Uses the buffers' data
+ * region (nothing of a level's histograms may be pending there) and `epoch`
+ * like yabt_grow_xreduce (one sequence shared by both). Timeouts set a
+ * persistent error bit (yabt_grow_xerr; also OR-ed into later trees' meta).  */
+int yabt_grow_xallreduce(yabt_grower* g, void* const* bufs, long long buf_bytes, int rank, int nranks,
+                         const void* src, void* dst, long long count, int kind, unsigned epoch, void* stream);
+int yabt_grow_xerr(yabt_grower* g, unsigned* bits);
 void* yabt_grow_small_ptr(yabt_grower* g);
 long long yabt_grow_small_count(const yabt_grower* g, int level);
 /* Per-leaf row ranges of the last tree (device arrays inside the workspace):

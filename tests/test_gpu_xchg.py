@@ -8,6 +8,9 @@ or hanging it.
    usable.
 2. A one-rank exchange (the kernel's own flags only) leaves the level's
    histograms unchanged, so a tree grown with it equals a tree grown without.
+3. The small-vector all-reduce (yabt_grow_xallreduce): identity on one rank
+   for every element kind, a refused oversized vector, and the same bounded
+   wait and persistent error bit when a peer never arrives.
 """
 
 import ctypes
@@ -111,3 +114,61 @@ def test_single_rank_exchange_is_identity():
     finally:
         torch.cuda.synchronize()
         lib.yabt_xchg_free(b0)
+
+
+@pytest.mark.parametrize("kind,dtype", [(0, torch.int64), (1, torch.float64), (2, torch.int32), (3, torch.float32)])
+def test_single_rank_allreduce_is_identity(kind, dtype):
+    """yabt_grow_xallreduce with one rank copies src to dst (separate and aliased)."""
+    from yabt_b200 import _lib
+    gr, a, out = _setup(seed=3)
+    lib = gr.lib
+    s = _lib.stream_ptr()
+    (b0,), nbytes = _xchg_buffers(gr, 1)
+    try:
+        bufs = (ctypes.c_void_p * 1)(b0)
+        src = (torch.arange(1000, device="cuda") * 7 - 3000).to(dtype)
+        dst = torch.zeros_like(src)
+        _lib.check(lib.yabt_grow_xallreduce(gr.h, bufs, nbytes, 0, 1, src.data_ptr(), dst.data_ptr(), src.numel(),
+                                            kind, 1, s), "xallreduce")
+        x = src.clone()
+        _lib.check(lib.yabt_grow_xallreduce(gr.h, bufs, nbytes, 0, 1, x.data_ptr(), x.data_ptr(), x.numel(),
+                                            kind, 2, s), "xallreduce in place")
+        torch.cuda.synchronize()
+        assert torch.equal(dst, src) and torch.equal(x, src)
+        bits = ctypes.c_uint()
+        _lib.check(lib.yabt_grow_xerr(gr.h, ctypes.byref(bits)), "xerr")
+        assert bits.value == 0
+        # a vector larger than the buffers is refused before any launch
+        big = int(nbytes // src.element_size()) + 1
+        assert lib.yabt_grow_xallreduce(gr.h, bufs, nbytes, 0, 1, src.data_ptr(), dst.data_ptr(), big, kind, 3,
+                                        s) != 0
+    finally:
+        torch.cuda.synchronize()
+        lib.yabt_xchg_free(b0)
+
+
+def test_allreduce_wait_times_out_and_reports():
+    """A two-rank all-reduce whose second rank never arrives gives up after its
+    bounded wait and sets the persistent exchange-timeout bit, which the next
+    tree's meta reports too; the context stays usable."""
+    from yabt_b200 import _lib
+    gr, a, out = _setup(seed=4)
+    lib = gr.lib
+    s = _lib.stream_ptr()
+    (b0, b1), nbytes = _xchg_buffers(gr, 2)
+    try:
+        bufs = (ctypes.c_void_p * 2)(b0, b1)
+        t = torch.ones(64, dtype=torch.float64, device="cuda")
+        _lib.check(lib.yabt_grow_xallreduce(gr.h, bufs, nbytes, 0, 2, t.data_ptr(), t.data_ptr(), t.numel(), 1, 1,
+                                            s), "xallreduce")
+        torch.cuda.synchronize()
+        bits = ctypes.c_uint()
+        _lib.check(lib.yabt_grow_xerr(gr.h, ctypes.byref(bits)), "xerr")
+        assert bits.value & XCHG_TIMEOUT_BIT
+        gr.grow(a)
+        torch.cuda.synchronize()
+        assert int(out["meta"][2].item()) & XCHG_TIMEOUT_BIT
+    finally:
+        torch.cuda.synchronize()
+        lib.yabt_xchg_free(b0)
+        lib.yabt_xchg_free(b1)

@@ -119,6 +119,9 @@ SIGNATURES = [
     ("yabt_xchg_free", c_int, [c_vp]),
     ("yabt_grower_set_small", c_int, [c_vp, c_vp, c_ll]),
     ("yabt_grow_xreduce", c_int, [c_vp, ctypes.POINTER(c_vp), c_int, c_int, c_int, ctypes.c_uint, c_vp]),
+    ("yabt_grow_xallreduce", c_int, [c_vp, ctypes.POINTER(c_vp), c_ll, c_int, c_int, c_vp, c_vp, c_ll, c_int,
+                                     ctypes.c_uint, c_vp]),
+    ("yabt_grow_xerr", c_int, [c_vp, ctypes.POINTER(ctypes.c_uint)]),
     ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
     ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
     ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),

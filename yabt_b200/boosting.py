@@ -459,7 +459,7 @@ class Booster:
                                "yabt_leafnet_fit")
                 else:
                     from .distributed import fit_leaf_models
-                    fit_leaf_models(la, ln_ws, comm)
+                    fit_leaf_models(la, ln_ws, comm, grower)
             if scores is not None:
                 _lib.check(lib.yabt_interaction_update(forest.feature[t].data_ptr(), forest.left[t].data_ptr(),
                                                        forest.right[t].data_ptr(), forest.meta[t].data_ptr(),
@@ -492,8 +492,11 @@ class Booster:
                     break
             yield t
         if comm is not None and getattr(grower, "_exchange", None) is not None:
-            grower._exchange.close()
-            grower._exchange = None
+            try:
+                grower._exchange.check()
+            finally:
+                grower._exchange.close()
+                grower._exchange = None
         self._forest = forest
         self._margin_train = margin
         self.interaction_scores_ = scores

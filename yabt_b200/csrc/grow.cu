@@ -675,7 +675,7 @@ k_finish(GrowParams p, GrowBufs b, int* meta, long long n_root) {
   if (threadIdx.x == 0) {
     meta[0] = nn;
     meta[1] = st->depth_max + 1;
-    meta[2] = (int)st->err;
+    meta[2] = (int)(st->err | st->xerr);
     meta[3] = st->level;
     if (nn == 1) {   // single-leaf tree: the root owns every row
       b.leaf_src[0] = SRC_IDENTITY; b.leaf_begin[0] = 0; b.leaf_count[0] = (int)n_root;

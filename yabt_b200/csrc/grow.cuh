@@ -108,6 +108,7 @@ struct GrowState {
   long long acc_root_rows;   // accumulated since the last yabt_grower_acc_reset: root-level rows,
   long long acc_child_rows;  // smaller-child rows of deeper levels,
   long long acc_launches;    // histogram levels that did work
+  unsigned xerr;             // persistent error bits of the per-tree peer all-reduces (not reset per tree)
 };
 
 // Per-call grower parameters (copied by value into kernels).

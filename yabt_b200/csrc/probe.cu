@@ -21,7 +21,7 @@ constexpr int PROBE_THREADS = 1024;
 // active < 32: each lane issues a (row, feature)'s reductions only with
 // probability active/32 (a hash of the row and lane), the rest predicated off,
 // as a sparse-bin histogram skipping the default bin would issue them.
-template <int LIMBS, int S>
+template <int LIMBS, int S, bool MASKED>
 __global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsigned long long* sink, int active) {
   extern __shared__ __align__(16) unsigned psh[];
   constexpr int WORDS = LIMBS * S * YABT_NB * 32;
@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsig
       for (int s = 0; s < S; ++s) {
         const unsigned bin = (seed >> (24 - 8 * s)) & 0xFFu;
         const unsigned a = lb + (bin << 7) + s * YABT_NB * 32 * 4;
-        if (((seed >> (3 + 5 * s)) & 31u) >= (unsigned)active) continue;
+        if (MASKED && ((seed >> (3 + 5 * s)) & 31u) >= (unsigned)active) continue;
 #pragma unroll
         for (int l = 0; l < LIMBS; ++l)
           asm volatile("red.shared.add.u32 [%0], %1;\n" ::"r"(a + l * LS), "r"(l == LIMBS - 1 ? 1u : v & 0xFFFFu)
@@ -54,20 +54,20 @@ __global__ void __launch_bounds__(PROBE_THREADS, 1) k_probe_red(int iters, unsig
   atomicAdd(sink, acc);      // keeps the reductions observable
 }
 
-template <int LIMBS, int S>
+template <int LIMBS, int S, bool MASKED>
 int run_probe(int iters, unsigned long long* sink, cudaStream_t s, float* ms, long long* updates, int active) {
   constexpr int SMEM = LIMBS * S * YABT_NB * 32 * 4;
   int dev = 0, nsm = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_probe_red<LIMBS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_probe_red<LIMBS, S, MASKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   cudaEvent_t a = nullptr, b = nullptr;
   if (e == cudaSuccess) e = cudaEventCreate(&a);
   if (e == cudaSuccess) e = cudaEventCreate(&b);
   if (e == cudaSuccess) {
-    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink, active);        // warm-up
+    k_probe_red<LIMBS, S, MASKED><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink, active);        // warm-up
     cudaEventRecord(a, s);
-    k_probe_red<LIMBS, S><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink, active);
+    k_probe_red<LIMBS, S, MASKED><<<nsm, PROBE_THREADS, SMEM, s>>>(iters, sink, active);
     cudaEventRecord(b, s);
     e = cudaEventSynchronize(b);
   }
@@ -95,11 +95,20 @@ static int probe(int limbs, int iters, void* sink, void* stream, float* ms, long
   }
   auto* k = static_cast<unsigned long long*>(sink);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the unmasked form is a kernel of its own: no per-lane test in its loop
+  if (active >= 32) {
+    switch (limbs) {
+      case 2: return run_probe<2, 2, false>(iters, k, s, ms, updates, 32);
+      case 3: return run_probe<3, 2, false>(iters, k, s, ms, updates, 32);
+      case 4: return run_probe<4, 1, false>(iters, k, s, ms, updates, 32);
+      default: return run_probe<5, 1, false>(iters, k, s, ms, updates, 32);
+    }
+  }
   switch (limbs) {
-    case 2: return run_probe<2, 2>(iters, k, s, ms, updates, active);
-    case 3: return run_probe<3, 2>(iters, k, s, ms, updates, active);
-    case 4: return run_probe<4, 1>(iters, k, s, ms, updates, active);
-    default: return run_probe<5, 1>(iters, k, s, ms, updates, active);
+    case 2: return run_probe<2, 2, true>(iters, k, s, ms, updates, active);
+    case 3: return run_probe<3, 2, true>(iters, k, s, ms, updates, active);
+    case 4: return run_probe<4, 1, true>(iters, k, s, ms, updates, active);
+    default: return run_probe<5, 1, true>(iters, k, s, ms, updates, active);
   }
 }
 

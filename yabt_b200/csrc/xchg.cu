@@ -34,6 +34,7 @@ struct XHeader {                          // at the start of every rank's exchan
   unsigned ready[XR_MAX];                 // epoch when rank q's histograms were written
   unsigned done[XR_MAX];                  // epoch when rank q's slice of this buffer was summed
   unsigned blocks;                        // blocks of this rank's kernel that finished their stores
+  unsigned blocks2;                       // second-phase block count of k_xallreduce
 };
 static_assert(sizeof(XHeader) <= XCHG_HEADER, "exchange header");
 
@@ -118,6 +119,78 @@ __global__ void __launch_bounds__(512) k_xreduce(XArgs a, GrowState* st) {
   if (threadIdx.x == 0 && !wait_all(mine->done, a.nranks, a.epoch)) atomicOr(&st->err, DERR_XCHG_TIMEOUT);
 }
 
+// Small-vector all-reduce over the same mapped buffers (the per-tree
+// statistics a row-sharded fit reduces: quantisation words, leaf-model sums
+// and envelopes). The same two-shot scheme as k_xreduce: each rank copies its
+// vector into its own buffer and flags it; rank r reduces slice r over the
+// ranks in rank order (the same result on every rank) and stores it into
+// every buffer; the done flags complete it; each rank copies the result out.
+// T: element type; MAX: max instead of sum. Timeouts set st->xerr.
+struct XAllArgs {
+  char* buf[XR_MAX];
+  int rank, nranks;
+  unsigned epoch;
+  long long count;                        // elements
+  const void* src;
+  void* dst;
+};
+
+template <typename T, bool MAX>
+__global__ void __launch_bounds__(512) k_xallreduce(XAllArgs a, GrowState* st) {
+  __shared__ int s_ok, s_last;
+  XHeader* mine = reinterpret_cast<XHeader*>(a.buf[a.rank]);
+  T* own = reinterpret_cast<T*>(a.buf[a.rank] + XCHG_HEADER);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (long long i = tid; i < a.count; i += stride) own[i] = static_cast<const T*>(a.src)[i];
+  // every block's copy must land before any rank reads this buffer
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&mine->blocks, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) mine->blocks = 0;   // every block has counted itself
+  if (s_last && threadIdx.x < a.nranks) {
+    __threadfence_system();
+    st_flag(&reinterpret_cast<XHeader*>(a.buf[threadIdx.x])->ready[a.rank], a.epoch);
+  }
+  if (threadIdx.x == 0) s_ok = wait_all(mine->ready, a.nranks, a.epoch) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) {
+    if (threadIdx.x == 0) atomicOr(&st->xerr, DERR_XCHG_TIMEOUT);
+    return;
+  }
+  const long long lo = a.count * a.rank / a.nranks;
+  const long long hi = a.count * (a.rank + 1) / a.nranks;
+  for (long long i = lo + tid; i < hi; i += stride) {
+    T acc = __ldcv(reinterpret_cast<const T*>(a.buf[0] + XCHG_HEADER) + i);
+    for (int q = 1; q < a.nranks; ++q) {              // rank order: the same value everywhere
+      const T v = __ldcv(reinterpret_cast<const T*>(a.buf[q] + XCHG_HEADER) + i);
+      if constexpr (MAX) acc = v > acc ? v : acc;
+      else acc = acc + v;
+    }
+    for (int q = 0; q < a.nranks; ++q) reinterpret_cast<T*>(a.buf[q] + XCHG_HEADER)[i] = acc;
+  }
+  __threadfence_system();
+  __syncthreads();
+  // second phase: the done flags (a separate counter word: blocks was reset above)
+  if (threadIdx.x == 0) s_last = atomicAdd(&mine->blocks2, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) {
+    if (threadIdx.x == 0) mine->blocks2 = 0;
+    if (threadIdx.x < a.nranks) {
+      __threadfence_system();
+      st_flag(&reinterpret_cast<XHeader*>(a.buf[threadIdx.x])->done[a.rank], a.epoch);
+    }
+  }
+  if (threadIdx.x == 0) s_ok = wait_all(mine->done, a.nranks, a.epoch) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) {
+    if (threadIdx.x == 0) atomicOr(&st->xerr, DERR_XCHG_TIMEOUT);
+    return;
+  }
+  for (long long i = tid; i < a.count; i += stride) static_cast<T*>(a.dst)[i] = __ldcv(own + i);
+}
+
 }  // namespace yabt
 
 using namespace yabt;
@@ -186,6 +259,52 @@ int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, i
   count_launches(1);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) { set_error("yabt_grow_xreduce: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int yabt_grow_xallreduce(yabt_grower* g, void* const* bufs, long long buf_bytes, int rank, int nranks,
+                         const void* src, void* dst, long long count, int kind, unsigned epoch, void* stream) {
+  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks || count < 0 ||
+      (count > 0 && (!src || !dst)) || kind < 0 || kind > 3) {
+    set_error("yabt_grow_xallreduce: bad arguments (at most %d ranks, kind 0..3)", XR_MAX);
+    return YABT_ERR_ARG;
+  }
+  const long long esize = kind < 2 ? 8 : 4;
+  if (count * esize > buf_bytes) {
+    set_error("yabt_grow_xallreduce: %lld bytes exceed the exchange buffers' %lld", count * esize, buf_bytes);
+    return YABT_ERR_ARG;
+  }
+  if (count == 0) return YABT_OK;
+  XAllArgs a;
+  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
+  for (int q = 0; q < nranks; ++q)
+    if (!a.buf[q]) { set_error("yabt_grow_xallreduce: missing buffer of rank %d", q); return YABT_ERR_ARG; }
+  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.count = count; a.src = src; a.dst = dst;
+  GrowState* st = grower_state(g);
+  if (!st) { set_error("yabt_grow_xallreduce: grower not bound"); return YABT_ERR_ARG; }
+  // few blocks (all resident: every block waits on the flags)
+  const unsigned grid = (unsigned)std::min<long long>(8, std::max<long long>(1, (count + 4095) / 4096));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    PhaseScope ph(PH_XCHG, s);
+    switch (kind) {
+      case 0: k_xallreduce<long long, false><<<grid, 512, 0, s>>>(a, st); break;
+      case 1: k_xallreduce<double, false><<<grid, 512, 0, s>>>(a, st); break;
+      case 2: k_xallreduce<int, true><<<grid, 512, 0, s>>>(a, st); break;
+      default: k_xallreduce<float, true><<<grid, 512, 0, s>>>(a, st); break;
+    }
+  }
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("yabt_grow_xallreduce: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int yabt_grow_xerr(yabt_grower* g, unsigned* bits) {
+  GrowState* st = grower_state(g);
+  if (!st || !bits) { set_error("yabt_grow_xerr: grower not bound"); return YABT_ERR_ARG; }
+  const cudaError_t e = cudaMemcpy(bits, &st->xerr, sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) { set_error("yabt_grow_xerr: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
   return YABT_OK;
 }
 

@@ -19,6 +19,11 @@ identical decisions and holds an identical model:
   input envelopes);
 * the base score (sum of y).
 
+With the NVLink exchange (one rank per GPU), the per-tree reductions (the
+quantisation words and the leaf-model statistics) run through the same mapped
+buffers as the level histograms (yabt_grow_xallreduce: one small kernel, summed
+in rank order, no host round trip); otherwise through the process group.
+
 Margins, gradients, row partitions and leaf assignments stay rank-local.
 Float64 sums of the leaf-model statistics change order with the rank count,
 so leaf values agree with a single-GPU fit to rounding, not bit for bit.
@@ -234,6 +239,7 @@ class PeerExchange:
             ptrs.append(pq.value)
         self.bufs = (ctypes.c_void_p * comm.world)(*ptrs)
         _lib.check(lib.yabt_grower_set_small(h, self.own + hdr, nbytes), "yabt_grower_set_small")
+        self.nbytes = nbytes
         self.epoch = 0
         comm.dist.barrier(group=comm.group)
 
@@ -241,6 +247,30 @@ class PeerExchange:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         _lib.check(self.lib.yabt_grow_xreduce(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
                                               self.epoch, _lib.stream_ptr()), "yabt_grow_xreduce")
+
+    _KINDS = {(torch.int64, "sum"): 0, (torch.float64, "sum"): 1, (torch.int32, "max"): 2,
+              (torch.float32, "max"): 3}
+
+    def allreduce_(self, t: torch.Tensor, op: str) -> bool:
+        """In-place all-reduce of a small contiguous device tensor through the
+        exchange buffers (yabt_grow_xallreduce: one kernel, rank-ordered, no
+        host round trip). False when the dtype / op or the size does not fit
+        (the caller then uses the process group)."""
+        kind = self._KINDS.get((t.dtype, op))
+        if kind is None or not t.is_contiguous() or t.numel() * t.element_size() > self.nbytes:
+            return False
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        _lib.check(self.lib.yabt_grow_xallreduce(self.grower.h, self.bufs, self.nbytes, self.comm.rank,
+                                                 self.comm.world, t.data_ptr(), t.data_ptr(), t.numel(), kind,
+                                                 self.epoch, _lib.stream_ptr()), "yabt_grow_xallreduce")
+        return True
+
+    def check(self) -> None:
+        """Raises if a per-tree all-reduce timed out (reads one device word)."""
+        bits = ctypes.c_uint()
+        _lib.check(self.lib.yabt_grow_xerr(self.grower.h, ctypes.byref(bits)), "yabt_grow_xerr")
+        if bits.value:
+            raise _lib.YabtError(f"peer all-reduce timed out (device error bits 0x{bits.value:x})")
 
     def close(self) -> None:
         torch.cuda.synchronize()
@@ -252,6 +282,17 @@ class PeerExchange:
         if self.own:
             self.lib.yabt_xchg_free(self.own)
             self.own = None
+
+
+def _reduce_sum(comm: ShardComm, xchg, t: torch.Tensor) -> None:
+    """Sum over the ranks in place: the exchange kernel when it can, else the process group."""
+    if xchg is None or not xchg.allreduce_(t, "sum"):
+        comm.sum_(t)
+
+
+def _reduce_max(comm: ShardComm, xchg, t: torch.Tensor) -> None:
+    if xchg is None or not xchg.allreduce_(t, "max"):
+        comm.max_(t)
 
 
 def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
@@ -273,12 +314,12 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
         grower._level_event = torch.cuda.Event()
     info, ev = grower._level_host, grower._level_event
     state = _view(grower.ws, lib.yabt_grow_level_ptr(h), 4, torch.int32)
-    _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
-    comm.max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
-    _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
     xchg = getattr(grower, "_exchange", None)
     if xchg is None and comm.peer_exchange:
         xchg = grower._exchange = PeerExchange(grower, comm)
+    _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
+    _reduce_max(comm, xchg, _view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
+    _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
     if xchg is not None:
         # the NVLink exchange sizes itself from the device state; the host reads
         # each level's state LOOKAHEAD levels later (the GPU keeps that many
@@ -337,12 +378,12 @@ def grow_tree_bestfirst(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
                               for _ in range(8)]
     ring = grower._level_ring
     state = _view(grower.ws, lib.yabt_grow_level_ptr(h), 4, torch.int32)
-    _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
-    comm.max_(_view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
-    _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
     xchg = getattr(grower, "_exchange", None)
     if xchg is None and comm.peer_exchange:
         xchg = grower._exchange = PeerExchange(grower, comm)
+    _lib.check(lib.yabt_grow_begin(h, ref, s), "yabt_grow_begin")
+    _reduce_max(comm, xchg, _view(grower.ws, lib.yabt_grow_amax_ptr(h), 2, torch.int32))   # non-negative float bits
+    _lib.check(lib.yabt_grow_init(h, ref, s), "yabt_grow_init")
     small = None
     if xchg is None:   # with the exchange the histograms live in its buffer, outside the workspace
         small = _view(grower.ws, lib.yabt_grow_small_ptr(h), int(lib.yabt_grow_small_count(h, 0)), torch.int64)
@@ -371,7 +412,7 @@ def grow_tree_bestfirst(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     _lib.check(lib.yabt_grow_end(h, ref, s), "yabt_grow_end")
 
 
-def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, comm: ShardComm) -> None:
+def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, comm: ShardComm, grower=None) -> None:
     """Leaf models of one tree over the rows of every rank: the three stages
     of yabt_leafnet_stage with the statistics reduced in between."""
     lib = _lib.load()
@@ -388,9 +429,10 @@ def fit_leaf_models(la: _lib.LeafNetArgs, ws: torch.Tensor, comm: ShardComm) -> 
 
     def stage(k):
         _lib.check(lib.yabt_leafnet_stage(ref, k, ws.data_ptr(), ws.numel(), s), "yabt_leafnet_stage")
+    xchg = getattr(grower, "_exchange", None) if grower is not None else None
     stage(0)
-    comm.sum_(stats)
+    _reduce_sum(comm, xchg, stats)
     stage(1)
-    comm.sum_(totals)
-    comm.max_(env)
+    _reduce_sum(comm, xchg, totals)
+    _reduce_max(comm, xchg, env)
     stage(2)
