@@ -316,7 +316,7 @@ def run_multiclass(args):
     # as a histogram that skips each feature's default bin would issue them
     sink = torch.zeros(1, dtype=torch.int64, device=dev)
     probe = {}
-    for active in (31, 22):
+    for active in (32, 31, 22, 8):
         rate = 0.0
         for _ in range(3):
             pms, pupd = ctypes.c_float(), ctypes.c_longlong()
@@ -339,8 +339,8 @@ def run_multiclass(args):
         "clocks": clocks, "e2e": None, "cpu_baseline": None,
         "sparse_bin_probe": {"unit": "G (row, feature) updates/s", "limbs": 5, **probe,
                              "how": "yabt_probe_shared_red_masked: k_hist's reductions alone, all lanes "
-                                    "with the per-lane test (31 of 32 lanes issuing) vs 22 of 32 lanes issuing "
-                                    "(30% default-bin entries skipped)"}}))
+                                    "without a per-lane test (32), with it and 31, 22 (30% default-bin entries "
+                                    "skipped) or 8 of 32 lanes issuing; updates/s count every (row, feature)"}}))
 
 
 PHASE_TREES = 3      # trees grown after the timed ones with per-phase timing on
