@@ -13,7 +13,9 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libyabt_b200.so")
+# YABT_LIB_VARIANT=checked loads the bounds-checked build (python -m yabt_b200.build --bounds-check)
+LIB_PATH = os.path.join(_HERE, "libyabt_b200_checked.so" if os.environ.get("YABT_LIB_VARIANT") == "checked"
+                        else "libyabt_b200.so")
 _LOCK = threading.Lock()
 _LIB = None
 

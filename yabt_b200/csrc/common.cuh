@@ -47,11 +47,53 @@ enum : unsigned {
   DERR_NODE_OVERFLOW = 1u << 5,
   DERR_NONFINITE = 1u << 6,
   DERR_XCHG_TIMEOUT = 1u << 7,    // a cross-GPU exchange gave up waiting for a peer
+  DERR_BOUNDS = 1u << 8,          // bounds-checked build: an index outside its array (access skipped)
 };
+
+// Bounds-checked build (-DYABT_BOUNDS_CHECK, libyabt_b200_checked.so): the
+// index checks below run before the accesses they guard; a failing one sets
+// DERR_BOUNDS in the kernel's error word and the access is skipped. In the
+// ordinary build they compile to nothing.
+#ifdef YABT_BOUNDS_CHECK
+#define YABT_BOUNDS_CHECKED 1
+#else
+#define YABT_BOUNDS_CHECKED 0
+#endif
 
 void set_error(const char* fmt, ...);
 // host-side count of kernel launches issued by the library (gpu_launches)
 void count_launches(int k);
+
+// ---------------------------------------------------------------- dependent launches
+// Programmatic dependent launch (sm_90 and later): a kernel launched with
+// launch_pdl may begin while its predecessor in the stream finishes, hiding
+// the launch latency between the short kernels of a tree level. Such a kernel
+// calls pdl_wait() first, unconditionally, before it reads or writes anything
+// (it returns once the predecessor grid has completed and its memory is
+// visible; without a predecessor launched this way it returns at once).
+// Single-block kernels call pdl_trigger() after it, so their successor's
+// blocks are scheduled while they run. YABT_NO_PDL=1 in the environment
+// launches everything the ordinary way.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // ---------------------------------------------------------------- phases
 // Launch groups by phase (phase.cu): an NVTX range always, CUDA events on the

@@ -43,6 +43,7 @@ __device__ int warp_excl_scan(const int* in, int* out, int n) {
 // ------------------------------------------------------------------ per-tree setup
 __global__ void k_absmax(const float* __restrict__ g, const float* __restrict__ h, long long n,
                          const int* __restrict__ root, GrowState* st) {
+  pdl_wait();
   unsigned mg = 0, mh = 0;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -80,10 +81,12 @@ __device__ __forceinline__ int item_chunk(long long R, int U) {
 }
 
 __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
+  pdl_wait();
+  pdl_trigger();
   GrowState* st = b.st;
   for (int m = threadIdx.x; m < p.maxa; m += blockDim.x) b.node_key[m] = 0ULL;
   if (threadIdx.x == 0) {
-    st->level = 0; st->active = 1; st->M = 1; st->P = 0; st->n_nodes = 1;
+    st->level = 0; st->active = 1; st->M = 1; st->P = 0; st->n_nodes = 1; st->n_rows = p.n;
     st->remaining = p.max_leaves - 1; st->part_level = -1; st->plan_level = -1;
     st->depth_max = 0; st->n_leaves = 0; st->err = 0; st->tile_counter = 0; st->n_tiles = 0;
     quant_scale(st->amax_g, &st->qe_g, &st->gscale, &st->ginv);
@@ -130,6 +133,7 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
 template <int C>
 __global__ void __launch_bounds__(SCAN_WARPS * 32)
 k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
+  pdl_wait();
   GrowState* st = b.st;
   if (st->level != level_gate || !st->active) return;
   const int d = level_gate;
@@ -287,12 +291,19 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
 // partition of this level.
 __global__ void __launch_bounds__(1024)
 k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
+  pdl_wait();
+  pdl_trigger();
   GrowState* st = b.st;
   if (st->level != level_gate || !st->active) return;
   const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
   const int M = st->M;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __shared__ int s_P, s_ntiles, s_remaining, s_nnodes;
+  // per-node gains and tile prefixes staged in shared memory (the rank loop and
+  // the tile search read them many times); larger levels read global memory
+  __shared__ float s_gain[FIN_SMEM_NODES];
+  __shared__ int s_tpre[FIN_SMEM_NODES + 1];
+  const bool staged = M <= FIN_SMEM_NODES;
   // A: per node argmax over features (k_scan left the winner in node_key)
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     const int bf = (int)(0xffffffffu - (unsigned)(b.node_key[m] & 0xffffffffULL));
@@ -300,21 +311,21 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     b.nbest[m] = nb;
     b.split_f[m] = bf;
     b.split_b[m] = nb.bin;
+    if (staged) s_gain[m] = nb.gain;
   }
   __syncthreads();
   // the next level's scan accumulates into node_key again
   for (int m = threadIdx.x; m < p.maxa; m += blockDim.x) b.node_key[m] = 0ULL;
-  __syncthreads();
   const bool loop_ok = d < p.max_depth && st->remaining > 0;
   const int remaining = st->remaining;
   // B: budget rank (parallel) -> split_pair = 1 tentatively
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    const float gm = b.nbest[m].gain;
+    const float gm = staged ? s_gain[m] : b.nbest[m].gain;
     int keep = loop_ok && gm > 0.f;
     if (keep) {
       int rank = 0;
       for (int q = 0; q < M; ++q) {
-        const float gq = b.nbest[q].gain;
+        const float gq = staged ? s_gain[q] : b.nbest[q].gain;
         if (gq > 0.f && (gq > gm || (gq == gm && q < m))) ++rank;
       }
       keep = rank < remaining;
@@ -397,12 +408,13 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     }
   }
   // D: partition tiles over every active node's rows (stopping nodes move to fin)
+  int* tpre = staged ? s_tpre : b.node_tpre;
   for (int m = threadIdx.x; m < M; m += blockDim.x)
-    b.node_tpre[m] = P > 0 ? (b.seg_count[cur][m] + PART_TILE - 1) / PART_TILE : 0;
+    tpre[m] = P > 0 ? (b.seg_count[cur][m] + PART_TILE - 1) / PART_TILE : 0;
   __syncthreads();
   if (warp == 0) {
-    const int nt = warp_excl_scan(b.node_tpre, b.node_tpre, M);
-    if (lane == 0) { b.node_tpre[M] = nt; s_ntiles = nt <= p.max_tiles ? nt : 0; }
+    const int nt = warp_excl_scan(tpre, tpre, M);
+    if (lane == 0) { tpre[M] = nt; s_ntiles = nt <= p.max_tiles ? nt : 0; }
     if (lane == 0 && nt > p.max_tiles) atomicOr(&st->err, DERR_TILE_OVERFLOW);
   }
   __syncthreads();
@@ -411,10 +423,10 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     int lo = 0, hi = M - 1;            // last node with tpre <= e
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (b.node_tpre[mid] <= e) lo = mid; else hi = mid - 1;
+      if (tpre[mid] <= e) lo = mid; else hi = mid - 1;
     }
-    const int m = lo, q = e - b.node_tpre[m];
-    const int k = b.node_tpre[m + 1] - b.node_tpre[m];
+    const int m = lo, q = e - tpre[m];
+    const int k = tpre[m + 1] - tpre[m];
     const int B = b.seg_begin[cur][m], cnt = b.seg_count[cur][m];
     PartTile t;
     t.pos = m; t.begin = B + q * PART_TILE; t.end = min(B + cnt, t.begin + PART_TILE);
@@ -454,6 +466,7 @@ __device__ __forceinline__ unsigned long long lb_word(unsigned epoch, unsigned f
 
 __global__ void __launch_bounds__(PART_THREADS)
 k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
+  pdl_wait();
   GrowState* st = b.st;
   if (st->part_level != level_gate) return;
   const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
@@ -482,6 +495,11 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
       const int idx = T.begin + i * PART_THREADS + t;
       ok[i] = idx < T.end;
       row[i] = ok[i] ? (src ? src[idx] : idx) : 0;
+      if (YABT_BOUNDS_CHECKED && ok[i] && (row[i] < 0 || row[i] >= p.n)) {
+        atomicOr(&st->err, DERR_BOUNDS);
+        ok[i] = false;
+        row[i] = 0;
+      }
     }
     if (pr < 0) {
 #pragma unroll
@@ -593,6 +611,8 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
 // the pair's chunk count and pre_q its exclusive prefix over pairs.
 __global__ void __launch_bounds__(1024)
 k_plan(GrowParams p, GrowBufs b, int level_gate) {
+  pdl_wait();
+  pdl_trigger();
   GrowState* st = b.st;
   if (st->plan_level != level_gate) return;
   const int d = level_gate, nxt = (d + 1) & 1;
@@ -638,6 +658,41 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
   __syncthreads();
   const int chunk = s_chunk;
   if (s_total == 0) return;
+  if (P <= FIN_SMEM_NODES) {
+    // pair tables staged in shared memory, then one thread per item slot: slot i
+    // of pair q, unit u, chunk c is U * pre[q] + u * nch[q] + c
+    __shared__ int s_pre[FIN_SMEM_NODES + 1], s_nch[FIN_SMEM_NODES], s_sb[FIN_SMEM_NODES], s_sc[FIN_SMEM_NODES];
+    for (int q = threadIdx.x; q < P; q += blockDim.x) {
+      const int sp = b.pair_sil[q] ? 2 * q : 2 * q + 1;
+      s_pre[q] = b.job_nitems[q];
+      s_nch[q] = b.node_tpre[q];
+      s_sb[q] = b.seg_begin[nxt][sp];
+      s_sc[q] = b.seg_count[nxt][sp];
+    }
+    if (threadIdx.x == 0) s_pre[P] = s_total / p.U;
+    __syncthreads();
+    for (int e = threadIdx.x; e < P * p.U; e += blockDim.x) {
+      const int q = e / p.U, u = e % p.U;
+      b.job_first[e] = p.U * s_pre[q] + u * s_nch[q];
+      b.job_nitems[e] = s_nch[q];
+    }
+    for (int i = threadIdx.x; i < s_total; i += blockDim.x) {
+      int lo = 0, hi = P - 1;                 // last pair with U * pre <= i
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.U * s_pre[mid] <= i) lo = mid; else hi = mid - 1;
+      }
+      const int q = lo, r = i - p.U * s_pre[q], nch = s_nch[q];
+      const int u = r / nch, c = r - u * nch;
+      HistItem it;
+      it.begin = s_sb[q] + c * chunk;
+      it.count = min(chunk, s_sc[q] - c * chunk);
+      it.unit = u; it.job = q; it.slot = i;
+      it.used = 0; it.pad[0] = it.pad[1] = 0;
+      b.items[i] = it;
+    }
+    return;
+  }
   // job tables (pair-major, unit-minor)
   for (int e = threadIdx.x; e < P * p.U; e += blockDim.x) {
     const int q = e / p.U, u = e % p.U;
@@ -669,6 +724,8 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
 // its leaf with a binary search.
 __global__ void __launch_bounds__(1024)
 k_finish(GrowParams p, GrowBufs b, int* meta, long long n_root) {
+  pdl_wait();
+  pdl_trigger();
   GrowState* st = b.st;
   const int nn = st->n_nodes;
   __shared__ int s_nl;
@@ -706,6 +763,7 @@ k_finish(GrowParams p, GrowBufs b, int* meta, long long n_root) {
 // (SRC_IDENTITY positions are root positions: root[i], or i without a root list).
 __global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_of_row, const int* __restrict__ root,
                               long long n_root) {
+  pdl_wait();
   GrowState* st = b.st;
   const int nl = st->n_leaves;
   extern __shared__ int sm_leaf[];          // [nl] begins, [nl] gids, [nl] srcs
@@ -729,6 +787,10 @@ __global__ void k_leaf_assign(GrowParams p, GrowBufs b, int* __restrict__ leaf_o
     if (src == SRC_IDENTITY) row = root ? root[i] : (int)i;
     else if (src == SRC_FIN) row = b.fin[i];
     else row = b.rows[src == SRC_LIST0 ? 0 : 1][i];
+    if (YABT_BOUNDS_CHECKED && (row < 0 || row >= p.n || sg[lo] < 0 || sg[lo] >= p.maxn)) {
+      atomicOr(&st->err, DERR_BOUNDS);
+      continue;
+    }
     leaf_of_row[row] = sg[lo];
   }
 }
@@ -742,6 +804,11 @@ __global__ void k_apply_all(GrowParams p, GrowBufs b, TreeIO io) {
     long long node = 0;
     for (int depth = 0; depth <= p.levels_max && io.feature[node] >= 0; ++depth) {
       const long long f = io.feature[node];
+      if (YABT_BOUNDS_CHECKED && (f >= p.F || io.left[node] < 0 || io.left[node] >= p.maxn ||
+                                  io.right[node] < 0 || io.right[node] >= p.maxn)) {
+        atomicOr(&b.st->err, DERR_BOUNDS);
+        break;
+      }
       const unsigned bin = io.bins_fm[f * p.n + i];
       node = bin <= (unsigned)b.node_bin[node] ? io.left[node] : io.right[node];
     }
@@ -1315,25 +1382,30 @@ cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const Tre
                                int nsm, cudaStream_t s) {
   const int jobs = jobs_bound(d, p.max_pairs);
   const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  cudaError_t e;
   {
     PhaseScope ph(PH_SCAN, s);
-    if (!p.general) k_scan<2><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
-    else k_scan<3><<<jobs * fblocks, SCAN_WARPS * 32, 0, s>>>(p, b, io, d);
+    e = p.general ? launch_pdl(k_scan<3>, dim3(jobs * fblocks), dim3(SCAN_WARPS * 32), 0, s, p, b, io, d)
+                  : launch_pdl(k_scan<2>, dim3(jobs * fblocks), dim3(SCAN_WARPS * 32), 0, s, p, b, io, d);
   }
+  if (e != cudaSuccess) return e;
   {
     PhaseScope ph(PH_FINALIZE, s);
-    k_finalize<<<1, 1024, 0, s>>>(p, b, io, d);
+    e = launch_pdl(k_finalize, dim3(1), dim3(1024), 0, s, p, b, io, d);
   }
+  if (e != cudaSuccess) return e;
   const int pgrid = std::max(1, std::min(p.max_tiles, 4 * nsm));
   {
     PhaseScope ph(PH_PARTITION, s);
-    k_partition<<<pgrid, PART_THREADS, 0, s>>>(p, b, io, d);
+    e = launch_pdl(k_partition, dim3(pgrid), dim3(PART_THREADS), 0, s, p, b, io, d);
   }
+  if (e != cudaSuccess) return e;
   {
     PhaseScope ph(PH_PLAN, s);
-    k_plan<<<1, 1024, 0, s>>>(p, b, d);
+    e = launch_pdl(k_plan, dim3(1), dim3(1024), 0, s, p, b, d);
   }
   count_launches(4);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -1344,26 +1416,31 @@ cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const Tree
   if (e != cudaSuccess) return e;
 
   const int grid = (int)std::min<long long>((io.n_root + 255) / 256, 8LL * nsm);
-  k_absmax<<<std::max(grid, 1), 256, 0, s>>>(io.g, p.general ? io.h : nullptr, io.n_root, io.root_rows, b.st);
+  e = launch_pdl(k_absmax, dim3(std::max(grid, 1)), dim3(256), 0, s, io.g, (const float*)(p.general ? io.h : nullptr),
+                 (long long)io.n_root, io.root_rows, b.st);
   count_launches(1);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 cudaError_t launch_tree_init(const GrowParams& p, const GrowBufs& b, const TreeIO& io, cudaStream_t s) {
   PhaseScope ph(PH_BEGIN, s);
-  k_tree_init<<<1, 1024, 0, s>>>(p, b, io);
+  const cudaError_t e = launch_pdl(k_tree_init, dim3(1), dim3(1024), 0, s, p, b, io);
   count_launches(1);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 cudaError_t launch_tree_finish(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int* meta,
                                int* leaf_of_row, int nsm, cudaStream_t s) {
   PhaseScope ph(PH_FINISH, s);
-  k_finish<<<1, 1024, 0, s>>>(p, b, meta, io.n_root);
+  cudaError_t e = launch_pdl(k_finish, dim3(1), dim3(1024), 0, s, p, b, meta, (long long)io.n_root);
+  if (e != cudaSuccess) return e;
   const int grid = (int)std::min<long long>((io.n_root + 511) / 512, 4LL * nsm);
-  k_leaf_assign<<<std::max(grid, 1), 512, 3 * (p.max_leaves + 1) * sizeof(int), s>>>(p, b, leaf_of_row,
-                                                                                     io.root_rows, io.n_root);
+  e = launch_pdl(k_leaf_assign, dim3(std::max(grid, 1)), dim3(512), 3 * (p.max_leaves + 1) * sizeof(int), s, p, b,
+                 leaf_of_row, (const int*)io.root_rows, (long long)io.n_root);
   count_launches(2);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

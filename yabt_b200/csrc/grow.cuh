@@ -21,6 +21,7 @@ __host__ __device__ constexpr long long small_job_words(int C, int F) {
   return (long long)(C - 1) * F * YABT_NB + (long long)F * (YABT_NB / 2);
 }
 constexpr int SCAN_WARPS = 8;         // k_scan: one warp per feature
+constexpr int FIN_SMEM_NODES = 2048;  // k_finalize: active nodes whose gains / tile prefixes fit shared memory
 
 // leaf row sources
 enum : int { SRC_FIN = 0, SRC_LIST0 = 1, SRC_LIST1 = 2, SRC_IDENTITY = 3 };
@@ -109,6 +110,7 @@ struct GrowState {
   long long acc_child_rows;  // smaller-child rows of deeper levels,
   long long acc_launches;    // histogram levels that did work
   unsigned xerr;             // persistent error bits of the per-tree peer all-reduces (not reset per tree)
+  long long n_rows;          // rows of the bin matrix (bounds-checked build)
 };
 
 // Per-call grower parameters (copied by value into kernels).

@@ -279,6 +279,7 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
   using Pipe = HistPipe<S, LIMBS>;
   extern __shared__ __align__(16) unsigned sh[];
   __shared__ int s_a, s_e;
+  pdl_wait();
   if (st->level != level_gate || !st->active) return;
   const int nitems = st->n_items;
   const float gs = st->gscale, hs = st->hscale;
@@ -332,6 +333,22 @@ k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
       const int w0 = min(item.count, warp * per), w1 = min(item.count, w0 + per);
       const int* lst = rows ? rows + item.begin : nullptr;
       const int base = rows ? w0 : item.begin + w0;
+      if (YABT_BOUNDS_CHECKED) {
+        // every row of this warp's share must be a row of the matrix
+        bool bad = false;
+        if (lst) {
+          for (int k = lane; k < w1 - w0; k += 32) {
+            const int r = lst[base + k];
+            bad |= r < 0 || r >= st->n_rows;
+          }
+        } else {
+          bad = base < 0 || base + (w1 - w0) > st->n_rows;
+        }
+        if (__any_sync(0xffffffffu, bad)) {
+          if (lane == 0) atomicOr(&st->err, DERR_BOUNDS);
+          continue;
+        }
+      }
       const bool full = ud.width == 64 && (S == 1 || ud.nsub == 2);
       if (full)
         hist_warp<S, LIMBS, 64, true>(lb, ring, vslot, tb, lst, base, w1 - w0, g, h, gs, hs, ud.k0, ok0, ok1, lane);
@@ -363,6 +380,7 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
          const int* __restrict__ job_nitems, const HistItem* __restrict__ items,
          const UnitDesc* __restrict__ units, GrowState* st, long long* __restrict__ out,
          int F, int U, int level_gate, int igroups) {
+  pdl_wait();
   using Cfg = HistCfg<S, LIMBS>;
   constexpr int C = Cfg::HAS_H ? 3 : 2;       // output channels (counts last)
   constexpr int CW = Cfg::HAS_CNT ? C : C - 1; // channels written here (cached counts are copied in)
@@ -475,30 +493,39 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
     const cudaError_t e = cudaMemsetAsync(b.small, 0, (size_t)jobs * small_job_words(p.C, p.F) * 8, s);
     if (e != cudaSuccess) return e;
   }
+  cudaError_t le = cudaSuccess;
   if (!p.general && root_counts != 2) {
-    { PhaseScope ph(PH_HIST, s); k_hist<2, 3><<<nsm, HistPipe<2, 3>::THREADS, HistPipe<2, 3>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+    { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<2, 3>, dim3(nsm), dim3(HistPipe<2, 3>::THREADS), HistPipe<2, 3>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d); }
+    if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
-    { PhaseScope ph(PH_REDUCE, s); k_reduce<2, 3><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+    { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<2, 3>, dim3(jobs * p.U * 2 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
         b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
+    if (le != cudaSuccess) return le;
   } else if (!p.general) {
-    { PhaseScope ph(PH_HIST, s); k_hist<2, 2><<<nsm, HistPipe<2, 2>::THREADS, HistPipe<2, 2>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+    { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<2, 2>, dim3(nsm), dim3(HistPipe<2, 2>::THREADS), HistPipe<2, 2>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d); }
+    if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
-    { PhaseScope ph(PH_REDUCE, s); k_reduce<2, 2><<<jobs * p.U * 2 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+    { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<2, 2>, dim3(jobs * p.U * 2 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
         b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
+    if (le != cudaSuccess) return le;
   } else if (root_counts != 2) {
-    { PhaseScope ph(PH_HIST, s); k_hist<1, 5><<<nsm, HistPipe<1, 5>::THREADS, HistPipe<1, 5>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+    { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<1, 5>, dim3(nsm), dim3(HistPipe<1, 5>::THREADS), HistPipe<1, 5>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d); }
+    if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
-    { PhaseScope ph(PH_REDUCE, s); k_reduce<1, 5><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+    { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<1, 5>, dim3(jobs * p.U * 1 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
         b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
+    if (le != cudaSuccess) return le;
   } else {
-    { PhaseScope ph(PH_HIST, s); k_hist<1, 4><<<nsm, HistPipe<1, 4>::THREADS, HistPipe<1, 4>::SMEM, s>>>(io.bins, rows, io.g, io.h, b.items, b.units,
+    { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<1, 4>, dim3(nsm), dim3(HistPipe<1, 4>::THREADS), HistPipe<1, 4>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
                                                       b.st, b.partials, d); }
+    if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
-    { PhaseScope ph(PH_REDUCE, s); k_reduce<1, 4><<<jobs * p.U * 1 * RED_PARTS * igroups, RED_THREADS, 0, s>>>(
+    { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<1, 4>, dim3(jobs * p.U * 1 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
         b.partials, b.job_first, b.job_nitems, b.items, b.units, b.st, b.small, p.F, p.U, d, igroups); }
+    if (le != cudaSuccess) return le;
   }
   count_launches(2);
   cudaError_t e = cudaGetLastError();

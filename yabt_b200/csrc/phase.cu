@@ -12,6 +12,7 @@
 // on; scopes on other devices are not timed. Timing adds one event record per
 // scope boundary, so measure phases in a pass of their own, not inside a timed
 // region.
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -21,6 +22,14 @@
 #include "../../include/yabt_b200.h"
 
 namespace yabt {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("YABT_NO_PDL");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
+}
 
 static const char* const kPhaseNames[PH_COUNT] = {
     "begin", "hist", "reduce", "exchange", "scan", "finalize", "partition", "plan",
