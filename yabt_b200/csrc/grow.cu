@@ -157,13 +157,26 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
 
   int nchild, pos_small, pos_other = -1;
   const long long* par = nullptr;
-  if (d == 0) { nchild = 1; pos_small = 0; }
-  else {
+  // interaction steering: max over the node's path features p of imat[p][f];
+  // both children of a pair share it: max(parent's, imat[parent's split feature][f])
+  float pm = 0.f;
+  if (d == 0) {
+    nchild = 1; pos_small = 0;
+    if (p.use_imat) pm = b.pathmax[0][f];
+  } else {
     nchild = 2;
     const int sil = b.pair_sil[job];
     pos_small = sil ? 2 * job : 2 * job + 1;
     pos_other = sil ? 2 * job + 1 : 2 * job;
-    par = b.hist[prv] + (size_t)b.pair_pos[job] * HN + (size_t)f * YABT_NB + lane * 8;
+    const int m = b.pair_pos[job];
+    par = b.hist[prv] + (size_t)m * HN + (size_t)f * YABT_NB + lane * 8;
+    if (p.use_imat) {
+      pm = fmaxf(b.pathmax[prv][(size_t)m * p.F + f], io.imat[(size_t)b.split_f[m] * p.F + f]);
+      if (lane == 0) {     // the children's own path max, read by their children's scan
+        b.pathmax[cur][(size_t)(2 * job) * p.F + f] = pm;
+        b.pathmax[cur][(size_t)(2 * job + 1) * p.F + f] = pm;
+      }
+    }
   }
   long long vs[C][8];
 #pragma unroll
@@ -235,7 +248,7 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     const float Cn = __ll2float_rn(lt[C - 1]);
     const float t3 = __fdiv_rn(__fmul_rn(G, G), __fadd_rn(H, lam));
     float boost = 1.f;
-    if (p.use_imat) boost = __fadd_rn(1.f, __fmul_rn(p.ib, b.pathmax[cur][(size_t)pos * p.F + f]));
+    if (p.use_imat) boost = __fadd_rn(1.f, __fmul_rn(p.ib, pm));
     float bsel = -INFINITY, bgain = -INFINITY, bGL = 0.f, bHL = 0.f, bCL = 0.f;
     int bbin = 0;
     long long bcl = 0;
@@ -396,17 +409,7 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     b.seg_begin[nxt][2 * pr] = B; b.seg_count[nxt][2 * pr] = 0;
     b.seg_begin[nxt][2 * pr + 1] = B; b.seg_count[nxt][2 * pr + 1] = cnt;
   }
-  // children path max (interaction steering): max(parent, imat[f, :])
-  if (p.use_imat) {
-    for (int e = threadIdx.x; e < P * p.F; e += blockDim.x) {
-      const int pr = e / p.F, j = e % p.F;
-      const int m = b.pair_pos[pr];
-      const int f = b.split_f[m];
-      const float v = fmaxf(b.pathmax[cur][(size_t)m * p.F + j], io.imat[(size_t)f * p.F + j]);
-      b.pathmax[nxt][(size_t)(2 * pr) * p.F + j] = v;
-      b.pathmax[nxt][(size_t)(2 * pr + 1) * p.F + j] = v;
-    }
-  }
+  // (the children's interaction path max is formed by the next level's scan)
   // D: partition tiles over every active node's rows (stopping nodes move to fin)
   int* tpre = staged ? s_tpre : b.node_tpre;
   for (int m = threadIdx.x; m < M; m += blockDim.x)
