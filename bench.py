@@ -580,6 +580,7 @@ def run_ours(args):
         }
         print(json.dumps(line))
     if world > 1:
+        comm.release_exchange()          # collective: unmap the peers' exchange buffers, free ours
         dist.barrier()
         dist.destroy_process_group()
 

@@ -51,7 +51,7 @@ def _summary(b, Xt):
                 scales=scales.cpu().numpy(), trees=trees, pred=b.predict_margin(Xt))
 
 
-def _worker(rank, world, port, backend, neural, q, subsample=1.0, levelwise="auto"):
+def _worker(rank, world, port, backend, neural, q, subsample=1.0, levelwise="auto", fits=1):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -65,10 +65,17 @@ def _worker(rank, world, port, backend, neural, q, subsample=1.0, levelwise="aut
         X, y = _data()
         off = sum(SPLIT[:rank])
         sl = slice(off, off + SPLIT[rank])
-        b = Booster(_params(neural, subsample, levelwise), MSELoss())
-        b.fit(X[sl], y[sl], comm=ShardComm())
-        torch.cuda.synchronize()
-        q.put((rank, _summary(b, X[:1500])))
+        comm = ShardComm()
+        sums = []
+        for _ in range(fits):          # later fits reuse the group's mapped exchange buffers
+            b = Booster(_params(neural, subsample, levelwise), MSELoss())
+            b.fit(X[sl], y[sl], comm=comm)
+            torch.cuda.synchronize()
+            sums.append(_summary(b, X[:1500]))
+        for other in sums[1:]:
+            np.testing.assert_array_equal(other["pred"], sums[0]["pred"])
+        q.put((rank, sums[0]))
+        comm.release_exchange()
     except Exception as e:          # report instead of hanging the parent
         q.put((rank, repr(e)))
         raise
@@ -76,13 +83,14 @@ def _worker(rank, world, port, backend, neural, q, subsample=1.0, levelwise="aut
         dist.destroy_process_group()
 
 
-def _run_sharded(backend, neural, subsample=1.0, levelwise="auto"):
+def _run_sharded(backend, neural, subsample=1.0, levelwise="auto", fits=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q, subsample, levelwise)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, backend, neural, q, subsample, levelwise, fits))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in range(2))
@@ -145,3 +153,11 @@ def test_two_ranks_nccl(levelwise):
     """One rank per GPU: the level (or best-first step) histograms are summed by
     the NVLink exchange kernel."""
     _compare(_run_sharded("nccl", True, levelwise=levelwise), _single(True, levelwise=levelwise), True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_nccl_two_fits():
+    """Two fits in a row on one process group: the second reuses the mapped
+    exchange buffers (the exchange sequence numbers carry on) and grows the
+    same model as the first."""
+    _compare(_run_sharded("nccl", True, levelwise=True, fits=2), _single(True, levelwise=True), True)

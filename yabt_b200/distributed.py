@@ -92,6 +92,26 @@ class ShardComm:
     def min_(self, t: torch.Tensor) -> torch.Tensor:
         return self._reduce(t, self.dist.ReduceOp.MIN)
 
+    # NVLink exchange buffers (held across fits) ---------------------------
+    def exchange_buffers(self, nbytes: int) -> "ExchangeBuffers":
+        """This group's exchange buffers of at least ``nbytes`` data bytes
+        (collective when they have to be created or grown: every rank asks for
+        the same size at the same point of the fit)."""
+        x = getattr(self, "_xbufs", None)
+        if x is not None and x.nbytes >= nbytes:
+            return x
+        if x is not None:
+            x.release()
+        self._xbufs = ExchangeBuffers(self, nbytes)
+        return self._xbufs
+
+    def release_exchange(self) -> None:
+        """Collective: free the exchange buffers (they are otherwise kept until exit)."""
+        x = getattr(self, "_xbufs", None)
+        if x is not None:
+            x.release()
+            self._xbufs = None
+
     # scalars and gathers -------------------------------------------------
     def int_values(self, v: int) -> list[int]:
         """Every rank's value of an integer, in rank order."""
@@ -205,23 +225,23 @@ def column_stats(Xfm: torch.Tensor, n_local: int, comm: ShardComm) -> tuple[torc
     return mean, std
 
 
-class PeerExchange:
-    """Every rank's level-histogram exchange buffer, mapped into this process
-    (CUDA IPC over NVLink, plain peer loads and stores), bound to a grower as
-    its small-child histogram buffer. ``reduce(level)`` launches
-    yabt_grow_xreduce: no host synchronisation and exactly the level's bytes.
-    ``close()`` must be called on every rank (it synchronises the ranks)."""
+class ExchangeBuffers:
+    """Every rank's exchange buffer, mapped into this process (CUDA IPC over
+    NVLink, plain peer loads and stores). Held by the ShardComm across fits:
+    setting up and tearing down the IPC mappings costs a synchronisation of the
+    ranks and can take longer than a whole fit, so a fit binds its grower to
+    the buffers instead and leaves them mapped (``ShardComm.release_exchange``
+    frees them). ``epoch`` numbers the exchange calls; every rank makes the
+    same calls in the same order, so the sequences agree."""
 
-    def __init__(self, grower, comm: ShardComm):
-        self.lib = lib = grower.lib
-        self.grower, self.comm = grower, comm
-        h = grower.h
-        nbytes = int(lib.yabt_grow_small_count(h, 62)) * 8          # the largest level
+    def __init__(self, comm: "ShardComm", nbytes: int):
+        self.lib = lib = _lib.load()
+        self.comm = comm
         handle = (ctypes.c_char * 64)()
         own = ctypes.c_void_p()
         _lib.check(lib.yabt_xchg_alloc(nbytes, ctypes.byref(own), handle), "yabt_xchg_alloc")
         self.own = own.value
-        hdr = int(lib.yabt_xchg_header_bytes())
+        self.header = int(lib.yabt_xchg_header_bytes())
         dev = torch.device("cuda", torch.cuda.current_device())
         mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(dev)
         parts = [torch.empty_like(mine) for _ in range(comm.world)]
@@ -238,15 +258,47 @@ class PeerExchange:
             self.opened.append(pq.value)
             ptrs.append(pq.value)
         self.bufs = (ctypes.c_void_p * comm.world)(*ptrs)
-        _lib.check(lib.yabt_grower_set_small(h, self.own + hdr, nbytes), "yabt_grower_set_small")
         self.nbytes = nbytes
         self.epoch = 0
         comm.dist.barrier(group=comm.group)
 
-    def reduce(self, level: int) -> None:
+    def next_epoch(self) -> int:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        return self.epoch
+
+    def release(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        torch.cuda.synchronize()
+        self.comm.dist.barrier(group=self.comm.group)     # no rank still reads or writes a peer buffer
+        for p in self.opened:
+            self.lib.yabt_xchg_close(p)
+        self.opened = []
+        self.comm.dist.barrier(group=self.comm.group)
+        if self.own:
+            self.lib.yabt_xchg_free(self.own)
+            self.own = None
+
+
+class PeerExchange:
+    """A grower bound to the ShardComm's exchange buffers (its smaller-child
+    histogram buffer is this rank's exchange buffer). ``reduce(level)``
+    launches yabt_grow_xreduce: no host synchronisation and exactly the level's
+    bytes; ``allreduce_`` the small per-tree reductions. ``close()`` must be
+    called on every rank at the end of the fit; the buffers stay mapped for the
+    next fit."""
+
+    def __init__(self, grower, comm: ShardComm):
+        self.lib = lib = grower.lib
+        self.grower, self.comm = grower, comm
+        need = int(lib.yabt_grow_small_count(grower.h, 62)) * 8          # the largest level
+        self.x = comm.exchange_buffers(need)
+        _lib.check(lib.yabt_grower_set_small(grower.h, self.x.own + self.x.header, self.x.nbytes),
+                   "yabt_grower_set_small")
+        self.bufs, self.nbytes = self.x.bufs, self.x.nbytes
+
+    def reduce(self, level: int) -> None:
         _lib.check(self.lib.yabt_grow_xreduce(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
-                                              self.epoch, _lib.stream_ptr()), "yabt_grow_xreduce")
+                                              self.x.next_epoch(), _lib.stream_ptr()), "yabt_grow_xreduce")
 
     _KINDS = {(torch.int64, "sum"): 0, (torch.float64, "sum"): 1, (torch.int32, "max"): 2,
               (torch.float32, "max"): 3}
@@ -259,10 +311,9 @@ class PeerExchange:
         kind = self._KINDS.get((t.dtype, op))
         if kind is None or not t.is_contiguous() or t.numel() * t.element_size() > self.nbytes:
             return False
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         _lib.check(self.lib.yabt_grow_xallreduce(self.grower.h, self.bufs, self.nbytes, self.comm.rank,
                                                  self.comm.world, t.data_ptr(), t.data_ptr(), t.numel(), kind,
-                                                 self.epoch, _lib.stream_ptr()), "yabt_grow_xallreduce")
+                                                 self.x.next_epoch(), _lib.stream_ptr()), "yabt_grow_xallreduce")
         return True
 
     def check(self) -> None:
@@ -273,15 +324,8 @@ class PeerExchange:
             raise _lib.YabtError(f"peer all-reduce timed out (device error bits 0x{bits.value:x})")
 
     def close(self) -> None:
-        torch.cuda.synchronize()
-        self.comm.dist.barrier(group=self.comm.group)     # no rank still reads or writes a peer buffer
-        for p in self.opened:
-            self.lib.yabt_xchg_close(p)
-        self.opened = []
-        self.comm.dist.barrier(group=self.comm.group)
-        if self.own:
-            self.lib.yabt_xchg_free(self.own)
-            self.own = None
+        """End of the fit: the grower lets go of the buffers (which stay mapped)."""
+        self.grower = None
 
 
 def _reduce_sum(comm: ShardComm, xchg, t: torch.Tensor) -> None:
