@@ -7,8 +7,9 @@ cudaMalloc (which may synchronise the device and can fail under memory
 pressure) is not allowed. It keeps its scratch in a fixed array inside the
 library instead of a caller workspace. This test calls it through the C ABI
 twice in a row, on different data, and checks every output bit for bit
-against ``yabt_bin_fit`` with a caller-allocated workspace; it also checks
-that a fit too large for the fixed array is refused with a clear error.
+against ``yabt_bin_fit`` with a caller-allocated workspace, checks that the
+call leaves torch's allocated bytes and the device's free memory unchanged,
+and that a fit too large for the fixed array is refused with a clear error.
 
 The file is named so that pytest collects it last.
 """
@@ -65,15 +66,28 @@ def _data(seed, n, F):
     return X
 
 
+def _free_device_bytes() -> int:
+    free, _ = torch.cuda.mem_get_info()
+    return int(free)
+
+
 def test_static_bin_fit_matches_workspace_fit_twice():
     from yabt_b200 import _lib
     for seed, n, F in ((0, 6000, 12), (1, 3001, 7)):      # two calls in a row, different shapes
         X = _data(seed, n, F)
         Xfm = _xfm(X)
         ref = _fit_workspace(Xfm, n, F, n)
-        rc, got = _fit_static(Xfm, n, F, n)
+        outs = _outs(F)                                   # outputs allocated before the measured call
+        torch.cuda.synchronize()
+        torch_before, free_before = torch.cuda.memory_allocated(), _free_device_bytes()
+        rc = _lib.load().yabt_bin_fit_static(Xfm.data_ptr(), n, F, None, n, 256, *[t.data_ptr() for t in outs],
+                                             _lib.stream_ptr())
         assert rc == 0, _lib.last_error()
         torch.cuda.synchronize()
+        # the call allocates nothing: neither torch's allocator nor the device's free memory moves
+        assert torch.cuda.memory_allocated() == torch_before
+        assert _free_device_bytes() == free_before
+        got = outs
         for a, b, name in zip(got, ref, ("medians", "edges", "edge_cnt", "scales")):
             if name == "edges":
                 c = ref[2].cpu().numpy()

@@ -660,16 +660,27 @@ constexpr int MAX_DEVICES = 64;
 static std::mutex g_static_mu;
 static void* g_static_ptr[MAX_DEVICES] = {};
 
-// Device address of the scratch array on the current device, looked up once per
-// device (host code must not pass the symbol itself: in host code its name is
-// only a stand-in, not a device address).
-static int bin_fit_scratch_ptr(void** out) {
+// Device address of the scratch array on the current device (host code must
+// not pass the symbol itself: in host code its name is only a stand-in, not a
+// device address). Outside stream capture the address is looked up on every
+// call (a cheap host query), so it follows a device reset or a different
+// context; during capture, where the lookup might not be allowed, the last
+// address seen on this device is used -- so the first call on a device must
+// come before any capture.
+static int bin_fit_scratch_ptr(void** out, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) { set_error("yabt_bin_fit_static: cudaGetDevice: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
   if (dev < 0 || dev >= MAX_DEVICES) { set_error("yabt_bin_fit_static: device %d out of range", dev); return YABT_ERR_ARG; }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) { set_error("yabt_bin_fit_static: cudaStreamIsCapturing: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
   std::lock_guard<std::mutex> lk(g_static_mu);
-  if (!g_static_ptr[dev]) {
+  if (cap == cudaStreamCaptureStatusNone || !g_static_ptr[dev]) {
+    if (cap != cudaStreamCaptureStatusNone) {
+      set_error("yabt_bin_fit_static: the first call on a device must come before stream capture");
+      return YABT_ERR_ARG;
+    }
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_bin_fit_scratch);
     if (e != cudaSuccess || !p) {
@@ -691,7 +702,18 @@ long long yabt_bin_fit_static_capacity(void) { return BIN_FIT_STATIC_BYTES; }
 int yabt_bin_fit_static(const float* Xfm, long long n, int F, const int32_t* sample_idx, long long nq,
                         int max_bins, float* medians, float* edges, int32_t* edge_cnt, float* scales,
                         void* stream) {
-  if (!Xfm || n <= 0 || F <= 0 || nq <= 0) { set_error("yabt_bin_fit_static: bad arguments"); return YABT_ERR_ARG; }
+  // every argument is checked before any size arithmetic or device query
+  if (!Xfm || n <= 0 || F <= 0 || nq <= 0 || max_bins < 2 || max_bins > 256 || !medians || !edges || !edge_cnt ||
+      !scales) {
+    set_error("yabt_bin_fit_static: bad arguments");
+    return YABT_ERR_ARG;
+  }
+  // the sorted sample alone takes 4 F nq bytes: anything larger cannot fit
+  if (nq > BIN_FIT_STATIC_BYTES / (4LL * F) || n > (1LL << 40)) {
+    set_error("yabt_bin_fit_static: %lld sample rows x %d features exceed the static buffer of %lld bytes; "
+              "use yabt_bin_fit with a caller workspace", nq, F, BIN_FIT_STATIC_BYTES);
+    return YABT_ERR_UNSUPPORTED;
+  }
   const long long need = yabt_bin_fit_workspace_bytes(n, F, nq);
   if (need > BIN_FIT_STATIC_BYTES) {
     set_error("yabt_bin_fit_static: this fit needs %lld bytes of scratch but the static buffer holds %lld "
@@ -700,7 +722,7 @@ int yabt_bin_fit_static(const float* Xfm, long long n, int F, const int32_t* sam
     return YABT_ERR_UNSUPPORTED;
   }
   void* ws = nullptr;
-  int rc = bin_fit_scratch_ptr(&ws);
+  int rc = bin_fit_scratch_ptr(&ws, (cudaStream_t)stream);
   if (rc) return rc;
   // yabt_bin_fit clears every scratch region it accumulates into before use
   // (NaN counts, digit histograms) and fully writes the rest, so the contents
