@@ -130,8 +130,11 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
 
 // ------------------------------------------------------------------ split scan
 // grid: jobs x ceil(F / SCAN_WARPS); one warp per feature, lane L owns bins 8L..8L+7.
+// The unit-hessian form is held to 3 resident blocks per SM (at most 80
+// registers; 89 otherwise, 2 blocks): the kernel waits on its histogram loads,
+// and the extra warps cut its time per tree by 8-9% (C4, 10M and 1.25M rows).
 template <int C>
-__global__ void __launch_bounds__(SCAN_WARPS * 32)
+__global__ void __launch_bounds__(SCAN_WARPS * 32, C == 2 ? 3 : 2)
 k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   pdl_wait();
   GrowState* st = b.st;
