@@ -491,13 +491,23 @@ def run_ours(args):
     # 3 u32 reductions per (row, feature) on the unit-hessian path, 5 otherwise)
     limbs = 3 if loss_name == "mse" else 5
     sink = torch.zeros(1, dtype=torch.int64, device=dev)
-    pms, pupd = ctypes.c_float(), ctypes.c_longlong()
-    red_peak = 0.0
-    for _ in range(3):
-        _lib.check(lib.yabt_probe_shared_red(limbs, 400, sink.data_ptr(), _lib.stream_ptr(), ctypes.byref(pms),
-                                             ctypes.byref(pupd)), "yabt_probe_shared_red")
-        red_peak = max(red_peak, pupd.value / (pms.value / 1000.0) / 1e9)
+
+    def red_rate(nl: int) -> float:
+        pms, pupd = ctypes.c_float(), ctypes.c_longlong()
+        best = 0.0
+        for _ in range(3):
+            _lib.check(lib.yabt_probe_shared_red(nl, 400, sink.data_ptr(), _lib.stream_ptr(), ctypes.byref(pms),
+                                                 ctypes.byref(pupd)), "yabt_probe_shared_red")
+            best = max(best, pupd.value / (pms.value / 1000.0) / 1e9)
+        return best
+    red_peak = red_rate(limbs)
+    red_peak_root = red_rate(limbs - 1)      # the cached-count root issues one reduction fewer
     red_achieved = (root_rows + child_rows) * F / (hist_total_ms / 1000.0) / 1e9 if hist_total_ms > 0 else 0.0
+    # the exact-sum scheme's own ceiling: the timed trees' (row, feature) updates at
+    # the measured reduction rates (the root's counts cached after the first tree),
+    # i.e. the HBM throughput k_hist would reach with nothing but its reductions
+    floor_s = (root_rows * F / (red_peak_root * 1e9) + child_rows * F / (red_peak * 1e9)) if red_peak > 0 else 0.0
+    scheme_gbs = alg_bytes / floor_s / 1e9 if floor_s > 0 else float("nan")
     rows_hist = torch.tensor([float(root_rows + child_rows)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(rows_hist)
@@ -571,7 +581,13 @@ def run_ours(args):
                                 # the root level of every tree after the first reuses the fit's
                                 # per-bin row counts and issues one reduction fewer per update
                                 "root_reductions_per_update_cached_counts": limbs - 1,
-                                "peak_source": "yabt_probe_shared_red, measured in this run"},
+                                "peak_root": red_peak_root,
+                                "peak_source": "yabt_probe_shared_red, measured in this run",
+                                # HBM throughput at that ceiling (algorithmic bytes / time of the
+                                # reductions alone) and k_hist's share of it
+                                "scheme_ceiling_gbs": scheme_gbs,
+                                "scheme_ceiling_frac_of_hbm": scheme_gbs / peak,
+                                "achieved_frac_of_scheme_ceiling": achieved / scheme_gbs},
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
