@@ -306,6 +306,26 @@ int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, i
 int yabt_grow_xallreduce(yabt_grower* g, void* const* bufs, long long buf_bytes, int rank, int nranks,
                          const void* src, void* dst, long long count, int kind, unsigned epoch, void* stream);
 int yabt_grow_xerr(yabt_grower* g, unsigned* bits);
+/* Feature-sliced level-wise growth over sharded rows (the same split
+ * decisions as yabt_grow_tree on one GPU over all rows, yabt/tree.py:504-560;
+ * less scan work and half the exchange bytes per rank). Rank r of N scans only
+ * features [F r / N, F (r + 1) / N) (yabt_grower_set_feature_slice, exactly
+ * that range). Per level: yabt_grow_hist; yabt_grow_xreduce_sliced (every
+ * rank sums only its slice's words over the ranks, into its own buffer);
+ * yabt_grow_scan (the slice's split scan); yabt_grow_xgather (every rank's
+ * best split per node exchanged through records at rec_offset bytes after the
+ * data start of every exchange buffer, yabt_grow_xgather_bytes of room; the
+ * largest key wins, the first maximum over all features); yabt_grow_choose
+ * (k_finalize, partition, next level's plan). yabt_grow_scan + yabt_grow_choose
+ * on one GPU are yabt_grow_split. epochs as for yabt_grow_xreduce.          */
+int yabt_grower_set_feature_slice(yabt_grower* g, int f_lo, int f_hi);
+int yabt_grow_scan(yabt_grower* g, const yabt_tree_args* a, int level, void* stream);
+int yabt_grow_choose(yabt_grower* g, const yabt_tree_args* a, int level, void* stream);
+int yabt_grow_xreduce_sliced(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                             void* stream);
+int yabt_grow_xgather(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                      long long rec_offset, void* stream);
+long long yabt_grow_xgather_bytes(const yabt_grower* g);
 void* yabt_grow_small_ptr(yabt_grower* g);
 long long yabt_grow_small_count(const yabt_grower* g, int level);
 /* Per-leaf row ranges of the last tree (device arrays inside the workspace):

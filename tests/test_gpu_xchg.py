@@ -11,6 +11,8 @@ or hanging it.
 3. The small-vector all-reduce (yabt_grow_xallreduce): identity on one rank
    for every element kind, a refused oversized vector, and the same bounded
    wait and persistent error bit when a peer never arrives.
+4. Feature-sliced levels (reduce-scatter, slice scan, best-split gather,
+   choice) on one rank grow the same tree as the whole-tree call.
 """
 
 import ctypes
@@ -172,3 +174,50 @@ def test_allreduce_wait_times_out_and_reports():
         torch.cuda.synchronize()
         lib.yabt_xchg_free(b0)
         lib.yabt_xchg_free(b1)
+
+
+def test_single_rank_sliced_levels_are_identity():
+    """Feature-sliced levels on one rank (the slice is every feature): the
+    reduce-scatter, the split scan, the gather of the best split per node and
+    the choice grow the same tree as yabt_grow_tree."""
+    from yabt_b200 import _lib
+    gr_ref, a_ref, out_ref = _setup(seed=6)
+    gr_ref.grow(a_ref)
+    gr, a, out = _setup(seed=6)
+    lib = gr.lib
+    s = _lib.stream_ptr()
+    hist = int(lib.yabt_grow_small_count(gr.h, 62)) * 8
+    rec_off = (hist + 255) // 256 * 256
+    nbytes = rec_off + int(lib.yabt_grow_xgather_bytes(gr.h))
+    p, hnd = ctypes.c_void_p(), (ctypes.c_char * 64)()
+    _lib.check(lib.yabt_xchg_alloc(nbytes, ctypes.byref(p), hnd), "yabt_xchg_alloc")
+    b0 = p.value
+    hdr = int(lib.yabt_xchg_header_bytes())
+    try:
+        _lib.check(lib.yabt_grower_set_small(gr.h, b0 + hdr, nbytes), "set_small")
+        _lib.check(lib.yabt_grower_set_feature_slice(gr.h, 0, gr.F), "slice")
+        assert lib.yabt_grower_set_feature_slice(gr.h, 3, 3) != 0          # an empty slice is refused
+        ref = ctypes.byref(a)
+        bufs = (ctypes.c_void_p * 1)(b0)
+        _lib.check(lib.yabt_grow_begin(gr.h, ref, s), "begin")
+        _lib.check(lib.yabt_grow_init(gr.h, ref, s), "init")
+        e = 0
+        for d in range(gr.levels):
+            _lib.check(lib.yabt_grow_hist(gr.h, ref, d, s), "hist")
+            e += 1
+            _lib.check(lib.yabt_grow_xreduce_sliced(gr.h, bufs, 0, 1, d, e, s), "xreduce_sliced")
+            _lib.check(lib.yabt_grow_scan(gr.h, ref, d, s), "scan")
+            e += 1
+            _lib.check(lib.yabt_grow_xgather(gr.h, bufs, 0, 1, d, e, rec_off, s), "xgather")
+            _lib.check(lib.yabt_grow_choose(gr.h, ref, d, s), "choose")
+        _lib.check(lib.yabt_grow_end(gr.h, ref, s), "end")
+        torch.cuda.synchronize()
+        assert int(out["meta"][2].item()) == 0
+        nn = int(out_ref["meta"][0].item())
+        assert int(out["meta"][0].item()) == nn > 1
+        for k in ("feature", "threshold", "left", "right", "value"):
+            np.testing.assert_array_equal(out[k][:nn].cpu().numpy(), out_ref[k][:nn].cpu().numpy(), err_msg=k)
+        np.testing.assert_array_equal(out["leaf_of_row"].cpu().numpy(), out_ref["leaf_of_row"].cpu().numpy())
+    finally:
+        torch.cuda.synchronize()
+        lib.yabt_xchg_free(b0)

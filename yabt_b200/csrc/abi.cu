@@ -26,6 +26,8 @@ void set_error(const char* fmt, ...) {
 cudaError_t launch_level_hist(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t,
                               cudaEvent_t after_hist, int root_counts);
 cudaError_t launch_level_split(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_level_scan(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
+cudaError_t launch_level_choose(const GrowParams&, const GrowBufs&, const TreeIO&, int, int, cudaStream_t);
 cudaError_t launch_tree_begin(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaStream_t);
 cudaError_t launch_tree_init(const GrowParams&, const GrowBufs&, const TreeIO&, cudaStream_t);
 cudaError_t launch_tree_finish(const GrowParams&, const GrowBufs&, const TreeIO&, int*, int*, int, cudaStream_t);
@@ -161,6 +163,16 @@ static long long al(long long x) { return (x + 255) & ~255LL; }
 
 namespace yabt {
 GrowState* grower_state(yabt_grower* g) { return g && g->bound ? g->b.st : nullptr; }
+int grower_slice(yabt_grower* g, int* F, int* C, int* f_lo, int* f_hi) {
+  if (!g || !g->bound) return 1;
+  *F = g->p.F; *C = g->p.C; *f_lo = g->p.f_lo; *f_hi = g->p.f_hi;
+  return 0;
+}
+void grower_best_bufs(yabt_grower* g, unsigned long long** node_key, NodeBest** best) {
+  *node_key = g && g->bound ? g->b.node_key : nullptr;
+  *best = g && g->bound ? g->b.best : nullptr;
+}
+int grower_maxa(const yabt_grower* g) { return g ? g->p.maxa : 0; }
 }  // namespace yabt
 
 extern "C" {
@@ -176,6 +188,7 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
   GrowParams& p = g->p;
   memset(&p, 0, sizeof(p));
   p.n = n; p.F = F; p.general = general ? 1 : 0;
+  p.f_lo = 0; p.f_hi = F;
   p.S = general ? 1 : 2; g->LIMBS = general ? 5 : 3; p.C = general ? 3 : 2;
   p.max_leaves = max_leaves; p.max_depth = max_depth;
   p.maxa = max_leaves;
@@ -434,6 +447,34 @@ int yabt_grow_split(yabt_grower* g, const yabt_tree_args* a, int level, void* st
   if (rc) return rc;
   if (level < 0 || level >= g->p.levels_max) { set_error("level out of range"); return YABT_ERR_ARG; }
   CUDA_TRY(launch_level_split(g->p, g->b, io, level, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_scan(yabt_grower* g, const yabt_tree_args* a, int level, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (level < 0 || level >= g->p.levels_max) { set_error("level out of range"); return YABT_ERR_ARG; }
+  CUDA_TRY(launch_level_scan(g->p, g->b, io, level, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grow_choose(yabt_grower* g, const yabt_tree_args* a, int level, void* stream) {
+  TreeIO io;
+  int rc = fill_io(g, a, &io);
+  if (rc) return rc;
+  if (level < 0 || level >= g->p.levels_max) { set_error("level out of range"); return YABT_ERR_ARG; }
+  CUDA_TRY(launch_level_choose(g->p, g->b, io, level, g->nsm, (cudaStream_t)stream));
+  return YABT_OK;
+}
+
+int yabt_grower_set_feature_slice(yabt_grower* g, int f_lo, int f_hi) {
+  if (!g || f_lo < 0 || f_hi > g->p.F || f_lo >= f_hi) {
+    set_error("yabt_grower_set_feature_slice: need 0 <= f_lo < f_hi <= F");
+    return YABT_ERR_ARG;
+  }
+  g->p.f_lo = f_lo;
+  g->p.f_hi = f_hi;
   return YABT_OK;
 }
 

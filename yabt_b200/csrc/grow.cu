@@ -141,12 +141,12 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   if (st->level != level_gate || !st->active) return;
   const int d = level_gate;
   const int njobs = d == 0 ? 1 : st->P;
-  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  const int fblocks = (p.f_hi - p.f_lo + SCAN_WARPS - 1) / SCAN_WARPS;
   const int job = blockIdx.x / fblocks;
   if (job >= njobs) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f = (blockIdx.x % fblocks) * SCAN_WARPS + warp;
-  if (f >= p.F) return;
+  const int f = p.f_lo + (blockIdx.x % fblocks) * SCAN_WARPS + warp;
+  if (f >= p.f_hi) return;
   const int cur = d & 1, prv = cur ^ 1;
   const bool write_hist = d + 1 < p.levels_max;
   const float ginv = st->ginv, hinv = st->hinv;
@@ -292,7 +292,7 @@ k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
       b.best[(size_t)pos * p.F + f] = nb;
       // node argmax over features: larger sel, ties -> lower feature
       atomicMax(&b.node_key[pos], ((unsigned long long)f2ord(bsel) << 32) | (0xffffffffu - (unsigned)f));
-      if (f == 0) {
+      if (f == p.f_lo) {      // every feature's bins sum to the node total; the slice's first one records it
         NodeTot t; t.G = G; t.H = H; t.C = Cn; t.pad = 0; t.c = lt[C - 1];
         b.tot[pos] = t;
       }
@@ -1384,17 +1384,29 @@ cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const Tree
   return launch_hist_kernels(p, b, io, d, jobs_bound(d, p.max_pairs), nsm, s, after_hist, root_counts);
 }
 
-cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
-                               int nsm, cudaStream_t s) {
+// The split of a level in two halves: the scan (features [f_lo, f_hi)) and
+// the choice of the splits with the partition and the next level's plan. A
+// feature-sliced sharded fit gathers every rank's best split per node between
+// the two (yabt_grow_xgather).
+cudaError_t launch_level_scan(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
+                              int nsm, cudaStream_t s) {
+  (void)nsm;
   const int jobs = jobs_bound(d, p.max_pairs);
-  const int fblocks = (p.F + SCAN_WARPS - 1) / SCAN_WARPS;
+  const int fblocks = (p.f_hi - p.f_lo + SCAN_WARPS - 1) / SCAN_WARPS;
   cudaError_t e;
   {
     PhaseScope ph(PH_SCAN, s);
     e = p.general ? launch_pdl(k_scan<3>, dim3(jobs * fblocks), dim3(SCAN_WARPS * 32), 0, s, p, b, io, d)
                   : launch_pdl(k_scan<2>, dim3(jobs * fblocks), dim3(SCAN_WARPS * 32), 0, s, p, b, io, d);
   }
+  count_launches(1);
   if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_level_choose(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
+                                int nsm, cudaStream_t s) {
+  cudaError_t e;
   {
     PhaseScope ph(PH_FINALIZE, s);
     e = launch_pdl(k_finalize, dim3(1), dim3(1024), 0, s, p, b, io, d);
@@ -1410,9 +1422,16 @@ cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const Tre
     PhaseScope ph(PH_PLAN, s);
     e = launch_pdl(k_plan, dim3(1), dim3(1024), 0, s, p, b, d);
   }
-  count_launches(4);
+  count_launches(3);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
+                               int nsm, cudaStream_t s) {
+  const cudaError_t e = launch_level_scan(p, b, io, d, nsm, s);
+  if (e != cudaSuccess) return e;
+  return launch_level_choose(p, b, io, d, nsm, s);
 }
 
 cudaError_t launch_tree_begin(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm,

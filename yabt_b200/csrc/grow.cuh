@@ -130,6 +130,7 @@ struct GrowParams {
   int use_imat;
   int use_fmask;
   int bf_f64;           // best-first in the C / Numba grower's arithmetic (float64 scan, slot tie order)
+  int f_lo, f_hi;       // level-wise scan: features [f_lo, f_hi) (a rank's slice in feature-sliced sharding)
 };
 
 // Device pointers of one grower workspace.
@@ -218,5 +219,8 @@ struct MtBufs {
 
 // the device state of a bound grower (C ABI handle), or nullptr
 GrowState* grower_state(struct yabt_grower* g);
+int grower_slice(struct yabt_grower* g, int* F, int* C, int* f_lo, int* f_hi);   // 0 if bound
+void grower_best_bufs(struct yabt_grower* g, unsigned long long** node_key, NodeBest** best);
+int grower_maxa(const struct yabt_grower* g);
 
 }  // namespace yabt

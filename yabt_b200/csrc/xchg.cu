@@ -35,6 +35,7 @@ struct XHeader {                          // at the start of every rank's exchan
   unsigned done[XR_MAX];                  // epoch when rank q's slice of this buffer was summed
   unsigned blocks;                        // blocks of this rank's kernel that finished their stores
   unsigned blocks2;                       // second-phase block count of k_xallreduce
+  unsigned gready[XR_MAX];                // epoch when rank q's per-node best splits were written (k_xgather)
 };
 static_assert(sizeof(XHeader) <= XCHG_HEADER, "exchange header");
 
@@ -44,7 +45,13 @@ struct XArgs {
   unsigned epoch;
   int level;
   long long per_job;                      // int64 words per job
+  int sliced;                             // 1: reduce-scatter of this rank's feature slice only
+  int F, C;                               // features, histogram channels (the slice's word ranges)
 };
+
+// Feature slice of rank r of N: [F r / N, F (r + 1) / N) (the same rule as
+// yabt_b200.distributed's feature_slice).
+__host__ __device__ inline int slice_lo(int F, int r, int N) { return (int)((long long)F * r / N); }
 
 __device__ __forceinline__ void st_flag(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
@@ -83,6 +90,37 @@ __global__ void __launch_bounds__(512) k_xreduce(XArgs a, GrowState* st) {
     if (threadIdx.x == 0) atomicOr(&st->err, DERR_XCHG_TIMEOUT);
     return;
   }
+  if (a.sliced) {
+    // reduce-scatter: this rank sums only the words of its feature slice, in
+    // rank order, into its own buffer (its scan reads nothing else); per job
+    // the value channels [C-1][F][256] and the packed counts [F][128]
+    const int flo = slice_lo(a.F, a.rank, a.nranks), fhi = slice_lo(a.F, a.rank + 1, a.nranks);
+    const long long nf = fhi - flo;
+    const long long vw = (long long)(a.C - 1) * YABT_NB * nf;       // value words of the slice per job
+    const long long per = vw + (YABT_NB / 2) * nf;                  // + count words
+    long long* own = reinterpret_cast<long long*>(a.buf[a.rank] + XCHG_HEADER);
+    for (long long t = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x); t < jobs * per;
+         t += 2LL * gridDim.x * blockDim.x) {
+      const long long j = t / per, w = t - j * per;
+      long long i;
+      if (w < vw) {
+        const long long c = w / (YABT_NB * nf), off = w - c * (YABT_NB * nf);
+        i = j * a.per_job + c * (long long)a.F * YABT_NB + flo * YABT_NB + off;
+      } else {
+        i = j * a.per_job + (long long)(a.C - 1) * a.F * YABT_NB + flo * (YABT_NB / 2) + (w - vw);
+      }
+      long long s0 = 0, s1 = 0;
+      for (int q = 0; q < a.nranks; ++q) {           // rank order
+        const longlong2 v = __ldcv(reinterpret_cast<const longlong2*>(
+            reinterpret_cast<const long long*>(a.buf[q] + XCHG_HEADER) + i));
+        s0 += v.x; s1 += v.y;
+      }
+      *reinterpret_cast<longlong2*>(own + i) = make_longlong2(s0, s1);
+    }
+    // no done phase: a rank overwrites its buffer only after the level's best
+    // splits were gathered (k_xgather), which every rank reaches after its reads
+    return;
+  }
   // slice of this rank: words [lo, hi), in pairs of int64
   const long long lo = words * a.rank / a.nranks & ~1LL;
   const long long hi = a.rank + 1 == a.nranks ? words : (words * (a.rank + 1) / a.nranks & ~1LL);
@@ -117,6 +155,74 @@ __global__ void __launch_bounds__(512) k_xreduce(XArgs a, GrowState* st) {
   }
   __syncthreads();
   if (threadIdx.x == 0 && !wait_all(mine->done, a.nranks, a.epoch)) atomicOr(&st->err, DERR_XCHG_TIMEOUT);
+}
+
+// Per-node best split of every rank (feature-sliced growth): after each rank
+// scanned its slice of the features, the ranks exchange, per active node, the
+// best of their slice (the ordered key of k_scan and its NodeBest), and every
+// rank keeps the largest key -- the first maximum over all features, as one
+// GPU would choose it -- so k_finalize sees the same node_key and best split
+// everywhere. The node totals need no exchange: every slice's features sum to
+// the same node total. One block; records of 64 bytes at rec_off.
+struct XGArgs {
+  char* buf[XR_MAX];
+  int rank, nranks;
+  unsigned epoch;
+  int level;
+  long long rec_off;                      // bytes from the data start to the records
+  int F;
+};
+
+struct XRec {
+  unsigned long long key;
+  NodeBest nb;
+  long long pad[3];
+};
+static_assert(sizeof(XRec) == 64, "exchange record");
+
+__global__ void __launch_bounds__(256) k_xgather(XGArgs a, GrowState* st, unsigned long long* node_key,
+                                                 NodeBest* best) {
+  __shared__ int s_ok;
+  if (st->level != a.level || !st->active) return;   // the same on every rank
+  const int M = st->M;
+  XRec* mine_rec = reinterpret_cast<XRec*>(a.buf[a.rank] + XCHG_HEADER + a.rec_off);
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const unsigned long long key = node_key[m];
+    const int f = (int)(0xffffffffu - (unsigned)(key & 0xffffffffULL));
+    XRec r;
+    r.key = key;
+    r.nb = best[(size_t)m * a.F + (f >= 0 && f < a.F ? f : 0)];
+    r.pad[0] = r.pad[1] = r.pad[2] = 0;
+    mine_rec[m] = r;
+  }
+  __threadfence_system();
+  __syncthreads();
+  XHeader* mine = reinterpret_cast<XHeader*>(a.buf[a.rank]);
+  if (threadIdx.x < a.nranks) st_flag(&reinterpret_cast<XHeader*>(a.buf[threadIdx.x])->gready[a.rank], a.epoch);
+  if (threadIdx.x == 0) s_ok = wait_all(mine->gready, a.nranks, a.epoch) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) {
+    if (threadIdx.x == 0) atomicOr(&st->err, DERR_XCHG_TIMEOUT);
+    return;
+  }
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    unsigned long long bk = 0;
+    int bq = a.rank;
+    for (int q = 0; q < a.nranks; ++q) {             // largest key; equal keys cannot come from two slices
+      const XRec* rq = reinterpret_cast<const XRec*>(a.buf[q] + XCHG_HEADER + a.rec_off) + m;
+      const unsigned long long k = __ldcv(reinterpret_cast<const unsigned long long*>(&rq->key));
+      if (k > bk) { bk = k; bq = q; }
+    }
+    const int f = (int)(0xffffffffu - (unsigned)(bk & 0xffffffffULL));
+    if (bq != a.rank && f >= 0 && f < a.F) {
+      const XRec* rq = reinterpret_cast<const XRec*>(a.buf[bq] + XCHG_HEADER + a.rec_off) + m;
+      const longlong2* src = reinterpret_cast<const longlong2*>(&rq->nb);
+      longlong2* dst = reinterpret_cast<longlong2*>(&best[(size_t)m * a.F + f]);
+      dst[0] = __ldcv(src);
+      dst[1] = __ldcv(src + 1);
+    }
+    node_key[m] = bk;
+  }
 }
 
 // Small-vector all-reduce over the same mapped buffers (the per-tree
@@ -247,6 +353,7 @@ int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, i
     if (!a.buf[q]) { set_error("yabt_grow_xreduce: missing buffer of rank %d", q); return YABT_ERR_ARG; }
   a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level;
   a.per_job = yabt_grow_small_count(g, 0);
+  a.sliced = 0; a.F = 0; a.C = 0;
   GrowState* st = grower_state(g);
   if (!st) { set_error("yabt_grow_xreduce: grower not bound"); return YABT_ERR_ARG; }
   int dev = 0, nsm = YABT_SMS_HINT;
@@ -306,6 +413,71 @@ int yabt_grow_xerr(yabt_grower* g, unsigned* bits) {
   const cudaError_t e = cudaMemcpy(bits, &st->xerr, sizeof(unsigned), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) { set_error("yabt_grow_xerr: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
   return YABT_OK;
+}
+
+int yabt_grow_xreduce_sliced(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                             void* stream) {
+  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks || level < 0) {
+    set_error("yabt_grow_xreduce_sliced: bad arguments (at most %d ranks)", XR_MAX);
+    return YABT_ERR_ARG;
+  }
+  int F = 0, C = 0, flo = 0, fhi = 0;
+  if (grower_slice(g, &F, &C, &flo, &fhi) || flo != slice_lo(F, rank, nranks) || fhi != slice_lo(F, rank + 1, nranks)) {
+    set_error("yabt_grow_xreduce_sliced: the grower's feature slice must be [F r / N, F (r + 1) / N)");
+    return YABT_ERR_ARG;
+  }
+  XArgs a;
+  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
+  for (int q = 0; q < nranks; ++q)
+    if (!a.buf[q]) { set_error("yabt_grow_xreduce_sliced: missing buffer of rank %d", q); return YABT_ERR_ARG; }
+  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level;
+  a.per_job = yabt_grow_small_count(g, 0);
+  a.sliced = 1; a.F = F; a.C = C;
+  GrowState* st = grower_state(g);
+  if (!st) { set_error("yabt_grow_xreduce_sliced: grower not bound"); return YABT_ERR_ARG; }
+  int dev = 0, nsm = YABT_SMS_HINT;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  {
+    PhaseScope ph(PH_XCHG, static_cast<cudaStream_t>(stream));
+    k_xreduce<<<nsm, 512, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
+  }
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("yabt_grow_xreduce_sliced: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int yabt_grow_xgather(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                      long long rec_offset, void* stream) {
+  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks || level < 0 || rec_offset < 0 ||
+      (rec_offset & 255)) {
+    set_error("yabt_grow_xgather: bad arguments (at most %d ranks, 256-byte aligned record offset)", XR_MAX);
+    return YABT_ERR_ARG;
+  }
+  int F = 0, C = 0, flo = 0, fhi = 0;
+  if (grower_slice(g, &F, &C, &flo, &fhi)) { set_error("yabt_grow_xgather: grower not bound"); return YABT_ERR_ARG; }
+  XGArgs a;
+  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
+  for (int q = 0; q < nranks; ++q)
+    if (!a.buf[q]) { set_error("yabt_grow_xgather: missing buffer of rank %d", q); return YABT_ERR_ARG; }
+  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level; a.rec_off = rec_offset; a.F = F;
+  GrowState* st = grower_state(g);
+  unsigned long long* key = nullptr;
+  NodeBest* best = nullptr;
+  grower_best_bufs(g, &key, &best);
+  if (!st || !key || !best) { set_error("yabt_grow_xgather: grower not bound"); return YABT_ERR_ARG; }
+  {
+    PhaseScope ph(PH_XCHG, static_cast<cudaStream_t>(stream));
+    k_xgather<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, st, key, best);
+  }
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("yabt_grow_xgather: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+long long yabt_grow_xgather_bytes(const yabt_grower* g) {
+  return g ? ((long long)grower_maxa(g) * 64 + 255) / 256 * 256 : -1;
 }
 
 }  // extern "C"

@@ -47,10 +47,13 @@ class ShardComm:
     reduced in place on the device; with any other backend (gloo) they are
     staged through host memory."""
 
-    def __init__(self, group=None, peer_exchange: bool = True):
+    def __init__(self, group=None, peer_exchange: bool = True, feature_sliced: bool = True):
         """``peer_exchange``: sum the level histograms with the library's own
         NVLink kernel (yabt_grow_xreduce) when every rank has its own GPU on
-        this node and the backend is NCCL; otherwise with all-reduces."""
+        this node and the backend is NCCL; otherwise with all-reduces.
+        ``feature_sliced`` (with the exchange, level-wise trees): each rank
+        reduces and scans only its slice of the features and the ranks
+        exchange each node's best split."""
         import torch.distributed as dist
         if not dist.is_initialized():
             raise RuntimeError("ShardComm needs an initialised torch.distributed process group")
@@ -60,6 +63,7 @@ class ShardComm:
         self.world = dist.get_world_size(group)
         self.on_device = dist.get_backend(group) == "nccl"
         self.peer_exchange = bool(peer_exchange) and self.on_device and 1 < self.world <= 8
+        self.feature_sliced = bool(feature_sliced)
         if self.peer_exchange:
             import hashlib
             uuid = str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
@@ -279,22 +283,52 @@ class ExchangeBuffers:
             self.own = None
 
 
+def feature_slice(F: int, rank: int, world: int) -> tuple[int, int]:
+    """Features [lo, hi) that rank scans in feature-sliced growth (the rule of
+    yabt_grow_xreduce_sliced)."""
+    return F * rank // world, F * (rank + 1) // world
+
+
 class PeerExchange:
     """A grower bound to the ShardComm's exchange buffers (its smaller-child
     histogram buffer is this rank's exchange buffer). ``reduce(level)``
     launches yabt_grow_xreduce: no host synchronisation and exactly the level's
-    bytes; ``allreduce_`` the small per-tree reductions. ``close()`` must be
-    called on every rank at the end of the fit; the buffers stay mapped for the
-    next fit."""
+    bytes; ``allreduce_`` the small per-tree reductions. With ``sliced`` (the
+    level-wise grower, at least one feature per rank) each level is instead
+    reduce-scattered by feature slices (``reduce_sliced``), scanned on the
+    rank's slice and the ranks' best splits gathered (``gather``). ``close()``
+    must be called on every rank at the end of the fit; the buffers stay mapped
+    for the next fit."""
 
     def __init__(self, grower, comm: ShardComm):
         self.lib = lib = grower.lib
         self.grower, self.comm = grower, comm
-        need = int(lib.yabt_grow_small_count(grower.h, 62)) * 8          # the largest level
+        hist = int(lib.yabt_grow_small_count(grower.h, 62)) * 8          # the largest level
+        self.rec_offset = (hist + 255) // 256 * 256                       # per-node best-split records after it
+        need = self.rec_offset + int(lib.yabt_grow_xgather_bytes(grower.h))
         self.x = comm.exchange_buffers(need)
         _lib.check(lib.yabt_grower_set_small(grower.h, self.x.own + self.x.header, self.x.nbytes),
                    "yabt_grower_set_small")
         self.bufs, self.nbytes = self.x.bufs, self.x.nbytes
+        self.sliced = False
+
+    def set_sliced(self, on: bool) -> None:
+        """Feature-sliced levels (needs at least one feature per rank)."""
+        F = self.grower.F
+        on = bool(on) and F >= self.comm.world
+        lo, hi = feature_slice(F, self.comm.rank, self.comm.world) if on else (0, F)
+        _lib.check(self.lib.yabt_grower_set_feature_slice(self.grower.h, lo, hi), "yabt_grower_set_feature_slice")
+        self.sliced = on
+
+    def reduce_sliced(self, level: int) -> None:
+        _lib.check(self.lib.yabt_grow_xreduce_sliced(self.grower.h, self.bufs, self.comm.rank, self.comm.world,
+                                                     level, self.x.next_epoch(), _lib.stream_ptr()),
+                   "yabt_grow_xreduce_sliced")
+
+    def gather(self, level: int) -> None:
+        _lib.check(self.lib.yabt_grow_xgather(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
+                                              self.x.next_epoch(), self.rec_offset, _lib.stream_ptr()),
+                   "yabt_grow_xgather")
 
     def reduce(self, level: int) -> None:
         _lib.check(self.lib.yabt_grow_xreduce(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
@@ -325,6 +359,8 @@ class PeerExchange:
 
     def close(self) -> None:
         """End of the fit: the grower lets go of the buffers (which stay mapped)."""
+        if self.sliced:
+            self.set_sliced(False)
         self.grower = None
 
 
@@ -367,15 +403,26 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
     if xchg is not None:
         # the NVLink exchange sizes itself from the device state; the host reads
         # each level's state LOOKAHEAD levels later (the GPU keeps that many
-        # levels queued) and stops launching once the tree is complete
+        # levels queued) and stops launching once the tree is complete. With
+        # feature slices each rank sums and scans only its slice of the
+        # features, and the ranks' best splits per node are gathered before
+        # the splits are chosen.
+        if not xchg.sliced and comm.feature_sliced:
+            xchg.set_sliced(True)
         if not hasattr(grower, "_level_ring"):
             grower._level_ring = [(torch.cuda.Event(), torch.zeros(4, dtype=torch.int32).pin_memory())
                                   for _ in range(8)]
         ring = grower._level_ring
         for d in range(grower.levels):
             _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
-            xchg.reduce(d)
-            _lib.check(lib.yabt_grow_split(h, ref, d, s), "yabt_grow_split")
+            if xchg.sliced:
+                xchg.reduce_sliced(d)
+                _lib.check(lib.yabt_grow_scan(h, ref, d, s), "yabt_grow_scan")
+                xchg.gather(d)
+                _lib.check(lib.yabt_grow_choose(h, ref, d, s), "yabt_grow_choose")
+            else:
+                xchg.reduce(d)
+                _lib.check(lib.yabt_grow_split(h, ref, d, s), "yabt_grow_split")
             if not getattr(grower, "level_wait", True):
                 continue                         # every level queued (finished levels are no-ops on every rank)
             ev_d, host_d = ring[d % 8]
