@@ -273,13 +273,17 @@ def run_multiclass(args):
     lib = _lib.load()
     X, y = make_data("c5", n, F, dev, seed=1000)
     W, K = args.warmup, args.steps
-    params = BoostParams(n_estimators=W + K, max_leaves=leaves, max_depth=depth, learning_rate=lr)
+    # one round after the timed ones: with the device-side level loop (whose
+    # graph carries no events) the k_hist launches are timed in that round
+    params = BoostParams(n_estimators=W + K + 1, max_leaves=leaves, max_depth=depth, learning_rate=lr)
     mc = MulticlassBooster(params)
     ev, marks = {}, {}
 
     def cb(r, streams):
         main = torch.cuda.current_stream()
-        if r == 0:
+        loop = mc.boosters_[0].grower_.level_loop_start() > 0
+        marks["loop"] = loop
+        if r == 0 and not loop:
             for b in mc.boosters_:
                 b.grower_.set_timing(K * b.grower_.levels)
         if r == W - 1 or r == W + K - 1:
@@ -292,8 +296,18 @@ def run_multiclass(args):
             if r == W - 1:
                 marks["t0"] = time.time()
                 for b in mc.boosters_:
-                    b.grower_.set_timing(K * b.grower_.levels)
+                    if not loop:
+                        b.grower_.set_timing(K * b.grower_.levels)
                     b.grower_.acc_reset()
+                _lib.check(lib.yabt_launch_count_device_reset(_lib.stream_ptr()), "yabt_launch_count_device_reset")
+                for st in streams:
+                    st.wait_stream(main)
+            else:
+                marks["acc"] = [b.grower_.acc_read() for b in mc.boosters_]   # waits for the timed rounds
+                marks["loop_launches"] = int(lib.yabt_launch_count_device())
+                if loop:
+                    for b in mc.boosters_:
+                        b.grower_.set_timing(b.grower_.levels)      # the extra round, timed per launch
     torch.cuda.synchronize()
     mc.fit(X, y.cpu().numpy(), round_callback=cb)
     torch.cuda.synchronize()
@@ -301,7 +315,9 @@ def run_multiclass(args):
     ms = ev["start"].elapsed_time(ev["stop"])
     nc = len(mc.boosters_)
     hist_ms = sum(sum(b.grower_.hist_times()) for b in mc.boosters_)
-    acc = [b.grower_.acc_read() for b in mc.boosters_]
+    if marks["loop"]:
+        hist_ms *= K                      # one round's k_hist time, for K rounds
+    acc = marks["acc"]
     root, child, launches = (sum(a[i] for a in acc) for i in range(3))
     alg = root * (F + 8) + child * (F + 12)
     achieved = alg / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else float("nan")
@@ -331,10 +347,18 @@ def run_multiclass(args):
         "config": {"workload": f"c5: {n}x{F}, {nc} classes one-vs-rest, one tree per class per round on "
                                f"{nc} CUDA streams, {leaves} leaves, logloss, neural leaves",
                    "global_rows": n, "l2": "inputs larger than L2"},
-        "gpu_launches": marks["l1"] - marks["l0"],
+        "gpu_launches": marks["l1"] - marks["l0"] + marks.get("loop_launches", 0),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "kernel": "k_hist", "launches_timed": launches,
-                     "hist_share_of_step": hist_ms / ms,
+                     "concurrent_streams": nc,
+                     "hist_time_source": "the round after the timed ones, CUDA events around each k_hist launch"
+                     + (" (the timed rounds run their deeper levels in the device-side level loop)"
+                        if marks["loop"] else ""),
+                     "hist_launch_ms_over_step": hist_ms / ms,
+                     "achieved_over_step": alg / (ms / 1000.0) / 1e9,
+                     "how": f"achieved: k_hist's algorithmic bytes over the sum of its launch durations; the {nc} "
+                            "class streams overlap, so each launch shares the GPU and the sum exceeds the step "
+                            "(hist_launch_ms_over_step > 1); achieved_over_step: the same bytes over the step",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
         "clocks": clocks, "e2e": None, "cpu_baseline": None,
         "sparse_bin_probe": {"unit": "G (row, feature) updates/s", "limbs": 5, **probe,
@@ -431,11 +455,18 @@ def run_ours(args):
     marks = {}
 
     def cb(t, grower):
-        if t == 0:
+        # trees whose deeper levels run in the device-side level loop (a CUDA
+        # graph) cannot carry events around each histogram launch; their k_hist
+        # time comes from the phase pass instead
+        loop = grower.level_loop_start() > 0 and world == 1
+        marks["loop"] = loop
+        if t == 0 and not loop:
             grower.set_timing(K * grower.levels)      # create the event pool early
         if t == W - 1:
-            grower.set_timing(K * grower.levels)      # restart recording (no allocation)
+            if not loop:
+                grower.set_timing(K * grower.levels)  # restart recording (no allocation)
             grower.acc_reset()
+            _lib.check(lib.yabt_launch_count_device_reset(_lib.stream_ptr()), "yabt_launch_count_device_reset")
             ev["start"] = torch.cuda.Event(enable_timing=True)
             ev["start"].record()
             marks["launches0"] = int(lib.yabt_launch_count())
@@ -445,6 +476,7 @@ def run_ours(args):
             ev["stop"].record()
             marks["launches1"] = int(lib.yabt_launch_count())
             marks["acc"] = grower.acc_read()          # rows histogrammed by the timed trees (waits for them)
+            marks["loop_launches"] = int(lib.yabt_launch_count_device())   # kernels the level loops ran
             if P:
                 phases.start()                        # the untimed phase pass: trees W+K .. W+K+P-1
 
@@ -458,8 +490,11 @@ def run_ours(args):
     phase_split = phase_summary(phases, P, dist if world > 1 else None, dev) if P else None
     clocks = sampler.stop((marks["t0"], time.time())) if sampler else None
     ms = ev["start"].elapsed_time(ev["stop"])
-    hist_ms = booster.grower_.hist_times()
     root_rows, child_rows, hist_launches = marks["acc"]
+    if marks.get("loop") and phase_split and "hist" in phase_split["ms_per_tree"]:
+        hist_ms = [phase_split["ms_per_tree"]["hist"] * K]     # phase pass, per tree, times the timed trees
+    else:
+        hist_ms = booster.grower_.hist_times()
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -563,7 +598,7 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch Philox, config shapes)",
             "config": workload_config(cfg, world),
             "bin_reads_per_sec": bin_reads_per_s,
-            "gpu_launches": marks.get("launches1", 0) - marks.get("launches0", 0),
+            "gpu_launches": marks.get("launches1", 0) - marks.get("launches0", 0) + marks.get("loop_launches", 0),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic_per_launch,
                          "traffic_source": "ncu capture of one 2M-row C4 tree, scaled by algorithmic bytes"
@@ -571,6 +606,9 @@ def run_ours(args):
                          "kernel": "k_hist", "alg_bytes_per_launch": alg_per_launch,
                          "avg_launch_ms": avg_hist_ms, "launches_timed": hist_launches,
                          "hist_share_of_step": hist_total_ms / ms,
+                         "hist_time_source": "phase pass (the timed trees run their deeper levels in the "
+                                             "device-side level loop, which carries no events)"
+                         if marks.get("loop") else "CUDA events around each timed k_hist launch",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
             # k_hist is bound by shared-memory reductions, not HBM: its (row, feature)
             # update rate against the same reductions issued alone (yabt_probe_shared_red)

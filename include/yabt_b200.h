@@ -33,8 +33,14 @@ int yabt_version(void);
 /* Copy the last error message of this thread into buf (NUL-terminated). */
 int yabt_last_error(char* buf, int len);
 
-/* Number of kernels the library has launched so far in this process. */
+/* Number of kernels the library has launched so far in this process from the
+ * host. Kernels that device-side level loops ran (yabt_grower_set_level_loop)
+ * are counted on the device of the calling thread: yabt_launch_count_device
+ * reads that counter (waits for the device; -1 on error) and
+ * yabt_launch_count_device_reset zeroes it in stream order. */
 long long yabt_launch_count(void);
+long long yabt_launch_count_device(void);
+int yabt_launch_count_device_reset(void* stream);
 
 /* Measurement only (no reference counterpart): the shared-memory reduction
  * ceiling of the histogram kernel. Issues k_hist's u32 reductions (limbs = 3:
@@ -174,10 +180,25 @@ typedef struct {
 /* Grow one tree (single device). The host stops queuing levels once the tree
  * is complete: after each level's split the level state is copied to pinned
  * host memory and read three levels later, so the GPU keeps three levels
- * queued while the host waits. yabt_grower_set_level_wait(g, 0) queues every
- * level without waiting instead (for callers that interleave several growers
- * on several streams from one host thread).                              */
+ * queued while the host waits. yabt_grower_set_level_wait(g, 0) queues the
+ * levels without waiting instead (for callers that interleave several growers
+ * on several streams from one host thread): every level, or the levels below
+ * the device-side level loop's start and then the loop (below).           */
 int yabt_grower_set_level_wait(yabt_grower* g, int wait);
+/* Device-side level loop (on by default; no reference counterpart: the
+ * reference's level loop is a host while loop, yabt/tree.py:484-625). Without level
+ * wait, a tree whose levels may go far deeper than it grows (max_depth well
+ * above log2(max_leaves)) would otherwise queue every possible level, most of
+ * them device-side no-ops. With the loop, yabt_grow_tree launches levels
+ * 0 .. L-1 as usual and then one CUDA graph whose conditional WHILE node
+ * repeats one level's kernels while the tree is active; the graph is captured
+ * on first use and again when the grower's parameters or workspace change.
+ * yabt_grower_level_loop_start returns L, or -1 when the loop is off or would
+ * not pay (level wait on, fewer than 9 leaves, fewer than two levels past L).
+ * The loop is not used while histogram or phase timing records events, or
+ * when the stream is being captured.                                       */
+int yabt_grower_set_level_loop(yabt_grower* g, int on);
+int yabt_grower_level_loop_start(const yabt_grower* g);
 /* Root-level row counts cached across the trees of a fit: with on = 1, the
  * next root histogram over all rows (no root_rows) keeps its per-bin row
  * counts, and later root histograms over all rows skip the count channel and

@@ -66,6 +66,8 @@ SIGNATURES = [
     ("yabt_version", c_int, []),
     ("yabt_last_error", c_int, [ctypes.c_char_p, c_int]),
     ("yabt_launch_count", c_ll, []),
+    ("yabt_launch_count_device", c_ll, []),
+    ("yabt_launch_count_device_reset", c_int, [c_vp]),
     ("yabt_probe_shared_red", c_int, [c_int, c_int, c_vp, c_vp, ctypes.POINTER(ctypes.c_float),
                                       ctypes.POINTER(ctypes.c_longlong)]),
     ("yabt_probe_shared_red_masked", c_int, [c_int, c_int, c_int, c_vp, c_vp, ctypes.POINTER(ctypes.c_float),
@@ -111,6 +113,8 @@ SIGNATURES = [
     ("yabt_grow_small_ptr", c_vp, [c_vp]),
     ("yabt_grow_level_ptr", c_vp, [c_vp]),
     ("yabt_grower_set_level_wait", c_int, [c_vp, c_int]),
+    ("yabt_grower_set_level_loop", c_int, [c_vp, c_int]),
+    ("yabt_grower_level_loop_start", c_int, [c_vp]),
     ("yabt_grow_apply_all", c_int, [c_vp, ctypes.POINTER(TreeArgs), c_vp]),
     ("yabt_group_rows_workspace_bytes", c_ll, [c_ll, c_int]),
     ("yabt_group_rows", c_int, [c_vp, c_ll, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_vp]),

@@ -331,12 +331,16 @@ class Booster:
         # the bin matrix is fixed for the fit: root histograms over all rows reuse
         # the first tree's per-bin row counts (trees grown on a row sample do not)
         _lib.check(lib.yabt_grower_set_root_count_cache(grower.h, 1), "yabt_grower_set_root_count_cache")
-        # level-wise trees queue every level (a finished tree's remaining levels
-        # are cheap device-side no-ops, cheaper than the host waiting to stop
-        # and leaving the GPU idle while it queues the next tree); best-first
+        # level-wise trees queue their levels without host waits (a finished
+        # tree's remaining levels are device-side no-ops, or are skipped by the
+        # device-side level loop below, both cheaper than the host waiting to
+        # stop and leaving the GPU idle while it queues the next tree); best-first
         # trees, with up to max_leaves - 1 steps, stop queuing once complete
         lw = getattr(self, "_level_wait", None)
         grower.set_level_wait(bestfirst if lw is None else lw)
+        # levels past level_loop_start() run in the device-side level loop
+        # (one CUDA graph per tree, repeated on the device while the tree grows)
+        grower.set_level_loop(getattr(self, "_level_loop", True))
         self.grower_ = grower
         K = min(p.leaf_net_features, F) if p.neural_leaves else 0
         if p.neural_leaves and not 1 <= K <= 8:

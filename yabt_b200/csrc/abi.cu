@@ -14,7 +14,9 @@ namespace yabt {
 static thread_local char g_err[512] = "";
 static std::atomic<long long> g_launches{0};
 
-void count_launches(int k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
+void count_launches(int k) {
+  if (!capturing_level_loop()) g_launches.fetch_add(k, std::memory_order_relaxed);   // graph loops count on the device
+}
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -45,6 +47,11 @@ cudaError_t launch_mt_values(const GrowParams&, const GrowBufs&, const MtBufs&, 
 cudaError_t launch_mt_update(const int*, const float*, int, long long, float*, const float*, float*, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
 cudaError_t launch_unpack_counts(const GrowParams&, const GrowBufs&, long long*, cudaStream_t);
+cudaError_t launch_level_loop_body(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaGraphConditionalHandle,
+                                   cudaStream_t);
+cudaError_t launch_level_loop_cond(const GrowParams&, const GrowBufs&, cudaGraphConditionalHandle, cudaStream_t);
+cudaError_t loop_launches_reset(cudaStream_t);
+cudaError_t loop_launches_read(long long*);
 
 // ---------------------------------------------------------------- pack kernel
 __global__ void k_pack_bins(const uint8_t* __restrict__ plain, long long n, int F,
@@ -85,6 +92,21 @@ extern "C" {
 int yabt_version(void) { return 100; }
 
 long long yabt_launch_count(void) { return g_launches.load(); }
+
+long long yabt_launch_count_device(void) {
+  long long v = 0;
+  if (loop_launches_read(&v) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("yabt_launch_count_device: reading the device counter failed");
+    return -1;
+  }
+  return v;
+}
+
+int yabt_launch_count_device_reset(void* stream) {
+  CUDA_TRY(loop_launches_reset((cudaStream_t)stream));
+  return YABT_OK;
+}
 
 int yabt_last_error(char* buf, int len) {
   if (!buf || len <= 0) return YABT_ERR_ARG;
@@ -155,6 +177,16 @@ struct yabt_grower {
   // cached root-level counts (yabt_grower_set_root_count_cache): 0 off; 1 on,
   // recorded by the next root histogram over all rows and reused after that
   int rc_mode = 0, rc_valid = 0;
+  // device-side level loop (yabt_grower_set_level_loop): yabt_grow_tree
+  // launches the levels below level_loop_start() as usual, then one CUDA graph
+  // whose WHILE node repeats a level's kernels while the tree is active, so a
+  // tree that finishes early leaves no queued no-op levels behind. The graph
+  // bakes in p and b; it is captured again when either changes.
+  int level_loop = 1;
+  cudaGraphExec_t loop_exec = nullptr;
+  cudaStream_t loop_cap = nullptr;         // capture stream
+  GrowParams loop_p;
+  GrowBufs loop_b;
 };
 
 static constexpr int LEVEL_SLOTS = 8, LEVEL_LOOKAHEAD = 3;
@@ -232,6 +264,7 @@ int yabt_grower_create(long long n, int F, int max_leaves, int max_depth, int ge
   const long long words = (long long)g->LIMBS * p.S * YABT_NB * 32;
   auto add = [&](const char* nm, long long bytes) { g->offs.push_back({nm, bytes, 0}); };
   add("st", sizeof(GrowState));
+  add("io", sizeof(TreeIO));
   add("rows0", n * 4); add("rows1", n * 4); add("fin", n * 4);
   add("segb0", std::max(p.maxa, 2) * 4); add("segb1", std::max(p.maxa, 2) * 4);
   add("segc0", std::max(p.maxa, 2) * 4); add("segc1", std::max(p.maxa, 2) * 4);
@@ -290,6 +323,7 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
   };
   GrowBufs& b = g->b;
   b.st = (GrowState*)P("st");
+  b.io_dev = (TreeIO*)P("io");
   b.rows[0] = (int*)P("rows0"); b.rows[1] = (int*)P("rows1"); b.fin = (int*)P("fin");
   b.seg_begin[0] = (int*)P("segb0"); b.seg_begin[1] = (int*)P("segb1");
   b.seg_count[0] = (int*)P("segc0"); b.seg_count[1] = (int*)P("segc1");
@@ -324,6 +358,8 @@ int yabt_grower_bind(yabt_grower* g, void* ws, long long bytes, void* stream) {
 
 int yabt_grower_destroy(yabt_grower* g) {
   if (g) {
+    if (g->loop_exec) cudaGraphExecDestroy(g->loop_exec);
+    if (g->loop_cap) cudaStreamDestroy(g->loop_cap);
     for (auto e : g->ev) cudaEventDestroy(e);
     for (auto e : g->lvl_ev) if (e) cudaEventDestroy(e);
     if (g->host_state) cudaFreeHost(g->host_state);
@@ -486,11 +522,103 @@ int yabt_grow_end(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   return YABT_OK;
 }
 
+// First level of the device-side loop, or -1 when the loop would not pay: the
+// loop's launches are sized for max_pairs jobs and need at least 8 of them
+// (one reduce group per job), so it starts at the first level whose job bound
+// reaches max_pairs, and only when at least two levels are left after it.
+static int level_loop_first(const yabt_grower* g) {
+  const GrowParams& p = g->p;
+  if (!g->level_loop || g->level_wait || p.max_pairs < 8) return -1;
+  int L = 4;
+  while (L < 31 && (1LL << (L - 1)) < p.max_pairs) ++L;
+  return p.levels_max - L >= 2 ? L : -1;
+}
+
+// Captures the loop graph: [condition] -> WHILE { level at the state's level;
+// condition }. Returns a CUDA error; on failure nothing is kept.
+static cudaError_t build_level_loop(yabt_grower* g, const TreeIO& io) {
+  if (g->loop_exec) { cudaGraphExecDestroy(g->loop_exec); g->loop_exec = nullptr; }
+  cudaError_t e = cudaSuccess;
+  if (!g->loop_cap && (e = cudaStreamCreateWithFlags(&g->loop_cap, cudaStreamNonBlocking)) != cudaSuccess) return e;
+  cudaGraph_t graph = nullptr;
+  if ((e = cudaGraphCreate(&graph, 0)) != cudaSuccess) return e;
+  cudaGraphConditionalHandle h;
+  cudaGraphNode_t pre = nullptr;
+  size_t npre = 1;
+  cudaGraphNodeParams cp = {};
+  bool capturing = false;
+  auto fail = [&](cudaError_t err) {
+    if (capturing) {
+      cudaGraph_t partial = nullptr;
+      cudaStreamEndCapture(g->loop_cap, &partial);
+    }
+    set_capturing_level_loop(false);
+    cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return err;
+  };
+  if ((e = cudaGraphConditionalHandleCreate(&h, graph, 0, 0)) != cudaSuccess) return fail(e);
+  set_capturing_level_loop(true);
+  if ((e = cudaStreamBeginCaptureToGraph(g->loop_cap, graph, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed)) !=
+      cudaSuccess)
+    return fail(e);
+  capturing = true;
+  if ((e = launch_level_loop_cond(g->p, g->b, h, g->loop_cap)) != cudaSuccess) return fail(e);
+  capturing = false;
+  if ((e = cudaStreamEndCapture(g->loop_cap, &graph)) != cudaSuccess) return fail(e);
+  if ((e = cudaGraphGetNodes(graph, &pre, &npre)) != cudaSuccess || npre != 1)
+    return fail(e != cudaSuccess ? e : cudaErrorInvalidValue);
+  cp.type = cudaGraphNodeTypeConditional;
+  cp.conditional.handle = h;
+  cp.conditional.type = cudaGraphCondTypeWhile;
+  cp.conditional.size = 1;
+  cudaGraphNode_t cond = nullptr;
+  if ((e = cudaGraphAddNode(&cond, graph, &pre, 1, &cp)) != cudaSuccess) return fail(e);
+  cudaGraph_t body = cp.conditional.phGraph_out[0];
+  if ((e = cudaStreamBeginCaptureToGraph(g->loop_cap, body, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed)) !=
+      cudaSuccess)
+    return fail(e);
+  capturing = true;
+  if ((e = launch_level_loop_body(g->p, g->b, io, g->nsm, h, g->loop_cap)) != cudaSuccess) return fail(e);
+  capturing = false;
+  if ((e = cudaStreamEndCapture(g->loop_cap, &body)) != cudaSuccess) return fail(e);
+  set_capturing_level_loop(false);
+  e = cudaGraphInstantiate(&g->loop_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) { g->loop_exec = nullptr; cudaGetLastError(); return e; }
+  memcpy(&g->loop_p, &g->p, sizeof(GrowParams));
+  memcpy(&g->loop_b, &g->b, sizeof(GrowBufs));
+  return cudaSuccess;
+}
+
 int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   int rc;
   if ((rc = yabt_grow_begin(g, a, stream))) return rc;
   if ((rc = yabt_grow_init(g, a, stream))) return rc;
   cudaStream_t s = (cudaStream_t)stream;
+  const int L = level_loop_first(g);
+  cudaStreamCaptureStatus cst = cudaStreamCaptureStatusNone;
+  if (L > 0 && !g->timing && !phase_timing_on() && cudaStreamIsCapturing(s, &cst) == cudaSuccess &&
+      cst == cudaStreamCaptureStatusNone) {
+    for (int d = 0; d < L; ++d) {
+      if ((rc = yabt_grow_hist(g, a, d, stream))) return rc;
+      if ((rc = yabt_grow_split(g, a, d, stream))) return rc;
+    }
+    if (!g->loop_exec || memcmp(&g->loop_p, &g->p, sizeof(GrowParams)) ||
+        memcmp(&g->loop_b, &g->b, sizeof(GrowBufs))) {
+      TreeIO io;
+      if ((rc = fill_io(g, a, &io))) return rc;
+      const cudaError_t e = build_level_loop(g, io);
+      if (e != cudaSuccess) {
+        set_error("yabt_grow_tree: capturing the level-loop graph failed: %s", cudaGetErrorString(e));
+        return YABT_ERR_CUDA;
+      }
+    }
+    CUDA_TRY(cudaGraphLaunch(g->loop_exec, s));
+    count_launches(1);                       // the condition before the loop; the loop counts on the device
+    return yabt_grow_end(g, a, stream);
+  }
+  cudaGetLastError();
   if (!g->host_state) {
     CUDA_TRY(cudaHostAlloc((void**)&g->host_state, sizeof(int) * 4 * LEVEL_SLOTS, cudaHostAllocDefault));
     for (auto& e : g->lvl_ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -719,6 +847,14 @@ int yabt_grower_set_level_wait(yabt_grower* g, int wait) {
   g->level_wait = wait ? 1 : 0;
   return YABT_OK;
 }
+
+int yabt_grower_set_level_loop(yabt_grower* g, int on) {
+  if (!g) { set_error("null grower"); return YABT_ERR_ARG; }
+  g->level_loop = on ? 1 : 0;
+  return YABT_OK;
+}
+
+int yabt_grower_level_loop_start(const yabt_grower* g) { return g ? level_loop_first(g) : -1; }
 
 int yabt_grower_set_small(yabt_grower* g, void* ptr, long long bytes) {
   if (!g || !g->bound || !ptr || ((uintptr_t)ptr & 255)) {

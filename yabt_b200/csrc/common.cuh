@@ -79,6 +79,15 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();
 
+// ---------------------------------------------------------------- device-side level loop
+// A level kernel launched with level_gate == LEVEL_DYN takes its level from the
+// grower's device state instead of the launch (kernels inside the CUDA graph of
+// a device-side level loop, abi.cu). While the calling thread captures that
+// graph, launches go in without PDL, phase events or host launch counts.
+constexpr int LEVEL_DYN = -1;
+bool capturing_level_loop();
+void set_capturing_level_loop(bool on);
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                               Args... args) {
@@ -91,7 +100,7 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = pdl_enabled() && !capturing_level_loop() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
@@ -116,6 +125,8 @@ enum Phase : int {
   PH_OTHER,
   PH_COUNT
 };
+
+bool phase_timing_on();     // yabt_phase_timing is recording
 
 class PhaseScope {
  public:

@@ -86,6 +86,7 @@ __global__ void k_tree_init(GrowParams p, GrowBufs b, TreeIO io) {
   GrowState* st = b.st;
   for (int m = threadIdx.x; m < p.maxa; m += blockDim.x) b.node_key[m] = 0ULL;
   if (threadIdx.x == 0) {
+    *b.io_dev = io;                    // the tree's inputs for launches of a device-side level loop
     st->level = 0; st->active = 1; st->M = 1; st->P = 0; st->n_nodes = 1; st->n_rows = p.n;
     st->remaining = p.max_leaves - 1; st->part_level = -1; st->plan_level = -1;
     st->depth_max = 0; st->n_leaves = 0; st->err = 0; st->tile_counter = 0; st->n_tiles = 0;
@@ -138,6 +139,10 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32, C == 2 ? 3 : 2)
 k_scan(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   pdl_wait();
   GrowState* st = b.st;
+  if (level_gate == LEVEL_DYN) {
+    if ((level_gate = st->level) < 1) return;
+    io = *b.io_dev;
+  }
   if (st->level != level_gate || !st->active) return;
   const int d = level_gate;
   const int njobs = d == 0 ? 1 : st->P;
@@ -310,6 +315,10 @@ k_finalize(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   pdl_wait();
   pdl_trigger();
   GrowState* st = b.st;
+  if (level_gate == LEVEL_DYN) {
+    if ((level_gate = st->level) < 1) return;
+    io = *b.io_dev;
+  }
   if (st->level != level_gate || !st->active) return;
   const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
   const int M = st->M;
@@ -474,6 +483,10 @@ __global__ void __launch_bounds__(PART_THREADS)
 k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   pdl_wait();
   GrowState* st = b.st;
+  if (level_gate == LEVEL_DYN) {
+    if ((level_gate = st->part_level) < 1) return;
+    io = *b.io_dev;
+  }
   if (st->part_level != level_gate) return;
   const int d = level_gate, cur = d & 1, nxt = cur ^ 1;
   const int ntiles = st->n_tiles;
@@ -620,6 +633,7 @@ k_plan(GrowParams p, GrowBufs b, int level_gate) {
   pdl_wait();
   pdl_trigger();
   GrowState* st = b.st;
+  if (level_gate == LEVEL_DYN && (level_gate = st->plan_level) < 1) return;
   if (st->plan_level != level_gate) return;
   const int d = level_gate, nxt = (d + 1) & 1;
   const int P = st->P;
@@ -1373,9 +1387,61 @@ struct HostStep {
 };
 
 static inline int jobs_bound(int d, int max_pairs) {
+  if (d == LEVEL_DYN) return max_pairs;       // any level of a device-side loop
   if (d == 0) return 1;
   long long j = 1LL << min(d - 1, 30);
   return (int)std::min<long long>(j, max_pairs);
+}
+
+// ------------------------------------------------------------------ device-side level loop
+// Kernels run inside device-side level loops, counted on the device (the host
+// cannot know how many levels a loop ran): every pass of a loop's body adds
+// its kernels here.
+__device__ unsigned long long g_loop_launches;
+
+// Condition of a device-side level loop (a CUDA graph WHILE node, abi.cu):
+// another level runs while the tree is active and below its level limit.
+// Inside the loop body (body_kernels > 0) it also counts the body's kernels.
+__global__ void k_level_loop_cond(const GrowState* __restrict__ st, int levels_max, cudaGraphConditionalHandle h,
+                                  int body_kernels) {
+  const bool more = st->active && st->level < levels_max;
+  cudaGraphSetConditional(h, more ? 1u : 0u);
+  if (body_kernels > 0) atomicAdd(&g_loop_launches, (unsigned long long)body_kernels);
+}
+
+cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d, int nsm,
+                              cudaStream_t s, cudaEvent_t after_hist, int root_counts);
+cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d, int nsm,
+                               cudaStream_t s);
+
+// The body of the loop: one level at the level the device state is at
+// (LEVEL_DYN launches, grids sized for max_pairs jobs), then the condition.
+cudaError_t launch_level_loop_body(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm,
+                                   cudaGraphConditionalHandle h, cudaStream_t s) {
+  cudaError_t e = launch_level_hist(p, b, io, LEVEL_DYN, nsm, s, nullptr, 0);
+  if (e == cudaSuccess) e = launch_level_split(p, b, io, LEVEL_DYN, nsm, s);
+  if (e != cudaSuccess) return e;
+  k_level_loop_cond<<<1, 1, 0, s>>>(b.st, p.levels_max, h, LEVEL_LOOP_BODY_KERNELS);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_level_loop_cond(const GrowParams& p, const GrowBufs& b, cudaGraphConditionalHandle h,
+                                   cudaStream_t s) {
+  k_level_loop_cond<<<1, 1, 0, s>>>(b.st, p.levels_max, h, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t loop_launches_reset(cudaStream_t s) {
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_loop_launches);
+  return e != cudaSuccess ? e : cudaMemsetAsync(ptr, 0, sizeof(unsigned long long), s);
+}
+
+cudaError_t loop_launches_read(long long* out) {
+  unsigned long long v = 0;
+  const cudaError_t e = cudaMemcpyFromSymbol(&v, g_loop_launches, sizeof(v));
+  *out = (long long)v;
+  return e;
 }
 
 // Launches of one level. Returns a CUDA error code (0 on success).

@@ -9,7 +9,7 @@ namespace yabt {
 constexpr int HIST_THREADS = 1024;    // k_hist block size (one block per SM)
 constexpr int PART_TILE = 4096;       // rows per partition tile
 constexpr int PART_THREADS = 512;     // 8 rows per thread
-constexpr int ITEM_TARGET = 8 * YABT_SMS_HINT;  // histogram work items per level (target)
+constexpr int ITEM_TARGET = 4 * YABT_SMS_HINT;  // histogram work items per level (target)
 constexpr int CHUNK_MIN = 4096;       // rows per histogram item (lower bound)
 constexpr int CHUNK_MAX = 65536;      // rows per item and per flushed segment (u32 limb overflow bound)
 constexpr int RUN_MAX = 16;          // items per claimed run (k_hist)
@@ -21,6 +21,9 @@ __host__ __device__ constexpr long long small_job_words(int C, int F) {
   return (long long)(C - 1) * F * YABT_NB + (long long)F * (YABT_NB / 2);
 }
 constexpr int SCAN_WARPS = 8;         // k_scan: one warp per feature
+// kernels of one pass of a device-side level loop: k_hist, k_reduce, k_scan,
+// k_finalize, k_partition, k_plan and the loop condition
+constexpr int LEVEL_LOOP_BODY_KERNELS = 7;
 constexpr int FIN_SMEM_NODES = 2048;  // k_finalize: active nodes whose gains / tile prefixes fit shared memory
 
 // leaf row sources
@@ -134,8 +137,11 @@ struct GrowParams {
 };
 
 // Device pointers of one grower workspace.
+struct TreeIO;
+
 struct GrowBufs {
   GrowState* st;
+  TreeIO* io_dev;        // the current tree's TreeIO (written by k_tree_init)
   int* rows[2];          // active row lists (ping-pong by level parity)
   int* fin;              // rows of nodes that stopped (same offsets as the lists)
   int* seg_begin[2];     // [maxa] per level parity

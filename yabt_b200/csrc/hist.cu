@@ -269,17 +269,27 @@ __device__ __forceinline__ void hist_warp_narrow(unsigned lb, unsigned ring, con
 // Persistent: one block per SM claims runs of consecutive work items from a
 // device counter; the warps stream contiguous shares of each item's rows into
 // a shared histogram that is flushed once per (job, unit) segment of the run.
+// level_gate == LEVEL_DYN (device-side level loop): the level is the state's,
+// the inputs are the tree's (io_dev) and the row list is rows (even levels) or
+// rows_odd (odd levels).
 template <int S, int LIMBS>
 __global__ void __launch_bounds__(HistPipe<S, LIMBS>::THREADS, 1)
 k_hist(const uint8_t* __restrict__ bins, const int* __restrict__ rows,
        const float* __restrict__ g, const float* __restrict__ h,
        HistItem* __restrict__ items, const UnitDesc* __restrict__ units,
-       GrowState* st, unsigned* __restrict__ partials, int level_gate) {
+       GrowState* st, unsigned* __restrict__ partials, int level_gate,
+       const TreeIO* __restrict__ io_dev, const int* __restrict__ rows_odd) {
   using Cfg = HistCfg<S, LIMBS>;
   using Pipe = HistPipe<S, LIMBS>;
   extern __shared__ __align__(16) unsigned sh[];
   __shared__ int s_a, s_e;
   pdl_wait();
+  if (level_gate == LEVEL_DYN) {
+    level_gate = st->level;
+    if (level_gate < 1) return;
+    bins = io_dev->bins; g = io_dev->g; h = io_dev->h;
+    if (level_gate & 1) rows = rows_odd;
+  }
   if (st->level != level_gate || !st->active) return;
   const int nitems = st->n_items;
   const float gs = st->gscale, hs = st->hscale;
@@ -386,6 +396,7 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
   constexpr int CW = Cfg::HAS_CNT ? C : C - 1; // channels written here (cached counts are copied in)
   constexpr int BPP = YABT_NB / RED_PARTS;     // bins per part (16)
   __shared__ long long tsm[C][32][BPP + 1];
+  if (level_gate == LEVEL_DYN && (level_gate = st->level) < 1) return;
   if (st->level != level_gate || !st->active) return;
   const int njobs = (level_gate == 0) ? 1 : st->P;
   int b = blockIdx.x;
@@ -482,7 +493,8 @@ k_reduce(const unsigned* __restrict__ partials, const int* __restrict__ job_firs
 // count limb, the counts copied in from b.root_cnt.
 cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d,
                                 int jobs, int nsm, cudaStream_t s, cudaEvent_t after_hist, int root_counts) {
-  const int* rows = d == 0 ? io.root_rows : b.rows[d & 1];   // nullptr: identity
+  // nullptr: identity; a device-side loop level picks rows[0] / rows[1] by its parity
+  const int* rows = d == 0 ? io.root_rows : d == LEVEL_DYN ? b.rows[0] : b.rows[d & 1];
   if (d != 0 || io.root_rows) root_counts = 0;
   const size_t cnt_off = (size_t)(p.C - 1) * p.F * YABT_NB;      // count words of job 0 in `small`
   const size_t cnt_bytes = (size_t)p.F * (YABT_NB / 2) * 8;
@@ -496,7 +508,7 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
   cudaError_t le = cudaSuccess;
   if (!p.general && root_counts != 2) {
     { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<2, 3>, dim3(nsm), dim3(HistPipe<2, 3>::THREADS), HistPipe<2, 3>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d); }
+                                                      b.st, b.partials, d, b.io_dev, b.rows[1]); }
     if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
     { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<2, 3>, dim3(jobs * p.U * 2 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
@@ -504,7 +516,7 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
     if (le != cudaSuccess) return le;
   } else if (!p.general) {
     { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<2, 2>, dim3(nsm), dim3(HistPipe<2, 2>::THREADS), HistPipe<2, 2>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d); }
+                                                      b.st, b.partials, d, b.io_dev, b.rows[1]); }
     if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
     { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<2, 2>, dim3(jobs * p.U * 2 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
@@ -512,7 +524,7 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
     if (le != cudaSuccess) return le;
   } else if (root_counts != 2) {
     { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<1, 5>, dim3(nsm), dim3(HistPipe<1, 5>::THREADS), HistPipe<1, 5>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d); }
+                                                      b.st, b.partials, d, b.io_dev, b.rows[1]); }
     if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
     { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<1, 5>, dim3(jobs * p.U * 1 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 
@@ -520,7 +532,7 @@ cudaError_t launch_hist_kernels(const GrowParams& p, const GrowBufs& b, const Tr
     if (le != cudaSuccess) return le;
   } else {
     { PhaseScope ph(PH_HIST, s); le = launch_pdl(k_hist<1, 4>, dim3(nsm), dim3(HistPipe<1, 4>::THREADS), HistPipe<1, 4>::SMEM, s, io.bins, rows, io.g, io.h, b.items, b.units,
-                                                      b.st, b.partials, d); }
+                                                      b.st, b.partials, d, b.io_dev, b.rows[1]); }
     if (le != cudaSuccess) return le;
     if (after_hist) cudaEventRecord(after_hist, s);
     { PhaseScope ph(PH_REDUCE, s); le = launch_pdl(k_reduce<1, 4>, dim3(jobs * p.U * 1 * RED_PARTS * igroups), dim3(RED_THREADS), 0, s, 

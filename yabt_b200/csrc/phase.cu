@@ -31,6 +31,12 @@ bool pdl_enabled() {
   return on;
 }
 
+namespace {
+thread_local bool t_capturing_level_loop = false;
+}
+bool capturing_level_loop() { return t_capturing_level_loop; }
+void set_capturing_level_loop(bool on) { t_capturing_level_loop = on; }
+
 static const char* const kPhaseNames[PH_COUNT] = {
     "begin", "hist", "reduce", "exchange", "scan", "finalize", "partition", "plan",
     "finish", "leafnet", "interaction", "update", "binning", "collective", "other"};
@@ -50,8 +56,15 @@ PhasePool& pool() {
 }
 }  // namespace
 
+bool phase_timing_on() {
+  PhasePool& p = pool();
+  std::lock_guard<std::mutex> lk(p.mu);
+  return p.on;
+}
+
 PhaseScope::PhaseScope(int ph, cudaStream_t s) : slot_(-1), s_(s) {
   nvtxRangePushA(kPhaseNames[ph < 0 || ph >= PH_COUNT ? PH_OTHER : ph]);
+  if (capturing_level_loop()) return;        // no event nodes inside a graph loop
   PhasePool& p = pool();
   std::lock_guard<std::mutex> lk(p.mu);
   if (!p.on || p.used >= (int)p.phase.size()) return;

@@ -110,6 +110,9 @@ class Grower:
         a.min_samples_leaf = int(params.min_samples_leaf)
         for k in ("feature", "threshold", "left", "right", "value", "gate_scale", "leaf_of_row", "meta"):
             setattr(a, k, out[k].data_ptr())
+        # the struct holds raw device addresses: keep every tensor behind them
+        # alive for as long as the struct is (a caller may pass temporaries)
+        a._keep = (bins, grad, hess, edges, out, feature_mask, interaction, bins_fm, root_rows)
         return a
 
     def grow(self, a: _lib.TreeArgs, stream=None, bestfirst: bool = False, f64: bool = False) -> None:
@@ -135,6 +138,16 @@ class Grower:
         once the tree is complete (off: every level is queued, no host waits)."""
         _lib.check(self.lib.yabt_grower_set_level_wait(self.h, 1 if wait else 0), "yabt_grower_set_level_wait")
         self.level_wait = bool(wait)
+
+    def set_level_loop(self, on: bool) -> None:
+        """Device-side level loop (a CUDA graph with a WHILE node) for the
+        levels past level_loop_start(); on by default."""
+        _lib.check(self.lib.yabt_grower_set_level_loop(self.h, 1 if on else 0), "yabt_grower_set_level_loop")
+
+    def level_loop_start(self) -> int:
+        """First level grown inside the device-side level loop, or -1 when the
+        loop is off or would not pay for this grower."""
+        return int(self.lib.yabt_grower_level_loop_start(self.h))
 
     def set_timing(self, max_launches: int) -> None:
         """Record CUDA events around up to max_launches histogram launches."""
