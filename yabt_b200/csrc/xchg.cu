@@ -19,6 +19,7 @@
 // buffer holds the full sums. Every wait is bounded: on timeout the kernel
 // sets an error bit in the grower state and returns.
 #include <cstdint>
+#include <cstddef>
 #include <cstring>
 
 #include "../../include/yabt_b200.h"
@@ -179,6 +180,8 @@ struct XRec {
   long long pad[3];
 };
 static_assert(sizeof(XRec) == 64, "exchange record");
+static_assert(sizeof(NodeBest) % 8 == 0 && alignof(NodeBest) == 8 && offsetof(XRec, nb) % 8 == 0,
+              "records are copied in 8-byte words");
 
 __global__ void __launch_bounds__(256) k_xgather(XGArgs a, GrowState* st, unsigned long long* node_key,
                                                  NodeBest* best) {
@@ -215,11 +218,13 @@ __global__ void __launch_bounds__(256) k_xgather(XGArgs a, GrowState* st, unsign
     }
     const int f = (int)(0xffffffffu - (unsigned)(bk & 0xffffffffULL));
     if (bq != a.rank && f >= 0 && f < a.F) {
+      // 8-byte words: a record's NodeBest sits 8 bytes into the record, so it
+      // is 8-byte but not 16-byte aligned
       const XRec* rq = reinterpret_cast<const XRec*>(a.buf[bq] + XCHG_HEADER + a.rec_off) + m;
-      const longlong2* src = reinterpret_cast<const longlong2*>(&rq->nb);
-      longlong2* dst = reinterpret_cast<longlong2*>(&best[(size_t)m * a.F + f]);
-      dst[0] = __ldcv(src);
-      dst[1] = __ldcv(src + 1);
+      const unsigned long long* src = reinterpret_cast<const unsigned long long*>(&rq->nb);
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(&best[(size_t)m * a.F + f]);
+#pragma unroll
+      for (int k = 0; k < (int)(sizeof(NodeBest) / 8); ++k) dst[k] = __ldcv(src + k);
     }
     node_key[m] = bk;
   }
