@@ -494,8 +494,8 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
   const int* src = d == 0 ? io.root_rows : b.rows[cur];   // nullptr: identity
   int* dst = b.rows[nxt];
   __shared__ int s_tile, s_excl;
-  __shared__ int s_wc[8][PART_THREADS / 32];
-  __shared__ int s_wpre[8][PART_THREADS / 32];
+  __shared__ int s_wc[PART_RPT][PART_THREADS / 32];
+  __shared__ int s_wpre[PART_RPT][PART_THREADS / 32];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   constexpr int NW = PART_THREADS / 32;
   for (;;) {
@@ -507,10 +507,10 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     const int m = T.pos;
     const int B = b.seg_begin[cur][m], cnt = b.seg_count[cur][m];
     const int pr = b.split_pair[m];
-    int row[8];
-    bool ok[8];
+    int row[PART_RPT];
+    bool ok[PART_RPT];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < PART_RPT; ++i) {
       const int idx = T.begin + i * PART_THREADS + t;
       ok[i] = idx < T.end;
       row[i] = ok[i] ? (src ? src[idx] : idx) : 0;
@@ -522,7 +522,7 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     }
     if (pr < 0) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < PART_RPT; ++i) {
         if (!ok[i]) continue;
         const int idx = T.begin + i * PART_THREADS + t;
         b.fin[idx] = row[i];
@@ -537,10 +537,10 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     const FeatAddr fa = b.faddr[f];
     const uint8_t* col = io.bins_fm ? io.bins_fm + (size_t)f * p.n : io.bins + fa.off + fa.pos;
     const size_t stride = io.bins_fm ? 1 : (size_t)fa.width;
-    bool lf[8];
-    unsigned bal[8];
+    bool lf[PART_RPT];
+    unsigned bal[PART_RPT];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < PART_RPT; ++i) {
       lf[i] = ok[i] && (unsigned)__ldg(col + (size_t)row[i] * stride) <= thr;
       bal[i] = __ballot_sync(0xffffffffu, lf[i]);
       if (lane == 0) s_wc[i][warp] = __popc(bal[i]);
@@ -551,7 +551,7 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     if (warp == 0) {
       int run = 0;
       if (t == 0) {
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < PART_RPT; ++i)
           for (int w = 0; w < NW; ++w) { s_wpre[i][w] = run; run += s_wc[i][w]; }
       }
       const unsigned Lt = (unsigned)__shfl_sync(0xffffffffu, run, 0);
@@ -607,7 +607,7 @@ k_partition(GrowParams p, GrowBufs b, TreeIO io, int level_gate) {
     const int off_in_node = T.begin - B;
     const unsigned lt_mask = (1u << lane) - 1u;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < PART_RPT; ++i) {
       if (!ok[i]) continue;
       const int rl = s_wpre[i][warp] + __popc(bal[i] & lt_mask);   // left rank in tile
       int pos;

@@ -8,7 +8,9 @@ namespace yabt {
 
 constexpr int HIST_THREADS = 1024;    // k_hist block size (one block per SM)
 constexpr int PART_TILE = 4096;       // rows per partition tile
-constexpr int PART_THREADS = 512;     // 8 rows per thread
+constexpr int PART_THREADS = 512;
+constexpr int PART_RPT = PART_TILE / PART_THREADS;   // rows per thread (8)
+static_assert(PART_TILE % PART_THREADS == 0, "partition tile");
 constexpr int ITEM_TARGET = 4 * YABT_SMS_HINT;  // histogram work items per level (target)
 constexpr int CHUNK_MIN = 4096;       // rows per histogram item (lower bound)
 constexpr int CHUNK_MAX = 65536;      // rows per item and per flushed segment (u32 limb overflow bound)
