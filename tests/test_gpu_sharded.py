@@ -161,3 +161,55 @@ def test_two_ranks_nccl_two_fits():
     exchange buffers (the exchange sequence numbers carry on) and grows the
     same model as the first."""
     _compare(_run_sharded("nccl", True, levelwise=True, fits=2), _single(True, levelwise=True), True)
+
+
+def _worker_classifier(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from yabt_b200 import YABTClassifier
+        from yabt_b200.distributed import ShardComm
+        X, y = _data()
+        yb = np.where(y > 0, 3.0, -1.0).astype(np.float32)       # labels other than 0 / 1
+        off = sum(SPLIT[:rank])
+        sl = slice(off, off + SPLIT[rank])
+        comm = ShardComm()
+        est = YABTClassifier(n_estimators=4, max_leaves=31, learning_rate=0.3, neural_leaves=False)
+        est.fit(X[sl], yb[sl], comm=comm)
+        torch.cuda.synchronize()
+        q.put((rank, dict(classes=est.classes_.tolist(), proba=est.predict_proba(X[:1500]))))
+        comm.release_exchange()
+    except Exception as e:
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_nccl_classifier():
+    """The estimator's own sharded fit (YABTClassifier.fit(..., comm=)): the
+    class labels are gathered over NCCL from host arrays, and the sharded model
+    equals the single-GPU one (no leaf models: bit for bit)."""
+    from yabt_b200 import YABTClassifier
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_worker_classifier, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    X, y = _data()
+    yb = np.where(y > 0, 3.0, -1.0).astype(np.float32)
+    ref = YABTClassifier(n_estimators=4, max_leaves=31, learning_rate=0.3, neural_leaves=False).fit(X, yb)
+    for r in range(2):
+        assert isinstance(res[r], dict), res[r]
+        assert res[r]["classes"] == [-1.0, 3.0]
+        np.testing.assert_array_equal(res[r]["proba"], ref.predict_proba(X[:1500]))

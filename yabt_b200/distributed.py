@@ -137,7 +137,9 @@ class ShardComm:
         F, m = x.shape
         sizes = self.int_values(m)
         mx = max(max(sizes), 1)
-        dev = x.device if self.on_device else torch.device("cpu")
+        # the collective runs where the backend works (NCCL: this rank's GPU,
+        # even for a host tensor such as an estimator's class labels)
+        dev = torch.device("cuda", torch.cuda.current_device()) if self.on_device else torch.device("cpu")
         pad = torch.zeros(F, mx, dtype=x.dtype, device=dev)
         pad[:, :m] = x.to(dev)
         parts = [torch.empty_like(pad) for _ in range(self.world)]
