@@ -147,3 +147,36 @@ def test_probe_rejects_bad_arguments_before_any_device_call(lib):
     for limbs in (1, 2, 3, 5):
         assert lib.yabt_probe_shared_red(limbs, 0, None, None, ctypes.byref(ms), ctypes.byref(upd)) == 1
         assert lib.yabt_probe_shared_red(limbs, 1, None, None, None, None) == 1
+
+
+def test_level_loop_start_rule(lib):
+    """Host-only: the first level of the device-side level loop. The loop runs
+    only without level wait, with at least 8 pairs, and when two or more
+    levels remain after its first level, which is the first level whose job
+    bound 2^(d-1) reaches max_pairs = max_leaves - 1 (at least 4)."""
+    def start(leaves, depth, wait=0, loop=1):
+        g = ctypes.c_void_p()
+        assert lib.yabt_grower_create(1000, 8, leaves, depth, 0, ctypes.byref(g)) == 0
+        try:
+            assert lib.yabt_grower_set_level_wait(g, wait) == 0
+            assert lib.yabt_grower_set_level_loop(g, loop) == 0
+            return int(lib.yabt_grower_level_loop_start(g))
+        finally:
+            lib.yabt_grower_destroy(g)
+
+    def rule(leaves, depth):
+        pairs = leaves - 1
+        levels = max(1, min(depth, leaves - 1))
+        if pairs < 8:
+            return -1
+        L = 4
+        while (1 << (L - 1)) < pairs:
+            L += 1
+        return L if levels - L >= 2 else -1
+
+    for leaves, depth in ((31, 64), (63, 64), (127, 64), (255, 10), (255, 64), (9, 64), (8, 64), (31, 7), (31, 8),
+                          (24, 64), (1000, 12)):
+        assert start(leaves, depth) == rule(leaves, depth), (leaves, depth)
+    assert start(31, 64) == 6 and start(255, 10) == -1
+    assert start(31, 64, wait=1) == -1
+    assert start(31, 64, loop=0) == -1
