@@ -481,7 +481,7 @@ def run_ours(args):
         # trees whose deeper levels run in the device-side level loop (a CUDA
         # graph) cannot carry events around each histogram launch; their k_hist
         # time comes from the phase pass instead
-        loop = grower.level_loop_start() > 0 and world == 1
+        loop = grower.level_loop_start() > 0
         marks["loop"] = loop
         if t == 0 and not loop:
             grower.set_timing(K * grower.levels)      # create the event pool early

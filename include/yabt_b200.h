@@ -347,6 +347,18 @@ int yabt_grow_xreduce_sliced(yabt_grower* g, void* const* bufs, int rank, int nr
 int yabt_grow_xgather(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
                       long long rec_offset, void* stream);
 long long yabt_grow_xgather_bytes(const yabt_grower* g);
+/* The device-side level loop of a feature-sliced sharded tree (no reference
+ * counterpart; the reference's level loop is a host while loop,
+ * yabt/tree.py:484-625): after the caller grew levels 0 .. L-1 with the calls
+ * above (L = yabt_grower_level_loop_start), one CUDA graph runs the remaining
+ * levels, each a histogram, reduce-scatter, slice scan, best-split gather and
+ * choice, while the tree is active. The loop's level d uses exchange epochs
+ * epoch0 + 2 (d - L) (reduce-scatter) and that + 1 (gather), so the caller
+ * reserves 2 (levels - L) epochs from epoch0 on every rank alike. *used is 0
+ * (nothing launched: the caller grows the levels itself) when the loop is off
+ * or histogram / phase timing records events.                              */
+int yabt_grow_level_loop_sharded(yabt_grower* g, const yabt_tree_args* a, void* const* bufs, int rank, int nranks,
+                                 long long rec_offset, unsigned epoch0, int* used, void* stream);
 void* yabt_grow_small_ptr(yabt_grower* g);
 long long yabt_grow_small_count(const yabt_grower* g, int level);
 /* Per-leaf row ranges of the last tree (device arrays inside the workspace):

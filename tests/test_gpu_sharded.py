@@ -213,3 +213,90 @@ def test_two_ranks_nccl_classifier():
         assert isinstance(res[r], dict), res[r]
         assert res[r]["classes"] == [-1.0, 3.0]
         np.testing.assert_array_equal(res[r]["proba"], ref.predict_proba(X[:1500]))
+
+
+def _chain(n=8192, F=12, seed=3, chain=10):
+    """Nested target (the level-loop tests' data): trees grow about `chain`
+    levels deep, past the device-side loop's first level."""
+    rng = np.random.default_rng(seed)
+    X = rng.normal(size=(n, F)).astype(np.float32)
+    on = np.ones(n, dtype=bool)
+    y = np.zeros(n, dtype=np.float32)
+    for k in range(chain):
+        on &= X[:, k] > -0.3
+        y += 2.0 * on
+    return X, y
+
+
+def _loop_params():
+    from yabt_b200.boosting import BoostParams
+    return BoostParams(n_estimators=4, max_leaves=31, max_depth=64, learning_rate=0.3, neural_leaves=False,
+                       min_samples_leaf=5, levelwise=True)
+
+
+def _worker_loop(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from yabt_b200 import _lib
+        from yabt_b200.boosting import Booster, MSELoss
+        from yabt_b200.distributed import ShardComm
+        lib = _lib.load()
+        X, y = _chain()
+        off = sum(SPLIT[:rank])
+        sl = slice(off, off + SPLIT[rank])
+        comm = ShardComm()
+        out = {}
+        for loop in (True, False):
+            torch.cuda.synchronize()
+            _lib.check(lib.yabt_launch_count_device_reset(_lib.stream_ptr()), "reset")
+            b = Booster(_loop_params(), MSELoss())
+            b._level_loop = loop
+            b.fit(X[sl], y[sl], comm=comm)
+            torch.cuda.synchronize()
+            out[loop] = dict(trees=[{k: getattr(t, k).cpu().numpy() for k in ("feature", "threshold", "left",
+                                                                              "right", "value")} for t in b.trees],
+                             pred=b.predict_margin(X[:2000]), dev=int(lib.yabt_launch_count_device()),
+                             start=b.grower_.level_loop_start())
+        q.put((rank, out))
+        comm.release_exchange()
+    except Exception as e:
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_nccl_level_loop():
+    """Sharded feature-sliced trees with their deeper levels in the device-side
+    level loop (reduce-scatter and best-split gather inside the loop's body):
+    the same bits as the same fit with every level driven by the host, and as
+    a single-GPU fit; the loop ran on every rank."""
+    from yabt_b200.boosting import Booster, MSELoss
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_worker_loop, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    X, y = _chain()
+    ref = Booster(_loop_params(), MSELoss()).fit(X, y)
+    for r in range(2):
+        assert isinstance(res[r], dict), res[r]
+        on, off = res[r][True], res[r][False]
+        assert on["start"] > 0
+        assert on["dev"] >= 9 and off["dev"] == 0, (on["dev"], off["dev"])
+        for t, (a, b, c) in enumerate(zip(on["trees"], off["trees"], ref.trees)):
+            for k in ("feature", "threshold", "left", "right", "value"):
+                np.testing.assert_array_equal(a[k], b[k], err_msg=f"rank {r} tree {t} {k}")
+                np.testing.assert_array_equal(a[k], getattr(c, k).cpu().numpy(), err_msg=f"rank {r} tree {t} {k}")
+        np.testing.assert_array_equal(on["pred"], ref.predict_margin(X[:2000]))

@@ -134,6 +134,7 @@ SIGNATURES = [
     ("yabt_grow_xreduce_sliced", c_int, [c_vp, ctypes.POINTER(c_vp), c_int, c_int, c_int, ctypes.c_uint, c_vp]),
     ("yabt_grow_xgather", c_int, [c_vp, ctypes.POINTER(c_vp), c_int, c_int, c_int, ctypes.c_uint, c_ll, c_vp]),
     ("yabt_grow_xgather_bytes", c_ll, [c_vp]),
+    ("yabt_grow_level_loop_sharded", c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_ll, ctypes.c_uint, c_vp, c_vp]),
     ("yabt_grow_small_count", c_ll, [c_vp, c_int]),
     ("yabt_grow_leaf_rows", c_int, [c_vp] + [ctypes.POINTER(c_vp)] * 6),
     ("yabt_transpose", c_int, [c_vp, c_ll, c_int, c_vp, c_vp]),

@@ -47,9 +47,7 @@ cudaError_t launch_mt_values(const GrowParams&, const GrowBufs&, const MtBufs&, 
 cudaError_t launch_mt_update(const int*, const float*, int, long long, float*, const float*, float*, int, cudaStream_t);
 cudaError_t set_hist_smem_attrs();
 cudaError_t launch_unpack_counts(const GrowParams&, const GrowBufs&, long long*, cudaStream_t);
-cudaError_t launch_level_loop_body(const GrowParams&, const GrowBufs&, const TreeIO&, int, cudaGraphConditionalHandle,
-                                   cudaStream_t);
-cudaError_t launch_level_loop_cond(const GrowParams&, const GrowBufs&, cudaGraphConditionalHandle, cudaStream_t);
+cudaError_t launch_level_loop_cond(const GrowParams&, const GrowBufs&, cudaGraphConditionalHandle, int, cudaStream_t);
 cudaError_t loop_launches_reset(cudaStream_t);
 cudaError_t loop_launches_read(long long*);
 
@@ -151,6 +149,15 @@ int yabt_pack_bins(const uint8_t* plain, long long n, int F, uint8_t* tiled, voi
 }  // extern "C"
 
 // ---------------------------------------------------------------- grower
+// The feature-sliced exchange of a sharded device-side level loop (all zero
+// for a single-GPU loop).
+struct LoopXchg {
+  int on;
+  int rank, nranks, first;
+  long long rec_offset;
+  void* bufs[8];
+};
+
 struct yabt_grower {
   GrowParams p;
   GrowBufs b;
@@ -187,6 +194,7 @@ struct yabt_grower {
   cudaStream_t loop_cap = nullptr;         // capture stream
   GrowParams loop_p;
   GrowBufs loop_b;
+  LoopXchg loop_x = {};                    // the exchange the graph was captured with (sharded trees)
 };
 
 static constexpr int LEVEL_SLOTS = 8, LEVEL_LOOKAHEAD = 3;
@@ -535,19 +543,26 @@ static int level_loop_first(const yabt_grower* g) {
 }
 
 // Captures the loop graph: [condition] -> WHILE { level at the state's level;
-// condition }. Returns a CUDA error; on failure nothing is kept.
-static cudaError_t build_level_loop(yabt_grower* g, const TreeIO& io) {
+// condition }. With x.on the level also reduce-scatters its histograms and
+// gathers the best splits (the sharded feature-sliced level). Returns a YABT
+// status; on failure nothing is kept.
+static int build_level_loop(yabt_grower* g, const TreeIO& io, const LoopXchg& x) {
   if (g->loop_exec) { cudaGraphExecDestroy(g->loop_exec); g->loop_exec = nullptr; }
   cudaError_t e = cudaSuccess;
-  if (!g->loop_cap && (e = cudaStreamCreateWithFlags(&g->loop_cap, cudaStreamNonBlocking)) != cudaSuccess) return e;
+  auto cuda_fail = [&](cudaError_t err) {
+    set_error("capturing the level-loop graph failed: %s", cudaGetErrorString(err));
+    return YABT_ERR_CUDA;
+  };
+  if (!g->loop_cap && (e = cudaStreamCreateWithFlags(&g->loop_cap, cudaStreamNonBlocking)) != cudaSuccess)
+    return cuda_fail(e);
   cudaGraph_t graph = nullptr;
-  if ((e = cudaGraphCreate(&graph, 0)) != cudaSuccess) return e;
+  if ((e = cudaGraphCreate(&graph, 0)) != cudaSuccess) return cuda_fail(e);
   cudaGraphConditionalHandle h;
   cudaGraphNode_t pre = nullptr;
   size_t npre = 1;
   cudaGraphNodeParams cp = {};
   bool capturing = false;
-  auto fail = [&](cudaError_t err) {
+  auto fail = [&](int rc) {
     if (capturing) {
       cudaGraph_t partial = nullptr;
       cudaStreamEndCapture(g->loop_cap, &partial);
@@ -555,40 +570,103 @@ static cudaError_t build_level_loop(yabt_grower* g, const TreeIO& io) {
     set_capturing_level_loop(false);
     cudaGraphDestroy(graph);
     cudaGetLastError();
-    return err;
+    return rc;
   };
-  if ((e = cudaGraphConditionalHandleCreate(&h, graph, 0, 0)) != cudaSuccess) return fail(e);
+  auto fail_cuda = [&](cudaError_t err) { return fail(cuda_fail(err)); };
+  if ((e = cudaGraphConditionalHandleCreate(&h, graph, 0, 0)) != cudaSuccess) return fail_cuda(e);
   set_capturing_level_loop(true);
   if ((e = cudaStreamBeginCaptureToGraph(g->loop_cap, graph, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed)) !=
       cudaSuccess)
-    return fail(e);
+    return fail_cuda(e);
   capturing = true;
-  if ((e = launch_level_loop_cond(g->p, g->b, h, g->loop_cap)) != cudaSuccess) return fail(e);
+  if ((e = launch_level_loop_cond(g->p, g->b, h, 0, g->loop_cap)) != cudaSuccess) return fail_cuda(e);
   capturing = false;
-  if ((e = cudaStreamEndCapture(g->loop_cap, &graph)) != cudaSuccess) return fail(e);
+  if ((e = cudaStreamEndCapture(g->loop_cap, &graph)) != cudaSuccess) return fail_cuda(e);
   if ((e = cudaGraphGetNodes(graph, &pre, &npre)) != cudaSuccess || npre != 1)
-    return fail(e != cudaSuccess ? e : cudaErrorInvalidValue);
+    return fail_cuda(e != cudaSuccess ? e : cudaErrorInvalidValue);
   cp.type = cudaGraphNodeTypeConditional;
   cp.conditional.handle = h;
   cp.conditional.type = cudaGraphCondTypeWhile;
   cp.conditional.size = 1;
   cudaGraphNode_t cond = nullptr;
-  if ((e = cudaGraphAddNode(&cond, graph, &pre, 1, &cp)) != cudaSuccess) return fail(e);
+  if ((e = cudaGraphAddNode(&cond, graph, &pre, 1, &cp)) != cudaSuccess) return fail_cuda(e);
   cudaGraph_t body = cp.conditional.phGraph_out[0];
   if ((e = cudaStreamBeginCaptureToGraph(g->loop_cap, body, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed)) !=
       cudaSuccess)
-    return fail(e);
+    return fail_cuda(e);
   capturing = true;
-  if ((e = launch_level_loop_body(g->p, g->b, io, g->nsm, h, g->loop_cap)) != cudaSuccess) return fail(e);
+  // one level at the state's level (LEVEL_DYN launches, grids sized for max_pairs jobs)
+  if ((e = launch_level_hist(g->p, g->b, io, LEVEL_DYN, g->nsm, g->loop_cap, nullptr, 0)) != cudaSuccess)
+    return fail_cuda(e);
+  if (x.on) {
+    int rc = xchg_sliced_launch(g, x.bufs, x.rank, x.nranks, LEVEL_DYN, 0u, x.first, g->loop_cap);
+    if (rc) return fail(rc);
+    if ((e = launch_level_scan(g->p, g->b, io, LEVEL_DYN, g->nsm, g->loop_cap)) != cudaSuccess) return fail_cuda(e);
+    rc = xchg_gather_launch(g, x.bufs, x.rank, x.nranks, LEVEL_DYN, 0u, x.rec_offset, x.first, g->loop_cap);
+    if (rc) return fail(rc);
+    if ((e = launch_level_choose(g->p, g->b, io, LEVEL_DYN, g->nsm, g->loop_cap)) != cudaSuccess) return fail_cuda(e);
+  } else if ((e = launch_level_split(g->p, g->b, io, LEVEL_DYN, g->nsm, g->loop_cap)) != cudaSuccess) {
+    return fail_cuda(e);
+  }
+  const int body_kernels = x.on ? LEVEL_LOOP_BODY_KERNELS_SHARDED : LEVEL_LOOP_BODY_KERNELS;
+  if ((e = launch_level_loop_cond(g->p, g->b, h, body_kernels, g->loop_cap)) != cudaSuccess) return fail_cuda(e);
   capturing = false;
-  if ((e = cudaStreamEndCapture(g->loop_cap, &body)) != cudaSuccess) return fail(e);
+  if ((e = cudaStreamEndCapture(g->loop_cap, &body)) != cudaSuccess) return fail_cuda(e);
   set_capturing_level_loop(false);
   e = cudaGraphInstantiate(&g->loop_exec, graph, 0);
   cudaGraphDestroy(graph);
-  if (e != cudaSuccess) { g->loop_exec = nullptr; cudaGetLastError(); return e; }
+  if (e != cudaSuccess) { g->loop_exec = nullptr; cudaGetLastError(); return cuda_fail(e); }
   memcpy(&g->loop_p, &g->p, sizeof(GrowParams));
   memcpy(&g->loop_b, &g->b, sizeof(GrowBufs));
-  return cudaSuccess;
+  memcpy(&g->loop_x, &x, sizeof(LoopXchg));
+  return YABT_OK;
+}
+
+// Whether a tree's levels from level_loop_first() on can run in the loop graph
+// now: no event timing (event nodes cannot sit in a conditional body) and no
+// capture of the caller's stream in progress.
+static bool level_loop_usable(yabt_grower* g, cudaStream_t s) {
+  cudaStreamCaptureStatus cst = cudaStreamCaptureStatusNone;
+  const bool ok = level_loop_first(g) > 0 && !g->timing && !phase_timing_on() &&
+                  cudaStreamIsCapturing(s, &cst) == cudaSuccess && cst == cudaStreamCaptureStatusNone;
+  cudaGetLastError();
+  return ok;
+}
+
+// Launches the loop graph, capturing it first when it is missing or was
+// captured with other parameters, buffers or exchange.
+static int launch_level_loop(yabt_grower* g, const yabt_tree_args* a, const LoopXchg& x, cudaStream_t s) {
+  if (!g->loop_exec || memcmp(&g->loop_p, &g->p, sizeof(GrowParams)) ||
+      memcmp(&g->loop_b, &g->b, sizeof(GrowBufs)) || memcmp(&g->loop_x, &x, sizeof(LoopXchg))) {
+    TreeIO io;
+    int rc = fill_io(g, a, &io);
+    if (rc) return rc;
+    if ((rc = build_level_loop(g, io, x))) return rc;
+  }
+  CUDA_TRY(cudaGraphLaunch(g->loop_exec, s));
+  count_launches(1);                       // the condition before the loop; the loop counts on the device
+  return YABT_OK;
+}
+
+int yabt_grow_level_loop_sharded(yabt_grower* g, const yabt_tree_args* a, void* const* bufs, int rank, int nranks,
+                                 long long rec_offset, unsigned epoch0, int* used, void* stream) {
+  if (!g || !a || !bufs || !used || nranks < 2 || nranks > 8 || rank < 0 || rank >= nranks) {
+    set_error("yabt_grow_level_loop_sharded: bad arguments (2 to 8 ranks)");
+    return YABT_ERR_ARG;
+  }
+  *used = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  TreeIO io;
+  int rc = fill_io(g, a, &io);               // also refreshes the per-call parameters
+  if (rc) return rc;
+  if (!level_loop_usable(g, s)) return YABT_OK;
+  LoopXchg x = {};
+  x.on = 1; x.rank = rank; x.nranks = nranks; x.first = level_loop_first(g); x.rec_offset = rec_offset;
+  for (int q = 0; q < nranks; ++q) x.bufs[q] = bufs[q];
+  if ((rc = xchg_set_loop_epoch(g, epoch0, s))) return rc;
+  if ((rc = launch_level_loop(g, a, x, s))) return rc;
+  *used = 1;
+  return YABT_OK;
 }
 
 int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
@@ -596,29 +674,16 @@ int yabt_grow_tree(yabt_grower* g, const yabt_tree_args* a, void* stream) {
   if ((rc = yabt_grow_begin(g, a, stream))) return rc;
   if ((rc = yabt_grow_init(g, a, stream))) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  const int L = level_loop_first(g);
-  cudaStreamCaptureStatus cst = cudaStreamCaptureStatusNone;
-  if (L > 0 && !g->timing && !phase_timing_on() && cudaStreamIsCapturing(s, &cst) == cudaSuccess &&
-      cst == cudaStreamCaptureStatusNone) {
+  if (level_loop_usable(g, s)) {
+    const int L = level_loop_first(g);
     for (int d = 0; d < L; ++d) {
       if ((rc = yabt_grow_hist(g, a, d, stream))) return rc;
       if ((rc = yabt_grow_split(g, a, d, stream))) return rc;
     }
-    if (!g->loop_exec || memcmp(&g->loop_p, &g->p, sizeof(GrowParams)) ||
-        memcmp(&g->loop_b, &g->b, sizeof(GrowBufs))) {
-      TreeIO io;
-      if ((rc = fill_io(g, a, &io))) return rc;
-      const cudaError_t e = build_level_loop(g, io);
-      if (e != cudaSuccess) {
-        set_error("yabt_grow_tree: capturing the level-loop graph failed: %s", cudaGetErrorString(e));
-        return YABT_ERR_CUDA;
-      }
-    }
-    CUDA_TRY(cudaGraphLaunch(g->loop_exec, s));
-    count_launches(1);                       // the condition before the loop; the loop counts on the device
+    const LoopXchg none = {};
+    if ((rc = launch_level_loop(g, a, none, s))) return rc;
     return yabt_grow_end(g, a, stream);
   }
-  cudaGetLastError();
   if (!g->host_state) {
     CUDA_TRY(cudaHostAlloc((void**)&g->host_state, sizeof(int) * 4 * LEVEL_SLOTS, cudaHostAllocDefault));
     for (auto& e : g->lvl_ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));

@@ -1414,20 +1414,11 @@ cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const Tree
 cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d, int nsm,
                                cudaStream_t s);
 
-// The body of the loop: one level at the level the device state is at
-// (LEVEL_DYN launches, grids sized for max_pairs jobs), then the condition.
-cudaError_t launch_level_loop_body(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int nsm,
-                                   cudaGraphConditionalHandle h, cudaStream_t s) {
-  cudaError_t e = launch_level_hist(p, b, io, LEVEL_DYN, nsm, s, nullptr, 0);
-  if (e == cudaSuccess) e = launch_level_split(p, b, io, LEVEL_DYN, nsm, s);
-  if (e != cudaSuccess) return e;
-  k_level_loop_cond<<<1, 1, 0, s>>>(b.st, p.levels_max, h, LEVEL_LOOP_BODY_KERNELS);
-  return cudaGetLastError();
-}
-
+// The condition kernel of a loop: before the loop (body_kernels 0) or as the
+// body's last kernel (body_kernels = the body's kernels, itself included).
 cudaError_t launch_level_loop_cond(const GrowParams& p, const GrowBufs& b, cudaGraphConditionalHandle h,
-                                   cudaStream_t s) {
-  k_level_loop_cond<<<1, 1, 0, s>>>(b.st, p.levels_max, h, 0);
+                                   int body_kernels, cudaStream_t s) {
+  k_level_loop_cond<<<1, 1, 0, s>>>(b.st, p.levels_max, h, body_kernels);
   return cudaGetLastError();
 }
 

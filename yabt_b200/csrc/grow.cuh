@@ -24,8 +24,10 @@ __host__ __device__ constexpr long long small_job_words(int C, int F) {
 }
 constexpr int SCAN_WARPS = 8;         // k_scan: one warp per feature
 // kernels of one pass of a device-side level loop: k_hist, k_reduce, k_scan,
-// k_finalize, k_partition, k_plan and the loop condition
+// k_finalize, k_partition, k_plan and the loop condition; a sharded loop adds
+// the reduce-scatter and the best-split gather
 constexpr int LEVEL_LOOP_BODY_KERNELS = 7;
+constexpr int LEVEL_LOOP_BODY_KERNELS_SHARDED = 9;
 constexpr int FIN_SMEM_NODES = 2048;  // k_finalize: active nodes whose gains / tile prefixes fit shared memory
 
 // leaf row sources
@@ -115,6 +117,7 @@ struct GrowState {
   long long acc_child_rows;  // smaller-child rows of deeper levels,
   long long acc_launches;    // histogram levels that did work
   unsigned xerr;             // persistent error bits of the per-tree peer all-reduces (not reset per tree)
+  unsigned xepoch0;          // first exchange epoch of the tree's device-side level loop (sharded trees)
   long long n_rows;          // rows of the bin matrix (bounds-checked build)
 };
 
@@ -228,6 +231,13 @@ struct MtBufs {
 // the device state of a bound grower (C ABI handle), or nullptr
 GrowState* grower_state(struct yabt_grower* g);
 int grower_slice(struct yabt_grower* g, int* F, int* C, int* f_lo, int* f_hi);   // 0 if bound
+// feature-sliced exchange launchers (xchg.cu); level may be LEVEL_DYN inside a
+// device-side level loop whose first level is loop_first
+int xchg_sliced_launch(struct yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                       int loop_first, cudaStream_t s);
+int xchg_gather_launch(struct yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                       long long rec_offset, int loop_first, cudaStream_t s);
+int xchg_set_loop_epoch(struct yabt_grower* g, unsigned epoch0, cudaStream_t s);
 void grower_best_bufs(struct yabt_grower* g, unsigned long long** node_key, NodeBest** best);
 int grower_maxa(const struct yabt_grower* g);
 

@@ -48,7 +48,15 @@ struct XArgs {
   long long per_job;                      // int64 words per job
   int sliced;                             // 1: reduce-scatter of this rank's feature slice only
   int F, C;                               // features, histogram channels (the slice's word ranges)
+  int loop_first;                         // level == LEVEL_DYN: first level of the device-side loop
 };
+
+// Exchange epochs of a device-side level loop: the host reserves two per loop
+// level starting at st->xepoch0 (every rank the same numbers), the
+// reduce-scatter of level d uses xepoch0 + 2 (d - first), the gather one more.
+__device__ __forceinline__ unsigned loop_epoch(const GrowState* st, int level, int first, unsigned k) {
+  return st->xepoch0 + 2u * (unsigned)(level - first) + k;
+}
 
 // Feature slice of rank r of N: [F r / N, F (r + 1) / N) (the same rule as
 // yabt_b200.distributed's feature_slice).
@@ -77,6 +85,11 @@ __device__ bool wait_all(const unsigned* flags, int nranks, unsigned epoch) {
 
 __global__ void __launch_bounds__(512) k_xreduce(XArgs a, GrowState* st) {
   __shared__ int s_ok, s_last;
+  if (a.level == LEVEL_DYN) {                        // inside a device-side level loop
+    a.level = st->level;
+    if (a.level < a.loop_first) return;
+    a.epoch = loop_epoch(st, a.level, a.loop_first, 0u);
+  }
   if (st->level != a.level || !st->active) return;   // the same on every rank
   const long long jobs = a.level == 0 ? 1 : st->P;
   const long long words = jobs * a.per_job;
@@ -172,6 +185,7 @@ struct XGArgs {
   int level;
   long long rec_off;                      // bytes from the data start to the records
   int F;
+  int loop_first;                         // level == LEVEL_DYN: first level of the device-side loop
 };
 
 struct XRec {
@@ -186,6 +200,11 @@ static_assert(sizeof(NodeBest) % 8 == 0 && alignof(NodeBest) == 8 && offsetof(XR
 __global__ void __launch_bounds__(256) k_xgather(XGArgs a, GrowState* st, unsigned long long* node_key,
                                                  NodeBest* best) {
   __shared__ int s_ok;
+  if (a.level == LEVEL_DYN) {                        // inside a device-side level loop
+    a.level = st->level;
+    if (a.level < a.loop_first) return;
+    a.epoch = loop_epoch(st, a.level, a.loop_first, 1u);
+  }
   if (st->level != a.level || !st->active) return;   // the same on every rank
   const int M = st->M;
   XRec* mine_rec = reinterpret_cast<XRec*>(a.buf[a.rank] + XCHG_HEADER + a.rec_off);
@@ -306,6 +325,90 @@ __global__ void __launch_bounds__(512) k_xallreduce(XAllArgs a, GrowState* st) {
 
 using namespace yabt;
 
+namespace yabt {
+
+// Launchers of the feature-sliced exchange (the C ABI below, and the capture of
+// a sharded device-side level loop in abi.cu, which passes level = LEVEL_DYN
+// and the loop's first level). They check the arguments and return a YABT
+// status.
+int xchg_sliced_launch(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                       int loop_first, cudaStream_t s) {
+  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks ||
+      (level < 0 && level != LEVEL_DYN)) {
+    set_error("yabt_grow_xreduce_sliced: bad arguments (at most %d ranks)", XR_MAX);
+    return YABT_ERR_ARG;
+  }
+  int F = 0, C = 0, flo = 0, fhi = 0;
+  if (grower_slice(g, &F, &C, &flo, &fhi) || flo != slice_lo(F, rank, nranks) || fhi != slice_lo(F, rank + 1, nranks)) {
+    set_error("yabt_grow_xreduce_sliced: the grower's feature slice must be [F r / N, F (r + 1) / N)");
+    return YABT_ERR_ARG;
+  }
+  XArgs a;
+  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
+  for (int q = 0; q < nranks; ++q)
+    if (!a.buf[q]) { set_error("yabt_grow_xreduce_sliced: missing buffer of rank %d", q); return YABT_ERR_ARG; }
+  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level;
+  a.per_job = yabt_grow_small_count(g, 0);
+  a.sliced = 1; a.F = F; a.C = C; a.loop_first = loop_first;
+  GrowState* st = grower_state(g);
+  if (!st) { set_error("yabt_grow_xreduce_sliced: grower not bound"); return YABT_ERR_ARG; }
+  int dev = 0, nsm = YABT_SMS_HINT;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  {
+    PhaseScope ph(PH_XCHG, s);
+    k_xreduce<<<nsm, 512, 0, s>>>(a, st);
+  }
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("yabt_grow_xreduce_sliced: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+int xchg_gather_launch(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
+                       long long rec_offset, int loop_first, cudaStream_t s) {
+  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks ||
+      (level < 0 && level != LEVEL_DYN) || rec_offset < 0 || (rec_offset & 255)) {
+    set_error("yabt_grow_xgather: bad arguments (at most %d ranks, 256-byte aligned record offset)", XR_MAX);
+    return YABT_ERR_ARG;
+  }
+  int F = 0, C = 0, flo = 0, fhi = 0;
+  if (grower_slice(g, &F, &C, &flo, &fhi)) { set_error("yabt_grow_xgather: grower not bound"); return YABT_ERR_ARG; }
+  XGArgs a;
+  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
+  for (int q = 0; q < nranks; ++q)
+    if (!a.buf[q]) { set_error("yabt_grow_xgather: missing buffer of rank %d", q); return YABT_ERR_ARG; }
+  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level; a.rec_off = rec_offset; a.F = F;
+  a.loop_first = loop_first;
+  GrowState* st = grower_state(g);
+  unsigned long long* key = nullptr;
+  NodeBest* best = nullptr;
+  grower_best_bufs(g, &key, &best);
+  if (!st || !key || !best) { set_error("yabt_grow_xgather: grower not bound"); return YABT_ERR_ARG; }
+  {
+    PhaseScope ph(PH_XCHG, s);
+    k_xgather<<<1, 256, 0, s>>>(a, st, key, best);
+  }
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("yabt_grow_xgather: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+__global__ void k_set_loop_epoch(GrowState* st, unsigned epoch0) { st->xepoch0 = epoch0; }
+
+// The first exchange epoch of the next device-side level loop, in stream order.
+int xchg_set_loop_epoch(yabt_grower* g, unsigned epoch0, cudaStream_t s) {
+  GrowState* st = grower_state(g);
+  if (!st) { set_error("grower not bound"); return YABT_ERR_ARG; }
+  k_set_loop_epoch<<<1, 1, 0, s>>>(st, epoch0);
+  count_launches(1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { set_error("xchg_set_loop_epoch: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
+  return YABT_OK;
+}
+
+}  // namespace yabt
+
 extern "C" {
 
 long long yabt_xchg_header_bytes(void) { return XCHG_HEADER; }
@@ -358,7 +461,7 @@ int yabt_grow_xreduce(yabt_grower* g, void* const* bufs, int rank, int nranks, i
     if (!a.buf[q]) { set_error("yabt_grow_xreduce: missing buffer of rank %d", q); return YABT_ERR_ARG; }
   a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level;
   a.per_job = yabt_grow_small_count(g, 0);
-  a.sliced = 0; a.F = 0; a.C = 0;
+  a.sliced = 0; a.F = 0; a.C = 0; a.loop_first = 0;
   GrowState* st = grower_state(g);
   if (!st) { set_error("yabt_grow_xreduce: grower not bound"); return YABT_ERR_ARG; }
   int dev = 0, nsm = YABT_SMS_HINT;
@@ -422,63 +525,14 @@ int yabt_grow_xerr(yabt_grower* g, unsigned* bits) {
 
 int yabt_grow_xreduce_sliced(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
                              void* stream) {
-  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks || level < 0) {
-    set_error("yabt_grow_xreduce_sliced: bad arguments (at most %d ranks)", XR_MAX);
-    return YABT_ERR_ARG;
-  }
-  int F = 0, C = 0, flo = 0, fhi = 0;
-  if (grower_slice(g, &F, &C, &flo, &fhi) || flo != slice_lo(F, rank, nranks) || fhi != slice_lo(F, rank + 1, nranks)) {
-    set_error("yabt_grow_xreduce_sliced: the grower's feature slice must be [F r / N, F (r + 1) / N)");
-    return YABT_ERR_ARG;
-  }
-  XArgs a;
-  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
-  for (int q = 0; q < nranks; ++q)
-    if (!a.buf[q]) { set_error("yabt_grow_xreduce_sliced: missing buffer of rank %d", q); return YABT_ERR_ARG; }
-  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level;
-  a.per_job = yabt_grow_small_count(g, 0);
-  a.sliced = 1; a.F = F; a.C = C;
-  GrowState* st = grower_state(g);
-  if (!st) { set_error("yabt_grow_xreduce_sliced: grower not bound"); return YABT_ERR_ARG; }
-  int dev = 0, nsm = YABT_SMS_HINT;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  {
-    PhaseScope ph(PH_XCHG, static_cast<cudaStream_t>(stream));
-    k_xreduce<<<nsm, 512, 0, static_cast<cudaStream_t>(stream)>>>(a, st);
-  }
-  count_launches(1);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) { set_error("yabt_grow_xreduce_sliced: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
-  return YABT_OK;
+  if (level < 0) { set_error("yabt_grow_xreduce_sliced: bad level"); return YABT_ERR_ARG; }
+  return xchg_sliced_launch(g, bufs, rank, nranks, level, epoch, 0, static_cast<cudaStream_t>(stream));
 }
 
 int yabt_grow_xgather(yabt_grower* g, void* const* bufs, int rank, int nranks, int level, unsigned epoch,
                       long long rec_offset, void* stream) {
-  if (!g || !bufs || nranks < 1 || nranks > XR_MAX || rank < 0 || rank >= nranks || level < 0 || rec_offset < 0 ||
-      (rec_offset & 255)) {
-    set_error("yabt_grow_xgather: bad arguments (at most %d ranks, 256-byte aligned record offset)", XR_MAX);
-    return YABT_ERR_ARG;
-  }
-  int F = 0, C = 0, flo = 0, fhi = 0;
-  if (grower_slice(g, &F, &C, &flo, &fhi)) { set_error("yabt_grow_xgather: grower not bound"); return YABT_ERR_ARG; }
-  XGArgs a;
-  for (int q = 0; q < XR_MAX; ++q) a.buf[q] = q < nranks ? static_cast<char*>(bufs[q]) : nullptr;
-  for (int q = 0; q < nranks; ++q)
-    if (!a.buf[q]) { set_error("yabt_grow_xgather: missing buffer of rank %d", q); return YABT_ERR_ARG; }
-  a.rank = rank; a.nranks = nranks; a.epoch = epoch; a.level = level; a.rec_off = rec_offset; a.F = F;
-  GrowState* st = grower_state(g);
-  unsigned long long* key = nullptr;
-  NodeBest* best = nullptr;
-  grower_best_bufs(g, &key, &best);
-  if (!st || !key || !best) { set_error("yabt_grow_xgather: grower not bound"); return YABT_ERR_ARG; }
-  {
-    PhaseScope ph(PH_XCHG, static_cast<cudaStream_t>(stream));
-    k_xgather<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, st, key, best);
-  }
-  count_launches(1);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) { set_error("yabt_grow_xgather: %s", cudaGetErrorString(e)); return YABT_ERR_CUDA; }
-  return YABT_OK;
+  if (level < 0) { set_error("yabt_grow_xgather: bad level"); return YABT_ERR_ARG; }
+  return xchg_gather_launch(g, bufs, rank, nranks, level, epoch, rec_offset, 0, static_cast<cudaStream_t>(stream));
 }
 
 long long yabt_grow_xgather_bytes(const yabt_grower* g) {

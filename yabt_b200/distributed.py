@@ -272,6 +272,15 @@ class ExchangeBuffers:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         return self.epoch
 
+    def reserve_epochs(self, count: int) -> int:
+        """The first of ``count`` consecutive epochs (a device-side level loop
+        numbers its exchange calls from it); no wrap-around inside the block."""
+        if self.epoch + count + 1 > 0xFFFFFFFF:
+            self.epoch = 0
+        first = self.epoch + 1
+        self.epoch += count
+        return first
+
     def release(self) -> None:
         """Collective: unmap the peers' buffers and free this rank's."""
         torch.cuda.synchronize()
@@ -331,6 +340,19 @@ class PeerExchange:
         _lib.check(self.lib.yabt_grow_xgather(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
                                               self.x.next_epoch(), self.rec_offset, _lib.stream_ptr()),
                    "yabt_grow_xgather")
+
+    def level_loop(self, a: _lib.TreeArgs) -> bool:
+        """The tree's remaining levels (from the grower's level_loop_start())
+        as one device-side loop with the sliced exchange inside it; False when
+        the loop cannot run now (the caller then drives those levels)."""
+        g = self.grower
+        first = g.level_loop_start()
+        e0 = self.x.reserve_epochs(2 * max(g.levels - first, 0))
+        used = ctypes.c_int()
+        _lib.check(self.lib.yabt_grow_level_loop_sharded(g.h, ctypes.byref(a), self.bufs, self.comm.rank,
+                                                         self.comm.world, self.rec_offset, e0, ctypes.byref(used),
+                                                         _lib.stream_ptr()), "yabt_grow_level_loop_sharded")
+        return bool(used.value)
 
     def reduce(self, level: int) -> None:
         _lib.check(self.lib.yabt_grow_xreduce(self.grower.h, self.bufs, self.comm.rank, self.comm.world, level,
@@ -415,7 +437,12 @@ def grow_tree(grower, a: _lib.TreeArgs, comm: ShardComm) -> None:
             grower._level_ring = [(torch.cuda.Event(), torch.zeros(4, dtype=torch.int32).pin_memory())
                                   for _ in range(8)]
         ring = grower._level_ring
+        # feature-sliced trees run their levels from level_loop_start() on in
+        # the device-side level loop (every rank takes the same branch)
+        loop_from = grower.level_loop_start() if xchg.sliced else -1
         for d in range(grower.levels):
+            if d == loop_from and xchg.level_loop(a):
+                break
             _lib.check(lib.yabt_grow_hist(h, ref, d, s), "yabt_grow_hist")
             if xchg.sliced:
                 xchg.reduce_sliced(d)
