@@ -1409,11 +1409,6 @@ __global__ void k_level_loop_cond(const GrowState* __restrict__ st, int levels_m
   if (body_kernels > 0) atomicAdd(&g_loop_launches, (unsigned long long)body_kernels);
 }
 
-cudaError_t launch_level_hist(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d, int nsm,
-                              cudaStream_t s, cudaEvent_t after_hist, int root_counts);
-cudaError_t launch_level_split(const GrowParams& p, const GrowBufs& b, const TreeIO& io, int d, int nsm,
-                               cudaStream_t s);
-
 // The condition kernel of a loop: before the loop (body_kernels 0) or as the
 // body's last kernel (body_kernels = the body's kernels, itself included).
 cudaError_t launch_level_loop_cond(const GrowParams& p, const GrowBufs& b, cudaGraphConditionalHandle h,
