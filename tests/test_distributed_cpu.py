@@ -86,3 +86,23 @@ def test_quantile_sample_split(n_total, sizes):
     if n_total > QUANTILE_SAMPLE:
         ref = np.random.default_rng(0).choice(n_total, QUANTILE_SAMPLE, replace=False)
         np.testing.assert_array_equal(rows, ref)
+
+
+def test_reserve_epochs_blocks_never_wrap():
+    """The exchange epochs a device-side level loop numbers from: consecutive,
+    after every epoch already handed out, never containing 0 and never
+    wrapping inside a block (every rank computes the same numbers)."""
+    from types import SimpleNamespace
+
+    from yabt_b200.distributed import ExchangeBuffers
+    x = SimpleNamespace(epoch=0)
+    assert ExchangeBuffers.next_epoch(x) == 1
+    first = ExchangeBuffers.reserve_epochs(x, 20)
+    assert first == 2 and x.epoch == 21
+    assert ExchangeBuffers.next_epoch(x) == 22
+    x.epoch = 0xFFFFFFFF - 5
+    first = ExchangeBuffers.reserve_epochs(x, 10)       # would cross 2^32: restarts at 1
+    assert first == 1 and x.epoch == 10
+    x.epoch = 0xFFFFFFFF - 12
+    first = ExchangeBuffers.reserve_epochs(x, 10)
+    assert first == 0xFFFFFFFF - 11 and first + 9 <= 0xFFFFFFFF
