@@ -34,7 +34,7 @@ import time
 
 import numpy as np
 
-HIST_TRAFFIC_PER_ALG_BYTE = 3077.9 / 1609.9   # k_hist DRAM bytes per algorithmic byte (C4 shape, ncu)
+HIST_TRAFFIC_PER_ALG_BYTE = 3000.9 / 1548.1   # k_hist DRAM bytes per algorithmic byte (C4 shape, ncu)
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
@@ -535,7 +535,7 @@ def run_ours(args):
     alg_per_launch = alg_bytes / max(hist_launches, 1)
     # DRAM traffic of k_hist per launch: one ncu capture (dram__bytes_read.sum +
     # dram__bytes_write.sum over the k_hist launches of one 2M-row C4 tree) gave
-    # 3077.9 MB against 1609.9 MB of algorithmic bytes; scaled by the same
+    # 3000.9 MB against 1548.1 MB of algorithmic bytes; scaled by the same
     # algorithmic bytes here (levels below the root read nearly the whole bin
     # matrix, so traffic grows with the rows as the algorithmic bytes do)
     traffic_per_launch = HIST_TRAFFIC_PER_ALG_BYTE * alg_per_launch if cfg == "c4" else None
