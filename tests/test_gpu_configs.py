@@ -194,3 +194,41 @@ def test_c5_slice_one_vs_rest():
             _check_root_counts(bins, gb)
         _check_trees(X, ob, gb, 5)
         _check_predictions(X, ob, gb)
+
+
+def _chain(n=30000, F=12, seed=3, chain=10):
+    """A nested target whose trees grow a long chain (about `chain` levels),
+    far past the device-side level loop's first level."""
+    rng = np.random.default_rng(seed)
+    X = rng.normal(size=(n, F)).astype(np.float32)
+    X[:, chain:][rng.random(size=(n, F - chain)) < 0.02] = np.nan
+    on = np.ones(n, dtype=bool)
+    y = np.zeros(n, dtype=np.float32)
+    for k in range(chain):
+        on &= X[:, k] > -0.3
+        y += 2.0 * on
+    return X, y + 0.01 * rng.normal(size=n).astype(np.float32)
+
+
+def test_deep_trees_in_level_loop():
+    """Trees whose deeper levels run in the device-side level loop (31 leaves,
+    the default depth limit of 64, trees about ten levels deep), with leaf
+    models and interaction steering, against the oracle booster."""
+    X, y = _chain()
+    ob, gb = _fit(X, y, "mse", 6, max_leaves=31, learning_rate=0.3, min_samples_leaf=5, levelwise=True)
+    first = gb.grower_.level_loop_start()
+    assert first > 0
+    depth = []
+    for t in ob.trees:
+        d, st = 0, [(0, 0)]
+        while st:
+            i, k = st.pop()
+            d = max(d, k)
+            if t.left[i] >= 0:
+                st += [(int(t.left[i]), k + 1), (int(t.right[i]), k + 1)]
+        depth.append(d)
+    assert max(depth) > first, depth
+    bins = _check_binning(X, ob, gb)
+    _check_root_counts(bins, gb)
+    _check_trees(X, ob, gb, 6)
+    _check_predictions(X, ob, gb)
